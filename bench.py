@@ -1,0 +1,342 @@
+#!/usr/bin/env python
+"""Benchmark of the cluster AllReduce hot path on B200 (one JSON line on rank 0).
+
+Workload (the catalogue sweep, at its AllReduce / cluster-8 point, with the
+bytes per CTA of the north-star target; configs[0]'s 16 KiB ring / recursive-doubling numbers are added
+under "single_cluster"): a grid-filled batch of independent cluster-8 AllReduce(sum) problems, f32,
+P = 64 KiB per CTA, inputs U(-1,1) (seeded). One step = one launch of the persistent batch kernel over
+the whole batch (inputs 2 GiB per GPU, far larger than the 126 MB L2, so no flush is needed).
+    value        aggregate algbw = (problems x N x P) / step time, whole job (sum over GPUs), GB/s
+    e2e          the same metric through the public API (dsmem_b200.collective) with the step's input
+                 copied from pinned host memory and its output read back inside the timed region
+    roofline     HBM: algorithmic bytes per launch = problems x N x 2P (read in, write out)
+    cpu_baseline the CPU oracle (C restatement of the reference's reference()) on a bounded sample
+--impl reference runs the reference's own CPU path (collectives/harness/main.cu reference(), compiled
+from the reference sources into oracle/_ref/) on all host cores, same metric and config.
+Multi-GPU: one process per GPU (torchrun), each GPU its own batch (weak scaling, no inter-GPU traffic).
+"""
+import argparse
+import json
+import math
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+PKG = ROOT / "h100-dsmem-collectives_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "cluster AllReduce algbw GB/s & µs vs bytes/CTA; fused RMSNorm rows/s"
+CLUSTER_N = 8
+PAYLOAD = 65536           # bytes per CTA (f32: M = 16384)
+BATCH_BYTES = 2 << 30     # input bytes per GPU per step
+HBM_FALLBACK_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--payload", type=int, default=PAYLOAD)
+    ap.add_argument("--alg", default="auto")
+    ap.add_argument("--no-extras", action="store_true", help="skip the single-cluster latency table")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d.get("hbm_gbs", HBM_FALLBACK_GBS)), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return HBM_FALLBACK_GBS, "fallback 6.65 TB/s"
+
+
+def profile_traffic(kernel_key):
+    """Per-launch DRAM bytes of the headline kernel from the committed ncu summary, or None."""
+    f = ROOT / "profiles" / "ncu_traffic.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == kernel_key and not line.startswith("#"):
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """NVML samples of SM clock and throttle reasons while the timed region runs."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+               0x80: "hw_power_brake_slowdown", 0x1: "gpu_idle"}
+
+    def __init__(self, device_index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.nv is not None:
+            self.t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def dist_setup(gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != gpus and world > 1:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE {world}")
+    return rank, world, local
+
+
+# --------------------------------------------------------------------------------------------- reference
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    cfg = {"workload": f"allreduce cluster{CLUSTER_N} {args.payload // 1024}KiB/CTA f32, host reference()",
+           "cluster_size": CLUSTER_N, "bytes_per_cta": args.payload, "dtype": "f32"}
+    m = args.payload // 4
+    exe = ROOT / "oracle" / "_ref" / f"ref_op0_N{CLUSTER_N}_M{m}_float"
+    threads = os.cpu_count() or 1
+    samples = []
+    kind = "reference"
+    if exe.exists():
+        for i in range(args.warmup + args.steps):
+            out = subprocess.run([str(exe), "bench", "0.25" if i < args.warmup else "1.0", str(threads)],
+                                 check=True, capture_output=True, text=True).stdout
+            d = json.loads(out)
+            if i >= args.warmup:
+                samples.append(d["problems"] * CLUSTER_N * args.payload / d["seconds"] / 1e9)
+        sample_desc = f"reference() of collectives/harness/main.cu on {threads} threads, 1 s per step"
+    else:
+        kind = "port"
+        threads = 1
+        samples = [oracle_rate(args.payload, seconds=1.0) for _ in range(args.steps)]
+        sample_desc = "oracle port (C), 1 thread, 1 s per step (oracle/_ref not built)"
+    v = statistics.median(samples)
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (pattern B inputs)",
+            "config": cfg,
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                             "sample": sample_desc},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def oracle_rate(payload, seconds):
+    """CPU oracle (C, single thread) on a bounded sample: GB/s of per-CTA payload."""
+    from oracle import oracle as orc
+
+    n, m, clusters = CLUSTER_N, payload // 4, 16
+    host = orc.uniform_real(orc.F32, clusters * n * m, 1, -1.0, 1.0)
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        orc.reference(orc.ALLREDUCE, orc.F32, n, m, clusters, host)
+        done += clusters
+    el = time.perf_counter() - t0
+    return done * n * payload / el / 1e9
+
+
+# --------------------------------------------------------------------------------------------- ours
+def single_cluster_latency(torch, D, reps=200):
+    """one cluster per launch, N = 8, 16 KiB/CTA f32; in-kernel %globaltimer span
+    (max exit - min entry, main.cu:344-349), median over reps, next to the reference's H100 numbers."""
+    n, p = 8, 16384
+    m = p // 4
+    res = {}
+    ref_h100 = {"ring": 9024, "recursive_doubling": 4864, "two_shot_push": 1440}
+    for name, alg in (("ring", D.Alg.RING), ("recursive_doubling", D.Alg.RECURSIVE_DOUBLING),
+                      ("two_shot_push", D.Alg.TWO_SHOT_PUSH), ("one_shot_pull", D.Alg.ONE_SHOT_PULL)):
+        tin = torch.rand(n * m, device="cuda") * 2 - 1
+        tout = torch.empty_like(tin)
+        stamps = torch.zeros(n * 32, dtype=torch.int64, device="cuda")
+        lat = []
+        for i in range(reps + 20):
+            D.collective(D.Op.ALLREDUCE, alg, tin, tout, n, p, stamps=stamps)
+            if i >= 20:
+                st = stamps.view(n, 32)
+                lat.append((st[:, 1].max() - st[:, 0].min()).item())
+        D.check()
+        med = statistics.median(lat)
+        res[name] = {"latency_ns_median": med, "algbw_GBps": round(p / med, 3),
+                     "busbw_GBps": round(p / med * 2 * (n - 1) / n, 3),
+                     "h100_reference_ns": ref_h100.get(name)}
+    return res
+
+
+def run_ours(args, rank, world, local):
+    import torch
+
+    import dsmem_b200 as D
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    n, p = CLUSTER_N, args.payload
+    m = p // 4
+    alg = D.Alg[args.alg.upper()] if args.alg.lower() != "auto" else D.Alg.AUTO
+    resolved = D.autotune_pick(D.Op.ALLREDUCE, D.Dtype.F32, n, p) if alg == D.Alg.AUTO else alg
+    problems = BATCH_BYTES // (n * p)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    tin = torch.rand(problems * n * m, device=dev, generator=g) * 2 - 1
+    tout = torch.empty_like(tin)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        D.collective(D.Op.ALLREDUCE, alg, tin, tout, n, p, stream=stream.cuda_stream)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    D.check(stream.cuda_stream)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    D.check(stream.cuda_stream)
+    ms = e0.elapsed_time(e1) / args.steps
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+        dist.barrier()
+    payload_bytes = problems * n * p                     # per GPU per step
+    value = world * payload_bytes / (ms * 1e-3) / 1e9    # GB/s, whole job
+    hbm_peak, peak_src = peaks()
+    algo_bytes = problems * n * 2 * p                    # read in + write out, one launch
+    achieved = algo_bytes / (ms * 1e-3) / 1e9
+    kernel_key = f"allreduce_{resolved.name.lower()}_N{n}_P{p}_f32"
+    traffic = profile_traffic(kernel_key)
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                "peak_source": peak_src, "algorithmic_bytes_per_launch": algo_bytes,
+                "kernel": f"batch_kernel<AR_{resolved.name}<8,float,Sum>>"}
+
+    # end to end through the public API, host buffers: H2D of the step's input, launch, D2H of its output
+    hin = torch.empty(tin.numel(), dtype=torch.float32, pin_memory=True)
+    hin.copy_(tin)
+    hout = torch.empty(tout.numel(), dtype=torch.float32, pin_memory=True)
+    e2e_steps = max(2, min(args.steps, 5))
+
+    def e2e_step():
+        tin.copy_(hin, non_blocking=True)
+        step()
+        hout.copy_(tout, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    a1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = a0.elapsed_time(a1) / e2e_steps
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+    _ = time.perf_counter() - t0
+    D.check(stream.cuda_stream)
+    e2e = {"value": round(world * payload_bytes / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+           "h2d_bytes_per_step": tin.numel() * 4, "d2h_bytes_per_step": tout.numel() * 4,
+           "ms_per_step": round(e2e_ms, 3)}
+
+    extras = {}
+    if rank == 0 and not args.no_extras:
+        extras["single_cluster"] = single_cluster_latency(torch, D)
+
+    cpu = None
+    if rank == 0 and world == 1:
+        v = oracle_rate(p, seconds=10.0)
+        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"oracle reference() restatement (C), 1 thread, 16 cluster problems of the same "
+                         f"shape repeated for 10 s"}
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic U(-1,1)",
+            "config": {"workload": f"allreduce cluster{n} {p // 1024}KiB/CTA f32, grid-filled persistent batch",
+                       "alg": resolved.name.lower(), "cluster_size": n, "bytes_per_cta": p,
+                       "problems_per_gpu": problems, "input_bytes_per_gpu": problems * n * p,
+                       "l2": "inputs 2 GiB per GPU > 126 MB L2 (no flush)", "parallelism": f"shard{world}"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+            "clocks": clocks.summary()}
+    line.update(extras)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,1551 @@
+// dsmem_b200_algos.cuh -- the DSMEM collective catalogue for B200 (sm_100a), one template per algorithm.
+//
+// Every algorithm of the reference catalogue (collectives/<op>__<alg>__<src>.cu, 29 files) is a struct
+//   template <int N, typename T, class Op> struct <Alg> {
+//     static constexpr OpKind kOp;  static constexpr int kBars;           // op and mbarriers used
+//     static constexpr bool   legal(uint32_t M);                           // N/M constraints
+//     static constexpr uint32_t smem_bytes(uint32_t M);                    // dynamic smem of one CTA
+//     static __device__ void load(Ctx&, const T* g, uint32_t M);          // HBM -> smem of this rank
+//     static __device__ void exec(Ctx&, uint32_t M);                      // the collective proper
+//     static __device__ void store(Ctx&, T* g, uint32_t M);               // smem -> HBM of this rank
+//   };
+// with the message size M (elements per rank block, MSG_ELEMS in the reference) a RUNTIME value, so one
+// instantiation serves every payload. Rounds, partners and message sizes follow the reference file named
+// in each struct's comment. Two drivers run them:
+//   * batch_kernel<A>: persistent clusters; cluster q processes problems q, q + nclusters, ... of a batch
+//     (one independent collective per problem, per-cluster offsets from %clusterid), with one entry and
+//     one exit cluster barrier per problem.
+//   * run_single<A>: the reference harness contract (one cluster per launch, collective_kernel).
+// Synchronisation differences from the reference (results identical):
+//   * Barriers that only protected buffers against the "next stage" (the reference's trailing
+//     cluster_sync inside one-shot pull, direct pulls, replicated push, hpcops' leading sync) are dropped
+//     where the driver's exit/entry cluster barrier already gives the same guarantee.
+//   * mbarrier waits are deadline-bounded (Ctx::deadline); after a time-out the CTA records the error
+//     and later waits of the launch return at once. Every CTA executes the same sequence of
+//     barrier.cluster instructions, so a time-out can never turn into a hang.
+//   * Bulk pushes check 16-B alignment and the window bounds in the issuing thread and record
+//     DSMEM_ERR_BIT_BOUNDS instead of issuing an out-of-range copy.
+// Layout of the dynamic shared-memory window: bytes [0, kBarArea) hold up to 16 mbarriers; data
+// buffers start at kD0 and are 16-B aligned (every legal M makes M*sizeof(T) a multiple of 16).
+#pragma once
+#include "dsmem_primitives.cuh"
+
+namespace dsb {
+using namespace dsmem;
+
+enum class OpKind : int { AllReduce = 0, AllGather = 1, ReduceScatter = 2, AllToAll = 3 };
+
+constexpr uint32_t kBarArea = 128;
+constexpr uint32_t kD0 = kBarArea;
+constexpr uint32_t kSmemLimit = 232448;   // 227 KiB: the per-block opt-in maximum of sm_100a
+
+__host__ __device__ constexpr bool is_pow2(int n) { return n > 0 && (n & (n - 1)) == 0; }
+__host__ __device__ constexpr int ilog2(int n) { return n <= 1 ? 0 : 1 + ilog2(n / 2); }
+
+// --------------------------------------------------------------------------- per-CTA context
+struct Ctx {
+    unsigned char* sm;                // generic pointer to the dynamic window
+    uint32_t sa;                      // its shared::cta address
+    uint32_t smem_bytes;              // bytes of the window valid in this launch
+    uint32_t rank;                    // %cluster_ctarank
+    uint32_t phase;                   // parity bit per mbarrier (bit i <-> barrier i)
+    bool dead;                        // a wait timed out: later waits do not block
+    unsigned long long wait_limit;    // ns per problem
+    unsigned long long deadline;      // %globaltimer value after which waits give up
+    unsigned* err;                    // error word (nullptr: this translation unit's dsmem_wait_error)
+    Stamps st;
+
+    __device__ __forceinline__ uint32_t bar(int i) const { return sa + 8u * (uint32_t)i; }
+    template <class U>
+    __device__ __forceinline__ U* ptr(uint32_t off) const { return reinterpret_cast<U*>(sm + off); }
+};
+
+__device__ __forceinline__ void report(Ctx& c, unsigned bits) {
+    atomicOr(c.err != nullptr ? c.err : &dsmem_wait_error, bits);
+}
+
+// Wait for the current phase of barrier i (all threads). Bounded by c.deadline.
+__device__ __forceinline__ void wait(Ctx& c, int i) {
+    const uint32_t par = (c.phase >> i) & 1u;
+    c.phase ^= 1u << i;
+    if (c.dead) return;
+    if (mbar_try_wait_parity(c.bar(i), par)) return;
+    if (!mbar_wait_parity_until(c.bar(i), par, c.deadline)) {
+        c.dead = true;
+        if ((threadIdx.x & 31) == 0) report(c, DSMEM_ERR_BIT_TIMEOUT);
+    }
+}
+
+// Checked bulk push of `bytes` from local window offset `src` to CTA `dst_rank`'s window offset `dst`,
+// completing on that CTA's barrier `bi`. One thread.
+template <int N>
+__device__ __forceinline__ void push(Ctx& c, uint32_t dst_rank, uint32_t dst, uint32_t src, uint32_t bytes, int bi) {
+    const bool ok = dst_rank < (uint32_t)N && bytes != 0u && ((dst | src | bytes) & 15u) == 0u && dst >= kD0 &&
+                    src >= kD0 && dst + bytes <= c.smem_bytes && src + bytes <= c.smem_bytes;
+    if (!ok) {
+        report(c, DSMEM_ERR_BIT_BOUNDS);
+        return;
+    }
+    bulk_push(dst_rank, c.sa + dst, c.sa + src, bytes, c.bar(bi));
+}
+
+__device__ __forceinline__ void arm(Ctx& c, int bi, uint32_t bytes) { mbar_arrive_expect_tx(c.bar(bi), bytes); }
+
+// --------------------------------------------------------------------------- 16-byte packets
+// Arithmetic on 16-byte packets of T. Multi-operand reductions accumulate in Acc (fp32 for bf16, so a
+// CTA-local reduction of k operands rounds to bf16 once).
+template <typename T, class Op>
+struct Pk;
+
+template <class Op>
+struct Pk<float, Op> {
+    struct Acc {
+        float v[4];
+    };
+    static __device__ __forceinline__ Acc open(uint4 p) {
+        return Acc{{__uint_as_float(p.x), __uint_as_float(p.y), __uint_as_float(p.z), __uint_as_float(p.w)}};
+    }
+    static __device__ __forceinline__ void add(Acc& a, uint4 p) {
+        const Op op{};
+        a.v[0] = op(a.v[0], __uint_as_float(p.x));
+        a.v[1] = op(a.v[1], __uint_as_float(p.y));
+        a.v[2] = op(a.v[2], __uint_as_float(p.z));
+        a.v[3] = op(a.v[3], __uint_as_float(p.w));
+    }
+    static __device__ __forceinline__ uint4 close(const Acc& a) {
+        return make_uint4(__float_as_uint(a.v[0]), __float_as_uint(a.v[1]), __float_as_uint(a.v[2]),
+                          __float_as_uint(a.v[3]));
+    }
+    static __device__ __forceinline__ uint4 identity() {
+        const uint32_t w = __float_as_uint(Op::template identity<float>());
+        return make_uint4(w, w, w, w);
+    }
+};
+
+template <class Op>
+struct Pk<int, Op> {
+    struct Acc {
+        int v[4];
+    };
+    static __device__ __forceinline__ Acc open(uint4 p) { return Acc{{(int)p.x, (int)p.y, (int)p.z, (int)p.w}}; }
+    static __device__ __forceinline__ void add(Acc& a, uint4 p) {
+        const Op op{};
+        a.v[0] = op(a.v[0], (int)p.x);
+        a.v[1] = op(a.v[1], (int)p.y);
+        a.v[2] = op(a.v[2], (int)p.z);
+        a.v[3] = op(a.v[3], (int)p.w);
+    }
+    static __device__ __forceinline__ uint4 close(const Acc& a) {
+        return make_uint4((uint32_t)a.v[0], (uint32_t)a.v[1], (uint32_t)a.v[2], (uint32_t)a.v[3]);
+    }
+    static __device__ __forceinline__ uint4 identity() {
+        const uint32_t w = (uint32_t)Op::template identity<int>();
+        return make_uint4(w, w, w, w);
+    }
+};
+
+template <class Op>
+struct Pk<__nv_bfloat16, Op> {
+    struct Acc {
+        float v[8];
+    };
+    static __device__ __forceinline__ float2 f2(uint32_t w) {
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+    }
+    static __device__ __forceinline__ uint32_t b2(float lo, float hi) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+    static __device__ __forceinline__ Acc open(uint4 p) {
+        Acc a;
+        const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = f2(w[k]);
+            a.v[2 * k] = f.x;
+            a.v[2 * k + 1] = f.y;
+        }
+        return a;
+    }
+    static __device__ __forceinline__ void add(Acc& a, uint4 p) {
+        const Op op{};
+        const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = f2(w[k]);
+            a.v[2 * k] = op(a.v[2 * k], f.x);
+            a.v[2 * k + 1] = op(a.v[2 * k + 1], f.y);
+        }
+    }
+    static __device__ __forceinline__ uint4 close(const Acc& a) {
+        return make_uint4(b2(a.v[0], a.v[1]), b2(a.v[2], a.v[3]), b2(a.v[4], a.v[5]), b2(a.v[6], a.v[7]));
+    }
+    static __device__ __forceinline__ uint4 identity() {
+        const float i = Op::template identity<float>();
+        const uint32_t w = b2(i, i);
+        return make_uint4(w, w, w, w);
+    }
+};
+
+template <typename T, class Op>
+__device__ __forceinline__ uint4 pk_op(uint4 a, uint4 b) {
+    auto x = Pk<T, Op>::open(a);
+    Pk<T, Op>::add(x, b);
+    return Pk<T, Op>::close(x);
+}
+
+// dst[u] = a[u] op b[u] for `bytes` bytes (window offsets; all threads).
+template <typename T, class Op>
+__device__ __forceinline__ void reduce2(const Ctx& c, uint32_t dst, uint32_t a, uint32_t b, uint32_t bytes) {
+    const uint4* pa = c.ptr<const uint4>(a);
+    const uint4* pb = c.ptr<const uint4>(b);
+    uint4* pd = c.ptr<uint4>(dst);
+    const uint32_t n = bytes >> 4;
+#pragma unroll 4
+    for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) pd[u] = pk_op<T, Op>(pa[u], pb[u]);
+}
+
+// Global <-> shared copies of whole 16-B units, all threads, streaming cache hints.
+__device__ __forceinline__ void g2s(const Ctx& c, uint32_t off, const void* g, uint32_t bytes) {
+    const uint4* src = static_cast<const uint4*>(g);
+    uint4* dst = c.ptr<uint4>(off);
+    const uint32_t n = bytes >> 4, st = blockDim.x;
+    uint32_t i = threadIdx.x;
+    for (; i + 3u * st < n; i += 4u * st) {
+        const uint4 v0 = __ldcs(src + i), v1 = __ldcs(src + i + st), v2 = __ldcs(src + i + 2u * st),
+                    v3 = __ldcs(src + i + 3u * st);
+        dst[i] = v0;
+        dst[i + st] = v1;
+        dst[i + 2u * st] = v2;
+        dst[i + 3u * st] = v3;
+    }
+    for (; i < n; i += st) dst[i] = __ldcs(src + i);
+}
+__device__ __forceinline__ void s2g(const Ctx& c, void* g, uint32_t off, uint32_t bytes) {
+    uint4* dst = static_cast<uint4*>(g);
+    const uint4* src = c.ptr<const uint4>(off);
+    const uint32_t n = bytes >> 4;
+#pragma unroll 4
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) __stcs(dst + i, src[i]);
+}
+// Local copy inside the window.
+__device__ __forceinline__ void s2s(const Ctx& c, uint32_t dst, uint32_t src, uint32_t bytes) {
+    const uint4* s = c.ptr<const uint4>(src);
+    uint4* d = c.ptr<uint4>(dst);
+    const uint32_t n = bytes >> 4;
+#pragma unroll 4
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) d[i] = s[i];
+}
+
+#define DSB_TRAITS(OPKIND, NBARS)                  \
+    static constexpr OpKind kOp = OpKind::OPKIND; \
+    static constexpr int kBars = NBARS;           \
+    static constexpr int kN = N_;                 \
+    using T = T_;                                 \
+    using Op = Op_;                               \
+    static constexpr uint32_t B = sizeof(T_);
+
+// Sum-only algorithms (hardware remote adds) test the reduction functor with this trait.
+template <class Op>
+struct IsSum {
+    static constexpr bool value = false;
+};
+template <>
+struct IsSum<Sum> {
+    static constexpr bool value = true;
+};
+
+__host__ __device__ constexpr bool mult16(uint32_t bytes) { return bytes != 0u && (bytes & 15u) == 0u; }
+__host__ __device__ constexpr bool fits(uint64_t bytes) { return bytes <= (uint64_t)kSmemLimit; }
+
+// =====================================================================================================
+//                                              ALLREDUCE
+// Per rank: in[M] -> out[M] = op over ranks.
+// =====================================================================================================
+
+// allreduce__recursive_doubling__clusterfusion.cu:27-52. log2 N rounds, stride s = 1,2,..: push the
+// running vector to (b+s) mod N's scratch, reduce into the ping-pong buffer, one cluster barrier per round.
+template <int N_, typename T_, class Op_>
+struct AR_RecursiveDoubling {
+    DSB_TRAITS(AllReduce, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 3ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, scr = kD0 + 2 * MB;
+        uint32_t cur = kD0, oth = kD0 + MB;
+        int round = 0;
+        for (int s = 1; s < N_; s <<= 1, ++round) {
+            if (threadIdx.x == 0) {
+                arm(c, 0, MB);
+                push<N_>(c, (c.rank + s) % N_, scr, cur, MB, 0);
+            }
+            wait(c, 0);
+            reduce2<T, Op>(c, oth, cur, scr, MB);   // cur may still be read by my own outgoing push
+            fence_proxy_async_smem();
+            cluster_sync();
+            const uint32_t t = cur;
+            cur = oth;
+            oth = t;
+            c.st.round(round);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, (ilog2(N_) % 2 == 0) ? kD0 : kD0 + M * B, M * B);
+    }
+};
+
+// allreduce__shift_accumulate_bulk__clusterfusion.cu:29-51 (as shipped: only N == 4 reduces correctly).
+// Rounds i = 1..N-2: push the running vector to (b+i) mod N, add what arrives from (b-i).
+template <int N_, typename T_, class Op_>
+struct AR_ShiftAccumulateBulk {
+    DSB_TRAITS(AllReduce, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return N_ == 4 && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 3ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, scr = kD0 + 2 * MB;
+        uint32_t cur = kD0, oth = kD0 + MB;
+        for (int i = 1; i < N_ - 1; ++i) {
+            if (threadIdx.x == 0) {
+                arm(c, 0, MB);
+                push<N_>(c, (c.rank + i) % N_, scr, cur, MB, 0);
+            }
+            wait(c, 0);
+            reduce2<T, Op>(c, oth, cur, scr, MB);
+            fence_proxy_async_smem();
+            cluster_sync();
+            const uint32_t t = cur;
+            cur = oth;
+            oth = t;
+            c.st.round(i - 1);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, ((N_ - 2) % 2 == 0) ? kD0 : kD0 + M * B, M * B);
+    }
+};
+
+// Remote element-wise add of one 16-byte packet of T into a peer's shared memory (fire-and-forget).
+template <typename T>
+__device__ __forceinline__ void red_add_packet(uint32_t caddr, uint4 v);
+template <>
+__device__ __forceinline__ void red_add_packet<float>(uint32_t a, uint4 v) {
+    red_cluster_add_f32(a, __uint_as_float(v.x));
+    red_cluster_add_f32(a + 4, __uint_as_float(v.y));
+    red_cluster_add_f32(a + 8, __uint_as_float(v.z));
+    red_cluster_add_f32(a + 12, __uint_as_float(v.w));
+}
+template <>
+__device__ __forceinline__ void red_add_packet<int>(uint32_t a, uint4 v) {
+    red_cluster_add_u32(a, v.x);
+    red_cluster_add_u32(a + 4, v.y);
+    red_cluster_add_u32(a + 8, v.z);
+    red_cluster_add_u32(a + 12, v.w);
+}
+template <>
+__device__ __forceinline__ void red_add_packet<__nv_bfloat16>(uint32_t a, uint4 v) {
+    red_cluster_add_bf16x2(a, v.x);
+    red_cluster_add_bf16x2(a + 4, v.y);
+    red_cluster_add_bf16x2(a + 8, v.z);
+    red_cluster_add_bf16x2(a + 12, v.w);
+}
+
+// allreduce__shift_accumulate_atomic__clusterfusion.cu:27-40 (sum only; N in {2,4}; 1 round at N = 2,
+// N-2 rounds at N = 4). Per round: snapshot the running value, barrier, remote add of the snapshot into
+// (b+i) mod N, barrier.
+template <int N_, typename T_, class Op_>
+struct AR_ShiftAccumulateAtomic {
+    DSB_TRAITS(AllReduce, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) {
+        return (N_ == 2 || N_ == 4) && mult16(M * B) && IsSum<Op_>::value;
+    }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) { g2s(c, kD0, g, M * B); }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, val = kD0, snap = kD0 + MB, n = MB >> 4;
+        constexpr int rounds = (N_ == 2) ? 1 : N_ - 2;
+        for (int i = 1; i <= rounds; ++i) {
+            s2s(c, snap, val, MB);
+            cluster_sync();   // every CTA snapshotted before any remote add lands in its `val`
+            const uint32_t peer_val = mapa(c.sa + val, (c.rank + i) % N_);
+            const uint4* sp = c.ptr<const uint4>(snap);
+            for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) red_add_packet<T>(peer_val + 16u * u, sp[u]);
+            cluster_sync();   // remote adds complete and visible
+            c.st.round(i - 1);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// allreduce__direct_replicated_push__credit.cu:26-44. Plain remote 16-B stores of my vector into
+// slot[b] of every CTA (self included), one cluster barrier, local reduction of the N slots.
+template <int N_, typename T_, class Op_>
+struct AR_DirectReplicatedPush {
+    DSB_TRAITS(AllReduce, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + (N_ + 2ull) * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) { g2s(c, kD0, g, M * B); }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, mine = kD0, slots = kD0 + MB, res = kD0 + (N_ + 1) * MB, n = MB >> 4;
+        const uint4* pm = c.ptr<const uint4>(mine);
+        for (uint32_t idx = threadIdx.x; idx < N_ * n; idx += blockDim.x) {
+            const uint32_t p = idx / n, u = idx - p * n;
+            st_cluster_v4(mapa(c.sa + slots + c.rank * MB + 16u * u, p), pm[u]);
+        }
+        cluster_sync();   // all pushed partials visible
+        c.st.round(0);
+        const uint4* ps = c.ptr<const uint4>(slots);
+        uint4* pr = c.ptr<uint4>(res);
+        for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) {
+            uint4 v[N_];
+#pragma unroll
+            for (int r = 0; r < N_; ++r) v[r] = ps[r * n + u];
+            auto a = Pk<T, Op>::open(v[0]);
+#pragma unroll
+            for (int r = 1; r < N_; ++r) Pk<T, Op>::add(a, v[r]);
+            pr[u] = Pk<T, Op>::close(a);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + (N_ + 1) * M * B, M * B);
+    }
+};
+
+// Unit helpers for the lane-group algorithm: U = uint4 (16-B packet) or a single element.
+template <typename T, class Op, typename U>
+struct Unit;
+template <typename T, class Op>
+struct Unit<T, Op, uint4> {
+    static __device__ __forceinline__ uint4 ld(uint32_t a) { return ld_cluster_v4(a); }
+    static __device__ __forceinline__ void st(uint32_t a, uint4 v) { st_cluster_v4(a, v); }
+    static __device__ __forceinline__ uint4 op(uint4 a, uint4 b) { return pk_op<T, Op>(a, b); }
+    static __device__ __forceinline__ uint4 identity() { return Pk<T, Op>::identity(); }
+    static __device__ __forceinline__ uint4 shfl_xor(uint4 v, int off, int width) {
+        return make_uint4(__shfl_xor_sync(0xffffffffu, v.x, off, width), __shfl_xor_sync(0xffffffffu, v.y, off, width),
+                          __shfl_xor_sync(0xffffffffu, v.z, off, width), __shfl_xor_sync(0xffffffffu, v.w, off, width));
+    }
+};
+template <class Op>
+struct Unit<float, Op, float> {
+    static __device__ __forceinline__ float ld(uint32_t a) { return ld_cluster_f32(a); }
+    static __device__ __forceinline__ void st(uint32_t a, float v) { st_cluster_f32(a, v); }
+    static __device__ __forceinline__ float op(float a, float b) { return Op{}(a, b); }
+    static __device__ __forceinline__ float identity() { return Op::template identity<float>(); }
+    static __device__ __forceinline__ float shfl_xor(float v, int off, int w) { return __shfl_xor_sync(0xffffffffu, v, off, w); }
+};
+template <class Op>
+struct Unit<int, Op, int> {
+    static __device__ __forceinline__ int ld(uint32_t a) { return (int)ld_cluster_u32(a); }
+    static __device__ __forceinline__ void st(uint32_t a, int v) { st_cluster_u32(a, (uint32_t)v); }
+    static __device__ __forceinline__ int op(int a, int b) { return Op{}(a, b); }
+    static __device__ __forceinline__ int identity() { return Op::template identity<int>(); }
+    static __device__ __forceinline__ int shfl_xor(int v, int off, int w) { return __shfl_xor_sync(0xffffffffu, v, off, w); }
+};
+template <class Op>
+struct Unit<__nv_bfloat16, Op, __nv_bfloat16> {
+    static __device__ __forceinline__ __nv_bfloat16 ld(uint32_t a) { return __ushort_as_bfloat16(ld_cluster_u16(a)); }
+    static __device__ __forceinline__ void st(uint32_t a, __nv_bfloat16 v) { st_cluster_u16(a, __bfloat16_as_ushort(v)); }
+    static __device__ __forceinline__ __nv_bfloat16 op(__nv_bfloat16 a, __nv_bfloat16 b) {
+        return __float2bfloat16_rn(Op{}(__bfloat162float(a), __bfloat162float(b)));
+    }
+    static __device__ __forceinline__ __nv_bfloat16 identity() {
+        return __float2bfloat16_rn(Op::template identity<float>());
+    }
+    static __device__ __forceinline__ __nv_bfloat16 shfl_xor(__nv_bfloat16 v, int off, int w) {
+        return __ushort_as_bfloat16((unsigned short)__shfl_xor_sync(0xffffffffu, (int)__bfloat16_as_ushort(v), off, w));
+    }
+};
+
+// allreduce__pull_reduce_scatter_push_allgather__hpcops.cu:27-49. CTA b owns elements [b*C, (b+1)*C),
+// C = M/N. Groups of N lanes: lane j of a group loads the owned unit from CTA j, the group reduces with
+// __shfl_xor, lane j stores the total back into CTA j. One round.
+template <int N_, typename T_, class Op_>
+struct AR_PullRsPushAg {
+    DSB_TRAITS(AllReduce, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) {
+        return (32 % N_) == 0 && M % N_ == 0 && mult16(M * B);
+    }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) { g2s(c, kD0, g, M * B); }
+    template <typename U>
+    static __device__ void run_units(Ctx& c, uint32_t units_per_rank) {
+        using X = Unit<T, Op, U>;
+        const uint32_t total = units_per_rank * N_;
+        for (uint32_t base = 0; base < total; base += blockDim.x) {   // same trip count on every thread
+            const uint32_t linear = base + threadIdx.x;
+            const bool active = linear < total;
+            const uint32_t e = c.rank * units_per_rank + (active ? linear : 0u) / N_;
+            const uint32_t peer = linear % N_;
+            const uint32_t a = mapa(c.sa + kD0 + e * (uint32_t)sizeof(U), peer);
+            U v = active ? X::ld(a) : X::identity();
+#pragma unroll
+            for (int off = N_ / 2; off > 0; off >>= 1) v = X::op(v, X::shfl_xor(v, off, N_));
+            if (active) X::st(a, v);
+        }
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t CB = (M / N_) * B;
+        if ((CB & 15u) == 0u) run_units<uint4>(c, CB >> 4);
+        else run_units<T>(c, M / N_);
+        c.st.round(0);
+        cluster_sync();   // every copy holds the total before anyone stores
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// allreduce__ring__nccl.cu:25-60. Ring reduce-scatter (N-1 steps: push chunk (b-s) to the successor's
+// scratch, add chunk (b-s-1)) then ring all-gather (N-1 steps forwarding into the same slot).
+template <int N_, typename T_, class Op_>
+struct AR_Ring {
+    DSB_TRAITS(AllReduce, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return M % N_ == 0 && mult16((M / N_) * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * M * B + (M / N_) * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t CB = (M / N_) * B, scr = kD0 + M * B, next = (c.rank + 1) % N_;
+        int round = 0;
+        for (int s = 0; s < N_ - 1; ++s, ++round) {
+            const uint32_t send_c = (c.rank + N_ - s) % N_, recv_c = (c.rank + 2 * N_ - s - 1) % N_;
+            if (threadIdx.x == 0) {
+                arm(c, 0, CB);
+                push<N_>(c, next, scr, kD0 + send_c * CB, CB, 0);
+            }
+            wait(c, 0);
+            reduce2<T, Op>(c, kD0 + recv_c * CB, kD0 + recv_c * CB, scr, CB);
+            fence_proxy_async_smem();
+            cluster_sync();   // scratch free again, updated chunk visible to the next push
+            c.st.round(round);
+        }
+        for (int s = 0; s < N_ - 1; ++s, ++round) {
+            const uint32_t send_c = (c.rank + 1 + N_ - s) % N_;
+            if (threadIdx.x == 0) {
+                arm(c, 0, CB);
+                push<N_>(c, next, kD0 + send_c * CB, kD0 + send_c * CB, CB, 0);
+            }
+            wait(c, 0);
+            cluster_sync();   // received chunk stable before it is forwarded
+            c.st.round(round);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// allreduce__rabenseifner__mpich.cu:25-67. Recursive-halving reduce-scatter with XOR partners
+// (d = N/2 .. 1), then recursive-doubling all-gather of the live ranges (d = 1 .. N/2).
+template <int N_, typename T_, class Op_>
+struct AR_Rabenseifner {
+    DSB_TRAITS(AllReduce, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) {
+        return is_pow2(N_) && M % N_ == 0 && mult16((M / N_) * B);
+    }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * M * B + (M / 2) * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t scr = kD0 + M * B;
+        uint32_t lo = 0, hi = M;
+        int round = 0;
+        for (int d = N_ / 2; d >= 1; d >>= 1, ++round) {
+            const uint32_t partner = c.rank ^ (uint32_t)d, mid = (lo + hi) / 2, len = hi - mid;
+            const bool upper = (c.rank & (uint32_t)d) != 0u;
+            const uint32_t send_lo = upper ? lo : mid, keep_lo = upper ? mid : lo;
+            if (threadIdx.x == 0) {
+                arm(c, 0, len * B);
+                push<N_>(c, partner, scr, kD0 + send_lo * B, len * B, 0);
+            }
+            wait(c, 0);
+            reduce2<T, Op>(c, kD0 + keep_lo * B, kD0 + keep_lo * B, scr, len * B);
+            lo = keep_lo;
+            hi = keep_lo + len;
+            fence_proxy_async_smem();
+            cluster_sync();
+            c.st.round(round);
+        }
+        for (int d = 1; d < N_; d <<= 1, ++round) {
+            const uint32_t partner = c.rank ^ (uint32_t)d, len = hi - lo;
+            if (threadIdx.x == 0) {
+                arm(c, 0, len * B);
+                push<N_>(c, partner, kD0 + lo * B, kD0 + lo * B, len * B, 0);
+            }
+            wait(c, 0);
+            if (c.rank & (uint32_t)d) lo -= len;
+            else hi += len;
+            cluster_sync();
+            c.st.round(round);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// allreduce__one_shot_pull__trtllm.cu:22-44. Every CTA loads all N vectors (16-B ld.shared::cluster,
+// all N loads of a packet in flight together) and reduces in rank order, so every CTA ends with the
+// same bits.
+template <int N_, typename T_, class Op_>
+struct AR_OneShotPull {
+    DSB_TRAITS(AllReduce, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) { g2s(c, kD0, g, M * B); }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, n = MB >> 4;
+        uint4* pr = c.ptr<uint4>(kD0 + MB);
+        uint32_t base[N_];
+#pragma unroll
+        for (int r = 0; r < N_; ++r) base[r] = mapa(c.sa + kD0, r);
+        for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) {
+            uint4 v[N_];
+#pragma unroll
+            for (int r = 0; r < N_; ++r) v[r] = ld_cluster_v4(base[r] + 16u * u);
+            auto a = Pk<T, Op>::open(v[0]);
+#pragma unroll
+            for (int r = 1; r < N_; ++r) Pk<T, Op>::add(a, v[r]);
+            pr[u] = Pk<T, Op>::close(a);
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + M * B, M * B);
+    }
+};
+
+// allreduce__two_shot_push__trtllm.cu:23-59. Shot 1: bulk-push chunk j into slot[b] of CTA j for all
+// j != b (one aggregate barrier), reduce my chunk. Shot 2: bulk-push my reduced chunk into position b
+// of every peer. No cluster barrier between the shots.
+template <int N_, typename T_, class Op_>
+struct AR_TwoShotPush {
+    DSB_TRAITS(AllReduce, 2)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return M % N_ == 0 && mult16((M / N_) * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t CB = (M / N_) * B, slots = kD0 + M * B, n = CB >> 4;
+        if (threadIdx.x == 0) {
+            arm(c, 0, (N_ - 1) * CB);
+            for (uint32_t j = 1; j < (uint32_t)N_; ++j) {
+                const uint32_t dst = (c.rank + j) % N_;
+                push<N_>(c, dst, slots + c.rank * CB, kD0 + dst * CB, CB, 0);
+            }
+        }
+        wait(c, 0);   // every peer's partial of my chunk has landed (so their reads of it are done)
+        uint4* mine = c.ptr<uint4>(kD0 + c.rank * CB);
+        const uint4* ps = c.ptr<const uint4>(slots);
+        for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) {
+            uint4 v[N_];
+#pragma unroll
+            for (int r = 0; r < N_; ++r) v[r] = (r == (int)c.rank) ? mine[u] : ps[r * n + u];
+            auto a = Pk<T, Op>::open(v[0]);
+#pragma unroll
+            for (int r = 1; r < N_; ++r) Pk<T, Op>::add(a, v[r]);
+            mine[u] = Pk<T, Op>::close(a);
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        c.st.round(0);
+        if (threadIdx.x == 0) {
+            arm(c, 1, (N_ - 1) * CB);
+            for (uint32_t j = 1; j < (uint32_t)N_; ++j) {
+                const uint32_t dst = (c.rank + j) % N_;
+                push<N_>(c, dst, kD0 + c.rank * CB, kD0 + c.rank * CB, CB, 1);
+            }
+        }
+        wait(c, 1);
+        c.st.round(1);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// allreduce__reduce_bcast_binomial__mpich.cu:23-61. Binomial reduce to rank 0 (d = 1,2,..: a rank with
+// bit d set pushes its partial to b-d and drops out), then binomial broadcast (d = N/2 .. 1).
+template <int N_, typename T_, class Op_>
+struct AR_ReduceBcastBinomial {
+    DSB_TRAITS(AllReduce, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, scr = kD0 + MB;
+        int round = 0;
+        bool active = true;
+        for (int d = 1; d < N_; d <<= 1, ++round) {
+            if (active) {
+                if (c.rank & (uint32_t)d) {
+                    if (threadIdx.x == 0) push<N_>(c, c.rank - d, scr, kD0, MB, 0);
+                    active = false;
+                } else {
+                    if (threadIdx.x == 0) arm(c, 0, MB);
+                    wait(c, 0);
+                    reduce2<T, Op>(c, kD0, kD0, scr, MB);
+                    fence_proxy_async_smem();
+                }
+            }
+            cluster_sync();
+            c.st.round(round);
+        }
+        for (int d = N_ / 2; d >= 1; d >>= 1, ++round) {
+            const uint32_t m = c.rank % (2u * d);
+            if (m == 0u) {
+                if (threadIdx.x == 0) push<N_>(c, c.rank + d, kD0, kD0, MB, 0);
+            } else if (m == (uint32_t)d) {
+                if (threadIdx.x == 0) arm(c, 0, MB);
+                wait(c, 0);
+            }
+            cluster_sync();
+            c.st.round(round);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// allreduce__atomic_all_push__generic.cu:25-41 (sum only). Accumulator = own input; every element is
+// added into every peer's accumulator with red.shared::cluster.add; one cluster barrier.
+template <int N_, typename T_, class Op_>
+struct AR_AtomicAllPush {
+    DSB_TRAITS(AllReduce, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B) && IsSum<Op_>::value; }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        __syncthreads();
+        s2s(c, kD0 + M * B, kD0, M * B);   // accumulator starts as my own vector
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, n = MB >> 4;
+        const uint4* pm = c.ptr<const uint4>(kD0);
+        for (uint32_t idx = threadIdx.x; idx < (N_ - 1) * n; idx += blockDim.x) {
+            const uint32_t k = idx / n, u = idx - k * n;
+            const uint32_t peer = (c.rank + 1 + k) % N_;
+            red_add_packet<T>(mapa(c.sa + kD0 + MB + 16u * u, peer), pm[u]);
+        }
+        c.st.round(0);
+        cluster_sync();   // all remote adds performed and visible
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + M * B, M * B);
+    }
+};
+
+template <int N>
+struct Grid2D {
+    static constexpr int R = (N >= 16) ? 4 : (N >= 4 ? 2 : 1);
+    static constexpr int C = N / R;
+};
+
+// allreduce__2d_mesh__generic.cu:27-96. R x C grid (16 = 4x4, 8 = 2x4, 4 = 2x2, 2 = 1x2): row
+// reduce-scatter push, column all-reduce push of the row partial, row all-gather push. No cluster
+// barrier inside; one aggregate mbarrier per phase.
+template <int N_, typename T_, class Op_>
+struct AR_Mesh2D {
+    DSB_TRAITS(AllReduce, 3)
+    static constexpr int R = Grid2D<N_>::R, C = Grid2D<N_>::C;
+    __host__ __device__ static constexpr bool legal(uint32_t M) {
+        return R * C == N_ && M % C == 0 && mult16((M / C) * B);
+    }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) {
+        return kD0 + 1ull * M * B + (C + R + 1ull) * (M / C) * B;
+    }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t KB = (M / C) * B, n = KB >> 4;
+        const uint32_t buf = kD0, rs = kD0 + M * B, cs = rs + C * KB, chunk = cs + R * KB;
+        const uint32_t row = c.rank / C, col = c.rank % C;
+        // phase 1: row reduce-scatter
+        if (threadIdx.x == 0) {
+            arm(c, 0, (C - 1) * KB);
+            for (uint32_t j = 1; j < (uint32_t)C; ++j) {
+                const uint32_t dc = (col + j) % C;
+                push<N_>(c, row * C + dc, rs + col * KB, buf + dc * KB, KB, 0);
+            }
+        }
+        wait(c, 0);
+        {
+            uint4* pb = c.ptr<uint4>(buf + col * KB);
+            const uint4* pr = c.ptr<const uint4>(rs);
+            for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) {
+                auto a = Pk<T, Op>::open(pb[u]);
+#pragma unroll
+                for (int k = 0; k < C; ++k)
+                    if (k != (int)col) Pk<T, Op>::add(a, pr[k * n + u]);
+                pb[u] = Pk<T, Op>::close(a);
+            }
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        c.st.round(0);
+        // phase 2: column all-reduce of chunk `col`
+        if (R > 1) {
+            if (threadIdx.x == 0) {
+                arm(c, 1, (R - 1) * KB);
+                for (uint32_t j = 1; j < (uint32_t)R; ++j) {
+                    const uint32_t dr = (row + j) % R;
+                    push<N_>(c, dr * C + col, cs + row * KB, buf + col * KB, KB, 1);
+                }
+            }
+            wait(c, 1);
+            const uint4* pb = c.ptr<const uint4>(buf + col * KB);
+            const uint4* pc = c.ptr<const uint4>(cs);
+            uint4* pk = c.ptr<uint4>(chunk);
+            for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) {   // my column push may still read buf
+                auto a = Pk<T, Op>::open(pb[u]);
+#pragma unroll
+                for (int k = 0; k < R; ++k)
+                    if (k != (int)row) Pk<T, Op>::add(a, pc[k * n + u]);
+                pk[u] = Pk<T, Op>::close(a);
+            }
+        } else {
+            s2s(c, chunk, buf + col * KB, KB);
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        c.st.round(1);
+        // phase 3: row all-gather
+        if (threadIdx.x == 0) {
+            arm(c, 2, (C - 1) * KB);
+            for (uint32_t j = 1; j < (uint32_t)C; ++j) {
+                const uint32_t dst = row * C + (col + j) % C;
+                push<N_>(c, dst, buf + col * KB, chunk, KB, 2);
+            }
+        }
+        wait(c, 2);
+        c.st.round(2);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        const uint32_t KB = (M / C) * B, nk = KB >> 4, n = (M * B) >> 4, col = c.rank % C;
+        const uint4* pb = c.ptr<const uint4>(kD0);
+        const uint4* pk = c.ptr<const uint4>(kD0 + M * B + (C + R) * KB);
+        uint4* dst = reinterpret_cast<uint4*>(g);
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint32_t k = i / nk;
+            __stcs(dst + i, (k == col) ? pk[i - k * nk] : pb[i]);
+        }
+    }
+};
+
+// =====================================================================================================
+//                                              ALLGATHER
+// Per rank: in[M] -> out[N*M], slot r = rank r's vector.
+// =====================================================================================================
+
+// Store a rotated gather buffer: slot k of D holds rank (b + sign*k) mod N.
+template <int N, int SIGN>
+__device__ __forceinline__ void store_rotated(const Ctx& c, void* g, uint32_t MB) {
+    const uint32_t nb = MB >> 4, n = N * nb;
+    const uint4* D = c.ptr<const uint4>(kD0);
+    uint4* o = static_cast<uint4*>(g);
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const uint32_t k = i / nb, e = i - k * nb;
+        const uint32_t r = (SIGN > 0) ? (c.rank + k) % N : (c.rank + N - k) % N;
+        __stcs(o + r * nb + e, D[i]);
+    }
+}
+
+// allgather__recursive_doubling__clusterfusion.cu:22-42 (+ un-rotation :66-72). Own data in slot 0;
+// stride s = 1,2,..: push D[0:s) to (b+s) mod N's D[s:2s). Slot k ends holding rank (b-k) mod N.
+template <int N_, typename T_, class Op_>
+struct AG_RecursiveDoubling {
+    DSB_TRAITS(AllGather, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B;
+        int round = 0;
+        for (int s = 1; s < N_; s <<= 1, ++round) {
+            const uint32_t bytes = s * MB;
+            if (threadIdx.x == 0) {
+                arm(c, 0, bytes);
+                push<N_>(c, (c.rank + s) % N_, kD0 + bytes, kD0, bytes, 0);
+            }
+            wait(c, 0);
+            cluster_sync();
+            c.st.round(round);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        store_rotated<N_, -1>(c, g, M * B);
+    }
+};
+
+// allgather__direct_shift__clusterfusion.cu:24-43. Own data in slot b. N-1 rounds; each round
+// re-initialises the mbarrier (inval + init), barrier, pushes slot b to (b+i) mod N, waits, barrier.
+template <int N_, typename T_, class Op_>
+struct AG_DirectShift {
+    DSB_TRAITS(AllGather, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0 + c.rank * M * B, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, seg = kD0 + c.rank * MB;
+        for (int i = 1; i < N_; ++i) {
+            if (threadIdx.x == 0) {
+                mbar_inval(c.bar(0));
+                mbar_init(c.bar(0), 1);
+                fence_mbar_init();
+                arm(c, 0, MB);
+            }
+            c.phase &= ~1u;   // a fresh barrier starts in phase 0
+            cluster_sync();   // re-initialised everywhere before anyone pushes
+            if (threadIdx.x == 0) push<N_>(c, (c.rank + i) % N_, seg, seg, MB, 0);
+            wait(c, 0);
+            cluster_sync();
+            c.st.round(i - 1);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, N_ * M * B);
+    }
+};
+
+// allgather__direct_replicated_push__credit.cu:20-29. Plain remote 16-B stores of my vector into
+// slot[b] of every CTA (self included), one cluster barrier.
+template <int N_, typename T_, class Op_>
+struct AG_DirectReplicatedPush {
+    DSB_TRAITS(AllGather, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + (N_ + 1ull) * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) { g2s(c, kD0, g, M * B); }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, n = MB >> 4, slots = kD0 + MB;
+        const uint4* pm = c.ptr<const uint4>(kD0);
+        for (uint32_t idx = threadIdx.x; idx < N_ * n; idx += blockDim.x) {
+            const uint32_t p = idx / n, u = idx - p * n;
+            st_cluster_v4(mapa(c.sa + slots + c.rank * MB + 16u * u, p), pm[u]);
+        }
+        cluster_sync();
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + M * B, N_ * M * B);
+    }
+};
+
+// allgather__ring__nccl.cu:19-36. Own data in slot b; step s forwards slot (b-s) to the successor's
+// same slot. N-1 steps.
+template <int N_, typename T_, class Op_>
+struct AG_Ring {
+    DSB_TRAITS(AllGather, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0 + c.rank * M * B, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, next = (c.rank + 1) % N_;
+        for (int s = 0; s < N_ - 1; ++s) {
+            const uint32_t slot = (c.rank + N_ - s) % N_;
+            if (threadIdx.x == 0) {
+                arm(c, 0, MB);
+                push<N_>(c, next, kD0 + slot * MB, kD0 + slot * MB, MB, 0);
+            }
+            wait(c, 0);
+            cluster_sync();
+            c.st.round(s);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, N_ * M * B);
+    }
+};
+
+// allgather__bruck__mpich.cu:22-41 (+ un-rotation :66-70). Own data in slot 0; d = 1,2,4..: send the
+// first min(d, N-d) slots to (b-d) mod N, which stores them at slots [d, d+cnt). Slot k ends holding
+// rank (b+k) mod N. Any N.
+template <int N_, typename T_, class Op_>
+struct AG_Bruck {
+    DSB_TRAITS(AllGather, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B;
+        int round = 0;
+        for (int d = 1; d < N_; d <<= 1, ++round) {
+            const uint32_t cnt = (d < N_ - d) ? d : N_ - d, bytes = cnt * MB;
+            if (threadIdx.x == 0) {
+                arm(c, 0, bytes);
+                push<N_>(c, (c.rank + N_ - d) % N_, kD0 + d * MB, kD0, bytes, 0);
+            }
+            wait(c, 0);
+            cluster_sync();
+            c.st.round(round);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        store_rotated<N_, +1>(c, g, M * B);
+    }
+};
+
+// allgather__direct_pull__generic.cu:17-33. Every CTA copies slot r straight out of CTA r's input
+// with 16-B ld.shared::cluster (own slot copied locally).
+template <int N_, typename T_, class Op_>
+struct AG_DirectPull {
+    DSB_TRAITS(AllGather, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + (N_ + 1ull) * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) { g2s(c, kD0, g, M * B); }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, n = MB >> 4;
+        const uint4* pm = c.ptr<const uint4>(kD0);
+        uint4* D = c.ptr<uint4>(kD0 + MB);
+        for (uint32_t idx = threadIdx.x; idx < N_ * n; idx += blockDim.x) {
+            const uint32_t r = idx / n, u = idx - r * n;
+            D[idx] = (r == c.rank) ? pm[u] : ld_cluster_v4(mapa(c.sa + kD0 + 16u * u, r));
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + M * B, N_ * M * B);
+    }
+};
+
+// allgather__gather_bcast_binomial__mpich.cu:24-57. Binomial gather to rank 0 (a rank with bit d set
+// sends its d accumulated slots to b-d's slots [d, 2d)), then binomial broadcast of all N slots.
+template <int N_, typename T_, class Op_>
+struct AG_GatherBcastBinomial {
+    DSB_TRAITS(AllGather, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B;
+        int round = 0;
+        bool active = true;
+        for (int d = 1; d < N_; d <<= 1, ++round) {
+            if (active) {
+                if (c.rank & (uint32_t)d) {
+                    if (threadIdx.x == 0) push<N_>(c, c.rank - d, kD0 + d * MB, kD0, d * MB, 0);
+                    active = false;
+                } else {
+                    if (threadIdx.x == 0) arm(c, 0, d * MB);
+                    wait(c, 0);
+                }
+            }
+            cluster_sync();
+            c.st.round(round);
+        }
+        for (int d = N_ / 2; d >= 1; d >>= 1, ++round) {
+            const uint32_t m = c.rank % (2u * d);
+            if (m == 0u) {
+                if (threadIdx.x == 0) push<N_>(c, c.rank + d, kD0, kD0, N_ * MB, 0);
+            } else if (m == (uint32_t)d) {
+                if (threadIdx.x == 0) arm(c, 0, N_ * MB);
+                wait(c, 0);
+            }
+            cluster_sync();
+            c.st.round(round);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, N_ * M * B);
+    }
+};
+
+// =====================================================================================================
+//                                            REDUCESCATTER
+// Per rank: in[N*M] (chunk j for rank j) -> out[M] = op over ranks of chunk b.
+// =====================================================================================================
+
+// reducescatter__ring__nccl.cu:18-37. Step s pushes the partial of chunk (b-s-1) to the successor's
+// scratch and adds the received partial into chunk (b-s-2); chunk b completes on b.
+template <int N_, typename T_, class Op_>
+struct RS_Ring {
+    DSB_TRAITS(ReduceScatter, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + (N_ + 1ull) * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, N_ * M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, scr = kD0 + N_ * MB, next = (c.rank + 1) % N_;
+        for (int s = 0; s < N_ - 1; ++s) {
+            const uint32_t send_c = (c.rank + 2 * N_ - s - 1) % N_, recv_c = (c.rank + 2 * N_ - s - 2) % N_;
+            if (threadIdx.x == 0) {
+                arm(c, 0, MB);
+                push<N_>(c, next, scr, kD0 + send_c * MB, MB, 0);
+            }
+            wait(c, 0);
+            reduce2<T, Op>(c, kD0 + recv_c * MB, kD0 + recv_c * MB, scr, MB);
+            fence_proxy_async_smem();
+            cluster_sync();
+            c.st.round(s);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + c.rank * M * B, M * B);
+    }
+};
+
+// reducescatter__recursive_halving__mpich.cu:19-44. XOR halving over the N*M buffer; the live range
+// ends as chunk b.
+template <int N_, typename T_, class Op_>
+struct RS_RecursiveHalving {
+    DSB_TRAITS(ReduceScatter, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) {
+        return kD0 + 1ull * N_ * M * B + (N_ / 2ull) * M * B;
+    }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, N_ * M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t scr = kD0 + N_ * M * B;
+        uint32_t lo = 0, hi = N_ * M;
+        int round = 0;
+        for (int d = N_ / 2; d >= 1; d >>= 1, ++round) {
+            const uint32_t partner = c.rank ^ (uint32_t)d, mid = (lo + hi) / 2, len = hi - mid;
+            const bool upper = (c.rank & (uint32_t)d) != 0u;
+            const uint32_t send_lo = upper ? lo : mid, keep_lo = upper ? mid : lo;
+            if (threadIdx.x == 0) {
+                arm(c, 0, len * B);
+                push<N_>(c, partner, scr, kD0 + send_lo * B, len * B, 0);
+            }
+            wait(c, 0);
+            reduce2<T, Op>(c, kD0 + keep_lo * B, kD0 + keep_lo * B, scr, len * B);
+            lo = keep_lo;
+            hi = keep_lo + len;
+            fence_proxy_async_smem();
+            cluster_sync();
+            c.st.round(round);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + c.rank * M * B, M * B);
+    }
+};
+
+// reducescatter__direct_push__generic.cu:19-40. N-1 bulk pushes of chunk j into slot[b] of CTA j,
+// one aggregate barrier, local reduction.
+template <int N_, typename T_, class Op_>
+struct RS_DirectPush {
+    DSB_TRAITS(ReduceScatter, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + (2ull * N_ + 1) * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, N_ * M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, n = MB >> 4, slots = kD0 + N_ * MB, res = slots + N_ * MB;
+        if (threadIdx.x == 0) {
+            arm(c, 0, (N_ - 1) * MB);
+            for (uint32_t j = 1; j < (uint32_t)N_; ++j) {
+                const uint32_t dst = (c.rank + j) % N_;
+                push<N_>(c, dst, slots + c.rank * MB, kD0 + dst * MB, MB, 0);
+            }
+        }
+        wait(c, 0);
+        const uint4* mine = c.ptr<const uint4>(kD0 + c.rank * MB);
+        const uint4* ps = c.ptr<const uint4>(slots);
+        uint4* pr = c.ptr<uint4>(res);
+        for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) {
+            uint4 v[N_];
+#pragma unroll
+            for (int r = 0; r < N_; ++r) v[r] = (r == (int)c.rank) ? mine[u] : ps[r * n + u];
+            auto a = Pk<T, Op>::open(v[0]);
+#pragma unroll
+            for (int r = 1; r < N_; ++r) Pk<T, Op>::add(a, v[r]);
+            pr[u] = Pk<T, Op>::close(a);
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + 2 * N_ * M * B, M * B);
+    }
+};
+
+// reducescatter__direct_pull__generic.cu:16-39. 16-B remote loads of chunk b from all N CTAs.
+template <int N_, typename T_, class Op_>
+struct RS_DirectPull {
+    DSB_TRAITS(ReduceScatter, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + (N_ + 1ull) * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) { g2s(c, kD0, g, N_ * M * B); }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, n = MB >> 4;
+        uint4* pr = c.ptr<uint4>(kD0 + N_ * MB);
+        uint32_t base[N_];
+#pragma unroll
+        for (int r = 0; r < N_; ++r) base[r] = mapa(c.sa + kD0 + c.rank * MB, r);
+        for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) {
+            uint4 v[N_];
+#pragma unroll
+            for (int r = 0; r < N_; ++r) v[r] = ld_cluster_v4(base[r] + 16u * u);
+            auto a = Pk<T, Op>::open(v[0]);
+#pragma unroll
+            for (int r = 1; r < N_; ++r) Pk<T, Op>::add(a, v[r]);
+            pr[u] = Pk<T, Op>::close(a);
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + N_ * M * B, M * B);
+    }
+};
+
+// =====================================================================================================
+//                                              ALLTOALL
+// Per rank: in[N*M] (chunk j for rank j) -> out[N*M], slot r = rank r's chunk b.
+// =====================================================================================================
+
+// alltoall__pairwise_exchange__fa4.cu:28-44 (N = 2). The sender arms the RECEIVER's mbarrier with a
+// remote arrive.expect_tx, then one bulk push of the half the peer owns.
+template <int N_, typename T_, class Op_>
+struct A2A_PairwiseExchange {
+    DSB_TRAITS(AllToAll, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return N_ == 2 && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 3ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, 2 * M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, peer = c.rank ^ 1u;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx_remote(c.bar(0), peer, MB);
+            push<N_>(c, peer, kD0 + 2 * MB, kD0 + peer * MB, MB, 0);
+        }
+        wait(c, 0);
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        const uint32_t MB = M * B;
+        s2g(c, g + c.rank * M, kD0 + c.rank * MB, MB);
+        s2g(c, g + (c.rank ^ 1u) * M, kD0 + 2 * MB, MB);
+    }
+};
+
+// alltoall__direct_push__generic.cu:17-33. N-1 bulk pushes (chunk j -> CTA j's recv[b]), one aggregate
+// barrier; own chunk copied locally.
+template <int N_, typename T_, class Op_>
+struct A2A_DirectPush {
+    DSB_TRAITS(AllToAll, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, N_ * M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, recv = kD0 + N_ * MB;
+        if (threadIdx.x == 0) {
+            arm(c, 0, (N_ - 1) * MB);
+            for (uint32_t j = 1; j < (uint32_t)N_; ++j) {
+                const uint32_t dst = (c.rank + j) % N_;
+                push<N_>(c, dst, recv + c.rank * MB, kD0 + dst * MB, MB, 0);
+            }
+        }
+        s2s(c, recv + c.rank * MB, kD0 + c.rank * MB, MB);
+        wait(c, 0);
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + N_ * M * B, N_ * M * B);
+    }
+};
+
+// alltoall__pairwise_xor__mpich.cu:19-38. Round i: partner b^i, one push + wait + cluster barrier.
+template <int N_, typename T_, class Op_>
+struct A2A_PairwiseXor {
+    DSB_TRAITS(AllToAll, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, N_ * M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, recv = kD0 + N_ * MB;
+        s2s(c, recv + c.rank * MB, kD0 + c.rank * MB, MB);
+        for (int i = 1; i < N_; ++i) {
+            const uint32_t p = c.rank ^ (uint32_t)i;
+            if (threadIdx.x == 0) {
+                arm(c, 0, MB);
+                push<N_>(c, p, recv + c.rank * MB, kD0 + p * MB, MB, 0);
+            }
+            wait(c, 0);
+            cluster_sync();
+            c.st.round(i - 1);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + N_ * M * B, N_ * M * B);
+    }
+};
+
+// alltoall__shift__generic.cu:19-37. Round i: push chunk (b+i) to CTA b+i, receive from b-i.
+template <int N_, typename T_, class Op_>
+struct A2A_Shift {
+    DSB_TRAITS(AllToAll, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, N_ * M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, recv = kD0 + N_ * MB;
+        s2s(c, recv + c.rank * MB, kD0 + c.rank * MB, MB);
+        for (int i = 1; i < N_; ++i) {
+            const uint32_t dst = (c.rank + i) % N_;
+            if (threadIdx.x == 0) {
+                arm(c, 0, MB);
+                push<N_>(c, dst, recv + c.rank * MB, kD0 + dst * MB, MB, 0);
+            }
+            wait(c, 0);
+            cluster_sync();
+            c.st.round(i - 1);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + N_ * M * B, N_ * M * B);
+    }
+};
+
+// alltoall__bruck__mpich.cu:24-56 (rotations :75-94). Load rotated (position i holds the chunk for rank
+// (b+i) mod N); round d sends the N/2 blocks whose position has bit d set to (b+d) mod N's staging
+// area, barrier, copy back, barrier; store with the inverse rotation.
+template <int N_, typename T_, class Op_>
+struct A2A_Bruck {
+    DSB_TRAITS(AllToAll, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) {
+        return kD0 + 1ull * N_ * M * B + (N_ / 2ull) * M * B;
+    }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        const uint32_t nb = (M * B) >> 4, n = N_ * nb;
+        const uint4* src = reinterpret_cast<const uint4*>(g);
+        uint4* D = c.ptr<uint4>(kD0);
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint32_t j = i / nb, e = i - j * nb;
+            D[((j + N_ - c.rank) % N_) * nb + e] = __ldcs(src + i);
+        }
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, nb = MB >> 4, tmp = kD0 + N_ * MB;
+        int round = 0;
+        for (int d = 1; d < N_; d <<= 1, ++round) {
+            const uint32_t to = (c.rank + d) % N_;
+            if (threadIdx.x == 0) {
+                arm(c, 0, (N_ / 2) * MB);
+                uint32_t s = 0;
+                for (uint32_t pos = 0; pos < (uint32_t)N_; ++pos)
+                    if (pos & (uint32_t)d) {
+                        push<N_>(c, to, tmp + s * MB, kD0 + pos * MB, MB, 0);
+                        ++s;
+                    }
+            }
+            wait(c, 0);
+            cluster_sync();   // my outgoing blocks were read: they may be overwritten
+            const uint4* pt = c.ptr<const uint4>(tmp);
+            uint4* D = c.ptr<uint4>(kD0);
+            for (uint32_t i = threadIdx.x; i < (N_ / 2) * nb; i += blockDim.x) {
+                const uint32_t s = i / nb, e = i - s * nb;
+                const uint32_t pos = (s / d) * 2u * d + d + (s % d);   // s-th position with bit d set
+                D[pos * nb + e] = pt[i];
+            }
+            fence_proxy_async_smem();
+            cluster_sync();   // staging free and D stable before the next round's pushes
+            c.st.round(round);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        const uint32_t nb = (M * B) >> 4, n = N_ * nb;
+        const uint4* D = c.ptr<const uint4>(kD0);
+        uint4* o = reinterpret_cast<uint4*>(g);
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint32_t pos = i / nb, e = i - pos * nb;
+            __stcs(o + ((c.rank + N_ - pos) % N_) * nb + e, D[i]);
+        }
+    }
+};
+
+// alltoall__direct_pull__generic.cu:16-31. 16-B remote loads of chunk b from every peer's send buffer.
+template <int N_, typename T_, class Op_>
+struct A2A_DirectPull {
+    DSB_TRAITS(AllToAll, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) { g2s(c, kD0, g, N_ * M * B); }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, nb = MB >> 4;
+        const uint4* mine = c.ptr<const uint4>(kD0 + c.rank * MB);
+        uint4* recv = c.ptr<uint4>(kD0 + N_ * MB);
+        const uint32_t my_chunk = c.sa + kD0 + c.rank * MB;
+        for (uint32_t idx = threadIdx.x; idx < N_ * nb; idx += blockDim.x) {
+            const uint32_t r = idx / nb, u = idx - r * nb;
+            recv[idx] = (r == c.rank) ? mine[u] : ld_cluster_v4(mapa(my_chunk + 16u * u, r));
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + N_ * M * B, N_ * M * B);
+    }
+};
+
+// --------------------------------------------------------------------------- element counts per rank
+template <class A>
+__host__ __device__ constexpr uint64_t in_elems_per_rank(uint32_t M) {
+    return (A::kOp == OpKind::AllReduce || A::kOp == OpKind::AllGather) ? (uint64_t)M : (uint64_t)A::kN * M;
+}
+template <class A>
+__host__ __device__ constexpr uint64_t out_elems_per_rank(uint32_t M) {
+    return (A::kOp == OpKind::AllReduce || A::kOp == OpKind::ReduceScatter) ? (uint64_t)M : (uint64_t)A::kN * M;
+}
+
+// --------------------------------------------------------------------------- drivers
+struct BatchArgs {
+    const void* in;
+    void* out;
+    long long num_problems;           // independent cluster problems in the batch
+    unsigned long long* stamps;       // nullable: [num_problems][N][kStamps]
+    unsigned* smid;                   // nullable: [num_problems][N]
+    unsigned* err;                    // error word (device memory)
+    unsigned long long wait_limit_ns; // per problem
+    uint32_t M;                       // elements per rank block
+    uint32_t smem_bytes;              // dynamic shared memory of the launch
+};
+
+__device__ __forceinline__ void ctx_init(Ctx& c, uint32_t smem_bytes, unsigned* err, unsigned long long limit) {
+    c.sm = dyn_smem_raw;
+    c.sa = smem_u32(dyn_smem_raw);
+    c.smem_bytes = smem_bytes;
+    c.rank = cluster_rank();
+    c.phase = 0u;
+    c.dead = false;
+    c.wait_limit = limit;
+    c.deadline = 0ull;
+    c.err = err;
+    c.st.base = nullptr;
+}
+
+template <class A>
+__device__ __forceinline__ void init_bars(Ctx& c) {
+    if (A::kBars > 0 && threadIdx.x == 0) {
+        for (int i = 0; i < A::kBars; ++i) mbar_init(c.bar(i), 1);
+        fence_mbar_init();
+    }
+}
+
+// Persistent batch driver: grid = (#resident clusters) x N CTAs, cluster dims (N,1,1).
+template <class A>
+__global__ void __launch_bounds__(256) batch_kernel(const BatchArgs a) {
+    using T = typename A::T;
+    constexpr int N = A::kN;
+    Ctx c;
+    ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
+    init_bars<A>(c);
+    const uint64_t in_r = in_elems_per_rank<A>(a.M), out_r = out_elems_per_rank<A>(a.M);
+    const long long step = (long long)num_clusters();
+    for (long long p = (long long)cluster_id(); p < a.num_problems; p += step) {
+        const uint64_t slot = (uint64_t)p * N + c.rank;
+        c.deadline = globaltimer() + c.wait_limit;
+        c.st.base = a.stamps != nullptr ? a.stamps + slot * kStamps : nullptr;
+        A::load(c, static_cast<const T*>(a.in) + slot * in_r, a.M);
+        if (a.smid != nullptr && threadIdx.x == 0) a.smid[slot] = smid();
+        cluster_sync();   // entry: inputs loaded, barriers initialised, previous problem fully retired
+        c.st.mark(0);
+        A::exec(c, a.M);
+        c.st.mark(1);
+        A::store(c, static_cast<T*>(a.out) + slot * out_r, a.M);
+        cluster_sync();   // exit: no peer still reads or writes my window for this problem
+    }
+}
+
+// Reference harness contract (collectives/harness/main.cu): one cluster, compile-time M.
+template <class A>
+__device__ __forceinline__ void run_single(const typename A::T* in, typename A::T* out, unsigned long long* ts,
+                                           unsigned* smid_out, uint32_t M, uint32_t smem_bytes) {
+    Ctx c;
+    ctx_init(c, smem_bytes, nullptr, DSMEM_WAIT_LIMIT_NS);
+    init_bars<A>(c);
+    c.st.base = ts != nullptr ? ts + c.rank * kStamps : nullptr;
+    c.deadline = globaltimer() + c.wait_limit;
+    A::load(c, in + c.rank * in_elems_per_rank<A>(M), M);
+    if (smid_out != nullptr && threadIdx.x == 0) smid_out[c.rank] = smid();
+    cluster_sync();
+    c.st.mark(0);
+    A::exec(c, M);
+    c.st.mark(1);
+    A::store(c, out + c.rank * out_elems_per_rank<A>(M), M);
+    cluster_sync();
+}
+
+}  // namespace dsb

@@ -1,0 +1,100 @@
+// instantiate.cu -- compiled once per (op, dtype) with -DDSB_OP=<0..3> -DDSB_DT=<0..2>; instantiates
+// batch_kernel<Alg<N, T, Sum>> for every algorithm of that op and every cluster size the algorithm's
+// static constraints allow, and registers them for the C ABI.
+#include "../collectives/dsmem_b200_algos.cuh"
+#include "registry.h"
+
+#ifndef DSB_OP
+#error "compile with -DDSB_OP=<0 allreduce|1 allgather|2 reducescatter|3 alltoall>"
+#endif
+#ifndef DSB_DT
+#error "compile with -DDSB_DT=<0 f32|1 bf16|2 i32>"
+#endif
+
+#if DSB_DT == 0
+using ElemT = float;
+#elif DSB_DT == 1
+using ElemT = __nv_bfloat16;
+#else
+using ElemT = int;
+#endif
+
+namespace dsb {
+namespace {
+
+template <class A>
+bool legal_fn(uint32_t m) {
+    return A::legal(m);
+}
+template <class A>
+uint64_t smem_fn(uint32_t m) {
+    return A::smem_bytes(m);
+}
+
+// Algorithm ids (dsmem_alg in include/dsmem_b200.h).
+enum : int {
+    kRing = 1, kRecursiveDoubling = 2, kShiftAccBulk = 3, kShiftAccAtomic = 4, kDirectReplicatedPush = 5,
+    kPullRsPushAg = 6, kRabenseifner = 7, kOneShotPull = 8, kTwoShotPush = 9, kReduceBcastBinomial = 10,
+    kAtomicAllPush = 11, kMesh2D = 12, kDirectShift = 13, kBruck = 14, kDirectPull = 15,
+    kGatherBcastBinomial = 16, kRecursiveHalving = 17, kDirectPush = 18, kPairwiseExchange = 19,
+    kPairwiseXor = 20, kShift = 21
+};
+
+template <template <int, typename, class> class A, int N>
+void add(Registry& r, int alg) {
+    using Alg = A<N, ElemT, Sum>;
+    r.push_back(KernelEntry{DSB_OP, alg, DSB_DT, N, (int)sizeof(ElemT),
+                            reinterpret_cast<const void*>(&batch_kernel<Alg>), &legal_fn<Alg>, &smem_fn<Alg>});
+}
+template <template <int, typename, class> class A>
+void add_all_n(Registry& r, int alg) {
+    add<A, 2>(r, alg);
+    add<A, 4>(r, alg);
+    add<A, 8>(r, alg);
+    add<A, 16>(r, alg);
+}
+
+}  // namespace
+
+#define DSB_CAT3(a, b, c, d) a##b##c##d
+#define DSB_REG_NAME(op, dt) DSB_CAT3(register_op, op, _dt, dt)
+
+void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
+#if DSB_OP == 0
+    add_all_n<AR_RecursiveDoubling>(r, kRecursiveDoubling);
+    add<AR_ShiftAccumulateBulk, 4>(r, kShiftAccBulk);
+    add<AR_ShiftAccumulateAtomic, 2>(r, kShiftAccAtomic);
+    add<AR_ShiftAccumulateAtomic, 4>(r, kShiftAccAtomic);
+    add_all_n<AR_DirectReplicatedPush>(r, kDirectReplicatedPush);
+    add_all_n<AR_PullRsPushAg>(r, kPullRsPushAg);
+    add_all_n<AR_Ring>(r, kRing);
+    add_all_n<AR_Rabenseifner>(r, kRabenseifner);
+    add_all_n<AR_OneShotPull>(r, kOneShotPull);
+    add_all_n<AR_TwoShotPush>(r, kTwoShotPush);
+    add_all_n<AR_ReduceBcastBinomial>(r, kReduceBcastBinomial);
+    add_all_n<AR_AtomicAllPush>(r, kAtomicAllPush);
+    add_all_n<AR_Mesh2D>(r, kMesh2D);
+#elif DSB_OP == 1
+    add_all_n<AG_RecursiveDoubling>(r, kRecursiveDoubling);
+    add_all_n<AG_DirectShift>(r, kDirectShift);
+    add_all_n<AG_DirectReplicatedPush>(r, kDirectReplicatedPush);
+    add_all_n<AG_Ring>(r, kRing);
+    add_all_n<AG_Bruck>(r, kBruck);
+    add_all_n<AG_DirectPull>(r, kDirectPull);
+    add_all_n<AG_GatherBcastBinomial>(r, kGatherBcastBinomial);
+#elif DSB_OP == 2
+    add_all_n<RS_Ring>(r, kRing);
+    add_all_n<RS_RecursiveHalving>(r, kRecursiveHalving);
+    add_all_n<RS_DirectPush>(r, kDirectPush);
+    add_all_n<RS_DirectPull>(r, kDirectPull);
+#else
+    add<A2A_PairwiseExchange, 2>(r, kPairwiseExchange);
+    add_all_n<A2A_DirectPush>(r, kDirectPush);
+    add_all_n<A2A_PairwiseXor>(r, kPairwiseXor);
+    add_all_n<A2A_Shift>(r, kShift);
+    add_all_n<A2A_Bruck>(r, kBruck);
+    add_all_n<A2A_DirectPull>(r, kDirectPull);
+#endif
+}
+
+}  // namespace dsb

@@ -1,0 +1,35 @@
+// registry.h -- host-side table of the compiled collective kernels (one entry per op x alg x dtype x N).
+#pragma once
+#include <cstdint>
+#include <vector>
+
+namespace dsb {
+
+struct KernelEntry {
+    int op;                              // dsmem_op
+    int alg;                             // dsmem_alg
+    int dtype;                           // dsmem_dtype
+    int n;                               // cluster size
+    int elem_bytes;                      // sizeof(T)
+    const void* fn;                      // __global__ batch_kernel<A>
+    bool (*legal)(uint32_t m);           // static N/M constraints of the reference file
+    uint64_t (*smem_bytes)(uint32_t m);  // dynamic shared memory per CTA
+};
+
+using Registry = std::vector<KernelEntry>;
+
+// One registration function per (op, dtype) translation unit (instantiate.cu).
+void register_op0_dt0(Registry&);
+void register_op0_dt1(Registry&);
+void register_op0_dt2(Registry&);
+void register_op1_dt0(Registry&);
+void register_op1_dt1(Registry&);
+void register_op1_dt2(Registry&);
+void register_op2_dt0(Registry&);
+void register_op2_dt1(Registry&);
+void register_op2_dt2(Registry&);
+void register_op3_dt0(Registry&);
+void register_op3_dt1(Registry&);
+void register_op3_dt2(Registry&);
+
+}  // namespace dsb

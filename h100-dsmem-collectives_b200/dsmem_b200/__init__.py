@@ -1,0 +1,301 @@
+"""dsmem_b200 -- Python host API of the B200 (sm_100a) DSMEM collective catalogue.
+
+A thin ctypes layer over the C ABI in include/dsmem_b200.h (lib/libdsmem_b200.so). It mirrors the
+reference's plugin interface: one collective = (op, alg, dtype, cluster size N, payload per CTA P),
+the reference's compile-time knobs COLL_OP / <alg> / ELEM_T / CLUSTER_N / MSG_ELEMS
+(collectives/harness/main.cu:1-10) as run-time arguments, run on a batch of independent cluster problems.
+Errors are raised as DsmemError carrying the C status; there is no fallback: without the compiled
+library every call fails.
+
+Device memory and streams come from the caller (torch tensors in the convenience wrappers; raw device
+pointers in `launch`).
+"""
+from __future__ import annotations
+
+import ctypes
+import enum
+import pathlib
+
+PKG_DIR = pathlib.Path(__file__).resolve().parent.parent
+LIB_PATH = PKG_DIR / "lib" / "libdsmem_b200.so"
+INCLUDE_DIR = PKG_DIR.parent / "include"
+COLLECTIVES_DIR = PKG_DIR / "collectives"
+
+
+class Op(enum.IntEnum):
+    ALLREDUCE = 0
+    ALLGATHER = 1
+    REDUCESCATTER = 2
+    ALLTOALL = 3
+
+
+class Alg(enum.IntEnum):
+    AUTO = 0
+    RING = 1
+    RECURSIVE_DOUBLING = 2
+    SHIFT_ACCUMULATE_BULK = 3
+    SHIFT_ACCUMULATE_ATOMIC = 4
+    DIRECT_REPLICATED_PUSH = 5
+    PULL_REDUCE_SCATTER_PUSH_ALLGATHER = 6
+    RABENSEIFNER = 7
+    ONE_SHOT_PULL = 8
+    TWO_SHOT_PUSH = 9
+    REDUCE_BCAST_BINOMIAL = 10
+    ATOMIC_ALL_PUSH = 11
+    MESH_2D = 12
+    DIRECT_SHIFT = 13
+    BRUCK = 14
+    DIRECT_PULL = 15
+    GATHER_BCAST_BINOMIAL = 16
+    RECURSIVE_HALVING = 17
+    DIRECT_PUSH = 18
+    PAIRWISE_EXCHANGE = 19
+    PAIRWISE_XOR = 20
+    SHIFT = 21
+
+
+class Dtype(enum.IntEnum):
+    F32 = 0
+    BF16 = 1
+    I32 = 2
+
+
+class Status(enum.IntEnum):
+    OK = 0
+    ILLEGAL_CONFIG = 1
+    SMEM_LIMIT = 2
+    TIMEOUT = 3
+    CUDA = 4
+    INVALID_ARGUMENT = 5
+    BOUNDS = 6
+    NCCL = 7
+
+
+ELEM_BYTES = {Dtype.F32: 4, Dtype.BF16: 2, Dtype.I32: 4}
+CLUSTER_SIZES = (2, 4, 8, 16)
+STAMPS_PER_RANK = 32  # dsmem_primitives.cuh kStamps
+
+# (op, alg) -> reference file stem collectives/<op>__<alg>__<src>.cu  (collectives/README.md:19-49)
+CATALOGUE = {
+    (Op.ALLREDUCE, Alg.RECURSIVE_DOUBLING): "allreduce__recursive_doubling__clusterfusion",
+    (Op.ALLREDUCE, Alg.SHIFT_ACCUMULATE_BULK): "allreduce__shift_accumulate_bulk__clusterfusion",
+    (Op.ALLREDUCE, Alg.SHIFT_ACCUMULATE_ATOMIC): "allreduce__shift_accumulate_atomic__clusterfusion",
+    (Op.ALLREDUCE, Alg.DIRECT_REPLICATED_PUSH): "allreduce__direct_replicated_push__credit",
+    (Op.ALLREDUCE, Alg.PULL_REDUCE_SCATTER_PUSH_ALLGATHER): "allreduce__pull_reduce_scatter_push_allgather__hpcops",
+    (Op.ALLREDUCE, Alg.RING): "allreduce__ring__nccl",
+    (Op.ALLREDUCE, Alg.RABENSEIFNER): "allreduce__rabenseifner__mpich",
+    (Op.ALLREDUCE, Alg.ONE_SHOT_PULL): "allreduce__one_shot_pull__trtllm",
+    (Op.ALLREDUCE, Alg.TWO_SHOT_PUSH): "allreduce__two_shot_push__trtllm",
+    (Op.ALLREDUCE, Alg.REDUCE_BCAST_BINOMIAL): "allreduce__reduce_bcast_binomial__mpich",
+    (Op.ALLREDUCE, Alg.ATOMIC_ALL_PUSH): "allreduce__atomic_all_push__generic",
+    (Op.ALLREDUCE, Alg.MESH_2D): "allreduce__2d_mesh__generic",
+    (Op.ALLGATHER, Alg.RECURSIVE_DOUBLING): "allgather__recursive_doubling__clusterfusion",
+    (Op.ALLGATHER, Alg.DIRECT_SHIFT): "allgather__direct_shift__clusterfusion",
+    (Op.ALLGATHER, Alg.DIRECT_REPLICATED_PUSH): "allgather__direct_replicated_push__credit",
+    (Op.ALLGATHER, Alg.RING): "allgather__ring__nccl",
+    (Op.ALLGATHER, Alg.BRUCK): "allgather__bruck__mpich",
+    (Op.ALLGATHER, Alg.DIRECT_PULL): "allgather__direct_pull__generic",
+    (Op.ALLGATHER, Alg.GATHER_BCAST_BINOMIAL): "allgather__gather_bcast_binomial__mpich",
+    (Op.REDUCESCATTER, Alg.RING): "reducescatter__ring__nccl",
+    (Op.REDUCESCATTER, Alg.RECURSIVE_HALVING): "reducescatter__recursive_halving__mpich",
+    (Op.REDUCESCATTER, Alg.DIRECT_PUSH): "reducescatter__direct_push__generic",
+    (Op.REDUCESCATTER, Alg.DIRECT_PULL): "reducescatter__direct_pull__generic",
+    (Op.ALLTOALL, Alg.PAIRWISE_EXCHANGE): "alltoall__pairwise_exchange__fa4",
+    (Op.ALLTOALL, Alg.DIRECT_PUSH): "alltoall__direct_push__generic",
+    (Op.ALLTOALL, Alg.PAIRWISE_XOR): "alltoall__pairwise_xor__mpich",
+    (Op.ALLTOALL, Alg.SHIFT): "alltoall__shift__generic",
+    (Op.ALLTOALL, Alg.BRUCK): "alltoall__bruck__mpich",
+    (Op.ALLTOALL, Alg.DIRECT_PULL): "alltoall__direct_pull__generic",
+}
+
+
+class DsmemError(RuntimeError):
+    def __init__(self, status, what=""):
+        self.status = Status(status)
+        super().__init__(f"{what}: {self.status.name} ({_status_string(status)})")
+
+
+_lib = None
+
+
+def lib():
+    """Load lib/libdsmem_b200.so (build it with `make -C h100-dsmem-collectives_b200 -j8`)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `make -C {PKG_DIR} -j8` "
+                           "(there is no CPU fallback)")
+    L = ctypes.CDLL(str(LIB_PATH))
+    c_int, c_size, c_vp, c_ll, c_ull = ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_ulonglong
+    sig = {
+        "dsmem_collective_launch": (c_int, [c_int, c_int, c_int, c_int, c_size, c_vp, c_vp, c_int, c_vp, c_vp]),
+        "dsmem_collective_launch_ex": (c_int, [c_int, c_int, c_int, c_int, c_size, c_vp, c_vp, c_ll, c_vp, c_vp,
+                                               c_int, c_vp]),
+        "dsmem_query": (c_int, [c_int, c_int, c_int, c_int, c_size, ctypes.POINTER(c_size), ctypes.POINTER(c_int)]),
+        "dsmem_max_active_clusters": (c_int, [c_int, c_int, c_int, c_int, c_size, ctypes.POINTER(c_int)]),
+        "dsmem_autotune_table_load": (c_int, [ctypes.c_char_p]),
+        "dsmem_autotune_pick": (c_int, [c_int, c_int, c_int, c_size]),
+        "dsmem_last_error": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
+        "dsmem_check": (c_int, [c_vp]),
+        "dsmem_op_name": (ctypes.c_char_p, [c_int]),
+        "dsmem_alg_name": (ctypes.c_char_p, [c_int]),
+        "dsmem_dtype_name": (ctypes.c_char_p, [c_int]),
+        "dsmem_status_string": (ctypes.c_char_p, [c_int]),
+        "dsmem_file_stem": (ctypes.c_char_p, [c_int, c_int]),
+        "dsmem_lookup": (c_int, [ctypes.c_char_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+        "dsmem_set_wait_limit_ns": (c_int, [c_ull]),
+        "dsmem_selftest_timeout": (c_int, [c_ull, c_vp]),
+        "dsmem_version": (ctypes.c_char_p, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _status_string(status):
+    try:
+        return lib().dsmem_status_string(int(status)).decode()
+    except Exception:  # noqa: BLE001 - message only
+        return "?"
+
+
+def _ok(status, what):
+    if status != 0:
+        raise DsmemError(status, what)
+
+
+# ----------------------------------------------------------------------------------- layouts
+def msg_elems(op, n, bytes_per_cta, dtype):
+    """M (elements per rank block) of payload P (nccl-tests convention, main.cu:97)."""
+    unit = ELEM_BYTES[Dtype(dtype)] * (1 if Op(op) == Op.ALLREDUCE else n)
+    if bytes_per_cta % unit:
+        raise ValueError(f"payload {bytes_per_cta} B is not a multiple of {unit} B")
+    return bytes_per_cta // unit
+
+
+def payload_bytes(op, n, m, dtype):
+    return m * ELEM_BYTES[Dtype(dtype)] * (1 if Op(op) == Op.ALLREDUCE else n)
+
+
+def in_elems_per_rank(op, n, m):
+    return m if Op(op) in (Op.ALLREDUCE, Op.ALLGATHER) else n * m
+
+
+def out_elems_per_rank(op, n, m):
+    return m if Op(op) in (Op.ALLREDUCE, Op.REDUCESCATTER) else n * m
+
+
+def algorithms(op):
+    """Algorithms of the catalogue for `op`, in reference file order."""
+    return [a for (o, a) in CATALOGUE if o == Op(op)]
+
+
+# ----------------------------------------------------------------------------------- C ABI calls
+def launch(op, alg, dtype, cluster_size, bytes_per_cta, in_ptr, out_ptr, num_clusters, stamps_ptr=0, smid_ptr=0,
+           max_resident_clusters=0, stream=0):
+    """dsmem_collective_launch_ex on raw device pointers (asynchronous on `stream`)."""
+    st = lib().dsmem_collective_launch_ex(int(op), int(alg), int(dtype), int(cluster_size), int(bytes_per_cta),
+                                          ctypes.c_void_p(in_ptr), ctypes.c_void_p(out_ptr), int(num_clusters),
+                                          ctypes.c_void_p(stamps_ptr or None), ctypes.c_void_p(smid_ptr or None),
+                                          int(max_resident_clusters), ctypes.c_void_p(stream or None))
+    _ok(st, f"dsmem_collective_launch({Op(op).name}, {Alg(alg).name}, {Dtype(dtype).name}, N={cluster_size}, "
+            f"P={bytes_per_cta})")
+
+
+def query(op, alg, dtype, cluster_size, bytes_per_cta):
+    """(status, smem_bytes, legal) without touching the GPU."""
+    smem = ctypes.c_size_t(0)
+    legal = ctypes.c_int(0)
+    st = lib().dsmem_query(int(op), int(alg), int(dtype), int(cluster_size), int(bytes_per_cta), ctypes.byref(smem),
+                           ctypes.byref(legal))
+    return Status(st), smem.value, bool(legal.value)
+
+
+def max_active_clusters(op, alg, dtype, cluster_size, bytes_per_cta):
+    n = ctypes.c_int(0)
+    _ok(lib().dsmem_max_active_clusters(int(op), int(alg), int(dtype), int(cluster_size), int(bytes_per_cta),
+                                        ctypes.byref(n)), "dsmem_max_active_clusters")
+    return n.value
+
+
+def check(stream=0):
+    """Synchronise `stream` and raise DsmemError(TIMEOUT/BOUNDS) if a device-side check fired."""
+    _ok(lib().dsmem_check(ctypes.c_void_p(stream or None)), "dsmem_check")
+
+
+def last_error(device=0):
+    bits = ctypes.c_uint(0)
+    _ok(lib().dsmem_last_error(int(device), ctypes.byref(bits)), "dsmem_last_error")
+    return bits.value
+
+
+def set_wait_limit_ns(ns):
+    _ok(lib().dsmem_set_wait_limit_ns(int(ns)), "dsmem_set_wait_limit_ns")
+
+
+def autotune_load(path):
+    _ok(lib().dsmem_autotune_table_load(str(path).encode()), f"dsmem_autotune_table_load({path})")
+
+
+def autotune_pick(op, dtype, cluster_size, bytes_per_cta):
+    return Alg(lib().dsmem_autotune_pick(int(op), int(dtype), int(cluster_size), int(bytes_per_cta)))
+
+
+def file_stem(op, alg):
+    s = lib().dsmem_file_stem(int(op), int(alg))
+    return s.decode() if s else None
+
+
+def lookup(stem):
+    op, alg = ctypes.c_int(0), ctypes.c_int(0)
+    _ok(lib().dsmem_lookup(stem.encode(), ctypes.byref(op), ctypes.byref(alg)), f"dsmem_lookup({stem})")
+    return Op(op.value), Alg(alg.value)
+
+
+def selftest_timeout(limit_ns, stream=0):
+    """Launch the bounded-wait self-test kernel (see dsmem_selftest_timeout)."""
+    _ok(lib().dsmem_selftest_timeout(int(limit_ns), ctypes.c_void_p(stream or None)), "dsmem_selftest_timeout")
+
+
+def version():
+    return lib().dsmem_version().decode()
+
+
+# ----------------------------------------------------------------------------------- torch helpers
+def dtype_of(tensor):
+    import torch
+
+    return {torch.float32: Dtype.F32, torch.bfloat16: Dtype.BF16, torch.int32: Dtype.I32}[tensor.dtype]
+
+
+def collective(op, alg, inp, out, cluster_size, bytes_per_cta, num_clusters=None, stamps=None, smid=None,
+               max_resident_clusters=0, stream=None):
+    """Run one batched collective on torch CUDA tensors (contiguous, cluster-major layout of
+    include/dsmem_b200.h). num_clusters defaults to what `inp` holds."""
+    import torch
+
+    dt = dtype_of(inp)
+    if out.dtype != inp.dtype or not (inp.is_cuda and out.is_cuda):
+        raise ValueError("inp/out must be CUDA tensors of the same dtype")
+    if not (inp.is_contiguous() and out.is_contiguous()):
+        raise ValueError("inp/out must be contiguous")
+    m = msg_elems(op, cluster_size, bytes_per_cta, dt)
+    per_in = cluster_size * in_elems_per_rank(op, cluster_size, m)
+    per_out = cluster_size * out_elems_per_rank(op, cluster_size, m)
+    if num_clusters is None:
+        num_clusters = inp.numel() // per_in
+    if inp.numel() < num_clusters * per_in or out.numel() < num_clusters * per_out:
+        raise ValueError(f"tensors too small for {num_clusters} cluster problems")
+    if stamps is not None and (stamps.dtype != torch.int64 or stamps.numel() < num_clusters * cluster_size * STAMPS_PER_RANK):
+        raise ValueError("stamps must be int64 with num_clusters*N*32 entries")
+    if smid is not None and (smid.dtype != torch.int32 or smid.numel() < num_clusters * cluster_size):
+        raise ValueError("smid must be int32 with num_clusters*N entries")
+    s = stream if stream is not None else torch.cuda.current_stream(inp.device).cuda_stream
+    launch(op, alg, dt, cluster_size, bytes_per_cta, inp.data_ptr(), out.data_ptr(), num_clusters,
+           stamps.data_ptr() if stamps is not None else 0, smid.data_ptr() if smid is not None else 0,
+           max_resident_clusters, s)
+    return out

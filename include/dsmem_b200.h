@@ -1,0 +1,168 @@
+/*
+ * dsmem_b200.h -- C ABI of the B200 (sm_100a) thread-block-cluster collective catalogue.
+ *
+ * The reference repository (lomolisso/h100-dsmem-collectives) has no library interface: each
+ * algorithm is a compile-time plugin, collectives/<op>__<alg>__<src>.cu, that defines
+ *     __global__ void __cluster_dims__(CLUSTER_N,1,1)
+ *     collective_kernel(const ELEM_T* in, ELEM_T* out, unsigned long long* ts, unsigned* smid);
+ * (contract: collectives/dsmem_primitives.cuh:205-220), compiled once per (file, CLUSTER_N, MSG_ELEMS,
+ * ELEM_T) and launched by collectives/harness/main.cu:267-275 as ONE cluster per launch. This header
+ * replaces that compile-time selection with run-time arguments: one call launches a batch of
+ * `num_clusters` independent problems, each exactly the reference kernel's problem, on resident
+ * persistent clusters. Plain pointers and sizes only; no CUDA or torch types in the signatures
+ * (dsmem_stream_t is ABI-identical to cudaStream_t).
+ *
+ * Data layout of a batch (cluster problem c, rank b, M = elements per rank block, cluster-major):
+ *   ALLREDUCE      in [c][b][M]            out[c][b][M]     (main.cu:132-136)
+ *   ALLGATHER      in [c][b][M]            out[c][b][N][M]  (main.cu:137-138)
+ *   REDUCESCATTER  in [c][b][N][M]         out[c][b][M]     (main.cu:139-142)
+ *   ALLTOALL       in [c][b][N][M]         out[c][b][N][M]  (main.cu:143-145)
+ * bytes_per_cta is the nccl-tests payload P of the reference sweep (main.cu:97, driver.py:156-163):
+ *   ALLREDUCE P = M * sizeof(T); every other op P = N * M * sizeof(T).
+ */
+#ifndef DSMEM_B200_H
+#define DSMEM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct CUstream_st;
+typedef struct CUstream_st* dsmem_stream_t; /* == cudaStream_t */
+
+/* Return codes. ILLEGAL_CONFIG mirrors the reference build matrix's SKIP:static_assert and
+ * SMEM_LIMIT its SKIP:smem (collectives/harness/driver.py:210-230, main.cu:90-92); TIMEOUT replaces
+ * the reference watchdog's DEADLOCK exit (main.cu:277-320): a device-side mbarrier wait gave up. */
+typedef enum {
+    DSMEM_OK = 0,
+    DSMEM_ERR_ILLEGAL_CONFIG = 1,
+    DSMEM_ERR_SMEM_LIMIT = 2,
+    DSMEM_ERR_TIMEOUT = 3,
+    DSMEM_ERR_CUDA = 4,
+    DSMEM_ERR_INVALID_ARGUMENT = 5,
+    DSMEM_ERR_BOUNDS = 6,
+    DSMEM_ERR_NCCL = 7
+} dsmem_status;
+
+/* COLL_OP values of collectives/harness/main.cu:7-8. */
+typedef enum {
+    DSMEM_OP_ALLREDUCE = 0,
+    DSMEM_OP_ALLGATHER = 1,
+    DSMEM_OP_REDUCESCATTER = 2,
+    DSMEM_OP_ALLTOALL = 3
+} dsmem_op;
+
+/* The <alg> component of the reference file names collectives/<op>__<alg>__<src>.cu
+ * (collectives/README.md:19-49). Not every algorithm exists for every op. */
+typedef enum {
+    DSMEM_ALG_AUTO = 0,                               /* measured table, else a built-in default */
+    DSMEM_ALG_RING = 1,                               /* allreduce, allgather, reducescatter     */
+    DSMEM_ALG_RECURSIVE_DOUBLING = 2,                 /* allreduce, allgather                    */
+    DSMEM_ALG_SHIFT_ACCUMULATE_BULK = 3,              /* allreduce (N = 4)                       */
+    DSMEM_ALG_SHIFT_ACCUMULATE_ATOMIC = 4,            /* allreduce (N = 2, 4)                    */
+    DSMEM_ALG_DIRECT_REPLICATED_PUSH = 5,             /* allreduce, allgather                    */
+    DSMEM_ALG_PULL_REDUCE_SCATTER_PUSH_ALLGATHER = 6, /* allreduce                               */
+    DSMEM_ALG_RABENSEIFNER = 7,                       /* allreduce                               */
+    DSMEM_ALG_ONE_SHOT_PULL = 8,                      /* allreduce                               */
+    DSMEM_ALG_TWO_SHOT_PUSH = 9,                      /* allreduce                               */
+    DSMEM_ALG_REDUCE_BCAST_BINOMIAL = 10,             /* allreduce                               */
+    DSMEM_ALG_ATOMIC_ALL_PUSH = 11,                   /* allreduce                               */
+    DSMEM_ALG_2D_MESH = 12,                           /* allreduce                               */
+    DSMEM_ALG_DIRECT_SHIFT = 13,                      /* allgather                               */
+    DSMEM_ALG_BRUCK = 14,                             /* allgather, alltoall                     */
+    DSMEM_ALG_DIRECT_PULL = 15,                       /* allgather, reducescatter, alltoall      */
+    DSMEM_ALG_GATHER_BCAST_BINOMIAL = 16,             /* allgather                               */
+    DSMEM_ALG_RECURSIVE_HALVING = 17,                 /* reducescatter                           */
+    DSMEM_ALG_DIRECT_PUSH = 18,                       /* reducescatter, alltoall                 */
+    DSMEM_ALG_PAIRWISE_EXCHANGE = 19,                 /* alltoall (N = 2)                        */
+    DSMEM_ALG_PAIRWISE_XOR = 20,                      /* alltoall                                */
+    DSMEM_ALG_SHIFT = 21,                             /* alltoall                                */
+    DSMEM_ALG_COUNT = 22
+} dsmem_alg;
+
+/* ELEM_T of the reference (float | int, main.cu:99) plus bf16. */
+typedef enum { DSMEM_F32 = 0, DSMEM_BF16 = 1, DSMEM_I32 = 2 } dsmem_dtype;
+
+/* Error bits of the device error word (dsmem_last_error). */
+#define DSMEM_ERRBIT_TIMEOUT 1u
+#define DSMEM_ERRBIT_BOUNDS 2u
+
+/*
+ * Launch one collective on `num_clusters` independent cluster problems (stream-ordered, asynchronous).
+ * Replaces: compiling collectives/<op>__<alg>__<src>.cu with -DCLUSTER_N -DMSG_ELEMS -DELEM_T
+ * (collectives/harness/driver.py:233-239) and launching collective_kernel<<<N, 256, smem>>>
+ * (collectives/harness/main.cu:267-275), once per problem.
+ *   cluster_size   N in {2, 4, 8, 16} (16 is a non-portable cluster size)
+ *   bytes_per_cta  P, see the header comment
+ *   in, out        device pointers, 16-byte aligned, sizes per the batch layout above
+ *   stamps         nullable; else [num_clusters][N][32] u64 %globaltimer slots per problem:
+ *                  [0] entry, [1] exit, [2 + r] end of round r (dsmem_primitives.cuh:216-218)
+ *   stream         CUDA stream (NULL = legacy default stream)
+ * Returns ILLEGAL_CONFIG for (op, alg, N, P, dtype) combinations the reference rejects by static_assert,
+ * SMEM_LIMIT when the algorithm's shared memory exceeds 227 KiB per CTA, CUDA on launch failure.
+ * Device-side timeouts are reported by dsmem_last_error / dsmem_check, not by this call.
+ */
+dsmem_status dsmem_collective_launch(dsmem_op op, dsmem_alg alg, dsmem_dtype dtype, int cluster_size,
+                                     size_t bytes_per_cta, const void* in, void* out, int num_clusters,
+                                     unsigned long long* stamps, dsmem_stream_t stream);
+
+/* As dsmem_collective_launch, plus SM ids ([num_clusters][N] u32, nullable: main.cu's smid array),
+ * and an explicit cap on resident clusters (0 = as many as fit). */
+dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype dtype, int cluster_size,
+                                        size_t bytes_per_cta, const void* in, void* out, long long num_clusters,
+                                        unsigned long long* stamps, unsigned* smid, int max_resident_clusters,
+                                        dsmem_stream_t stream);
+
+/* Static legality and shared-memory size of a configuration (the reference build matrix's
+ * classification, driver.py:210-230, and the COLLECTIVE_SMEM_BYTES tag, main.cu:104-121).
+ * legal = 1 if the configuration runs; smem_bytes = dynamic shared memory per CTA. */
+dsmem_status dsmem_query(dsmem_op op, dsmem_alg alg, dsmem_dtype dtype, int cluster_size, size_t bytes_per_cta,
+                         size_t* smem_bytes, int* legal);
+
+/* Resident clusters of one launch on the current device (cudaOccupancyMaxActiveClusters,
+ * main.cu:215-222) for a legal configuration. */
+dsmem_status dsmem_max_active_clusters(dsmem_op op, dsmem_alg alg, dsmem_dtype dtype, int cluster_size,
+                                       size_t bytes_per_cta, int* clusters);
+
+/* Variant selection for DSMEM_ALG_AUTO: a measured table of lines "op cluster_size bytes_per_cta dtype alg"
+ * (names as in dsmem_alg_name / dsmem_op_name). A lookup takes the entry with the same op, N and dtype
+ * and the largest bytes_per_cta <= the request. Replaces the "best per (op, N, payload)" selection of
+ * collectives/analysis/collectives_figures.py:549. */
+dsmem_status dsmem_autotune_table_load(const char* path);
+/* The algorithm AUTO resolves to (after legality) for this configuration. */
+dsmem_alg dsmem_autotune_pick(dsmem_op op, dsmem_dtype dtype, int cluster_size, size_t bytes_per_cta);
+
+/* Read and clear the device error word of `device` (synchronises that device). */
+dsmem_status dsmem_last_error(int device, unsigned* error_bits);
+/* Synchronise `stream`, then map the device error word to TIMEOUT / BOUNDS (and clear it). */
+dsmem_status dsmem_check(dsmem_stream_t stream);
+
+/* Names: "<op>", "<alg>" and the reference file stem "<op>__<alg>__<src>". */
+const char* dsmem_op_name(dsmem_op op);
+const char* dsmem_alg_name(dsmem_alg alg);
+const char* dsmem_dtype_name(dsmem_dtype dtype);
+const char* dsmem_status_string(dsmem_status status);
+/* Reference file stem of (op, alg), or NULL if the pair does not exist. */
+const char* dsmem_file_stem(dsmem_op op, dsmem_alg alg);
+/* Parse a reference file stem (e.g. "allreduce__ring__nccl"); returns INVALID_ARGUMENT if unknown. */
+dsmem_status dsmem_lookup(const char* file_stem, dsmem_op* op, dsmem_alg* alg);
+
+/* Per-device wait limit of the batch kernels in nanoseconds of %globaltimer (default 1e9). */
+dsmem_status dsmem_set_wait_limit_ns(unsigned long long ns);
+
+/* Failure-detection self-test: launches one 2-CTA cluster whose mbarrier is armed for 16 bytes that
+ * never arrive, with a wait limit of `limit_ns`; every wait gives up after the limit and the kernel
+ * exits normally. dsmem_check afterwards must report DSMEM_ERR_TIMEOUT. Replaces nothing in the
+ * reference (its hangs were caught by a host watchdog, collectives/harness/main.cu:277-320). */
+dsmem_status dsmem_selftest_timeout(unsigned long long limit_ns, dsmem_stream_t stream);
+
+/* Library version string. */
+const char* dsmem_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DSMEM_B200_H */

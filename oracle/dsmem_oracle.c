@@ -1,0 +1,237 @@
+/*
+ * dsmem_oracle.c -- CPU oracle (TEST INFRASTRUCTURE ONLY; see dsmem_oracle.h).
+ *
+ * Every function names the reference lines it restates. Arithmetic is the reference's: double
+ * accumulation for floating types, exact integer accumulation for int32 (main.cu:128, "sums
+ * accumulated in double (float) or int64 (int)").
+ */
+#include "dsmem_oracle.h"
+
+#include <math.h>
+#include <string.h>
+
+/* ----------------------------------------------------------------- mt19937_64 */
+#define MT_N 312
+#define MT_M 156
+#define MT_MATRIX_A 0xB5026F5AA96619E9ULL
+#define MT_UPPER 0xFFFFFFFF80000000ULL
+#define MT_LOWER 0x7FFFFFFFULL
+
+void orc_mt64_seed(orc_mt64* g, uint64_t seed) {
+    g->mt[0] = seed;
+    for (int i = 1; i < MT_N; ++i)
+        g->mt[i] = 6364136223846793005ULL * (g->mt[i - 1] ^ (g->mt[i - 1] >> 62)) + (uint64_t)i;
+    g->idx = MT_N;
+}
+
+static void mt_twist(orc_mt64* g) {
+    for (int i = 0; i < MT_N; ++i) {
+        const uint64_t y = (g->mt[i] & MT_UPPER) | (g->mt[(i + 1) % MT_N] & MT_LOWER);
+        uint64_t v = g->mt[(i + MT_M) % MT_N] ^ (y >> 1);
+        if (y & 1ULL) v ^= MT_MATRIX_A;
+        g->mt[i] = v;
+    }
+    g->idx = 0;
+}
+
+uint64_t orc_mt64_next(orc_mt64* g) {
+    if (g->idx >= MT_N) mt_twist(g);
+    uint64_t x = g->mt[g->idx++];
+    x ^= (x >> 29) & 0x5555555555555555ULL;
+    x ^= (x << 17) & 0x71D67FFFEDA60000ULL;
+    x ^= (x << 37) & 0xFFF7EEE000000000ULL;
+    x ^= x >> 43;
+    return x;
+}
+
+double orc_uniform_real(orc_mt64* g, double lo, double hi) {
+    const double two64 = 18446744073709551616.0;
+    double c = (double)orc_mt64_next(g) / two64;
+    if (c >= 1.0) c = nextafter(1.0, 0.0);
+    return (hi - lo) * c + lo;
+}
+
+int64_t orc_uniform_int(orc_mt64* g, int64_t lo, int64_t hi) {
+    const uint64_t range = (uint64_t)(hi - lo) + 1ULL;   /* hi - lo < 2^63 here */
+    unsigned __int128 prod = (unsigned __int128)orc_mt64_next(g) * range;
+    uint64_t low = (uint64_t)prod;
+    if (low < range) {
+        const uint64_t threshold = (0ULL - range) % range;
+        while (low < threshold) {
+            prod = (unsigned __int128)orc_mt64_next(g) * range;
+            low = (uint64_t)prod;
+        }
+    }
+    return lo + (int64_t)(uint64_t)(prod >> 64);
+}
+
+/* ------------------------------------------------------------------------ bf16 */
+uint16_t orc_f32_to_bf16(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) return (uint16_t)((u >> 16) | 0x40u); /* NaN */
+    const uint32_t rounding = 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)((u + rounding) >> 16);
+}
+
+float orc_bf16_to_f32(uint16_t h) {
+    const uint32_t u = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+static double load_elem(int dtype, const void* buf, size_t i) {
+    switch (dtype) {
+        case ORC_F32: return (double)((const float*)buf)[i];
+        case ORC_BF16: return (double)orc_bf16_to_f32(((const uint16_t*)buf)[i]);
+        default: return (double)((const int32_t*)buf)[i];
+    }
+}
+
+static void store_real(int dtype, void* buf, size_t i, double v) {
+    if (dtype == ORC_F32) ((float*)buf)[i] = (float)v;
+    else if (dtype == ORC_BF16) ((uint16_t*)buf)[i] = orc_f32_to_bf16((float)v);
+    else ((int32_t*)buf)[i] = (int32_t)v;
+}
+
+/* ------------------------------------------------------------ input patterns */
+void orc_fill_pattern_a(int dtype, void* buf, size_t n) {
+    for (size_t k = 0; k < n; ++k) store_real(dtype, buf, k, (double)((long long)((k * 7 + 3) % 17) - 8));
+}
+
+void orc_fill_pattern_b(int dtype, void* buf, size_t n) {
+    orc_mt64 g;
+    orc_mt64_seed(&g, 20261025ULL);
+    for (size_t k = 0; k < n; ++k) store_real(dtype, buf, k, orc_uniform_real(&g, -1.0, 1.0));
+}
+
+void orc_fill_uniform_real(int dtype, void* buf, size_t n, uint64_t seed, double lo, double hi) {
+    orc_mt64 g;
+    orc_mt64_seed(&g, seed);
+    for (size_t k = 0; k < n; ++k) store_real(dtype, buf, k, orc_uniform_real(&g, lo, hi));
+}
+
+void orc_fill_uniform_int(int32_t* buf, size_t n, uint64_t seed, int64_t lo, int64_t hi) {
+    orc_mt64 g;
+    orc_mt64_seed(&g, seed);
+    for (size_t k = 0; k < n; ++k) buf[k] = (int32_t)orc_uniform_int(&g, lo, hi);
+}
+
+void orc_fill_normal(int dtype, void* buf, size_t n, uint64_t seed, double mean, double std) {
+    orc_mt64 g;
+    orc_mt64_seed(&g, seed);
+    const double two_pi = 6.283185307179586476925286766559;
+    for (size_t k = 0; k < n; k += 2) {
+        double u1 = orc_uniform_real(&g, 0.0, 1.0);
+        const double u2 = orc_uniform_real(&g, 0.0, 1.0);
+        if (u1 <= 0.0) u1 = 5e-324;
+        const double r = sqrt(-2.0 * log(u1));
+        store_real(dtype, buf, k, mean + std * r * cos(two_pi * u2));
+        if (k + 1 < n) store_real(dtype, buf, k + 1, mean + std * r * sin(two_pi * u2));
+    }
+}
+
+/* ------------------------------------------------------------------ reference */
+size_t orc_in_elems(int op, int n, size_t m) {
+    return (op == ORC_ALLREDUCE || op == ORC_ALLGATHER) ? m : (size_t)n * m;
+}
+size_t orc_out_elems(int op, int n, size_t m) {
+    return (op == ORC_ALLREDUCE || op == ORC_REDUCESCATTER) ? m : (size_t)n * m;
+}
+
+/* main.cu:129-149, one problem per cluster c (offsets c*N*in_elems / c*N*out_elems). */
+void orc_reference(int op, int dtype, int n, size_t m, long long clusters, const void* in, double* ref) {
+    const size_t ie = orc_in_elems(op, n, m), oe = orc_out_elems(op, n, m);
+    for (long long c = 0; c < clusters; ++c) {
+        const size_t ib = (size_t)c * n * ie, ob = (size_t)c * n * oe;
+        for (int b = 0; b < n; ++b)
+            for (size_t i = 0; i < m; ++i) {
+                if (op == ORC_ALLREDUCE) {
+                    if (dtype == ORC_I32) {
+                        long long s = 0;
+                        for (int r = 0; r < n; ++r) s += ((const int32_t*)in)[ib + (size_t)r * m + i];
+                        ref[ob + (size_t)b * m + i] = (double)s;
+                    } else {
+                        double s = 0;
+                        for (int r = 0; r < n; ++r) s += load_elem(dtype, in, ib + (size_t)r * m + i);
+                        ref[ob + (size_t)b * m + i] = s;
+                    }
+                } else if (op == ORC_ALLGATHER) {
+                    for (int r = 0; r < n; ++r)
+                        ref[ob + (size_t)b * n * m + (size_t)r * m + i] = load_elem(dtype, in, ib + (size_t)r * m + i);
+                } else if (op == ORC_REDUCESCATTER) {
+                    if (dtype == ORC_I32) {
+                        long long s = 0;
+                        for (int r = 0; r < n; ++r)
+                            s += ((const int32_t*)in)[ib + (size_t)r * n * m + (size_t)b * m + i];
+                        ref[ob + (size_t)b * m + i] = (double)s;
+                    } else {
+                        double s = 0;
+                        for (int r = 0; r < n; ++r) s += load_elem(dtype, in, ib + (size_t)r * n * m + (size_t)b * m + i);
+                        ref[ob + (size_t)b * m + i] = s;
+                    }
+                } else {
+                    for (int r = 0; r < n; ++r)
+                        ref[ob + (size_t)b * n * m + (size_t)r * m + i] =
+                            load_elem(dtype, in, ib + (size_t)r * n * m + (size_t)b * m + i);
+                }
+            }
+    }
+}
+
+/* main.cu:156-173. */
+long long orc_check(int dtype, size_t n, const void* out, const double* ref, int mode, double tol, double* max_abs,
+                    double* max_rel) {
+    long long bad = 0;
+    double ma = 0.0, mr = 0.0;
+    for (size_t k = 0; k < n; ++k) {
+        const double got = load_elem(dtype, out, k);
+        const double err = fabs(got - ref[k]);
+        int is_bad;
+        if (mode == 1) {
+            is_bad = !(err <= tol * (1.0 + fabs(ref[k])));
+        } else {
+            double want;
+            if (dtype == ORC_I32) want = ref[k];
+            else if (dtype == ORC_F32) want = (double)(float)ref[k];
+            else want = (double)orc_bf16_to_f32(orc_f32_to_bf16((float)ref[k]));
+            is_bad = !(got == want);
+        }
+        bad += is_bad;
+        if (!(err <= ma)) ma = err;
+        const double rel = err / (1.0 + fabs(ref[k]));
+        if (!(rel <= mr)) mr = rel;
+    }
+    if (max_abs) *max_abs = ma;
+    if (max_rel) *max_rel = mr;
+    return bad;
+}
+
+/* ------------------------------------------------------------------- RMSNorm */
+void orc_rmsnorm(int dtype, size_t rows, size_t hidden, const void* x, const void* res, const void* w, double eps,
+                 double* y, double* pre) {
+    for (size_t r = 0; r < rows; ++r) {
+        double ss = 0.0;
+        for (size_t i = 0; i < hidden; ++i) {
+            double h = load_elem(dtype, x, r * hidden + i);
+            if (res) h += load_elem(dtype, res, r * hidden + i);
+            ss += h * h;
+        }
+        const double scale = 1.0 / sqrt(ss / (double)hidden + eps);
+        for (size_t i = 0; i < hidden; ++i) {
+            double h = load_elem(dtype, x, r * hidden + i);
+            if (res) h += load_elem(dtype, res, r * hidden + i);
+            if (pre) pre[r * hidden + i] = h;
+            y[r * hidden + i] = h * scale * load_elem(dtype, w, i);
+        }
+    }
+}
+
+void orc_sum_ranks(int dtype, size_t ranks, size_t n, const void* const* xs, double* out) {
+    for (size_t i = 0; i < n; ++i) {
+        double s = 0.0;
+        for (size_t r = 0; r < ranks; ++r) s += load_elem(dtype, xs[r], i);
+        out[i] = s;
+    }
+}

@@ -1,0 +1,160 @@
+"""ctypes wrapper of oracle/_build/liboracle.so -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg import this module. It restates the
+reference harness's host code (collectives/harness/main.cu:118-173) in C; see dsmem_oracle.h.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import subprocess
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB = HERE / "_build" / "liboracle.so"
+
+F32, BF16, I32 = 0, 1, 2
+ALLREDUCE, ALLGATHER, REDUCESCATTER, ALLTOALL = 0, 1, 2, 3
+NP_DTYPE = {F32: np.float32, BF16: np.uint16, I32: np.int32}  # bf16 carried as raw uint16 bits
+
+_lib = None
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            build()
+        L = ctypes.CDLL(str(LIB))
+        vp, sz, i, d, u64, i64 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_double, ctypes.c_uint64, ctypes.c_int64
+        L.orc_fill_pattern_a.argtypes = [i, vp, sz]
+        L.orc_fill_pattern_b.argtypes = [i, vp, sz]
+        L.orc_fill_uniform_real.argtypes = [i, vp, sz, u64, d, d]
+        L.orc_fill_uniform_int.argtypes = [vp, sz, u64, i64, i64]
+        L.orc_fill_normal.argtypes = [i, vp, sz, u64, d, d]
+        L.orc_reference.argtypes = [i, i, i, sz, ctypes.c_longlong, vp, vp]
+        L.orc_check.argtypes = [i, sz, vp, vp, i, d, ctypes.POINTER(d), ctypes.POINTER(d)]
+        L.orc_check.restype = ctypes.c_longlong
+        L.orc_rmsnorm.argtypes = [i, sz, sz, vp, vp, vp, d, vp, vp]
+        L.orc_sum_ranks.argtypes = [i, sz, sz, ctypes.POINTER(vp), vp]
+        L.orc_mt64_seed.argtypes = [vp, u64]
+        L.orc_mt64_next.argtypes = [vp]
+        L.orc_mt64_next.restype = u64
+        L.orc_uniform_int.argtypes = [vp, i64, i64]
+        L.orc_uniform_int.restype = i64
+        L.orc_uniform_real.argtypes = [vp, d, d]
+        L.orc_uniform_real.restype = d
+        L.orc_f32_to_bf16.argtypes = [ctypes.c_float]
+        L.orc_f32_to_bf16.restype = ctypes.c_uint16
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def in_elems(op, n, m):
+    return m if op in (ALLREDUCE, ALLGATHER) else n * m
+
+
+def out_elems(op, n, m):
+    return m if op in (ALLREDUCE, REDUCESCATTER) else n * m
+
+
+def pattern_a(dtype, count):
+    a = np.empty(count, NP_DTYPE[dtype])
+    lib().orc_fill_pattern_a(dtype, _p(a), count)
+    return a
+
+
+def pattern_b(dtype, count):
+    a = np.empty(count, NP_DTYPE[dtype])
+    lib().orc_fill_pattern_b(dtype, _p(a), count)
+    return a
+
+
+def uniform_real(dtype, count, seed, lo=-1.0, hi=1.0):
+    a = np.empty(count, NP_DTYPE[dtype])
+    lib().orc_fill_uniform_real(dtype, _p(a), count, seed, lo, hi)
+    return a
+
+
+def uniform_int(count, seed, lo, hi):
+    a = np.empty(count, np.int32)
+    lib().orc_fill_uniform_int(_p(a), count, seed, lo, hi)
+    return a
+
+
+def normal(dtype, count, seed, mean=0.0, std=1.0):
+    a = np.empty(count, NP_DTYPE[dtype])
+    lib().orc_fill_normal(dtype, _p(a), count, seed, mean, std)
+    return a
+
+
+def reference(op, dtype, n, m, clusters, inp):
+    inp = np.ascontiguousarray(inp)
+    assert inp.size >= clusters * n * in_elems(op, n, m)
+    ref = np.empty(clusters * n * out_elems(op, n, m), np.float64)
+    lib().orc_reference(op, dtype, n, m, clusters, _p(inp), _p(ref))
+    return ref
+
+
+def check(dtype, out, ref, mode, tol=0.0):
+    """(n_bad, max_abs, max_rel); mode 0 exact in the element type, 1 |err| <= tol*(1+|ref|)."""
+    out = np.ascontiguousarray(out)
+    ref = np.ascontiguousarray(ref, dtype=np.float64)
+    assert out.size == ref.size, (out.size, ref.size)
+    ma, mr = ctypes.c_double(0), ctypes.c_double(0)
+    bad = lib().orc_check(dtype, out.size, _p(out), _p(ref), mode, tol, ctypes.byref(ma), ctypes.byref(mr))
+    return int(bad), ma.value, mr.value
+
+
+def rmsnorm(dtype, x, w, eps, res=None):
+    rows, hidden = x.shape
+    y = np.empty((rows, hidden), np.float64)
+    pre = np.empty((rows, hidden), np.float64) if res is not None else None
+    lib().orc_rmsnorm(dtype, rows, hidden, _p(np.ascontiguousarray(x)),
+                      _p(np.ascontiguousarray(res)) if res is not None else None, _p(np.ascontiguousarray(w)), eps,
+                      _p(y), _p(pre) if pre is not None else None)
+    return y, pre
+
+
+def sum_ranks(dtype, xs):
+    xs = [np.ascontiguousarray(x) for x in xs]
+    arr = (ctypes.c_void_p * len(xs))(*[x.ctypes.data for x in xs])
+    out = np.empty(xs[0].size, np.float64)
+    lib().orc_sum_ranks(dtype, len(xs), xs[0].size, arr, _p(out))
+    return out
+
+
+def bf16_to_f32(u16):
+    return (np.asarray(u16, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(f):
+    """Round-to-nearest-even float32 -> bf16 bits (numpy, vectorised)."""
+    u = np.asarray(f, np.float32).view(np.uint32)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    nan = (u & 0x7F800000) == 0x7F800000
+    nan &= (u & 0x007FFFFF) != 0
+    return np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), r)
+
+
+class MT64(ctypes.Structure):
+    _fields_ = [("mt", ctypes.c_uint64 * 312), ("idx", ctypes.c_int)]
+
+
+def mt64(seed):
+    g = MT64()
+    lib().orc_mt64_seed(ctypes.byref(g), seed)
+    return g
+
+
+def mt64_next(g):
+    return lib().orc_mt64_next(ctypes.byref(g))

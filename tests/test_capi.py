@@ -1,0 +1,169 @@
+"""Host-side tests of the C ABI (no GPU): exported symbols, names, file stems, legality and shared-memory
+classification against the reference build matrix, AUTO tables.
+
+Legality restates the reference files' static_asserts (collectives/<file>.cu) and the per-file shared
+memory of collectives/docs/TESTING.md:28-39 (in elements of T); the B200 build adds a 128-byte mbarrier
+area and, uniformly, 16-byte whole messages (every M of the reference matrix satisfies it).
+"""
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "dsmem_b200.h"
+
+
+def declared_functions(path):
+    text = path.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(dsmem_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol(dsmem):
+    names = declared_functions(HEADER)
+    assert len(names) >= 15
+    lib = ctypes.CDLL(str(dsmem.LIB_PATH))
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_names_and_stems(dsmem):
+    L = dsmem.lib()
+    assert L.dsmem_op_name(0) == b"allreduce"
+    assert L.dsmem_alg_name(int(dsmem.Alg.TWO_SHOT_PUSH)) == b"two_shot_push"
+    assert L.dsmem_dtype_name(1) == b"bf16"
+    assert dsmem.version().startswith("dsmem_b200")
+    for (op, alg), stem in dsmem.CATALOGUE.items():
+        assert dsmem.file_stem(op, alg) == stem
+        assert dsmem.lookup(stem) == (op, alg)
+        assert dsmem.lookup(stem + ".cu") == (op, alg)
+        assert (dsmem.COLLECTIVES_DIR / f"{stem}.cu").exists(), f"missing harness-compatible file {stem}.cu"
+    assert len(dsmem.CATALOGUE) == 29
+    assert dsmem.file_stem(dsmem.Op.ALLTOALL, dsmem.Alg.RING) is None
+    with pytest.raises(dsmem.DsmemError):
+        dsmem.lookup("allreduce__nope__x")
+
+
+def pow2(n):
+    return n & (n - 1) == 0
+
+
+def grid2d(n):
+    r = 4 if n >= 16 else (2 if n >= 4 else 1)
+    return r, n // r
+
+
+# (op, alg) -> (constraint(N, M, B), smem elements(N, M)) restated from the reference files
+def rules(dsmem):
+    A, O = dsmem.Alg, dsmem.Op
+    m16 = lambda n, m, b: (m * b) % 16 == 0
+    return {
+        (O.ALLREDUCE, A.RECURSIVE_DOUBLING): (lambda n, m, b: pow2(n) and m16(n, m, b), lambda n, m: 3 * m),
+        (O.ALLREDUCE, A.SHIFT_ACCUMULATE_BULK): (lambda n, m, b: n == 4 and m16(n, m, b), lambda n, m: 3 * m),
+        (O.ALLREDUCE, A.SHIFT_ACCUMULATE_ATOMIC): (lambda n, m, b: n in (2, 4) and m16(n, m, b), lambda n, m: 2 * m),
+        (O.ALLREDUCE, A.DIRECT_REPLICATED_PUSH): (m16, lambda n, m: (n + 2) * m),
+        (O.ALLREDUCE, A.PULL_REDUCE_SCATTER_PUSH_ALLGATHER): (lambda n, m, b: 32 % n == 0 and m % n == 0 and m16(n, m, b),
+                                                              lambda n, m: m),
+        (O.ALLREDUCE, A.RING): (lambda n, m, b: m % n == 0 and ((m // n) * b) % 16 == 0, lambda n, m: m + m // n),
+        (O.ALLREDUCE, A.RABENSEIFNER): (lambda n, m, b: pow2(n) and m % n == 0 and ((m // n) * b) % 16 == 0,
+                                        lambda n, m: m + m // 2),
+        (O.ALLREDUCE, A.ONE_SHOT_PULL): (m16, lambda n, m: 2 * m),
+        (O.ALLREDUCE, A.TWO_SHOT_PUSH): (lambda n, m, b: m % n == 0 and ((m // n) * b) % 16 == 0, lambda n, m: 2 * m),
+        (O.ALLREDUCE, A.REDUCE_BCAST_BINOMIAL): (lambda n, m, b: pow2(n) and m16(n, m, b), lambda n, m: 2 * m),
+        (O.ALLREDUCE, A.ATOMIC_ALL_PUSH): (m16, lambda n, m: 2 * m),
+        (O.ALLREDUCE, A.MESH_2D): (lambda n, m, b: m % grid2d(n)[1] == 0 and ((m // grid2d(n)[1]) * b) % 16 == 0,
+                                   lambda n, m: m + (sum(grid2d(n)) + 1) * (m // grid2d(n)[1])),
+        (O.ALLGATHER, A.RECURSIVE_DOUBLING): (lambda n, m, b: pow2(n) and m16(n, m, b), lambda n, m: n * m),
+        (O.ALLGATHER, A.DIRECT_SHIFT): (m16, lambda n, m: n * m),
+        (O.ALLGATHER, A.DIRECT_REPLICATED_PUSH): (m16, lambda n, m: (n + 1) * m),
+        (O.ALLGATHER, A.RING): (m16, lambda n, m: n * m),
+        (O.ALLGATHER, A.BRUCK): (m16, lambda n, m: n * m),
+        (O.ALLGATHER, A.DIRECT_PULL): (m16, lambda n, m: (n + 1) * m),
+        (O.ALLGATHER, A.GATHER_BCAST_BINOMIAL): (lambda n, m, b: pow2(n) and m16(n, m, b), lambda n, m: n * m),
+        (O.REDUCESCATTER, A.RING): (m16, lambda n, m: n * m + m),
+        (O.REDUCESCATTER, A.RECURSIVE_HALVING): (lambda n, m, b: pow2(n) and m16(n, m, b), lambda n, m: n * m + n * m // 2),
+        (O.REDUCESCATTER, A.DIRECT_PUSH): (m16, lambda n, m: 2 * n * m + m),
+        (O.REDUCESCATTER, A.DIRECT_PULL): (m16, lambda n, m: n * m + m),
+        (O.ALLTOALL, A.PAIRWISE_EXCHANGE): (lambda n, m, b: n == 2 and m16(n, m, b), lambda n, m: n * m + m),
+        (O.ALLTOALL, A.DIRECT_PUSH): (m16, lambda n, m: 2 * n * m),
+        (O.ALLTOALL, A.PAIRWISE_XOR): (lambda n, m, b: pow2(n) and m16(n, m, b), lambda n, m: 2 * n * m),
+        (O.ALLTOALL, A.SHIFT): (m16, lambda n, m: 2 * n * m),
+        (O.ALLTOALL, A.BRUCK): (lambda n, m, b: pow2(n) and m16(n, m, b), lambda n, m: n * m + n * m // 2),
+        (O.ALLTOALL, A.DIRECT_PULL): (m16, lambda n, m: 2 * n * m),
+    }
+
+
+SMEM_LIMIT = 232448
+PAYLOADS = [2 ** k for k in range(4, 18)] + [192 * 1024, 48, 96, 200, 1000]
+
+
+def test_legality_and_smem_match_reference_matrix(dsmem):
+    R = rules(dsmem)
+    assert set(R) == set(dsmem.CATALOGUE)
+    checked = 0
+    for (op, alg), (legal_fn, smem_fn) in R.items():
+        for dt in dsmem.Dtype:
+            b = dsmem.ELEM_BYTES[dt]
+            for n in dsmem.CLUSTER_SIZES:
+                for p in PAYLOADS:
+                    unit = b * (1 if op == dsmem.Op.ALLREDUCE else n)
+                    status, smem, legal = dsmem.query(op, alg, dt, n, p)
+                    if p % unit:
+                        assert status == dsmem.Status.ILLEGAL_CONFIG and not legal
+                        continue
+                    m = p // unit
+                    if not legal_fn(n, m, b):
+                        assert status == dsmem.Status.ILLEGAL_CONFIG, (op, alg, dt, n, p)
+                        continue
+                    want = 128 + smem_fn(n, m) * b
+                    assert smem == want, (op.name, alg.name, dt.name, n, p, smem, want)
+                    if want > SMEM_LIMIT:
+                        assert status == dsmem.Status.SMEM_LIMIT
+                    else:
+                        assert status == dsmem.Status.OK and legal
+                    checked += 1
+    assert checked > 2000
+
+
+def test_auto_defaults_and_table(dsmem, tmp_path):
+    Op, Alg, Dt = dsmem.Op, dsmem.Alg, dsmem.Dtype
+    assert dsmem.autotune_pick(Op.ALLREDUCE, Dt.F32, 8, 16384) == Alg.TWO_SHOT_PUSH
+    # two-shot needs N | M with 16-B chunks; 64 B at N = 8 is not legal for it
+    pick = dsmem.autotune_pick(Op.ALLREDUCE, Dt.F32, 8, 64)
+    assert pick != Alg.TWO_SHOT_PUSH and dsmem.query(Op.ALLREDUCE, pick, Dt.F32, 8, 64)[2]
+    table = tmp_path / "tune.txt"
+    table.write_text("# op N bytes dtype alg\nallreduce 8 256 f32 ring\nallreduce 8 65536 f32 one_shot_pull\n")
+    dsmem.autotune_load(table)
+    try:
+        assert dsmem.autotune_pick(Op.ALLREDUCE, Dt.F32, 8, 4096) == Alg.RING
+        assert dsmem.autotune_pick(Op.ALLREDUCE, Dt.F32, 8, 65536) == Alg.ONE_SHOT_PULL
+        # 128 KiB: one-shot pull would need 256 KiB of shared memory, so AUTO falls back to a fitting one
+        big = dsmem.autotune_pick(Op.ALLREDUCE, Dt.F32, 8, 131072)
+        assert big != Alg.ONE_SHOT_PULL and dsmem.query(Op.ALLREDUCE, big, Dt.F32, 8, 131072)[0] == dsmem.Status.OK
+        # below the smallest entry: built-in default order
+        assert dsmem.autotune_pick(Op.ALLREDUCE, Dt.F32, 8, 128) != Alg.AUTO
+        # an entry whose algorithm is illegal at that size falls back to the defaults
+        assert dsmem.autotune_pick(Op.ALLREDUCE, Dt.BF16, 8, 4096) == Alg.TWO_SHOT_PUSH
+    finally:
+        empty = tmp_path / "empty.txt"
+        empty.write_text("")
+        dsmem.autotune_load(empty)
+    bad = tmp_path / "bad.txt"
+    bad.write_text("allreduce 8 256 f32 no_such_alg\n")
+    with pytest.raises(dsmem.DsmemError):
+        dsmem.autotune_load(bad)
+    bad.write_text("alltoall 8 256 f32 ring\n")   # ring does not exist for alltoall
+    with pytest.raises(dsmem.DsmemError):
+        dsmem.autotune_load(bad)
+
+
+def test_invalid_arguments(dsmem):
+    st, _, legal = dsmem.query(dsmem.Op.ALLREDUCE, dsmem.Alg.RING, dsmem.Dtype.F32, 3, 4096)
+    assert st == dsmem.Status.INVALID_ARGUMENT and not legal
+    st, _, _ = dsmem.query(dsmem.Op.ALLTOALL, dsmem.Alg.RING, dsmem.Dtype.F32, 4, 4096)
+    assert st == dsmem.Status.ILLEGAL_CONFIG
+    with pytest.raises(dsmem.DsmemError) as e:
+        dsmem.launch(dsmem.Op.ALLREDUCE, dsmem.Alg.RING, dsmem.Dtype.F32, 8, 4096, 16, 32, 1)
+    assert e.value.status == dsmem.Status.INVALID_ARGUMENT or e.value.status == dsmem.Status.CUDA
