@@ -334,29 +334,67 @@ struct AR_ShiftAccumulateBulk {
     }
 };
 
-// Remote element-wise add of one 16-byte packet of T into a peer's shared memory (fire-and-forget).
+// Accumulator element of the remote-atomic algorithms: bf16 sums accumulate in fp32 (a chain of N-1
+// remote adds rounded to bf16 after each add drifted beyond the bf16 tolerance at N = 16); f32 and int32
+// accumulate in their own type. Values are widened on load and narrowed on store.
 template <typename T>
-__device__ __forceinline__ void red_add_packet(uint32_t caddr, uint4 v);
+struct AccOf {
+    using type = T;
+};
 template <>
-__device__ __forceinline__ void red_add_packet<float>(uint32_t a, uint4 v) {
+struct AccOf<__nv_bfloat16> {
+    using type = float;
+};
+
+// Remote element-wise add of one 16-byte packet of accumulator elements into a peer (fire-and-forget).
+__device__ __forceinline__ void red_add_packet(float, uint32_t a, uint4 v) {
     red_cluster_add_f32(a, __uint_as_float(v.x));
     red_cluster_add_f32(a + 4, __uint_as_float(v.y));
     red_cluster_add_f32(a + 8, __uint_as_float(v.z));
     red_cluster_add_f32(a + 12, __uint_as_float(v.w));
 }
-template <>
-__device__ __forceinline__ void red_add_packet<int>(uint32_t a, uint4 v) {
+__device__ __forceinline__ void red_add_packet(int, uint32_t a, uint4 v) {
     red_cluster_add_u32(a, v.x);
     red_cluster_add_u32(a + 4, v.y);
     red_cluster_add_u32(a + 8, v.z);
     red_cluster_add_u32(a + 12, v.w);
 }
-template <>
-__device__ __forceinline__ void red_add_packet<__nv_bfloat16>(uint32_t a, uint4 v) {
-    red_cluster_add_bf16x2(a, v.x);
-    red_cluster_add_bf16x2(a + 4, v.y);
-    red_cluster_add_bf16x2(a + 8, v.z);
-    red_cluster_add_bf16x2(a + 12, v.w);
+
+// Global T[M] -> shared accumulator array (widening bf16 to fp32), all threads.
+template <typename T>
+__device__ __forceinline__ void g2s_acc(const Ctx& c, uint32_t off, const T* g, uint32_t M) {
+    if constexpr (sizeof(typename AccOf<T>::type) == sizeof(T)) {
+        g2s(c, off, g, M * (uint32_t)sizeof(T));
+    } else {
+        const uint4* src = reinterpret_cast<const uint4*>(g);
+        uint4* dst = c.ptr<uint4>(off);
+        const uint32_t n = (M * (uint32_t)sizeof(T)) >> 4;   // 8 bf16 per packet -> 2 fp32 packets
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+            const auto a = Pk<__nv_bfloat16, Sum>::open(__ldcs(src + i));
+            dst[2 * i] = make_uint4(__float_as_uint(a.v[0]), __float_as_uint(a.v[1]), __float_as_uint(a.v[2]),
+                                    __float_as_uint(a.v[3]));
+            dst[2 * i + 1] = make_uint4(__float_as_uint(a.v[4]), __float_as_uint(a.v[5]), __float_as_uint(a.v[6]),
+                                        __float_as_uint(a.v[7]));
+        }
+    }
+}
+// Shared accumulator array -> global T[M] (narrowing fp32 to bf16), all threads.
+template <typename T>
+__device__ __forceinline__ void s2g_acc(const Ctx& c, T* g, uint32_t off, uint32_t M) {
+    if constexpr (sizeof(typename AccOf<T>::type) == sizeof(T)) {
+        s2g(c, g, off, M * (uint32_t)sizeof(T));
+    } else {
+        const uint4* src = c.ptr<const uint4>(off);
+        uint4* dst = reinterpret_cast<uint4*>(g);
+        const uint32_t n = (M * (uint32_t)sizeof(T)) >> 4;
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint4 lo = src[2 * i], hi = src[2 * i + 1];
+            typename Pk<__nv_bfloat16, Sum>::Acc a{{__uint_as_float(lo.x), __uint_as_float(lo.y), __uint_as_float(lo.z),
+                                                    __uint_as_float(lo.w), __uint_as_float(hi.x), __uint_as_float(hi.y),
+                                                    __uint_as_float(hi.z), __uint_as_float(hi.w)}};
+            __stcs(dst + i, Pk<__nv_bfloat16, Sum>::close(a));
+        }
+    }
 }
 
 // allreduce__shift_accumulate_atomic__clusterfusion.cu:27-40 (sum only; N in {2,4}; 1 round at N = 2,
@@ -365,27 +403,29 @@ __device__ __forceinline__ void red_add_packet<__nv_bfloat16>(uint32_t a, uint4 
 template <int N_, typename T_, class Op_>
 struct AR_ShiftAccumulateAtomic {
     DSB_TRAITS(AllReduce, 0)
+    using AccT = typename AccOf<T_>::type;
+    static constexpr uint32_t AB = sizeof(AccT);
     __host__ __device__ static constexpr bool legal(uint32_t M) {
         return (N_ == 2 || N_ == 4) && mult16(M * B) && IsSum<Op_>::value;
     }
-    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * M * B; }
-    static __device__ void load(Ctx& c, const T* g, uint32_t M) { g2s(c, kD0, g, M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * M * AB; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) { g2s_acc<T>(c, kD0, g, M); }
     static __device__ void exec(Ctx& c, uint32_t M) {
-        const uint32_t MB = M * B, val = kD0, snap = kD0 + MB, n = MB >> 4;
+        const uint32_t MA = M * AB, val = kD0, snap = kD0 + MA, n = MA >> 4;
         constexpr int rounds = (N_ == 2) ? 1 : N_ - 2;
         for (int i = 1; i <= rounds; ++i) {
-            s2s(c, snap, val, MB);
+            s2s(c, snap, val, MA);
             cluster_sync();   // every CTA snapshotted before any remote add lands in its `val`
             const uint32_t peer_val = mapa(c.sa + val, (c.rank + i) % N_);
             const uint4* sp = c.ptr<const uint4>(snap);
-            for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) red_add_packet<T>(peer_val + 16u * u, sp[u]);
+            for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) red_add_packet(AccT{}, peer_val + 16u * u, sp[u]);
             cluster_sync();   // remote adds complete and visible
             c.st.round(i - 1);
         }
     }
     static __device__ void store(Ctx& c, T* g, uint32_t M) {
         __syncthreads();
-        s2g(c, g, kD0, M * B);
+        s2g_acc<T>(c, g, kD0, M);
     }
 };
 
@@ -741,27 +781,29 @@ struct AR_ReduceBcastBinomial {
 template <int N_, typename T_, class Op_>
 struct AR_AtomicAllPush {
     DSB_TRAITS(AllReduce, 0)
+    using AccT = typename AccOf<T_>::type;
+    static constexpr uint32_t AB = sizeof(AccT);
     __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B) && IsSum<Op_>::value; }
-    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * M * B; }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * M * AB; }
     static __device__ void load(Ctx& c, const T* g, uint32_t M) {
-        g2s(c, kD0, g, M * B);
+        g2s_acc<T>(c, kD0, g, M);
         __syncthreads();
-        s2s(c, kD0 + M * B, kD0, M * B);   // accumulator starts as my own vector
+        s2s(c, kD0 + M * AB, kD0, M * AB);   // accumulator starts as my own vector
     }
     static __device__ void exec(Ctx& c, uint32_t M) {
-        const uint32_t MB = M * B, n = MB >> 4;
+        const uint32_t MA = M * AB, n = MA >> 4;
         const uint4* pm = c.ptr<const uint4>(kD0);
         for (uint32_t idx = threadIdx.x; idx < (N_ - 1) * n; idx += blockDim.x) {
             const uint32_t k = idx / n, u = idx - k * n;
             const uint32_t peer = (c.rank + 1 + k) % N_;
-            red_add_packet<T>(mapa(c.sa + kD0 + MB + 16u * u, peer), pm[u]);
+            red_add_packet(AccT{}, mapa(c.sa + kD0 + MA + 16u * u, peer), pm[u]);
         }
         c.st.round(0);
         cluster_sync();   // all remote adds performed and visible
     }
     static __device__ void store(Ctx& c, T* g, uint32_t M) {
         __syncthreads();
-        s2g(c, g, kD0 + M * B, M * B);
+        s2g_acc<T>(c, g, kD0 + M * AB, M);
     }
 };
 
@@ -914,11 +956,14 @@ struct AG_RecursiveDoubling {
     }
 };
 
-// allgather__direct_shift__clusterfusion.cu:24-43. Own data in slot b. N-1 rounds; each round
-// re-initialises the mbarrier (inval + init), barrier, pushes slot b to (b+i) mod N, waits, barrier.
+// allgather__direct_shift__clusterfusion.cu:24-43. Own data in slot b. N-1 rounds; round i arms a fresh
+// barrier, cluster barrier, pushes slot b to (b+i) mod N, waits, cluster barrier. The reference re-runs
+// mbarrier.init on one barrier every round; re-initialising a barrier that has completed a phase timed
+// out on sm_100a, so each round owns its own barrier (initialised once per launch, phase-tracked across
+// problems). Rounds, partners, messages and the two cluster barriers per round are unchanged.
 template <int N_, typename T_, class Op_>
 struct AG_DirectShift {
-    DSB_TRAITS(AllGather, 1)
+    DSB_TRAITS(AllGather, N_ - 1)
     __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
     __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
     static __device__ void load(Ctx& c, const T* g, uint32_t M) {
@@ -928,16 +973,10 @@ struct AG_DirectShift {
     static __device__ void exec(Ctx& c, uint32_t M) {
         const uint32_t MB = M * B, seg = kD0 + c.rank * MB;
         for (int i = 1; i < N_; ++i) {
-            if (threadIdx.x == 0) {
-                mbar_inval(c.bar(0));
-                mbar_init(c.bar(0), 1);
-                fence_mbar_init();
-                arm(c, 0, MB);
-            }
-            c.phase &= ~1u;   // a fresh barrier starts in phase 0
-            cluster_sync();   // re-initialised everywhere before anyone pushes
-            if (threadIdx.x == 0) push<N_>(c, (c.rank + i) % N_, seg, seg, MB, 0);
-            wait(c, 0);
+            if (threadIdx.x == 0) arm(c, i - 1, MB);
+            cluster_sync();   // armed everywhere before anyone pushes
+            if (threadIdx.x == 0) push<N_>(c, (c.rank + i) % N_, seg, seg, MB, i - 1);
+            wait(c, i - 1);
             cluster_sync();
             c.st.round(i - 1);
         }
@@ -1481,6 +1520,7 @@ struct BatchArgs {
     unsigned long long wait_limit_ns; // per problem
     uint32_t M;                       // elements per rank block
     uint32_t smem_bytes;              // dynamic shared memory of the launch
+    uint32_t sub;                     // pipelined drivers: units per problem (M / sub elements each)
 };
 
 __device__ __forceinline__ void ctx_init(Ctx& c, uint32_t smem_bytes, unsigned* err, unsigned long long limit) {
@@ -1527,6 +1567,118 @@ __global__ void __launch_bounds__(256) batch_kernel(const BatchArgs a) {
         A::store(c, static_cast<T*>(a.out) + slot * out_r, a.M);
         cluster_sync();   // exit: no peer still reads or writes my window for this problem
     }
+}
+
+// -----------------------------------------------------------------------------------------------------
+// Pipelined persistent driver of the two-shot AllReduce (allreduce__two_shot_push__trtllm.cu:23-59) for
+// batches. Per problem the shots are exactly AR_TwoShotPush's (N-1 bulk pushes of chunk j into slot[b] of
+// CTA j, reduce, N-1 bulk pushes of the reduced chunk into position b of every peer), but:
+//   * the input arrives by a bulk global->shared copy into one of two X buffers, issued one problem ahead
+//     (right after this problem's first shot), and the output leaves by a bulk shared->global copy, so
+//     HBM traffic of neighbouring problems overlaps the SM-to-SM shots of the current one;
+//   * there is no per-problem cluster barrier. The shot barriers already order everything:
+//     my reduce(p) -> my shot 2(p) -> peer's shot-2 wait(p) -> peer's shot 1(p+1), so a peer writes my
+//     slots for p+1 only after I have consumed them for p; and a peer's shot 2(p+1) into my X buffer needs
+//     my shot 1(p+1), which I issue only after my load(p+1) has landed.
+//   * a problem may be split into `sub` sub-vector units that each run the two shots (the element-wise sum
+//     is separable), so large payloads keep a small shared-memory footprint and several CTAs per SM.
+// Layout per unit of U elements: barriers 0/1 = input landed in X0/X1, 2 = shot 1 (reduce-scatter),
+// 3 = shot 2 (all-gather); X0 = [kD0, +UB), X1 = [kD0+UB, +UB), slots = [kD0+2UB, +UB) (slot r at r*CB).
+template <int N_, typename T_, class Op_>
+struct AR_TwoShotPipelined {
+    DSB_TRAITS(AllReduce, 4)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return AR_TwoShotPush<N_, T_, Op_>::legal(M); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 3ull * M * B; }
+};
+
+template <class A>
+__global__ void __launch_bounds__(256) two_shot_pipelined_kernel(const BatchArgs a) {
+    using T = typename A::T;
+    using Op = typename A::Op;
+    constexpr int N = A::kN;
+    constexpr int kLoad0 = 0, kRS = 2, kAG = 3;
+    Ctx c;
+    ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
+    init_bars<A>(c);
+    cluster_sync();   // every barrier of the cluster initialised before any remote push
+    // A problem of M elements per rank flows through the pipeline as `sub` units of U = M / sub elements,
+    // each a complete two-shot AllReduce of its sub-vector (the element-wise sum is separable).
+    const uint32_t S = a.sub, U = a.M / S, UB = U * A::B, CB = UB / N, n = CB >> 4;
+    const uint32_t slots = kD0 + 2u * UB;
+    const T* in = static_cast<const T*>(a.in);
+    T* out = static_cast<T*>(a.out);
+    const long long step = (long long)num_clusters();
+    const long long first = (long long)cluster_id();
+    const long long mine = first < a.num_problems ? (a.num_problems - 1 - first) / step + 1 : 0;
+    const long long units = mine * S;
+    // element offset of unit k of this cluster (this rank's part)
+    auto unit_off = [&](long long k) -> uint64_t {
+        const long long p = first + (k / S) * step;
+        return ((uint64_t)p * N + c.rank) * a.M + (uint64_t)(k % S) * U;
+    };
+    if (threadIdx.x == 0 && units > 0) {
+        arm(c, kLoad0, UB);
+        bulk_load_g2s(c.sa + kD0, in + unit_off(0), UB, c.bar(kLoad0));
+    }
+    for (long long k = 0; k < units; ++k) {
+        const uint32_t x = (uint32_t)(k & 1), X = kD0 + x * UB, s = (uint32_t)(k % S);
+        const uint64_t slot = (uint64_t)(first + (k / S) * step) * N + c.rank;
+        c.deadline = globaltimer() + c.wait_limit;
+        c.st.base = a.stamps != nullptr ? a.stamps + slot * kStamps : nullptr;
+        if (s == 0 && a.smid != nullptr && threadIdx.x == 0) a.smid[slot] = smid();
+        wait(c, kLoad0 + (int)x);   // my input for unit k is in X
+        if (s == 0) c.st.mark(0);
+        if (threadIdx.x == 0) {
+            // shot 1: chunk j of my input -> slot[b] of CTA j
+            arm(c, kRS, (N - 1) * CB);
+            for (uint32_t j = 1; j < (uint32_t)N; ++j) {
+                const uint32_t dst = (c.rank + j) % N;
+                push<N>(c, dst, slots + c.rank * CB, X + dst * CB, CB, kRS);
+            }
+            // prefetch the next unit into the other buffer once the store of the previous one read it
+            if (k + 1 < units) {
+                bulk_wait_read0();
+                arm(c, kLoad0 + (int)(x ^ 1u), UB);
+                bulk_load_g2s(c.sa + kD0 + (x ^ 1u) * UB, in + unit_off(k + 1), UB, c.bar(kLoad0 + (int)(x ^ 1u)));
+            }
+        }
+        wait(c, kRS);   // all N-1 partials of my chunk landed (and the peers' reads of their chunk b are done)
+        {
+            uint4* my = c.ptr<uint4>(X + c.rank * CB);
+            const uint4* ps = c.ptr<const uint4>(slots);
+            for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) {
+                uint4 v[N];
+#pragma unroll
+                for (int r = 0; r < N; ++r) v[r] = (r == (int)c.rank) ? my[u] : ps[r * n + u];
+                auto acc = Pk<T, Op>::open(v[0]);
+#pragma unroll
+                for (int r = 1; r < N; ++r) Pk<T, Op>::add(acc, v[r]);
+                my[u] = Pk<T, Op>::close(acc);
+            }
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (s + 1 == S) c.st.round(0);
+        if (threadIdx.x == 0) {
+            // shot 2: my reduced chunk -> position b of every peer
+            arm(c, kAG, (N - 1) * CB);
+            for (uint32_t j = 1; j < (uint32_t)N; ++j) {
+                const uint32_t dst = (c.rank + j) % N;
+                push<N>(c, dst, X + c.rank * CB, X + c.rank * CB, CB, kAG);
+            }
+        }
+        wait(c, kAG);   // every reduced chunk is in X
+        if (s + 1 == S) {
+            c.st.round(1);
+            c.st.mark(1);
+        }
+        if (threadIdx.x == 0) {
+            bulk_store_s2g(out + unit_off(k), c.sa + X, UB);
+            bulk_commit();
+        }
+    }
+    if (threadIdx.x == 0) bulk_wait_all0();
+    cluster_sync();   // no CTA leaves while a peer may still push into it
 }
 
 // Reference harness contract (collectives/harness/main.cu): one cluster, compile-time M.

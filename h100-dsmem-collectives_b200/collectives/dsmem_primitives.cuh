@@ -137,8 +137,13 @@ __device__ __forceinline__ void red_cluster_add_f32(uint32_t caddr, float v) {
 __device__ __forceinline__ void red_cluster_add_u32(uint32_t caddr, uint32_t v) {
     asm volatile("red.shared::cluster.add.u32 [%0], %1;" ::"r"(caddr), "r"(v) : "memory");
 }
-__device__ __forceinline__ void red_cluster_add_bf16x2(uint32_t caddr, uint32_t v) {
-    asm volatile("red.shared::cluster.add.noftz.bf16x2 [%0], %1;" ::"r"(caddr), "r"(v) : "memory");
+__device__ __forceinline__ uint32_t atom_cas_cluster_b32(uint32_t caddr, uint32_t expected, uint32_t desired) {
+    uint32_t old;
+    asm volatile("atom.shared::cluster.cas.b32 %0, [%1], %2, %3;"
+                 : "=r"(old)
+                 : "r"(caddr), "r"(expected), "r"(desired)
+                 : "memory");
+    return old;
 }
 // Order this thread's generic-proxy shared-memory accesses against the async proxy (bulk copies,
 // st.async). Needed between writing a buffer with ordinary stores and handing it to a bulk copy.

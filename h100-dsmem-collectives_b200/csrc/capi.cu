@@ -114,6 +114,7 @@ struct State {
     std::map<int, DeviceState> dev;
     std::map<TuneKey, std::map<uint64_t, int>> tune;   // (op, N, dtype) -> {bytes -> alg}
     unsigned long long wait_limit_ns = 1000000000ull;
+    bool pipelined = true;   // batches use a pipelined driver where one exists
 };
 
 State& st() {
@@ -201,39 +202,39 @@ DeviceState& device_state(int dev) {
     return d;
 }
 
-cudaError_t ensure_attrs(DeviceState& d, const KernelEntry* e, uint64_t smem) {
-    auto it = d.smem_attr.find(e->fn);
+cudaError_t ensure_attrs(DeviceState& d, const void* fn, int n, uint64_t smem) {
+    auto it = d.smem_attr.find(fn);
     if (it == d.smem_attr.end() || (uint64_t)it->second < smem) {
         cudaError_t r;
-        if (e->n > 8) {
-            r = cudaFuncSetAttribute(e->fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (n > 8) {
+            r = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
             if (r != cudaSuccess) return r;
         }
         const int want = (int)std::max<uint64_t>(smem, it == d.smem_attr.end() ? 0 : (uint64_t)it->second);
-        r = cudaFuncSetAttribute(e->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
+        r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
         if (r != cudaSuccess) return r;
-        d.smem_attr[e->fn] = want;
+        d.smem_attr[fn] = want;
     }
     return cudaSuccess;
 }
 
-void fill_cfg(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, const KernelEntry* e, long long clusters,
-              uint64_t smem, cudaStream_t stream) {
+void fill_cfg(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, int n, long long clusters, uint64_t smem,
+              cudaStream_t stream) {
     cfg = cudaLaunchConfig_t{};
-    cfg.gridDim = dim3((unsigned)(clusters * e->n), 1, 1);
+    cfg.gridDim = dim3((unsigned)(clusters * n), 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = stream;
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)e->n;
+    attr[0].val.clusterDim.x = (unsigned)n;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
 }
 
-cudaError_t occupancy(DeviceState& d, const KernelEntry* e, uint64_t smem, int* out) {
-    auto key = std::make_pair(e->fn, smem);
+cudaError_t occupancy(DeviceState& d, const void* fn, int n_cta, uint64_t smem, int* out) {
+    auto key = std::make_pair(fn, smem);
     auto it = d.occupancy.find(key);
     if (it != d.occupancy.end()) {
         *out = it->second;
@@ -241,9 +242,9 @@ cudaError_t occupancy(DeviceState& d, const KernelEntry* e, uint64_t smem, int* 
     }
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[1];
-    fill_cfg(cfg, attr, e, 1, smem, nullptr);
+    fill_cfg(cfg, attr, n_cta, 1, smem, nullptr);
     int n = 0;
-    cudaError_t r = cudaOccupancyMaxActiveClusters(&n, e->fn, &cfg);
+    cudaError_t r = cudaOccupancyMaxActiveClusters(&n, fn, &cfg);
     if (r != cudaSuccess) return r;
     d.occupancy[key] = n;
     *out = n;
@@ -259,6 +260,17 @@ cudaError_t error_word(DeviceState& d, unsigned** out) {
     }
     *out = d.err;
     return cudaSuccess;
+}
+
+// Units per problem for a pipelined driver: the smallest split into legal sub-vectors of at most
+// kUnitBytes per CTA (16 KiB keeps three unit buffers at 48 KiB, i.e. four CTAs per SM); 0 if none.
+constexpr uint64_t kUnitBytes = 16384;
+uint32_t pipeline_units(const KernelEntry* e, uint32_t m) {
+    const uint64_t bytes = (uint64_t)m * e->elem_bytes;
+    const uint32_t s0 = (uint32_t)std::max<uint64_t>(1, (bytes + kUnitBytes - 1) / kUnitBytes);
+    for (uint32_t s = s0; s <= m && s < s0 + 4096; ++s)
+        if (m % s == 0 && e->legal(m / s)) return s;
+    return 0;
 }
 
 dsmem_status prepare(int op, int alg, int dtype, int n, size_t bytes, const KernelEntry** entry, uint32_t* m_out,
@@ -329,13 +341,25 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
     if (cudaGetDevice(&dev) != cudaSuccess) return DSMEM_ERR_CUDA;
     dsb::BatchArgs a{};
     int resident = 0;
+    const void* fn = e->fn;
     {
         State& g = st();
         std::lock_guard<std::mutex> lock(g.mu);
         DeviceState& d = device_state(dev);
         if (smem > (uint64_t)d.optin) return DSMEM_ERR_SMEM_LIMIT;
-        if (ensure_attrs(d, e, smem) != cudaSuccess) return DSMEM_ERR_CUDA;
-        if (occupancy(d, e, smem, &resident) != cudaSuccess) return DSMEM_ERR_CUDA;
+        // batches use the pipelined driver when the algorithm has one and its shared memory fits
+        a.sub = 1;
+        if (g.pipelined && num_clusters > 1 && e->fn_pipe != nullptr) {
+            const uint32_t sub = pipeline_units(e, m);
+            const uint64_t sp = sub ? e->smem_pipe(m / sub) : 0;
+            if (sub && sp <= dsb::kSmemLimit && sp <= (uint64_t)d.optin) {
+                fn = e->fn_pipe;
+                smem = sp;
+                a.sub = sub;
+            }
+        }
+        if (ensure_attrs(d, fn, e->n, smem) != cudaSuccess) return DSMEM_ERR_CUDA;
+        if (occupancy(d, fn, e->n, smem, &resident) != cudaSuccess) return DSMEM_ERR_CUDA;
         if (resident < 1) return DSMEM_ERR_SMEM_LIMIT;   // the cluster cannot be placed (main.cu:221)
         if (error_word(d, &a.err) != cudaSuccess) return DSMEM_ERR_CUDA;
         a.wait_limit_ns = g.wait_limit_ns;
@@ -351,9 +375,9 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
     a.smem_bytes = (uint32_t)smem;
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[1];
-    fill_cfg(cfg, attr, e, clusters, smem, reinterpret_cast<cudaStream_t>(stream));
+    fill_cfg(cfg, attr, e->n, clusters, smem, reinterpret_cast<cudaStream_t>(stream));
     void* args[] = {&a};
-    if (cudaLaunchKernelExC(&cfg, e->fn, args) != cudaSuccess) return DSMEM_ERR_CUDA;
+    if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess) return DSMEM_ERR_CUDA;
     return DSMEM_OK;
 }
 
@@ -390,9 +414,9 @@ dsmem_status dsmem_max_active_clusters(dsmem_op op, dsmem_alg alg, dsmem_dtype d
     std::lock_guard<std::mutex> lock(st().mu);
     DeviceState& d = device_state(dev);
     if (smem > (uint64_t)d.optin) return DSMEM_ERR_SMEM_LIMIT;
-    if (ensure_attrs(d, e, smem) != cudaSuccess) return DSMEM_ERR_CUDA;
+    if (ensure_attrs(d, e->fn, e->n, smem) != cudaSuccess) return DSMEM_ERR_CUDA;
     int n = 0;
-    if (occupancy(d, e, smem, &n) != cudaSuccess) return DSMEM_ERR_CUDA;
+    if (occupancy(d, e->fn, e->n, smem, &n) != cudaSuccess) return DSMEM_ERR_CUDA;
     if (clusters) *clusters = n;
     return DSMEM_OK;
 }
@@ -508,6 +532,12 @@ dsmem_status dsmem_set_wait_limit_ns(unsigned long long ns) {
     if (ns == 0) return DSMEM_ERR_INVALID_ARGUMENT;
     std::lock_guard<std::mutex> lock(st().mu);
     st().wait_limit_ns = ns;
+    return DSMEM_OK;
+}
+
+dsmem_status dsmem_set_pipelined(int enable) {
+    std::lock_guard<std::mutex> lock(st().mu);
+    st().pipelined = enable != 0;
     return DSMEM_OK;
 }
 

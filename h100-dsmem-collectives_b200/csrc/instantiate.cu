@@ -54,6 +54,17 @@ void add_all_n(Registry& r, int alg) {
     add<A, 16>(r, alg);
 }
 
+// Attach the pipelined batch driver P<N> to the entry of (alg, N) just registered.
+template <int N>
+void add_two_shot_pipelined(Registry& r) {
+    using P = AR_TwoShotPipelined<N, ElemT, Sum>;
+    for (KernelEntry& e : r)
+        if (e.op == 0 && e.alg == kTwoShotPush && e.dtype == DSB_DT && e.n == N) {
+            e.fn_pipe = reinterpret_cast<const void*>(&two_shot_pipelined_kernel<P>);
+            e.smem_pipe = &smem_fn<P>;
+        }
+}
+
 }  // namespace
 
 #define DSB_CAT3(a, b, c, d) a##b##c##d
@@ -71,6 +82,10 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<AR_Rabenseifner>(r, kRabenseifner);
     add_all_n<AR_OneShotPull>(r, kOneShotPull);
     add_all_n<AR_TwoShotPush>(r, kTwoShotPush);
+    add_two_shot_pipelined<2>(r);
+    add_two_shot_pipelined<4>(r);
+    add_two_shot_pipelined<8>(r);
+    add_two_shot_pipelined<16>(r);
     add_all_n<AR_ReduceBcastBinomial>(r, kReduceBcastBinomial);
     add_all_n<AR_AtomicAllPush>(r, kAtomicAllPush);
     add_all_n<AR_Mesh2D>(r, kMesh2D);

@@ -14,6 +14,10 @@ struct KernelEntry {
     const void* fn;                      // __global__ batch_kernel<A>
     bool (*legal)(uint32_t m);           // static N/M constraints of the reference file
     uint64_t (*smem_bytes)(uint32_t m);  // dynamic shared memory per CTA
+    // Optional pipelined batch driver (same collective, overlapped HBM traffic), used for batches of more
+    // than one problem when its shared memory fits; nullptr if the algorithm has none.
+    const void* fn_pipe = nullptr;
+    uint64_t (*smem_pipe)(uint32_t m) = nullptr;
 };
 
 using Registry = std::vector<KernelEntry>;

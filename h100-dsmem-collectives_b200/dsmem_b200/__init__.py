@@ -146,6 +146,13 @@ def lib():
         "dsmem_lookup": (c_int, [ctypes.c_char_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
         "dsmem_set_wait_limit_ns": (c_int, [c_ull]),
         "dsmem_selftest_timeout": (c_int, [c_ull, c_vp]),
+        "dsmem_set_pipelined": (c_int, [c_int]),
+        "dsmem_rmsnorm_launch": (c_int, [c_int, c_vp, c_vp, ctypes.c_float, c_ll, c_int, c_int, c_vp, c_vp]),
+        "dsmem_rmsnorm_residual_launch": (c_int, [c_int, c_vp, c_vp, c_vp, ctypes.c_float, c_ll, c_int, c_int,
+                                                  c_vp, c_vp, c_vp]),
+        "dsmem_rmsnorm_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
+        "dsmem_ceiling_dsmem_bw": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double),
+                                           ctypes.POINTER(c_ll), ctypes.POINTER(c_int)]),
         "dsmem_version": (ctypes.c_char_p, []),
     }
     for name, (res, args) in sig.items():
@@ -237,6 +244,11 @@ def set_wait_limit_ns(ns):
     _ok(lib().dsmem_set_wait_limit_ns(int(ns)), "dsmem_set_wait_limit_ns")
 
 
+def set_pipelined(enable):
+    """Use (True, default) or bypass (False) the pipelined batch drivers."""
+    _ok(lib().dsmem_set_pipelined(1 if enable else 0), "dsmem_set_pipelined")
+
+
 def autotune_load(path):
     _ok(lib().dsmem_autotune_table_load(str(path).encode()), f"dsmem_autotune_table_load({path})")
 
@@ -259,6 +271,60 @@ def lookup(stem):
 def selftest_timeout(limit_ns, stream=0):
     """Launch the bounded-wait self-test kernel (see dsmem_selftest_timeout)."""
     _ok(lib().dsmem_selftest_timeout(int(limit_ns), ctypes.c_void_p(stream or None)), "dsmem_selftest_timeout")
+
+
+def rmsnorm(x, w, eps=1e-6, cluster_size=8, out=None, residual=None, pre_norm=None, stream=None):
+    """Cluster-fused RMSNorm of the rows of x (torch CUDA tensor [rows, hidden], bf16 or f32):
+    y = h * rsqrt(mean(h^2) + eps) * w with h = x (+ residual, stored to pre_norm if given)."""
+    import torch
+
+    if x.dim() != 2 or not x.is_cuda or not x.is_contiguous():
+        raise ValueError("x must be a contiguous CUDA [rows, hidden] tensor")
+    dt = dtype_of(x)
+    rows, hidden = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    s = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+    for t in (w, out) + ((residual,) if residual is not None else ()) + ((pre_norm,) if pre_norm is not None else ()):
+        if t.dtype != x.dtype or not t.is_contiguous() or not t.is_cuda:
+            raise ValueError("w/out/residual/pre_norm must be contiguous CUDA tensors of x's dtype")
+    if residual is None:
+        st = lib().dsmem_rmsnorm_launch(int(dt), x.data_ptr(), w.data_ptr(), float(eps), rows, hidden,
+                                        int(cluster_size), out.data_ptr(), ctypes.c_void_p(s or None))
+    else:
+        st = lib().dsmem_rmsnorm_residual_launch(int(dt), x.data_ptr(), residual.data_ptr(), w.data_ptr(), float(eps),
+                                                 rows, hidden, int(cluster_size),
+                                                 pre_norm.data_ptr() if pre_norm is not None else None,
+                                                 out.data_ptr(), ctypes.c_void_p(s or None))
+    _ok(st, f"dsmem_rmsnorm({dt.name}, {rows}x{hidden}, cluster {cluster_size})")
+    return out
+
+
+def rmsnorm_check(device=0):
+    """Raise DsmemError(TIMEOUT) if an RMSNorm kernel's bounded wait gave up since the last check."""
+    bits = ctypes.c_uint(0)
+    _ok(lib().dsmem_rmsnorm_check(int(device), ctypes.byref(bits)), "dsmem_rmsnorm_check")
+    if bits.value & 1:
+        raise DsmemError(Status.TIMEOUT, "rmsnorm")
+
+
+def dsmem_bandwidth_point(mode, cluster_size, passes, reps=5):
+    """(median ms, payload bytes, clusters) of one DSMEM ceiling launch configuration (mode 0 pull, 1 push)."""
+    ms, nbytes, cl = ctypes.c_double(0), ctypes.c_longlong(0), ctypes.c_int(0)
+    _ok(lib().dsmem_ceiling_dsmem_bw(int(mode), int(cluster_size), int(passes), int(reps), ctypes.byref(ms),
+                                     ctypes.byref(nbytes), ctypes.byref(cl)), "dsmem_ceiling_dsmem_bw")
+    return ms.value, nbytes.value, cl.value
+
+
+def dsmem_bandwidth_peak(mode, cluster_size, passes=(4, 8, 16, 32), reps=5):
+    """GPU-wide SM-to-SM bandwidth in GB/s = 1 / slope of launch time over payload bytes (least squares),
+    the method of the reference's roofline/harness/ceilings/src/dsmem_bw.cu. Returns (GB/s, points)."""
+    pts = [dsmem_bandwidth_point(mode, cluster_size, p, reps) for p in passes]
+    xs = [b for (_, b, _) in pts]
+    ys = [ms * 1e-3 for (ms, _, _) in pts]
+    mx, my = sum(xs) / len(xs), sum(ys) / len(ys)
+    slope = sum((x - mx) * (y - my) for x, y in zip(xs, ys)) / sum((x - mx) ** 2 for x in xs)
+    return (1.0 / slope / 1e9 if slope > 0 else float("nan")), pts
 
 
 def version():

@@ -153,11 +153,47 @@ dsmem_status dsmem_lookup(const char* file_stem, dsmem_op* op, dsmem_alg* alg);
 /* Per-device wait limit of the batch kernels in nanoseconds of %globaltimer (default 1e9). */
 dsmem_status dsmem_set_wait_limit_ns(unsigned long long ns);
 
+/* Batches of more than one problem run on a pipelined driver where the algorithm has one (two-shot
+ * AllReduce: bulk HBM loads/stores overlapped with the shots, no per-problem cluster barrier). 0 forces
+ * the plain driver (load, entry barrier, collective, store, exit barrier per problem). Default 1. */
+dsmem_status dsmem_set_pipelined(int enable);
+
 /* Failure-detection self-test: launches one 2-CTA cluster whose mbarrier is armed for 16 bytes that
  * never arrive, with a wait limit of `limit_ns`; every wait gives up after the limit and the kernel
  * exits normally. dsmem_check afterwards must report DSMEM_ERR_TIMEOUT. Replaces nothing in the
  * reference (its hangs were caught by a host watchdog, collectives/harness/main.cu:277-320). */
 dsmem_status dsmem_selftest_timeout(unsigned long long limit_ns, dsmem_stream_t stream);
+
+/*
+ * Cluster-fused RMSNorm: y[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w, fp32 statistics, bf16 or f32 in/out.
+ * Row r is split across a cluster of `cluster_size` CTAs (1, 2, 4, 8, 16; hidden/cluster_size elements per
+ * CTA, a multiple of 16 bytes and at most 2 KiB), whose partial sums of squares meet in a DSMEM AllReduce.
+ * Replaces RMSNormKernel of kernels/rmsnorm__llama__clusterfusion.cu:35-108 (called as
+ * clusterfusion.rmsnorm(x, w), roofline/harness/workloads/clusterfusion_rmsnorm.py:50), generalised from
+ * fp16 / 64 x 8192 / cluster 2 compiled in to run-time dtype, shape and cluster size.
+ * x, y: [rows][hidden] row-major, 16-byte aligned; w: [hidden].
+ */
+dsmem_status dsmem_rmsnorm_launch(dsmem_dtype dtype, const void* x, const void* w, float eps, long long rows,
+                                  int hidden, int cluster_size, void* y, dsmem_stream_t stream);
+
+/* As dsmem_rmsnorm_launch on h = x + residual (rounded to dtype), written to pre_norm (nullable) -- the
+ * RMSNorm half of hpc-ops' fused AllReduce+RMSNorm, kernels/rmsnorm_lamport__fused_allreduce_rmsnorm__hpcops.cu:37-197
+ * (outputPreNorm / outputNorm, :182-187 / :179-196). */
+dsmem_status dsmem_rmsnorm_residual_launch(dsmem_dtype dtype, const void* x, const void* residual, const void* w,
+                                           float eps, long long rows, int hidden, int cluster_size, void* pre_norm,
+                                           void* y, dsmem_stream_t stream);
+
+/* Read and clear the RMSNorm kernels' device error word of `device` (synchronous). */
+dsmem_status dsmem_rmsnorm_check(int device, unsigned* error_bits);
+
+/* SM-to-SM bandwidth ceiling (the DSMEM roofline denominator). Replaces the reference's microbenchmark
+ * roofline/harness/ceilings/src/dsmem_bw.cu:1-40 (ops `ld` and `tma_put`, ring +1, max active clusters,
+ * 96 KiB per pass): mode 0 pull (ld.shared::cluster.v4), 1 push (cp.async.bulk) to the ring neighbour,
+ * 2 push to every peer (8 KiB per peer per pass, 4 KiB at cluster size 16; the fan-out pattern of the direct
+ * and two-shot algorithms, which the reference did not measure). Times `reps` launches of `passes` passes;
+ * the caller fits 1/slope over several pass counts. */
+dsmem_status dsmem_ceiling_dsmem_bw(int mode, int cluster_size, int passes, int reps, double* ms_median,
+                                    long long* bytes_per_launch, int* clusters);
 
 /* Library version string. */
 const char* dsmem_version(void);

@@ -97,16 +97,45 @@ def payloads(op, alg, n, dt):
 @pytest.mark.parametrize("op,alg,n", CASES, ids=[f"{D.CATALOGUE[(o, a)]}-N{n}" for (o, a, n) in CASES])
 def test_parity(cuda, orc, op, alg, n):
     torch = cuda
-    ran = 0
+    ran, failures = 0, []
     for dt in D.Dtype:
         for p in payloads(op, alg, n, dt):
             batches = (1, 37) if p <= 16384 else (1, 3)
             for clusters in batches:
                 for pattern in ("A", "R"):
-                    run_case(torch, orc, op, alg, n, dt, p, clusters, pattern, seed=p + clusters)
+                    try:
+                        run_case(torch, orc, op, alg, n, dt, p, clusters, pattern, seed=p + clusters)
+                    except (AssertionError, D.DsmemError) as e:
+                        failures.append(f"{dt.name} P={p} clusters={clusters} pattern={pattern}: {e}")
                     ran += 1
     if ran == 0:
         pytest.skip("no legal configuration (reference static_assert)")
+    assert not failures, "\n".join(failures)
+
+
+@pytest.mark.parametrize("n", D.CLUSTER_SIZES)
+def test_two_shot_pipelined_matches_plain(cuda, orc, n):
+    """The pipelined batch driver of the two-shot AllReduce against the oracle, with the plain driver
+    forced for comparison; many problems per resident cluster, every dtype."""
+    failures = []
+    try:
+        for pipelined in (True, False):
+            D.set_pipelined(pipelined)
+            for dt in D.Dtype:
+                for p in (256 * n // 8 if n >= 8 else 256, 4096, 16384, 65536):
+                    if D.query(D.Op.ALLREDUCE, D.Alg.TWO_SHOT_PUSH, dt, n, p)[0] != D.Status.OK:
+                        continue
+                    for clusters, pattern in ((2, "A"), (301, "R"), (1200, "A")):
+                        if p * n * clusters > (256 << 20):
+                            continue
+                        try:
+                            run_case(cuda, orc, D.Op.ALLREDUCE, D.Alg.TWO_SHOT_PUSH, n, dt, p, clusters, pattern,
+                                     seed=clusters)
+                        except (AssertionError, D.DsmemError) as e:
+                            failures.append(f"pipelined={pipelined} {dt.name} P={p} clusters={clusters}: {e}")
+    finally:
+        D.set_pipelined(True)
+    assert not failures, "\n".join(failures)
 
 
 def test_many_problems_per_cluster(cuda, orc):
