@@ -240,10 +240,15 @@ def rmsnorm_config3(torch, D, hbm_peak, reps=50):
 
 
 def dsmem_ceiling(D, n):
-    """Measured SM-to-SM bandwidth at cluster size n: ring push and all-peer push (1/slope, GB/s)."""
-    ring, _ = D.dsmem_bandwidth_peak(1, n)
-    fan, _ = D.dsmem_bandwidth_peak(2, n)
-    return {"push_ring_GBps": round(ring, 1), "push_all_peers_GBps": round(fan, 1)}
+    """Measured SM-to-SM bandwidth at cluster size n (1/slope, GB/s): ring and all-peers push, in the
+    reference's one-CTA-per-SM shape and with four CTAs per SM; the peak is the best of them."""
+    out = {}
+    for cps in (1, 4):
+        for mode, name in ((1, "push_ring"), (2, "push_all_peers")):
+            gbs, _ = D.dsmem_bandwidth_peak(mode, n, ctas_per_sm=cps)
+            out[f"{name}_{cps}cta_GBps"] = round(gbs, 1)
+    out["peak_GBps"] = max(out.values())
+    return out
 
 
 def run_ours(args, rank, world, local):
@@ -344,10 +349,10 @@ def run_ours(args, rank, world, local):
     ceil = dsmem_ceiling(D, n)
     dsmem_bytes = problems * n * 2 * (n - 1) / n * p
     dsmem_achieved = dsmem_bytes / (ms * 1e-3) / 1e9
-    roofline["dsmem"] = {"achieved": round(dsmem_achieved, 1), "peak": ceil["push_all_peers_GBps"], "unit": "GB/s",
-                         "frac": round(dsmem_achieved / ceil["push_all_peers_GBps"], 4),
+    roofline["dsmem"] = {"achieved": round(dsmem_achieved, 1), "peak": ceil["peak_GBps"], "unit": "GB/s",
+                         "frac": round(dsmem_achieved / ceil["peak_GBps"], 4),
                          "bytes_per_launch": int(dsmem_bytes), "ceilings": ceil,
-                         "peak_source": "measured live (dsmem_ceiling_dsmem_bw, all-peer push, 1/slope)"}
+                         "peak_source": "measured live (dsmem_ceiling_dsmem_bw, best push shape, 1/slope)"}
 
     extras = {}
     if rank == 0 and not args.no_extras:

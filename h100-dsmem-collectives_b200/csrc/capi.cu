@@ -114,7 +114,8 @@ struct State {
     std::map<int, DeviceState> dev;
     std::map<TuneKey, std::map<uint64_t, int>> tune;   // (op, N, dtype) -> {bytes -> alg}
     unsigned long long wait_limit_ns = 1000000000ull;
-    bool pipelined = true;   // batches use a pipelined driver where one exists
+    bool pipelined = true;        // batches use a pipelined driver where one exists
+    uint64_t unit_bytes = 16384;  // pipelined drivers: largest sub-vector per CTA
 };
 
 State& st() {
@@ -213,6 +214,9 @@ cudaError_t ensure_attrs(DeviceState& d, const void* fn, int n, uint64_t smem) {
         const int want = (int)std::max<uint64_t>(smem, it == d.smem_attr.end() ? 0 : (uint64_t)it->second);
         r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
         if (r != cudaSuccess) return r;
+        // the whole unified L1/shared array as shared memory, so several CTAs fit per SM
+        r = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+        if (r != cudaSuccess) return r;
         d.smem_attr[fn] = want;
     }
     return cudaSuccess;
@@ -263,11 +267,12 @@ cudaError_t error_word(DeviceState& d, unsigned** out) {
 }
 
 // Units per problem for a pipelined driver: the smallest split into legal sub-vectors of at most
-// kUnitBytes per CTA (16 KiB keeps three unit buffers at 48 KiB, i.e. four CTAs per SM); 0 if none.
-constexpr uint64_t kUnitBytes = 16384;
+// unit_bytes per CTA (default 16 KiB: three unit buffers in 48 KiB, four CTAs per SM); 0 if none.
+// Caller holds st().mu.
 uint32_t pipeline_units(const KernelEntry* e, uint32_t m) {
+    const uint64_t unit = st().unit_bytes;
     const uint64_t bytes = (uint64_t)m * e->elem_bytes;
-    const uint32_t s0 = (uint32_t)std::max<uint64_t>(1, (bytes + kUnitBytes - 1) / kUnitBytes);
+    const uint32_t s0 = (uint32_t)std::max<uint64_t>(1, (bytes + unit - 1) / unit);
     for (uint32_t s = s0; s <= m && s < s0 + 4096; ++s)
         if (m % s == 0 && e->legal(m / s)) return s;
     return 0;
@@ -538,6 +543,13 @@ dsmem_status dsmem_set_wait_limit_ns(unsigned long long ns) {
 dsmem_status dsmem_set_pipelined(int enable) {
     std::lock_guard<std::mutex> lock(st().mu);
     st().pipelined = enable != 0;
+    return DSMEM_OK;
+}
+
+dsmem_status dsmem_set_pipeline_unit_bytes(size_t bytes) {
+    if (bytes < 256 || bytes > 65536 || (bytes & 15u)) return DSMEM_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> lock(st().mu);
+    st().unit_bytes = bytes;
     return DSMEM_OK;
 }
 

@@ -20,24 +20,37 @@
 
 namespace {
 
-constexpr uint32_t kTile = 96u * 1024u;
-constexpr uint32_t kChunk = 16u * 1024u;
 constexpr int kMaxPasses = 32;
 constexpr uint32_t kBars = 256;                     // 32 mbarriers
 constexpr uint32_t kSrc = kBars;
-constexpr uint32_t kDst = kSrc + kTile;
-constexpr uint32_t kSmem = kDst + kTile + 4096;     // ~196 KiB: one CTA per SM
 
-template <int MODE>
-__global__ void __launch_bounds__(1024, 1) dsmem_bw_kernel(int passes, unsigned* err, unsigned* sink,
-                                                           unsigned long long limit) {
+// Two shapes: the reference's (96 KiB tiles, 1024 threads, ~196 KiB: one CTA per SM) and a small one
+// (24 KiB tiles, 256 threads, ~52 KiB: four CTAs per SM), which lets clusters of 8 and 16 use the SMs
+// that one-CTA-per-SM placement leaves idle in every GPC.
+template <uint32_t TILE>
+struct Shape {
+    static constexpr uint32_t kTile = TILE;
+    static constexpr uint32_t kChunk = TILE >= 96u * 1024u ? 16u * 1024u : 8u * 1024u;
+    static constexpr uint32_t kDst = kSrc + TILE;
+    static constexpr uint32_t kSmem = kDst + TILE + 4096;
+    // all-peers mode: bytes per peer per pass (a multiple of 1 KiB, at most 8 KiB, all peers within the tile)
+    static __host__ __device__ constexpr uint32_t fan_chunk(uint32_t cs) {
+        return (TILE / (cs - 1) / 1024u) * 1024u < 8192u ? (TILE / (cs - 1) / 1024u) * 1024u : 8192u;
+    }
+};
+
+template <int MODE, uint32_t TILE, int THREADS>
+__global__ void __launch_bounds__(THREADS, 1) dsmem_bw_kernel(int passes, unsigned* err, unsigned* sink,
+                                                              unsigned long long limit) {
     using namespace dsmem;
+    using Sh = Shape<TILE>;
+    constexpr uint32_t kTile = Sh::kTile, kChunk = Sh::kChunk, kDst = Sh::kDst;
     const uint32_t sa = smem_u32(dyn_smem_raw);
     const uint32_t rank = cluster_rank(), cs = cluster_size(), peer = (rank + 1) % cs;
     uint4* src = reinterpret_cast<uint4*>(dyn_smem_raw + kSrc);
     for (uint32_t i = threadIdx.x; i < kTile / 16; i += blockDim.x) src[i] = make_uint4(i, rank, i ^ 0x5a5a5a5au, ~i);
     // mode 2 (all peers): per pass every CTA sends one chunk of q bytes to each of its cs-1 peers
-    const uint32_t q = cs <= 8 ? 8192u : 4096u;
+    const uint32_t q = Sh::fan_chunk(cs);
     const uint32_t per_pass = MODE == 1 ? kTile : (cs - 1) * q;
     if (MODE != 0 && threadIdx.x == 0) {
         for (int p = 0; p < passes; ++p) {
@@ -93,16 +106,31 @@ extern "C" {
 // Time `reps` launches (after 2 warm-ups) of the DSMEM bandwidth kernel on the current device.
 // mode 0 = pull (ld.shared::cluster.v4), 1 = push to the ring neighbour (cp.async.bulk), 2 = push to every
 // peer (one chunk of 8 KiB, 4 KiB at CS 16, per peer per pass: the fan-out of the direct / two-shot
-// algorithms). Outputs: median ms per launch, payload bytes per launch and the resident clusters used.
-dsmem_status dsmem_ceiling_dsmem_bw(int mode, int cluster_size, int passes, int reps, double* ms_median,
-                                    long long* bytes_per_launch, int* clusters_out) {
+// algorithms). ctas_per_sm 1: 96 KiB tiles, 1024 threads (the reference's shape); 4: 24 KiB tiles, 256
+// threads. Outputs: median ms per launch, payload bytes per launch and the resident clusters used.
+dsmem_status dsmem_ceiling_dsmem_bw(int mode, int cluster_size, int ctas_per_sm, int passes, int reps,
+                                    double* ms_median, long long* bytes_per_launch, int* clusters_out) {
     if (mode < 0 || mode > 2 || passes < 1 || passes > kMaxPasses || reps < 1 ||
+        (ctas_per_sm != 1 && ctas_per_sm != 4) ||
         !(cluster_size == 2 || cluster_size == 4 || cluster_size == 8 || cluster_size == 16))
         return DSMEM_ERR_INVALID_ARGUMENT;
-    const void* fn = mode == 0   ? reinterpret_cast<const void*>(&dsmem_bw_kernel<0>)
-                     : mode == 1 ? reinterpret_cast<const void*>(&dsmem_bw_kernel<1>)
-                                 : reinterpret_cast<const void*>(&dsmem_bw_kernel<2>);
+    const bool big = ctas_per_sm == 1;
+    const void* const fns[2][3] = {
+        {reinterpret_cast<const void*>(&dsmem_bw_kernel<0, 24u * 1024u, 256>),
+         reinterpret_cast<const void*>(&dsmem_bw_kernel<1, 24u * 1024u, 256>),
+         reinterpret_cast<const void*>(&dsmem_bw_kernel<2, 24u * 1024u, 256>)},
+        {reinterpret_cast<const void*>(&dsmem_bw_kernel<0, 96u * 1024u, 1024>),
+         reinterpret_cast<const void*>(&dsmem_bw_kernel<1, 96u * 1024u, 1024>),
+         reinterpret_cast<const void*>(&dsmem_bw_kernel<2, 96u * 1024u, 1024>)}};
+    const void* fn = fns[big ? 1 : 0][mode];
+    const uint32_t kSmem = big ? Shape<96u * 1024u>::kSmem : Shape<24u * 1024u>::kSmem;
+    const uint32_t kTile = big ? 96u * 1024u : 24u * 1024u;
+    const uint32_t fan = big ? Shape<96u * 1024u>::fan_chunk((uint32_t)cluster_size)
+                             : Shape<24u * 1024u>::fan_chunk((uint32_t)cluster_size);
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) != cudaSuccess)
+        return DSMEM_ERR_CUDA;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) !=
+        cudaSuccess)
         return DSMEM_ERR_CUDA;
     if (cluster_size > 8 && cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
         return DSMEM_ERR_CUDA;
@@ -112,7 +140,7 @@ dsmem_status dsmem_ceiling_dsmem_bw(int mode, int cluster_size, int passes, int 
     attr[0].val.clusterDim.x = (unsigned)cluster_size;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(1024, 1, 1);
+    cfg.blockDim = dim3(big ? 1024 : 256, 1, 1);
     cfg.gridDim = dim3((unsigned)cluster_size, 1, 1);
     cfg.dynamicSmemBytes = kSmem;
     cfg.attrs = attr;
@@ -152,7 +180,7 @@ dsmem_status dsmem_ceiling_dsmem_bw(int mode, int cluster_size, int passes, int 
     if (h[0] & DSMEM_ERRBIT_TIMEOUT) return DSMEM_ERR_TIMEOUT;
     std::sort(t.begin(), t.end());
     if (ms_median) *ms_median = t[t.size() / 2];
-    const long long per_pass = mode == 2 ? (long long)(cluster_size - 1) * (cluster_size <= 8 ? 8192 : 4096) : kTile;
+    const long long per_pass = mode == 2 ? (long long)(cluster_size - 1) * fan : kTile;
     if (bytes_per_launch) *bytes_per_launch = (long long)clusters * cluster_size * passes * per_pass;
     if (clusters_out) *clusters_out = clusters;
     return DSMEM_OK;

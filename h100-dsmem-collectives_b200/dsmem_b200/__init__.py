@@ -147,11 +147,12 @@ def lib():
         "dsmem_set_wait_limit_ns": (c_int, [c_ull]),
         "dsmem_selftest_timeout": (c_int, [c_ull, c_vp]),
         "dsmem_set_pipelined": (c_int, [c_int]),
+        "dsmem_set_pipeline_unit_bytes": (c_int, [c_size]),
         "dsmem_rmsnorm_launch": (c_int, [c_int, c_vp, c_vp, ctypes.c_float, c_ll, c_int, c_int, c_vp, c_vp]),
         "dsmem_rmsnorm_residual_launch": (c_int, [c_int, c_vp, c_vp, c_vp, ctypes.c_float, c_ll, c_int, c_int,
                                                   c_vp, c_vp, c_vp]),
         "dsmem_rmsnorm_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
-        "dsmem_ceiling_dsmem_bw": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double),
+        "dsmem_ceiling_dsmem_bw": (c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double),
                                            ctypes.POINTER(c_ll), ctypes.POINTER(c_int)]),
         "dsmem_version": (ctypes.c_char_p, []),
     }
@@ -249,6 +250,11 @@ def set_pipelined(enable):
     _ok(lib().dsmem_set_pipelined(1 if enable else 0), "dsmem_set_pipelined")
 
 
+def set_pipeline_unit_bytes(nbytes):
+    """Largest sub-vector per CTA of the pipelined drivers (default 16 KiB)."""
+    _ok(lib().dsmem_set_pipeline_unit_bytes(int(nbytes)), "dsmem_set_pipeline_unit_bytes")
+
+
 def autotune_load(path):
     _ok(lib().dsmem_autotune_table_load(str(path).encode()), f"dsmem_autotune_table_load({path})")
 
@@ -308,18 +314,19 @@ def rmsnorm_check(device=0):
         raise DsmemError(Status.TIMEOUT, "rmsnorm")
 
 
-def dsmem_bandwidth_point(mode, cluster_size, passes, reps=5):
-    """(median ms, payload bytes, clusters) of one DSMEM ceiling launch configuration (mode 0 pull, 1 push)."""
+def dsmem_bandwidth_point(mode, cluster_size, passes, reps=5, ctas_per_sm=1):
+    """(median ms, payload bytes, clusters) of one DSMEM ceiling launch configuration (mode 0 pull, 1 ring
+    push, 2 all-peers push; ctas_per_sm 1 = 96 KiB tiles, 4 = 24 KiB tiles)."""
     ms, nbytes, cl = ctypes.c_double(0), ctypes.c_longlong(0), ctypes.c_int(0)
-    _ok(lib().dsmem_ceiling_dsmem_bw(int(mode), int(cluster_size), int(passes), int(reps), ctypes.byref(ms),
-                                     ctypes.byref(nbytes), ctypes.byref(cl)), "dsmem_ceiling_dsmem_bw")
+    _ok(lib().dsmem_ceiling_dsmem_bw(int(mode), int(cluster_size), int(ctas_per_sm), int(passes), int(reps),
+                                     ctypes.byref(ms), ctypes.byref(nbytes), ctypes.byref(cl)), "dsmem_ceiling_dsmem_bw")
     return ms.value, nbytes.value, cl.value
 
 
-def dsmem_bandwidth_peak(mode, cluster_size, passes=(4, 8, 16, 32), reps=5):
+def dsmem_bandwidth_peak(mode, cluster_size, passes=(4, 8, 16, 32), reps=5, ctas_per_sm=1):
     """GPU-wide SM-to-SM bandwidth in GB/s = 1 / slope of launch time over payload bytes (least squares),
     the method of the reference's roofline/harness/ceilings/src/dsmem_bw.cu. Returns (GB/s, points)."""
-    pts = [dsmem_bandwidth_point(mode, cluster_size, p, reps) for p in passes]
+    pts = [dsmem_bandwidth_point(mode, cluster_size, p, reps, ctas_per_sm) for p in passes]
     xs = [b for (_, b, _) in pts]
     ys = [ms * 1e-3 for (ms, _, _) in pts]
     mx, my = sum(xs) / len(xs), sum(ys) / len(ys)

@@ -157,6 +157,9 @@ dsmem_status dsmem_set_wait_limit_ns(unsigned long long ns);
  * AllReduce: bulk HBM loads/stores overlapped with the shots, no per-problem cluster barrier). 0 forces
  * the plain driver (load, entry barrier, collective, store, exit barrier per problem). Default 1. */
 dsmem_status dsmem_set_pipelined(int enable);
+/* Largest sub-vector per CTA the pipelined drivers stream at once (256 B .. 64 KiB, multiple of 16;
+ * default 16 KiB). Larger problems are split into equal legal sub-vectors no larger than this. */
+dsmem_status dsmem_set_pipeline_unit_bytes(size_t bytes);
 
 /* Failure-detection self-test: launches one 2-CTA cluster whose mbarrier is armed for 16 bytes that
  * never arrive, with a wait limit of `limit_ns`; every wait gives up after the limit and the kernel
@@ -190,10 +193,12 @@ dsmem_status dsmem_rmsnorm_check(int device, unsigned* error_bits);
  * roofline/harness/ceilings/src/dsmem_bw.cu:1-40 (ops `ld` and `tma_put`, ring +1, max active clusters,
  * 96 KiB per pass): mode 0 pull (ld.shared::cluster.v4), 1 push (cp.async.bulk) to the ring neighbour,
  * 2 push to every peer (8 KiB per peer per pass, 4 KiB at cluster size 16; the fan-out pattern of the direct
- * and two-shot algorithms, which the reference did not measure). Times `reps` launches of `passes` passes;
+ * and two-shot algorithms, which the reference did not measure). ctas_per_sm 1 is the reference's shape
+ * (96 KiB tiles, 1024 threads, one CTA per SM); 4 uses 24 KiB tiles and 256 threads so clusters of 8/16
+ * also occupy the SMs that one-CTA-per-SM placement leaves idle. Times `reps` launches of `passes` passes;
  * the caller fits 1/slope over several pass counts. */
-dsmem_status dsmem_ceiling_dsmem_bw(int mode, int cluster_size, int passes, int reps, double* ms_median,
-                                    long long* bytes_per_launch, int* clusters);
+dsmem_status dsmem_ceiling_dsmem_bw(int mode, int cluster_size, int ctas_per_sm, int passes, int reps,
+                                    double* ms_median, long long* bytes_per_launch, int* clusters);
 
 /* Library version string. */
 const char* dsmem_version(void);
