@@ -508,6 +508,7 @@ const char* dsmem_status_string(dsmem_status s) {
         case DSMEM_ERR_INVALID_ARGUMENT: return "invalid argument";
         case DSMEM_ERR_BOUNDS: return "device-side bounds check failed";
         case DSMEM_ERR_NCCL: return "NCCL error";
+        case DSMEM_ERR_SCRATCH_LIMIT: return "batch larger than the static scratch of the no-alloc entry point";
     }
     return "?";
 }

@@ -69,6 +69,7 @@ class Status(enum.IntEnum):
     INVALID_ARGUMENT = 5
     BOUNDS = 6
     NCCL = 7
+    SCRATCH_LIMIT = 8
 
 
 ELEM_BYTES = {Dtype.F32: 4, Dtype.BF16: 2, Dtype.I32: 4}
@@ -148,6 +149,8 @@ def lib():
         "dsmem_selftest_timeout": (c_int, [c_ull, c_vp]),
         "dsmem_set_pipelined": (c_int, [c_int]),
         "dsmem_set_pipeline_unit_bytes": (c_int, [c_size]),
+        "dsmem_allreduce_two_shot_noalloc": (c_int, [c_int, c_int, c_size, c_vp, c_vp, c_int,
+                                                     ctypes.POINTER(ctypes.c_uint), c_vp]),
         "dsmem_rmsnorm_launch": (c_int, [c_int, c_vp, c_vp, ctypes.c_float, c_ll, c_int, c_int, c_vp, c_vp]),
         "dsmem_rmsnorm_residual_launch": (c_int, [c_int, c_vp, c_vp, c_vp, ctypes.c_float, c_ll, c_int, c_int,
                                                   c_vp, c_vp, c_vp]),
@@ -277,6 +280,23 @@ def lookup(stem):
 def selftest_timeout(limit_ns, stream=0):
     """Launch the bounded-wait self-test kernel (see dsmem_selftest_timeout)."""
     _ok(lib().dsmem_selftest_timeout(int(limit_ns), ctypes.c_void_p(stream or None)), "dsmem_selftest_timeout")
+
+
+NOALLOC_MAX_PROBLEMS = 65536
+
+
+def allreduce_two_shot_noalloc(dtype, cluster_size, bytes_per_cta, in_ptr, out_ptr, num_clusters, stream=0,
+                               want_status=True):
+    """Two-shot batch AllReduce that allocates no device memory (dsmem_allreduce_two_shot_noalloc), for
+    callers that must not call cudaMalloc (stream capture in progress, a framework allocator that owns the
+    device memory). With want_status the call synchronises and returns the per-problem error bits (a list);
+    otherwise it returns None right after the launch."""
+    status = (ctypes.c_uint * max(1, num_clusters))() if want_status else None
+    st = lib().dsmem_allreduce_two_shot_noalloc(int(dtype), int(cluster_size), int(bytes_per_cta),
+                                                ctypes.c_void_p(in_ptr), ctypes.c_void_p(out_ptr), int(num_clusters),
+                                                status, ctypes.c_void_p(stream or None))
+    _ok(st, f"dsmem_allreduce_two_shot_noalloc(N={cluster_size}, P={bytes_per_cta}, clusters={num_clusters})")
+    return list(status)[:num_clusters] if want_status else None
 
 
 def rmsnorm(x, w, eps=1e-6, cluster_size=8, out=None, residual=None, pre_norm=None, stream=None):

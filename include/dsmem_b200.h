@@ -44,7 +44,8 @@ typedef enum {
     DSMEM_ERR_CUDA = 4,
     DSMEM_ERR_INVALID_ARGUMENT = 5,
     DSMEM_ERR_BOUNDS = 6,
-    DSMEM_ERR_NCCL = 7
+    DSMEM_ERR_NCCL = 7,
+    DSMEM_ERR_SCRATCH_LIMIT = 8
 } dsmem_status;
 
 /* COLL_OP values of collectives/harness/main.cu:7-8. */
@@ -199,6 +200,29 @@ dsmem_status dsmem_rmsnorm_check(int device, unsigned* error_bits);
  * the caller fits 1/slope over several pass counts. */
 dsmem_status dsmem_ceiling_dsmem_bw(int mode, int cluster_size, int ctas_per_sm, int passes, int reps,
                                     double* ms_median, long long* bytes_per_launch, int* clusters);
+
+/*
+ * Batch two-shot AllReduce that allocates no device memory. No counterpart in the reference (whose
+ * harness allocates every buffer itself); it exists for callers that cannot call cudaMalloc at this
+ * point: code running while a stream is captured into a CUDA graph, frameworks whose caching allocator
+ * owns the device memory, callers with a fixed memory map. dsmem_collective_launch allocates a device
+ * error word on its first call per device; this entry point instead keeps its scratch (error word + one
+ * status word per cluster problem) in a fixed static device array of 4 * (64 + 65536) bytes, resident on
+ * every GPU that loads the library until the process exits.
+ *   Same result as dsmem_collective_launch(DSMEM_OP_ALLREDUCE, DSMEM_ALG_TWO_SHOT_PUSH, ...) on the same
+ *   arguments (plain driver). num_clusters <= DSMEM_NOALLOC_MAX_PROBLEMS, else DSMEM_ERR_SCRATCH_LIMIT.
+ *   status_out: host array of num_clusters words or NULL. If given, the call synchronises `stream`,
+ *   copies each problem's error bits (DSMEM_ERRBIT_*) there and returns TIMEOUT/BOUNDS if any bit is set;
+ *   if NULL the call returns after the launch and device-side errors are not reported.
+ *   The first call on a device is its set-up: the CUDA runtime may load the library's device code (and
+ *   with it the static array), and the entry point looks up the array's address and sets kernel
+ *   attributes; make that first call before any stream capture. All calls share the array (cleared per
+ *   call on `stream`); calls whose kernels overlap on the GPU race on it.
+ */
+#define DSMEM_NOALLOC_MAX_PROBLEMS 65536
+dsmem_status dsmem_allreduce_two_shot_noalloc(dsmem_dtype dtype, int cluster_size, size_t bytes_per_cta,
+                                              const void* in, void* out, int num_clusters, unsigned* status_out,
+                                              dsmem_stream_t stream);
 
 /* Library version string. */
 const char* dsmem_version(void);
