@@ -25,8 +25,9 @@
 //     barrier.cluster instructions, so a time-out can never turn into a hang.
 //   * Bulk pushes check 16-B alignment and the window bounds in the issuing thread and record
 //     DSMEM_ERR_BIT_BOUNDS instead of issuing an out-of-range copy.
-// Layout of the dynamic shared-memory window: bytes [0, kBarArea) hold up to 16 mbarriers; data
-// buffers start at kD0 and are 16-B aligned (every legal M makes M*sizeof(T) a multiple of 16).
+// Layout of the dynamic shared-memory window: bytes [0, kBarArea) hold up to 15 mbarriers and, at byte
+// 120, the end-of-kernel flag word (finish()); data buffers start at kD0 and are 16-B aligned (every
+// legal M makes M*sizeof(T) a multiple of 16).
 #pragma once
 #include "dsmem_primitives.cuh"
 
@@ -52,7 +53,8 @@ struct Ctx {
     bool dead;                        // a wait timed out: later waits do not block
     unsigned long long wait_limit;    // ns per problem
     unsigned long long deadline;      // %globaltimer value after which waits give up
-    unsigned* err;                    // error word (nullptr: this translation unit's dsmem_wait_error)
+    unsigned* err;                    // error words [4] (nullptr: this translation unit's dsmem_wait_error)
+    uint32_t unit;                    // problem / unit counter of this CTA (error detail)
     Stamps st;
 
     __device__ __forceinline__ uint32_t bar(int i) const { return sa + 8u * (uint32_t)i; }
@@ -65,6 +67,16 @@ __device__ __forceinline__ void report(Ctx& c, unsigned bits) {
 }
 
 // Wait for the current phase of barrier i (all threads). Bounded by c.deadline.
+// Record a wait that gave up: the error bit, and (first one only, library kernels) a detail word
+// 0x80000000 | barrier << 24 | rank << 16 | unit (low 16 bits) in err[1] and the cluster id in err[2].
+__device__ __forceinline__ void report_timeout(Ctx& c, int bar_id) {
+    report(c, DSMEM_ERR_BIT_TIMEOUT);
+    if (c.err != nullptr &&
+        atomicCAS(c.err + 1, 0u, 0x80000000u | ((uint32_t)bar_id & 0x7fu) << 24 | (c.rank & 0xffu) << 16 |
+                                     (c.unit & 0xffffu)) == 0u)
+        c.err[2] = cluster_id();
+}
+
 __device__ __forceinline__ void wait(Ctx& c, int i) {
     const uint32_t par = (c.phase >> i) & 1u;
     c.phase ^= 1u << i;
@@ -72,7 +84,30 @@ __device__ __forceinline__ void wait(Ctx& c, int i) {
     if (mbar_try_wait_parity(c.bar(i), par)) return;
     if (!mbar_wait_parity_until(c.bar(i), par, c.deadline)) {
         c.dead = true;
-        if ((threadIdx.x & 31) == 0) report(c, DSMEM_ERR_BIT_TIMEOUT);
+        if ((threadIdx.x & 31) == 0) report_timeout(c, i);
+    }
+}
+
+// End of a kernel: a CTA whose wait gave up may have stopped waiting for bytes peers still push into
+// it. A CTA that gave up sets the flag word (byte 120 of the barrier area) of every CTA of the cluster
+// before the final cluster barrier; after it each CTA reads its own flag (no remote access after the
+// last barrier), and if any CTA gave up, all of them linger kSettleNs and meet once more, so those
+// copies land before any CTA of the cluster exits. flag_init must precede the kernel's first
+// cluster barrier.
+constexpr uint32_t kFlagOff = 120;
+constexpr unsigned long long kSettleNs = 20000000ull;
+__device__ __forceinline__ void flag_init(Ctx& c) {
+    if (threadIdx.x == 0) *c.ptr<uint32_t>(kFlagOff) = 0u;
+}
+__device__ __forceinline__ void finish(Ctx& c) {
+    const bool dead = __syncthreads_or(c.dead ? 1 : 0) != 0;
+    if (dead && threadIdx.x < cluster_size()) st_cluster_u32(mapa(c.sa + kFlagOff, threadIdx.x), 1u);
+    cluster_sync();
+    if (*c.ptr<volatile uint32_t>(kFlagOff) != 0u) {
+        const unsigned long long until = globaltimer() + kSettleNs;
+        while (globaltimer() < until) {
+        }
+        cluster_sync();
     }
 }
 
@@ -725,6 +760,51 @@ struct AR_TwoShotPush {
     static __device__ void store(Ctx& c, T* g, uint32_t M) {
         __syncthreads();
         s2g(c, g, kD0, M * B);
+    }
+};
+
+// B200 extension, not one of the reference files: the reduce-scatter shot of the two-shot AllReduce
+// (allreduce__two_shot_push__trtllm.cu:31-45) over the SM-to-SM network, then the all-gather through the
+// outputs: every rank's output row of a problem is the same vector, so CTA b writes its reduced chunk
+// straight into position b of all N output rows instead of first pushing it into the peers' shared
+// memory. Same result, half the SM-to-SM bytes ((N-1)/N * P per CTA), the same HBM bytes.
+template <int N_, typename T_, class Op_>
+struct AR_RsPushGlobalAg {
+    DSB_TRAITS(AllReduce, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return AR_TwoShotPush<N_, T_, Op_>::legal(M); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t CB = (M / N_) * B, slots = kD0 + M * B, n = CB >> 4;
+        if (threadIdx.x == 0) {
+            arm(c, 0, (N_ - 1) * CB);
+            for (uint32_t j = 1; j < (uint32_t)N_; ++j) {
+                const uint32_t dst = (c.rank + j) % N_;
+                push<N_>(c, dst, slots + c.rank * CB, kD0 + dst * CB, CB, 0);
+            }
+        }
+        wait(c, 0);
+        uint4* mine = c.ptr<uint4>(kD0 + c.rank * CB);
+        const uint4* ps = c.ptr<const uint4>(slots);
+        for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) {
+            uint4 v[N_];
+#pragma unroll
+            for (int r = 0; r < N_; ++r) v[r] = (r == (int)c.rank) ? mine[u] : ps[r * n + u];
+            auto a = Pk<T, Op>::open(v[0]);
+#pragma unroll
+            for (int r = 1; r < N_; ++r) Pk<T, Op>::add(a, v[r]);
+            mine[u] = Pk<T, Op>::close(a);
+        }
+        c.st.round(0);
+    }
+    // g is this rank's output row; the problem's rows are contiguous, row r at g + (r - b) * M.
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        const uint32_t C = M / N_, CB = C * B;
+        for (int r = 0; r < N_; ++r) s2g(c, g + ((long long)r - (long long)c.rank) * M + c.rank * C, kD0 + c.rank * CB, CB);
     }
 };
 
@@ -1533,11 +1613,13 @@ __device__ __forceinline__ void ctx_init(Ctx& c, uint32_t smem_bytes, unsigned* 
     c.wait_limit = limit;
     c.deadline = 0ull;
     c.err = err;
+    c.unit = 0u;
     c.st.base = nullptr;
 }
 
 template <class A>
 __device__ __forceinline__ void init_bars(Ctx& c) {
+    static_assert(A::kBars >= 0 && 8 * A::kBars <= (int)kFlagOff, "mbarriers overlap the finish flag");
     if (A::kBars > 0 && threadIdx.x == 0) {
         for (int i = 0; i < A::kBars; ++i) mbar_init(c.bar(i), 1);
         fence_mbar_init();
@@ -1551,10 +1633,11 @@ __global__ void __launch_bounds__(256) batch_kernel(const BatchArgs a) {
     constexpr int N = A::kN;
     Ctx c;
     ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
+    flag_init(c);
     init_bars<A>(c);
     const uint64_t in_r = in_elems_per_rank<A>(a.M), out_r = out_elems_per_rank<A>(a.M);
     const long long step = (long long)num_clusters();
-    for (long long p = (long long)cluster_id(); p < a.num_problems; p += step) {
+    for (long long p = (long long)cluster_id(); p < a.num_problems; p += step, ++c.unit) {
         const uint64_t slot = (uint64_t)p * N + c.rank;
         c.deadline = globaltimer() + c.wait_limit;
         c.st.base = a.stamps != nullptr ? a.stamps + slot * kStamps : nullptr;
@@ -1567,6 +1650,7 @@ __global__ void __launch_bounds__(256) batch_kernel(const BatchArgs a) {
         A::store(c, static_cast<T*>(a.out) + slot * out_r, a.M);
         cluster_sync();   // exit: no peer still reads or writes my window for this problem
     }
+    finish(c);
 }
 
 // -----------------------------------------------------------------------------------------------------
@@ -1587,6 +1671,21 @@ __global__ void __launch_bounds__(256) batch_kernel(const BatchArgs a) {
 template <int N_, typename T_, class Op_>
 struct AR_TwoShotPipelined {
     DSB_TRAITS(AllReduce, 4)
+    static constexpr bool kGlobalAllGather = false;
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return AR_TwoShotPush<N_, T_, Op_>::legal(M); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 3ull * M * B; }
+};
+
+// Pipelined batch driver of AR_RsPushGlobalAg (below): shot 1 exactly as the two-shot's; the all-gather
+// is replaced by bulk stores of the reduced chunk into all N ranks' output rows, so only the reduce-scatter
+// crosses the SM-to-SM network. Slot reuse, ordered by shot 2 in the two-shot, is ordered here by credits:
+// after its reduce, each CTA arrives on every peer's credit barrier (N-1 arrivals per unit), and a CTA
+// waits for the credits of unit k-1 before its shot 1 of unit k. The same credits tell it that its own
+// shot-1 copies of unit k-1 were received, i.e. finished reading the X buffer the next load refills.
+template <int N_, typename T_, class Op_>
+struct AR_RsPushGlobalAgPipelined {
+    DSB_TRAITS(AllReduce, 4)
+    static constexpr bool kGlobalAllGather = true;
     __host__ __device__ static constexpr bool legal(uint32_t M) { return AR_TwoShotPush<N_, T_, Op_>::legal(M); }
     __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 3ull * M * B; }
 };
@@ -1596,11 +1695,18 @@ __global__ void __launch_bounds__(256) two_shot_pipelined_kernel(const BatchArgs
     using T = typename A::T;
     using Op = typename A::Op;
     constexpr int N = A::kN;
-    constexpr int kLoad0 = 0, kRS = 2, kAG = 3;
+    constexpr bool kGlobalAG = A::kGlobalAllGather;
+    constexpr int kLoad0 = 0, kRS = 2, kAG = 3, kCredit = 3;   // barrier 3: shot 2, or the credits
     Ctx c;
     ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
-    init_bars<A>(c);
+    flag_init(c);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 3; ++i) mbar_init(c.bar(i), 1);
+        mbar_init(c.bar(3), kGlobalAG ? N - 1 : 1);
+        fence_mbar_init();
+    }
     cluster_sync();   // every barrier of the cluster initialised before any remote push
+    const uint64_t total = (uint64_t)a.num_problems * N * a.M;   // elements of `in` and of `out`
     // A problem of M elements per rank flows through the pipeline as `sub` units of U = M / sub elements,
     // each a complete two-shot AllReduce of its sub-vector (the element-wise sum is separable).
     const uint32_t S = a.sub, U = a.M / S, UB = U * A::B, CB = UB / N, n = CB >> 4;
@@ -1616,19 +1722,37 @@ __global__ void __launch_bounds__(256) two_shot_pipelined_kernel(const BatchArgs
         const long long p = first + (k / S) * step;
         return ((uint64_t)p * N + c.rank) * a.M + (uint64_t)(k % S) * U;
     };
-    if (threadIdx.x == 0 && units > 0) {
-        arm(c, kLoad0, UB);
-        bulk_load_g2s(c.sa + kD0, in + unit_off(0), UB, c.bar(kLoad0));
-    }
+    // checked one-CTA bulk load of unit k into X buffer xb (thread 0)
+    auto load_unit = [&](long long k, uint32_t xb) {
+        const uint64_t off = unit_off(k);
+        if (off + U > total) {
+            report(c, DSMEM_ERR_BIT_BOUNDS);
+            return;
+        }
+        arm(c, kLoad0 + (int)xb, UB);
+        bulk_load_g2s(c.sa + kD0 + xb * UB, in + off, UB, c.bar(kLoad0 + (int)xb));
+    };
+    // thread 0: the N-1 credits of the previous unit (global all-gather only)
+    auto credit_wait = [&]() {
+        const uint32_t par = (c.phase >> kCredit) & 1u;
+        c.phase ^= 1u << kCredit;
+        if (!c.dead && !mbar_wait_parity_until(c.bar(kCredit), par, c.deadline)) {
+            c.dead = true;
+            report_timeout(c, kCredit);
+        }
+    };
+    if (threadIdx.x == 0 && units > 0) load_unit(0, 0);
     for (long long k = 0; k < units; ++k) {
         const uint32_t x = (uint32_t)(k & 1), X = kD0 + x * UB, s = (uint32_t)(k % S);
         const uint64_t slot = (uint64_t)(first + (k / S) * step) * N + c.rank;
+        c.unit = (uint32_t)k;
         c.deadline = globaltimer() + c.wait_limit;
         c.st.base = a.stamps != nullptr ? a.stamps + slot * kStamps : nullptr;
         if (s == 0 && a.smid != nullptr && threadIdx.x == 0) a.smid[slot] = smid();
         wait(c, kLoad0 + (int)x);   // my input for unit k is in X
         if (s == 0) c.st.mark(0);
         if (threadIdx.x == 0) {
+            if (kGlobalAG && k > 0) credit_wait();   // every peer consumed its slots of unit k-1
             // shot 1: chunk j of my input -> slot[b] of CTA j
             arm(c, kRS, (N - 1) * CB);
             for (uint32_t j = 1; j < (uint32_t)N; ++j) {
@@ -1638,8 +1762,7 @@ __global__ void __launch_bounds__(256) two_shot_pipelined_kernel(const BatchArgs
             // prefetch the next unit into the other buffer once the store of the previous one read it
             if (k + 1 < units) {
                 bulk_wait_read0();
-                arm(c, kLoad0 + (int)(x ^ 1u), UB);
-                bulk_load_g2s(c.sa + kD0 + (x ^ 1u) * UB, in + unit_off(k + 1), UB, c.bar(kLoad0 + (int)(x ^ 1u)));
+                load_unit(k + 1, x ^ 1u);
             }
         }
         wait(c, kRS);   // all N-1 partials of my chunk landed (and the peers' reads of their chunk b are done)
@@ -1659,26 +1782,52 @@ __global__ void __launch_bounds__(256) two_shot_pipelined_kernel(const BatchArgs
         fence_proxy_async_smem();
         __syncthreads();
         if (s + 1 == S) c.st.round(0);
-        if (threadIdx.x == 0) {
-            // shot 2: my reduced chunk -> position b of every peer
-            arm(c, kAG, (N - 1) * CB);
-            for (uint32_t j = 1; j < (uint32_t)N; ++j) {
-                const uint32_t dst = (c.rank + j) % N;
-                push<N>(c, dst, X + c.rank * CB, X + c.rank * CB, CB, kAG);
+        if constexpr (kGlobalAG) {
+            if (threadIdx.x == 0) {
+                // credits: my slots of unit k are consumed (release orders the reduce's reads before them)
+                for (uint32_t j = 1; j < (uint32_t)N; ++j) mbar_arrive_remote(c.bar(kCredit), (c.rank + j) % N);
+                // all-gather through the outputs: my reduced chunk into row r of every rank of the problem
+                const uint64_t base = unit_off(k) - (uint64_t)c.rank * a.M + (uint64_t)c.rank * (CB / A::B);
+                for (uint32_t r = 0; r < (uint32_t)N; ++r) {
+                    const uint64_t off = base + (uint64_t)r * a.M;
+                    if (off + CB / A::B > total) {
+                        report(c, DSMEM_ERR_BIT_BOUNDS);
+                        continue;
+                    }
+                    bulk_store_s2g(out + off, c.sa + X + c.rank * CB, CB);
+                }
+                bulk_commit();
+            }
+            if (s + 1 == S) c.st.mark(1);
+        } else {
+            if (threadIdx.x == 0) {
+                // shot 2: my reduced chunk -> position b of every peer
+                arm(c, kAG, (N - 1) * CB);
+                for (uint32_t j = 1; j < (uint32_t)N; ++j) {
+                    const uint32_t dst = (c.rank + j) % N;
+                    push<N>(c, dst, X + c.rank * CB, X + c.rank * CB, CB, kAG);
+                }
+            }
+            wait(c, kAG);   // every reduced chunk is in X
+            if (s + 1 == S) {
+                c.st.round(1);
+                c.st.mark(1);
+            }
+            if (threadIdx.x == 0) {
+                bulk_store_s2g(out + unit_off(k), c.sa + X, UB);
+                bulk_commit();
             }
         }
-        wait(c, kAG);   // every reduced chunk is in X
-        if (s + 1 == S) {
-            c.st.round(1);
-            c.st.mark(1);
-        }
-        if (threadIdx.x == 0) {
-            bulk_store_s2g(out + unit_off(k), c.sa + X, UB);
-            bulk_commit();
-        }
+    }
+    if (kGlobalAG && threadIdx.x == 0 && units > 0) {
+        // the credits of the last unit: every remote arrive aimed at this CTA has been performed (and my
+        // last pushes were consumed) before the cluster's final barrier, so nothing is in flight at exit
+        c.unit = (uint32_t)units;
+        c.deadline = globaltimer() + c.wait_limit;
+        credit_wait();
     }
     if (threadIdx.x == 0) bulk_wait_all0();
-    cluster_sync();   // no CTA leaves while a peer may still push into it
+    finish(c);   // no CTA leaves while a peer may still push into it
 }
 
 // Reference harness contract (collectives/harness/main.cu): one cluster, compile-time M.
@@ -1687,6 +1836,7 @@ __device__ __forceinline__ void run_single(const typename A::T* in, typename A::
                                            unsigned* smid_out, uint32_t M, uint32_t smem_bytes) {
     Ctx c;
     ctx_init(c, smem_bytes, nullptr, DSMEM_WAIT_LIMIT_NS);
+    flag_init(c);
     init_bars<A>(c);
     c.st.base = ts != nullptr ? ts + c.rank * kStamps : nullptr;
     c.deadline = globaltimer() + c.wait_limit;
@@ -1697,7 +1847,7 @@ __device__ __forceinline__ void run_single(const typename A::T* in, typename A::
     A::exec(c, M);
     c.st.mark(1);
     A::store(c, out + c.rank * out_elems_per_rank<A>(M), M);
-    cluster_sync();
+    finish(c);
 }
 
 }  // namespace dsb

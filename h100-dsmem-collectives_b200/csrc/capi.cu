@@ -46,7 +46,8 @@ const char* const kAlgNames[DSMEM_ALG_COUNT] = {"auto",
                                                 "direct_push",
                                                 "pairwise_exchange",
                                                 "pairwise_xor",
-                                                "shift"};
+                                                "shift",
+                                                "rs_push_global_ag"};
 const char* const kDtypeNames[] = {"f32", "bf16", "i32"};
 
 // (op, alg) -> reference file stem collectives/<op>__<alg>__<src>.cu
@@ -95,8 +96,10 @@ const std::vector<int> kDefaultOrder[4] = {
     {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_DIRECT_PULL, DSMEM_ALG_SHIFT, DSMEM_ALG_PAIRWISE_XOR},
 };
 
+constexpr size_t kErrWords = 4;
+
 struct DeviceState {
-    unsigned* err = nullptr;                       // device error word
+    unsigned* err = nullptr;                       // device error words (kErrWords)
     std::map<const void*, int> smem_attr;          // largest MaxDynamicSharedMemorySize set per kernel
     std::map<std::pair<const void*, uint64_t>, int> occupancy;
     int optin = 0;
@@ -256,10 +259,10 @@ cudaError_t occupancy(DeviceState& d, const void* fn, int n_cta, uint64_t smem, 
 }
 
 cudaError_t error_word(DeviceState& d, unsigned** out) {
-    if (d.err == nullptr) {
-        cudaError_t r = cudaMalloc(reinterpret_cast<void**>(&d.err), sizeof(unsigned));
+    if (d.err == nullptr) {   // [error bits, first timeout detail, its cluster id, spare]
+        cudaError_t r = cudaMalloc(reinterpret_cast<void**>(&d.err), kErrWords * sizeof(unsigned));
         if (r != cudaSuccess) return r;
-        r = cudaMemset(d.err, 0, sizeof(unsigned));
+        r = cudaMemset(d.err, 0, kErrWords * sizeof(unsigned));
         if (r != cudaSuccess) return r;
     }
     *out = d.err;
@@ -460,7 +463,7 @@ dsmem_alg dsmem_autotune_pick(dsmem_op op, dsmem_dtype dtype, int cluster_size, 
     return (dsmem_alg)resolve_auto(op, dtype, cluster_size, bytes_per_cta);
 }
 
-dsmem_status dsmem_last_error(int device, unsigned* error_bits) {
+dsmem_status dsmem_last_error_detail(int device, unsigned* error_bits, unsigned* detail, unsigned* cluster) {
     int prev = 0;
     if (cudaGetDevice(&prev) != cudaSuccess) return DSMEM_ERR_CUDA;
     unsigned* w = nullptr;
@@ -469,17 +472,23 @@ dsmem_status dsmem_last_error(int device, unsigned* error_bits) {
         auto it = st().dev.find(device);
         if (it != st().dev.end()) w = it->second.err;
     }
-    unsigned v = 0;
+    unsigned v[kErrWords] = {};
     if (w != nullptr) {
         if (device != prev && cudaSetDevice(device) != cudaSuccess) return DSMEM_ERR_CUDA;
-        cudaError_t r = cudaMemcpy(&v, w, sizeof v, cudaMemcpyDeviceToHost);
+        cudaError_t r = cudaMemcpy(v, w, sizeof v, cudaMemcpyDeviceToHost);
         if (r == cudaSuccess) r = cudaMemset(w, 0, sizeof v);
         if (r == cudaSuccess) r = cudaDeviceSynchronize();
         if (device != prev) cudaSetDevice(prev);
         if (r != cudaSuccess) return DSMEM_ERR_CUDA;
     }
-    if (error_bits) *error_bits = v;
+    if (error_bits) *error_bits = v[0];
+    if (detail) *detail = v[1];
+    if (cluster) *cluster = v[2];
     return DSMEM_OK;
+}
+
+dsmem_status dsmem_last_error(int device, unsigned* error_bits) {
+    return dsmem_last_error_detail(device, error_bits, nullptr, nullptr);
 }
 
 dsmem_status dsmem_check(dsmem_stream_t stream) {

@@ -45,10 +45,11 @@ __global__ void __launch_bounds__(256) batch_status_kernel(const dsb::BatchArgs 
     constexpr int N = A::kN;
     dsb::Ctx c;
     dsb::ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
+    dsb::flag_init(c);
     dsb::init_bars<A>(c);
     const uint64_t in_r = dsb::in_elems_per_rank<A>(a.M), out_r = dsb::out_elems_per_rank<A>(a.M);
     const long long step = (long long)num_clusters();
-    for (long long p = (long long)cluster_id(); p < a.num_problems; p += step) {
+    for (long long p = (long long)cluster_id(); p < a.num_problems; p += step, ++c.unit) {
         const uint64_t slot = (uint64_t)p * N + c.rank;
         c.deadline = globaltimer() + c.wait_limit;
         A::load(c, static_cast<const T*>(a.in) + slot * in_r, a.M);
@@ -58,6 +59,7 @@ __global__ void __launch_bounds__(256) batch_status_kernel(const dsb::BatchArgs 
         if (__syncthreads_or(c.dead ? 1 : 0) && threadIdx.x == 0) atomicOr(&status[p], DSMEM_ERR_BIT_TIMEOUT);
         cluster_sync();
     }
+    dsb::finish(c);
 }
 
 template <int N, typename T>

@@ -6,19 +6,22 @@
 //     [b*H/N, (b+1)*H/N), partial sum of squares by warp shuffles, cluster AllReduce of one float;
 //   kernels/rmsnorm_lamport__fused_allreduce_rmsnorm__hpcops.cu:37-197   h = x + residual written back,
 //     replicated-push scalar AllReduce (one store into slot[b] of every CTA) (:153-169).
-// B200 design (one launch, persistent clusters of N CTAs, 256 threads = 8 warps per CTA):
-//   * rows are taken in groups of R = 8*K (K = 4 rows per warp, 2 for 2 KiB slices); cluster q handles
-//     groups q, q + nclusters, ...;
-//   * each CTA streams the R row slices of a group with one-CTA bulk copies (cp.async.bulk, no
-//     multicast) through a ring of 3 shared-memory stages (2 with a residual), refilled as soon as every
-//     warp has moved its rows into registers (full/empty mbarriers);
-//   * the AllReduce of the per-row partial sums is the replicated push of hpc-ops: lane 0 of each warp
-//     writes its K partials into slot[parity][b][warp*K..] of every CTA of the cluster with one st.async
-//     each, whose bytes complete on that CTA's mbarrier (armed for N*R*4 bytes per group), so no release
-//     fence or cluster barrier is needed per group; a warp waits and sums the N slots of each of its rows.
-//     Two slot sets alternate between groups; a peer can reuse a set only after it received all of this
-//     CTA's partials of the following group, which are sent after this CTA has read the set;
-//   * outputs leave from registers with 16-byte streaming stores.
+// B200 design (one launch, persistent clusters of N CTAs; per CTA 8 consumer warps + 1 producer warp):
+//   * rows are taken in groups of R = 16 (two per consumer warp); cluster q handles groups q,
+//     q + nclusters, ...; CTA b owns the column slice b of every row;
+//   * the producer warp streams each group's R row slices (and residual slices) with one-CTA bulk copies
+//     (cp.async.bulk, no multicast) into a ring of 4 shared-memory stages (full/empty mbarriers); a stage
+//     is released only after its rows are normalised, so x is read from shared memory twice and never
+//     held in registers;
+//   * the per-row partial sums of squares meet in the hpc-ops replicated push: lane 0 of each consumer
+//     warp writes its 2 partials into slot[set][b][warp*2..] of every CTA with one st.async, whose bytes
+//     complete on that CTA's mbarrier of the set (armed for N*R*4 bytes), so there is no release fence and
+//     no cluster barrier per group;
+//   * the exchange runs one group ahead: a warp sends group i+1's partials before it waits for group
+//     i's sums. A CTA can then write a peer's slot set for group i+2 while that peer still reads set i,
+//     so slot sets rotate over 4 groups: the set of group j is rewritten for j+4 only after the writer
+//     received the owner's partials of j+2, which the owner sends after reading set j;
+//   * outputs leave with 16-byte streaming stores.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -32,9 +35,15 @@ namespace {
 
 using namespace dsmem;
 
-constexpr int kWarps = 8;          // rows per group
-constexpr int kThreadsRms = kWarps * 32;
-constexpr int kMaxUnitsPerLane = 4;   // 16-byte units of a row slice per lane (slice <= 4*32*16 B = 2 KiB)
+constexpr int kConsumers = 8;                       // consumer warps
+constexpr int kThreadsRms = (kConsumers + 1) * 32;  // + one producer warp
+constexpr int kRowsPerWarp = 2;
+constexpr int kR = kConsumers * kRowsPerWarp;       // rows per group
+constexpr int kStages = 4;                          // most stages (barrier ids); a launch uses 2..4
+constexpr int kSets = 4;                            // partial-sum slot sets (see the header comment)
+constexpr int kMaxUnitsPerLane = 4;                 // 16-byte units of a row slice per lane (<= 2 KiB)
+// barrier ids: full[s] 0..3, empty[s] 4..7, sum[set] 8..11
+constexpr int kFull = 0, kEmpty = kStages, kSum = 2 * kStages;
 
 struct RmsArgs {
     const void* x;
@@ -49,6 +58,7 @@ struct RmsArgs {
     float eps;
     uint32_t slice_bytes;   // bytes of one row slice of one CTA
     uint32_t smem_bytes;
+    int stages;             // shared-memory stages of the row ring (2..kStages)
 };
 
 template <typename T>
@@ -89,61 +99,41 @@ struct RmsElem<float> {
     }
 };
 
-// Rows per warp per iteration for UPL 16-byte units per lane: x stays in registers as K*UPL packets.
-__host__ __device__ constexpr int rms_k(int upl) { return upl >= 4 ? 2 : 4; }
-__host__ __device__ constexpr int rms_stages(bool residual) { return residual ? 2 : 3; }
-
-// Shared-memory layout: [0,128) barriers | slots 2 x N x R floats | w slice | stages x R x slice (x2 with residual)
+// Shared-memory layout: [0,128) barriers | slots kSets x N x R floats | w slice | stages x R x slice (x2 with residual)
 __host__ __device__ constexpr uint32_t rms_slots_off() { return 128u; }
-__host__ __device__ constexpr uint32_t rms_w_off(int n, int r) { return 128u + ((2u * n * r * 4u + 15u) & ~15u); }
-__host__ __device__ constexpr uint32_t rms_stage_off(int n, int r, uint32_t slice) { return rms_w_off(n, r) + slice; }
-__host__ __device__ constexpr uint32_t rms_smem(int n, int r, uint32_t slice, bool residual) {
-    return rms_stage_off(n, r, slice) + (uint32_t)rms_stages(residual) * r * slice * (residual ? 2u : 1u);
+__host__ __device__ constexpr uint32_t rms_w_off(int n) { return 128u + (uint32_t)kSets * n * kR * 4u; }
+__host__ __device__ constexpr uint32_t rms_stage_off(int n, uint32_t slice) { return rms_w_off(n) + slice; }
+__host__ __device__ constexpr uint32_t rms_smem(int n, uint32_t slice, bool residual, int stages) {
+    return rms_stage_off(n, slice) + (uint32_t)stages * kR * slice * (residual ? 2u : 1u);
 }
 
-// One K-float remote store with completion on the destination's mbarrier (st.async, no release fence).
-template <int K>
-__device__ __forceinline__ void st_async_partials(uint32_t dst_rank, uint32_t dst, const float* v, uint32_t bar) {
-    const uint32_t rd = mapa(dst, dst_rank), rb = mapa(bar, dst_rank);
-    if constexpr (K == 4) {
-        asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1,%2,%3,%4}, [%5];" ::"r"(rd),
-                     "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "r"(rb)
-                     : "memory");
-    } else {
-        asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1,%2}, [%3];" ::"r"(rd),
-                     "f"(v[0]), "f"(v[1]), "r"(rb)
-                     : "memory");
-    }
-}
+// Bounded wait on barrier i by one thread (its own phase bookkeeping in c.phase).
+__device__ __forceinline__ void wait_one(dsb::Ctx& c, int i) { dsb::wait(c, i); }
 
 template <int N, typename T, bool RES, int UPL>
-__global__ void __launch_bounds__(kThreadsRms, 2) rmsnorm_cluster_kernel(const RmsArgs a) {
+__global__ void __launch_bounds__(kThreadsRms, 3) rmsnorm_cluster_kernel(const RmsArgs a) {
     using E = RmsElem<T>;
-    constexpr int K = rms_k(UPL);          // rows per warp per iteration
-    constexpr int R = kWarps * K;          // rows per CTA per iteration
-    constexpr int NS = rms_stages(RES);
     dsb::Ctx c;
     dsb::ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
+    dsb::flag_init(c);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t slice = a.slice_bytes, units = slice >> 4;   // 16-B units per row slice (<= 32 * UPL)
-    const uint32_t slots = rms_slots_off(), woff = rms_w_off(N, R), stage0 = rms_stage_off(N, R, slice);
-    const uint32_t stage_bytes = (uint32_t)R * slice * (RES ? 2u : 1u);
-    const long long groups = (a.rows + R - 1) / R;
+    const uint32_t slots = rms_slots_off(), woff = rms_w_off(N), stage0 = rms_stage_off(N, slice);
+    const uint32_t stage_bytes = (uint32_t)kR * slice * (RES ? 2u : 1u);
+    const long long nst = a.stages;
+    const long long groups = (a.rows + kR - 1) / kR;
     const long long step = (long long)num_clusters();
     const long long first = (long long)cluster_id();
+    const long long iters = first < groups ? (groups - 1 - first) / step + 1 : 0;
     const size_t row_bytes = (size_t)a.hidden * sizeof(T);
     const size_t col_off = (size_t)c.rank * slice;
-    const unsigned char* xb = static_cast<const unsigned char*>(a.x);
-    const unsigned char* rb = static_cast<const unsigned char*>(a.res);
-    constexpr int kFull = 0, kEmpty = NS, kSum = 2 * NS;   // barrier ids
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < NS; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(c.bar(kFull + s), 1);
-            mbar_init(c.bar(kEmpty + s), kWarps);
+            mbar_init(c.bar(kEmpty + s), kConsumers);
         }
-        mbar_init(c.bar(kSum + 0), 1);
-        mbar_init(c.bar(kSum + 1), 1);
+        for (int s = 0; s < kSets; ++s) mbar_init(c.bar(kSum + s), 1);
         fence_mbar_init();
     }
     {   // weight slice -> shared
@@ -153,127 +143,125 @@ __global__ void __launch_bounds__(kThreadsRms, 2) rmsnorm_cluster_kernel(const R
     }
     __syncthreads();
     cluster_sync();   // barriers of every CTA initialised before any remote store completes on them
+    c.deadline = globaltimer() + c.wait_limit;
 
-    // producer (thread 0): loads of local iteration i into stage i % NS
-    auto issue = [&](long long i_local) {
-        const long long g = first + i_local * step;
-        if (g >= groups) return;
-        const int s = (int)(i_local % NS);
-        const long long r0 = g * R;
-        const int nr = (int)min((long long)R, a.rows - r0);
-        const uint32_t dst = stage0 + (uint32_t)s * stage_bytes;
-        dsb::arm(c, kFull + s, (uint32_t)nr * slice * (RES ? 2u : 1u));
-        for (int r = 0; r < nr; ++r) {
-            const size_t src = (size_t)(r0 + r) * row_bytes + col_off;
-            bulk_load_g2s(c.sa + dst + (uint32_t)r * slice, xb + src, slice, c.bar(kFull + s));
-            if (RES) bulk_load_g2s(c.sa + dst + ((uint32_t)R + r) * slice, rb + src, slice, c.bar(kFull + s));
+    if (warp == kConsumers) {
+        // ---------------------------------------------------------------- producer warp (lane 0)
+        if (lane == 0) {
+            const unsigned char* xb = static_cast<const unsigned char*>(a.x);
+            const unsigned char* rb = static_cast<const unsigned char*>(a.res);
+            for (long long i = 0; i < iters; ++i) {
+                const int s = (int)(i % nst);
+                if (i >= nst) {   // the stage's previous group is normalised by every consumer warp
+                    c.deadline = globaltimer() + c.wait_limit;
+                    wait_one(c, kEmpty + s);
+                }
+                const long long r0 = (first + i * step) * kR;
+                const int nr = (int)min((long long)kR, a.rows - r0);
+                const uint32_t dst = stage0 + (uint32_t)s * stage_bytes;
+                dsb::arm(c, kFull + s, (uint32_t)nr * slice * (RES ? 2u : 1u));
+                for (int r = 0; r < nr; ++r) {
+                    const size_t src = (size_t)(r0 + r) * row_bytes + col_off;
+                    bulk_load_g2s(c.sa + dst + (uint32_t)r * slice, xb + src, slice, c.bar(kFull + s));
+                    if (RES)
+                        bulk_load_g2s(c.sa + dst + ((uint32_t)kR + r) * slice, rb + src, slice, c.bar(kFull + s));
+                }
+            }
         }
-    };
-    if (threadIdx.x == 0)
-        for (int i = 0; i < NS; ++i) issue(i);
-
-    const uint4* wp = c.ptr<const uint4>(woff);
-    long long i = 0;
-    for (long long g = first; g < groups; g += step, ++i) {
-        const int s = (int)(i % NS);
-        const uint32_t par = (uint32_t)(i & 1);
-        const long long row0 = g * R + (long long)warp * K;
-        c.deadline = globaltimer() + c.wait_limit;
-        // expect this iteration's partials: N CTAs x R rows x 4 bytes
-        if (threadIdx.x == 0) dsb::arm(c, kSum + (int)par, (uint32_t)N * R * 4u);
-        dsb::wait(c, kFull + s);
-        // ---- my K row slices -> registers (packed), sums of squares
-        uint4 xp[K][UPL];
-        float ss[K];
-        {
-            const uint4* xs = c.ptr<const uint4>(stage0 + (uint32_t)s * stage_bytes);
-            const uint4* rs = xs + (size_t)R * (slice >> 4);
+        __syncwarp();   // reconverge before the aligned cluster barrier
+    } else {
+        // ---------------------------------------------------------------- consumer warps
+        const uint4* wp = c.ptr<const uint4>(woff);
+        // h of row k of group i (slot of the stage), unit u, as floats
+        auto load_h = [&](long long i, int k, uint32_t u, float* f) {
+            const uint4* xs = c.ptr<const uint4>(stage0 + (uint32_t)(i % nst) * stage_bytes);
+            const uint32_t idx = (warp * kRowsPerWarp + k) * units + u;
+            E::unpack(xs[idx], f);
+            if (RES) {
+                float r[E::kPer16];
+                E::unpack(xs[(size_t)kR * units + idx], r);
 #pragma unroll
-            for (int k = 0; k < K; ++k) {
+                for (int e = 0; e < E::kPer16; ++e) f[e] += r[e];
+                E::unpack(E::pack(f), f);   // h rounded to the element type (the pre-norm output)
+            }
+        };
+        // wait for group j's rows, reduce my rows' sums of squares and push them to every CTA
+        auto send = [&](long long j) {
+            wait_one(c, kFull + (int)(j % nst));
+            const long long row0 = (first + j * step) * kR + (long long)warp * kRowsPerWarp;
+            float ss[kRowsPerWarp];
+#pragma unroll
+            for (int k = 0; k < kRowsPerWarp; ++k) {
                 ss[k] = 0.f;
-                const bool valid = row0 + k < a.rows;
+                if (row0 + k < a.rows) {
 #pragma unroll
-                for (int j = 0; j < UPL; ++j) {
-                    const uint32_t u = lane + 32u * j;
-                    if (valid && u < units) {
-                        const uint32_t idx = (warp * K + k) * units + u;
-                        float f[E::kPer16];
-                        E::unpack(xs[idx], f);
-                        if (RES) {
-                            float r[E::kPer16];
-                            E::unpack(rs[idx], r);
+                    for (int q = 0; q < UPL; ++q) {
+                        const uint32_t u = lane + 32u * q;
+                        if (u < units) {
+                            float f[E::kPer16];
+                            load_h(j, k, u, f);
 #pragma unroll
-                            for (int e = 0; e < E::kPer16; ++e) f[e] += r[e];
-                            xp[k][j] = E::pack(f);   // h rounded to the element type (the pre-norm output)
-                            E::unpack(xp[k][j], f);
-                        } else {
-                            xp[k][j] = xs[idx];
+                            for (int e = 0; e < E::kPer16; ++e) ss[k] = fmaf(f[e], f[e], ss[k]);
                         }
+                    }
+                }
 #pragma unroll
-                        for (int e = 0; e < E::kPer16; ++e) ss[k] = fmaf(f[e], f[e], ss[k]);
-                    } else {
-                        xp[k][j] = make_uint4(0, 0, 0, 0);
+                for (int off = 16; off > 0; off >>= 1) ss[k] += __shfl_xor_sync(0xffffffffu, ss[k], off);
+            }
+            const int set = (int)(j % kSets);
+            if (threadIdx.x == 0) dsb::arm(c, kSum + set, (uint32_t)N * kR * 4u);
+            if (lane == 0) {
+                const uint32_t dst = slots + (((uint32_t)set * N + c.rank) * kR + warp * kRowsPerWarp) * 4u;
+                const uint32_t bar = c.bar(kSum + set);
+                for (uint32_t q = 0; q < (uint32_t)N; ++q) {
+                    const uint32_t rd = mapa(c.sa + dst, q), rbar = mapa(bar, q);
+                    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1,%2}, [%3];" ::
+                                     "r"(rd),
+                                 "f"(ss[0]), "f"(ss[1]), "r"(rbar)
+                                 : "memory");
+                }
+            }
+        };
+        if (iters > 0) send(0);
+        for (long long i = 0; i < iters; ++i) {
+            c.deadline = globaltimer() + c.wait_limit;
+            if (i + 1 < iters) send(i + 1);   // one group ahead
+            const int set = (int)(i % kSets);
+            wait_one(c, kSum + set);
+            const long long row0 = (first + i * step) * kR + (long long)warp * kRowsPerWarp;
+            const float* sl = c.ptr<const float>(slots + (uint32_t)set * N * kR * 4u);
+#pragma unroll
+            for (int k = 0; k < kRowsPerWarp; ++k) {
+                const long long row = row0 + k;
+                float tot = 0.f;
+#pragma unroll
+                for (int q = 0; q < N; ++q) tot += sl[q * kR + warp * kRowsPerWarp + k];
+                const float scale = rsqrtf(tot / (float)a.hidden + a.eps);
+                if (row >= a.rows) continue;
+                uint4* yo = reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.y) + (size_t)row * row_bytes + col_off);
+                uint4* po = RES && a.pre != nullptr
+                                ? reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.pre) + (size_t)row * row_bytes +
+                                                           col_off)
+                                : nullptr;
+#pragma unroll
+                for (int q = 0; q < UPL; ++q) {
+                    const uint32_t u = lane + 32u * q;
+                    if (u < units) {
+                        float f[E::kPer16], w[E::kPer16];
+                        load_h(i, k, u, f);
+                        if (RES && po != nullptr) __stcs(po + u, E::pack(f));
+                        E::unpack(wp[u], w);
+#pragma unroll
+                        for (int e = 0; e < E::kPer16; ++e) f[e] = f[e] * scale * w[e];
+                        __stcs(yo + u, E::pack(f));
                     }
                 }
             }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(c.bar(kEmpty + s));   // this warp no longer needs the stage
-        if (threadIdx.x == 0) {   // refill the stage for iteration i + NS once every warp released it
-            const uint32_t epar = (c.phase >> (kEmpty + s)) & 1u;
-            c.phase ^= 1u << (kEmpty + s);
-            if (!c.dead && !mbar_wait_parity_until(c.bar(kEmpty + s), epar, c.deadline)) {
-                c.dead = true;
-                dsb::report(c, DSMEM_ERR_BIT_TIMEOUT);
-            }
-            issue(i + NS);
-        }
-        // ---- cluster AllReduce of the K partial sums: replicated push with st.async into slot[par][b][w*K..]
-#pragma unroll
-        for (int k = 0; k < K; ++k)
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) ss[k] += __shfl_xor_sync(0xffffffffu, ss[k], off);
-        if (lane == 0) {
-            const uint32_t dst = slots + ((par * N + c.rank) * R + warp * K) * 4u;
-            for (uint32_t q = 0; q < (uint32_t)N; ++q) st_async_partials<K>(q, c.sa + dst, ss, c.bar(kSum + (int)par));
-        }
-        dsb::wait(c, kSum + (int)par);
-        float scale[K];
-        {
-            const float* sl = c.ptr<const float>(slots + par * N * R * 4u);
-#pragma unroll
-            for (int k = 0; k < K; ++k) {
-                float tot = 0.f;
-#pragma unroll
-                for (int q = 0; q < N; ++q) tot += sl[q * R + warp * K + k];
-                scale[k] = rsqrtf(tot / (float)a.hidden + a.eps);
-            }
-        }
-        // ---- normalise and store
-#pragma unroll
-        for (int k = 0; k < K; ++k) {
-            const long long row = row0 + k;
-            if (row >= a.rows) continue;
-            uint4* yo = reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.y) + (size_t)row * row_bytes + col_off);
-            uint4* po = RES && a.pre != nullptr
-                            ? reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.pre) + (size_t)row * row_bytes + col_off)
-                            : nullptr;
-#pragma unroll
-            for (int j = 0; j < UPL; ++j) {
-                const uint32_t u = lane + 32u * j;
-                if (u < units) {
-                    if (RES && po != nullptr) __stcs(po + u, xp[k][j]);
-                    float f[E::kPer16], w[E::kPer16];
-                    E::unpack(xp[k][j], f);
-                    E::unpack(wp[u], w);
-#pragma unroll
-                    for (int e = 0; e < E::kPer16; ++e) f[e] = f[e] * scale[k] * w[e];
-                    __stcs(yo + u, E::pack(f));
-                }
-            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(c.bar(kEmpty + (int)(i % nst)));   // stage free for the producer
         }
     }
-    cluster_sync();   // no CTA leaves while a peer may still store into its slots
+    dsb::finish(c);   // no CTA leaves while a peer may still store into its slots
 }
 
 struct RmsKey {
@@ -328,8 +316,10 @@ dsmem_status rms_launch(int dtype, const void* x, const void* res, const void* w
     const bool has_res = res != nullptr;
     const uint32_t units = (uint32_t)(slice / 16);
     const int upl = units <= 32 ? 1 : units <= 64 ? 2 : 4;
-    const int r = kWarps * rms_k(upl);
-    const uint32_t smem = rms_smem(n, r, (uint32_t)slice, has_res);
+    // the deepest ring (at most kStages, at least 2) that fits the per-CTA shared-memory limit
+    int stages = kStages;
+    while (stages > 2 && rms_smem(n, (uint32_t)slice, has_res, stages) > dsb::kSmemLimit) --stages;
+    const uint32_t smem = rms_smem(n, (uint32_t)slice, has_res, stages);
     if (smem > dsb::kSmemLimit) return DSMEM_ERR_SMEM_LIMIT;
     const void* fn = dtype == DSMEM_BF16
                          ? (has_res ? pick<__nv_bfloat16, true>(n, upl) : pick<__nv_bfloat16, false>(n, upl))
@@ -351,9 +341,9 @@ dsmem_status rms_launch(int dtype, const void* x, const void* res, const void* w
     RmsArgs a{};
     {
         std::lock_guard<std::mutex> lock(g_mu);
-        if (g_err[dev] == nullptr) {
-            if (cudaMalloc(&g_err[dev], sizeof(unsigned)) != cudaSuccess) return DSMEM_ERR_CUDA;
-            cudaMemset(g_err[dev], 0, sizeof(unsigned));
+        if (g_err[dev] == nullptr) {   // error bits, timeout detail, cluster id, spare
+            if (cudaMalloc(&g_err[dev], 4 * sizeof(unsigned)) != cudaSuccess) return DSMEM_ERR_CUDA;
+            cudaMemset(g_err[dev], 0, 4 * sizeof(unsigned));
         }
         const RmsKey key{fn, dev, smem};
         auto it = g_occ.find(key);
@@ -374,7 +364,7 @@ dsmem_status rms_launch(int dtype, const void* x, const void* res, const void* w
         a.err = g_err[dev];
     }
     if (resident < 1) return DSMEM_ERR_SMEM_LIMIT;
-    const long long groups = (rows + r - 1) / r;
+    const long long groups = (rows + kR - 1) / kR;
     long long clusters = std::min<long long>(groups, resident);
     if (max_clusters > 0) clusters = std::min<long long>(clusters, max_clusters);
     cfg.gridDim = dim3((unsigned)(clusters * n), 1, 1);
@@ -389,6 +379,7 @@ dsmem_status rms_launch(int dtype, const void* x, const void* res, const void* w
     a.eps = eps;
     a.slice_bytes = (uint32_t)slice;
     a.smem_bytes = smem;
+    a.stages = stages;
     void* args[] = {&a};
     return cudaLaunchKernelExC(&cfg, fn, args) == cudaSuccess ? DSMEM_OK : DSMEM_ERR_CUDA;
 }
@@ -418,7 +409,7 @@ dsmem_status dsmem_rmsnorm_check(int device, unsigned* error_bits) {
         if (device < 0 || device >= 64) return DSMEM_ERR_INVALID_ARGUMENT;
         if (g_err[device] != nullptr) {
             if (cudaMemcpy(&v, g_err[device], sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return DSMEM_ERR_CUDA;
-            cudaMemset(g_err[device], 0, sizeof v);
+            cudaMemset(g_err[device], 0, 4 * sizeof(unsigned));
         }
     }
     if (error_bits) *error_bits = v;

@@ -37,7 +37,7 @@ enum : int {
     kPullRsPushAg = 6, kRabenseifner = 7, kOneShotPull = 8, kTwoShotPush = 9, kReduceBcastBinomial = 10,
     kAtomicAllPush = 11, kMesh2D = 12, kDirectShift = 13, kBruck = 14, kDirectPull = 15,
     kGatherBcastBinomial = 16, kRecursiveHalving = 17, kDirectPush = 18, kPairwiseExchange = 19,
-    kPairwiseXor = 20, kShift = 21
+    kPairwiseXor = 20, kShift = 21, kRsPushGlobalAg = 22
 };
 
 template <template <int, typename, class> class A, int N>
@@ -55,14 +55,21 @@ void add_all_n(Registry& r, int alg) {
 }
 
 // Attach the pipelined batch driver P<N> to the entry of (alg, N) just registered.
-template <int N>
-void add_two_shot_pipelined(Registry& r) {
-    using P = AR_TwoShotPipelined<N, ElemT, Sum>;
+template <template <int, typename, class> class P, int N>
+void add_pipelined(Registry& r, int alg) {
+    using PP = P<N, ElemT, Sum>;
     for (KernelEntry& e : r)
-        if (e.op == 0 && e.alg == kTwoShotPush && e.dtype == DSB_DT && e.n == N) {
-            e.fn_pipe = reinterpret_cast<const void*>(&two_shot_pipelined_kernel<P>);
-            e.smem_pipe = &smem_fn<P>;
+        if (e.op == 0 && e.alg == alg && e.dtype == DSB_DT && e.n == N) {
+            e.fn_pipe = reinterpret_cast<const void*>(&two_shot_pipelined_kernel<PP>);
+            e.smem_pipe = &smem_fn<PP>;
         }
+}
+template <template <int, typename, class> class P>
+void add_pipelined_all_n(Registry& r, int alg) {
+    add_pipelined<P, 2>(r, alg);
+    add_pipelined<P, 4>(r, alg);
+    add_pipelined<P, 8>(r, alg);
+    add_pipelined<P, 16>(r, alg);
 }
 
 }  // namespace
@@ -82,10 +89,9 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<AR_Rabenseifner>(r, kRabenseifner);
     add_all_n<AR_OneShotPull>(r, kOneShotPull);
     add_all_n<AR_TwoShotPush>(r, kTwoShotPush);
-    add_two_shot_pipelined<2>(r);
-    add_two_shot_pipelined<4>(r);
-    add_two_shot_pipelined<8>(r);
-    add_two_shot_pipelined<16>(r);
+    add_pipelined_all_n<AR_TwoShotPipelined>(r, kTwoShotPush);
+    add_all_n<AR_RsPushGlobalAg>(r, kRsPushGlobalAg);
+    add_pipelined_all_n<AR_RsPushGlobalAgPipelined>(r, kRsPushGlobalAg);
     add_all_n<AR_ReduceBcastBinomial>(r, kReduceBcastBinomial);
     add_all_n<AR_AtomicAllPush>(r, kAtomicAllPush);
     add_all_n<AR_Mesh2D>(r, kMesh2D);

@@ -52,6 +52,7 @@ class Alg(enum.IntEnum):
     PAIRWISE_EXCHANGE = 19
     PAIRWISE_XOR = 20
     SHIFT = 21
+    RS_PUSH_GLOBAL_AG = 22   # B200 extension (no reference file): DSMEM reduce-scatter, all-gather via the outputs
 
 
 class Dtype(enum.IntEnum):
@@ -110,6 +111,12 @@ CATALOGUE = {
 }
 
 
+# Algorithms of this build with no reference file (selectable, and candidates for AUTO).
+EXTENSIONS = {
+    (Op.ALLREDUCE, Alg.RS_PUSH_GLOBAL_AG): "allreduce__rs_push_global_ag (B200 extension)",
+}
+
+
 class DsmemError(RuntimeError):
     def __init__(self, status, what=""):
         self.status = Status(status)
@@ -138,6 +145,7 @@ def lib():
         "dsmem_autotune_table_load": (c_int, [ctypes.c_char_p]),
         "dsmem_autotune_pick": (c_int, [c_int, c_int, c_int, c_size]),
         "dsmem_last_error": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
+        "dsmem_last_error_detail": (c_int, [c_int] + [ctypes.POINTER(ctypes.c_uint)] * 3),
         "dsmem_check": (c_int, [c_vp]),
         "dsmem_op_name": (ctypes.c_char_p, [c_int]),
         "dsmem_alg_name": (ctypes.c_char_p, [c_int]),
@@ -242,6 +250,18 @@ def last_error(device=0):
     bits = ctypes.c_uint(0)
     _ok(lib().dsmem_last_error(int(device), ctypes.byref(bits)), "dsmem_last_error")
     return bits.value
+
+
+def last_error_detail(device=0):
+    """Read and clear the error words: {"bits", "timeout": None or {"barrier", "rank", "unit", "cluster"}}."""
+    bits, detail, cluster = ctypes.c_uint(0), ctypes.c_uint(0), ctypes.c_uint(0)
+    _ok(lib().dsmem_last_error_detail(int(device), ctypes.byref(bits), ctypes.byref(detail), ctypes.byref(cluster)),
+        "dsmem_last_error_detail")
+    d = detail.value
+    timeout = None
+    if d & 0x80000000:
+        timeout = {"barrier": (d >> 24) & 0x7F, "rank": (d >> 16) & 0xFF, "unit": d & 0xFFFF, "cluster": cluster.value}
+    return {"bits": bits.value, "timeout": timeout}
 
 
 def set_wait_limit_ns(ns):

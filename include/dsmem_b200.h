@@ -81,7 +81,10 @@ typedef enum {
     DSMEM_ALG_PAIRWISE_EXCHANGE = 19,                 /* alltoall (N = 2)                        */
     DSMEM_ALG_PAIRWISE_XOR = 20,                      /* alltoall                                */
     DSMEM_ALG_SHIFT = 21,                             /* alltoall                                */
-    DSMEM_ALG_COUNT = 22
+    /* B200 extension, no reference file: allreduce whose reduce-scatter shot (the two-shot's first) runs
+     * over DSMEM and whose all-gather goes straight into the N output rows (half the SM-to-SM bytes). */
+    DSMEM_ALG_RS_PUSH_GLOBAL_AG = 22,                 /* allreduce                               */
+    DSMEM_ALG_COUNT = 23
 } dsmem_alg;
 
 /* ELEM_T of the reference (float | int, main.cu:99) plus bf16. */
@@ -138,6 +141,11 @@ dsmem_alg dsmem_autotune_pick(dsmem_op op, dsmem_dtype dtype, int cluster_size, 
 
 /* Read and clear the device error word of `device` (synchronises that device). */
 dsmem_status dsmem_last_error(int device, unsigned* error_bits);
+/* As dsmem_last_error, plus where the first timed-out wait since the last read gave up:
+ * detail = 0x80000000 | barrier << 24 | cluster rank << 16 | problem-or-unit counter (low 16 bits),
+ * 0 if no wait timed out; cluster = its %clusterid.x. Any pointer may be NULL. No reference
+ * counterpart (the reference's hangs end in its host watchdog, collectives/harness/main.cu:277-320). */
+dsmem_status dsmem_last_error_detail(int device, unsigned* error_bits, unsigned* detail, unsigned* cluster);
 /* Synchronise `stream`, then map the device error word to TIMEOUT / BOUNDS (and clear it). */
 dsmem_status dsmem_check(dsmem_stream_t stream);
 

@@ -18,7 +18,8 @@ pytestmark = pytest.mark.gpu
 
 import dsmem_b200 as D  # noqa: E402  (path set up by conftest)
 
-CASES = [(op, alg, n) for (op, alg) in D.CATALOGUE for n in D.CLUSTER_SIZES]
+CASES = [(op, alg, n) for (op, alg) in list(D.CATALOGUE) + list(D.EXTENSIONS) for n in D.CLUSTER_SIZES]
+NAMES = {**D.CATALOGUE, **{k: v.split()[0] for k, v in D.EXTENSIONS.items()}}
 
 
 def _np_to_torch(torch, host, dt):
@@ -94,7 +95,7 @@ def payloads(op, alg, n, dt):
     return out
 
 
-@pytest.mark.parametrize("op,alg,n", CASES, ids=[f"{D.CATALOGUE[(o, a)]}-N{n}" for (o, a, n) in CASES])
+@pytest.mark.parametrize("op,alg,n", CASES, ids=[f"{NAMES[(o, a)]}-N{n}" for (o, a, n) in CASES])
 def test_parity(cuda, orc, op, alg, n):
     torch = cuda
     ran, failures = 0, []
@@ -113,24 +114,25 @@ def test_parity(cuda, orc, op, alg, n):
     assert not failures, "\n".join(failures)
 
 
+@pytest.mark.parametrize("alg", (D.Alg.TWO_SHOT_PUSH, D.Alg.RS_PUSH_GLOBAL_AG), ids=("two_shot", "rs_push_global_ag"))
 @pytest.mark.parametrize("n", D.CLUSTER_SIZES)
-def test_two_shot_pipelined_matches_plain(cuda, orc, n):
-    """The pipelined batch driver of the two-shot AllReduce against the oracle, with the plain driver
-    forced for comparison; many problems per resident cluster, every dtype."""
+def test_pipelined_matches_plain(cuda, orc, n, alg):
+    """The pipelined batch drivers (sub-vector units, bulk HBM copies, no per-problem cluster barrier)
+    against the oracle, with the plain driver forced for comparison; many problems per resident cluster,
+    every dtype, and payloads that split into several units."""
     failures = []
     try:
         for pipelined in (True, False):
             D.set_pipelined(pipelined)
             for dt in D.Dtype:
-                for p in (256 * n // 8 if n >= 8 else 256, 4096, 16384, 65536):
-                    if D.query(D.Op.ALLREDUCE, D.Alg.TWO_SHOT_PUSH, dt, n, p)[0] != D.Status.OK:
+                for p in (256 * n // 8 if n >= 8 else 256, 4096, 16384, 65536, 196608):
+                    if D.query(D.Op.ALLREDUCE, alg, dt, n, p)[0] != D.Status.OK:
                         continue
                     for clusters, pattern in ((2, "A"), (301, "R"), (1200, "A")):
                         if p * n * clusters > (256 << 20):
                             continue
                         try:
-                            run_case(cuda, orc, D.Op.ALLREDUCE, D.Alg.TWO_SHOT_PUSH, n, dt, p, clusters, pattern,
-                                     seed=clusters)
+                            run_case(cuda, orc, D.Op.ALLREDUCE, alg, n, dt, p, clusters, pattern, seed=clusters)
                         except (AssertionError, D.DsmemError) as e:
                             failures.append(f"pipelined={pipelined} {dt.name} P={p} clusters={clusters}: {e}")
     finally:
