@@ -196,9 +196,25 @@ __device__ __forceinline__ bool mbar_try_wait_parity(uint32_t bar, uint32_t pari
         : "memory");
     return done != 0;
 }
-// Wait until the phase completes or %globaltimer passes `deadline_ns`; false on time-out.
+// As mbar_try_wait_parity, but the thread may be suspended in hardware for up to `suspend_ns` while the
+// phase is incomplete (it resumes as soon as the phase completes), so a waiting warp stops competing for
+// issue slots with the warps doing work.
+__device__ __forceinline__ bool mbar_try_wait_parity_suspend(uint32_t bar, uint32_t parity, uint32_t suspend_ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity), "r"(suspend_ns)
+        : "memory");
+    return done != 0;
+}
+// Wait until the phase completes or %globaltimer passes `deadline_ns`; false on time-out. Each probe may
+// suspend the thread for up to 100 us, so the limit is honoured to within that.
+constexpr uint32_t kWaitSuspendNs = 100000u;
 __device__ __forceinline__ bool mbar_wait_parity_until(uint32_t bar, uint32_t parity, unsigned long long deadline_ns) {
-    while (!mbar_try_wait_parity(bar, parity)) {
+    while (!mbar_try_wait_parity_suspend(bar, parity, kWaitSuspendNs)) {
         if (globaltimer() > deadline_ns) return false;
     }
     return true;

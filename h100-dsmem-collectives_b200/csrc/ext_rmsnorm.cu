@@ -7,21 +7,22 @@
 //   kernels/rmsnorm_lamport__fused_allreduce_rmsnorm__hpcops.cu:37-197   h = x + residual written back,
 //     replicated-push scalar AllReduce (one store into slot[b] of every CTA) (:153-169).
 // B200 design (one launch, persistent clusters of N CTAs; per CTA 8 consumer warps + 1 producer warp):
-//   * rows are taken in groups of R = 16 (two per consumer warp); cluster q handles groups q,
-//     q + nclusters, ...; CTA b owns the column slice b of every row;
-//   * the producer warp streams each group's R row slices (and residual slices) with one-CTA bulk copies
-//     (cp.async.bulk, no multicast) into a ring of 4 shared-memory stages (full/empty mbarriers); a stage
-//     is released only after its rows are normalised, so x is read from shared memory twice and never
-//     held in registers;
-//   * the per-row partial sums of squares meet in the hpc-ops replicated push: lane 0 of each consumer
-//     warp writes its 2 partials into slot[set][b][warp*2..] of every CTA with one st.async, whose bytes
-//     complete on that CTA's mbarrier of the set (armed for N*R*4 bytes), so there is no release fence and
-//     no cluster barrier per group;
-//   * the exchange runs one group ahead: a warp sends group i+1's partials before it waits for group
-//     i's sums. A CTA can then write a peer's slot set for group i+2 while that peer still reads set i,
-//     so slot sets rotate over 4 groups: the set of group j is rewritten for j+4 only after the writer
-//     received the owner's partials of j+2, which the owner sends after reading set j;
-//   * outputs leave with 16-byte streaming stores.
+//   * cluster q of C owns the contiguous rows [q*rows/C, (q+1)*rows/C), taken in groups of R = 16 (two per
+//     consumer warp; the last group partial); CTA b owns the column slice b of every row;
+//   * the producer warp streams the weight slice and each group's R row slices (and residual slices) with
+//     one-CTA bulk copies (cp.async.bulk, no multicast) into a ring of 2..4 shared-memory stages (as many
+//     as fit; full/empty mbarriers); a stage is released only after its rows are normalised, so x is read
+//     from shared memory twice and never held in registers. The producer starts loading before the
+//     cluster rendezvous (split arrive/wait), which only the remote stores need;
+//   * the per-row partial sums of squares meet in the hpc-ops replicated push: lane q < N of each consumer
+//     warp writes the warp's 2 partials into slot[set][b][warp*2..] of CTA q with one st.async, whose
+//     bytes complete on that CTA's mbarrier of the set (armed for N*R*4 bytes), so there is no release
+//     fence and no cluster barrier per group;
+//   * the exchange runs L = 1 group ahead (rms_lookahead): a warp sends group i+L's partials before it
+//     waits for group i's sums. A writer sends group g after it received everyone's
+//     partials of g-L-1, so an owner may still be reading any set of groups g-L-1 .. g+L-1 when g's
+//     partials arrive: slot sets rotate over kSets >= 2L+2 groups, so g's set is none of those;
+//   * outputs leave with 16-byte streaming stores; the weight slice sits in registers when it fits.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -37,13 +38,22 @@ using namespace dsmem;
 
 constexpr int kConsumers = 8;                       // consumer warps
 constexpr int kThreadsRms = (kConsumers + 1) * 32;  // + one producer warp
-constexpr int kRowsPerWarp = 2;
+constexpr int kRowsPerWarp = 2;                     // one st.async.v2 / float2 of partials per warp
+static_assert(kRowsPerWarp == 2, "the partial exchange moves float2 pairs");
 constexpr int kR = kConsumers * kRowsPerWarp;       // rows per group
 constexpr int kStages = 4;                          // most stages (barrier ids); a launch uses 2..4
-constexpr int kSets = 4;                            // partial-sum slot sets (see the header comment)
+constexpr int kSets = 8;                            // partial-sum slot sets (see the header comment)
 constexpr int kMaxUnitsPerLane = 4;                 // 16-byte units of a row slice per lane (<= 2 KiB)
-// barrier ids: full[s] 0..3, empty[s] 4..7, sum[set] 8..11
-constexpr int kFull = 0, kEmpty = kStages, kSum = 2 * kStages;
+constexpr int kCtasPerSm = 3;                       // occupancy target (registers capped to fit it)
+constexpr uint32_t kSmemPerSm = 233472;             // 228 KiB of shared memory per SM
+// barrier ids: full[s] 0..3, empty[s] 4..7, weight 8, sum[set] 16..23 (id 15 would overlap the
+// end-of-kernel flag word at byte 120)
+constexpr int kFull = 0, kEmpty = kStages, kWBar = 2 * kStages, kSum = 16;
+static_assert(8 * kWBar < (int)dsb::kFlagOff && kSum * 8 > (int)dsb::kFlagOff, "barriers overlap the flag word");
+// partial sums are sent `lookahead` groups ahead of the group being normalised. One group hides the
+// exchange round trip; a deeper lookahead makes the first group wait for later groups' loads.
+__host__ __device__ constexpr int rms_lookahead(int) { return 1; }
+static_assert(kSets >= 2 * rms_lookahead(kStages) + 2, "slot sets must cover 2 * lookahead + 2 groups");
 
 struct RmsArgs {
     const void* x;
@@ -61,47 +71,72 @@ struct RmsArgs {
     int stages;             // shared-memory stages of the row ring (2..kStages)
 };
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction per two lanes of math, IEEE fp32 rounding
+// per element, so results equal the scalar fp32 ones).
+using f2x = unsigned long long;
+__device__ __forceinline__ f2x f2_make(float lo, float hi) {
+    f2x d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ float2 f2_split(f2x v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ f2x f2_mul(f2x a, f2x b) {
+    f2x d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ f2x f2_fma(f2x a, f2x b, f2x c) {
+    f2x d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ f2x f2_add(f2x a, f2x b) {
+    f2x d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// A 16-byte unit of elements as kPairs fp32 pairs.
 template <typename T>
 struct RmsElem;
 template <>
 struct RmsElem<__nv_bfloat16> {
-    static constexpr int kPer16 = 8;
-    static __device__ __forceinline__ void unpack(uint4 p, float* f) {
+    static constexpr int kPairs = 4;
+    static __device__ __forceinline__ void unpack(uint4 p, f2x* f) {   // bf16 -> f32 is a 16-bit shift
         const uint32_t w[4] = {p.x, p.y, p.z, p.w};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
-            f[2 * k] = v.x;
-            f[2 * k + 1] = v.y;
-        }
+        for (int k = 0; k < 4; ++k) f[k] = f2_make(__uint_as_float(w[k] << 16), __uint_as_float(w[k] & 0xffff0000u));
     }
-    static __device__ __forceinline__ uint4 pack(const float* f) {
+    static __device__ __forceinline__ uint4 pack(const f2x* f) {   // round to nearest even, two per cvt
         uint32_t w[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
-            w[k] = *reinterpret_cast<const uint32_t*>(&h);
+            const float2 v = f2_split(f[k]);
+            asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w[k]) : "f"(v.y), "f"(v.x));
         }
         return make_uint4(w[0], w[1], w[2], w[3]);
     }
 };
 template <>
 struct RmsElem<float> {
-    static constexpr int kPer16 = 4;
-    static __device__ __forceinline__ void unpack(uint4 p, float* f) {
-        f[0] = __uint_as_float(p.x);
-        f[1] = __uint_as_float(p.y);
-        f[2] = __uint_as_float(p.z);
-        f[3] = __uint_as_float(p.w);
+    static constexpr int kPairs = 2;
+    static __device__ __forceinline__ void unpack(uint4 p, f2x* f) {
+        f[0] = f2_make(__uint_as_float(p.x), __uint_as_float(p.y));
+        f[1] = f2_make(__uint_as_float(p.z), __uint_as_float(p.w));
     }
-    static __device__ __forceinline__ uint4 pack(const float* f) {
-        return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+    static __device__ __forceinline__ uint4 pack(const f2x* f) {
+        const float2 a = f2_split(f[0]), b = f2_split(f[1]);
+        return make_uint4(__float_as_uint(a.x), __float_as_uint(a.y), __float_as_uint(b.x), __float_as_uint(b.y));
     }
 };
 
-// Shared-memory layout: [0,128) barriers | slots kSets x N x R floats | w slice | stages x R x slice (x2 with residual)
-__host__ __device__ constexpr uint32_t rms_slots_off() { return 128u; }
-__host__ __device__ constexpr uint32_t rms_w_off(int n) { return 128u + (uint32_t)kSets * n * kR * 4u; }
+// Shared-memory layout: [0,256) barriers | slots kSets x N x R floats | w slice | stages x R x slice (x2 with residual)
+__host__ __device__ constexpr uint32_t rms_slots_off() { return 256u; }
+__host__ __device__ constexpr uint32_t rms_w_off(int n) { return rms_slots_off() + (uint32_t)kSets * n * kR * 4u; }
 __host__ __device__ constexpr uint32_t rms_stage_off(int n, uint32_t slice) { return rms_w_off(n) + slice; }
 __host__ __device__ constexpr uint32_t rms_smem(int n, uint32_t slice, bool residual, int stages) {
     return rms_stage_off(n, slice) + (uint32_t)stages * kR * slice * (residual ? 2u : 1u);
@@ -111,7 +146,7 @@ __host__ __device__ constexpr uint32_t rms_smem(int n, uint32_t slice, bool resi
 __device__ __forceinline__ void wait_one(dsb::Ctx& c, int i) { dsb::wait(c, i); }
 
 template <int N, typename T, bool RES, int UPL>
-__global__ void __launch_bounds__(kThreadsRms, 3) rmsnorm_cluster_kernel(const RmsArgs a) {
+__global__ void __launch_bounds__(kThreadsRms, kCtasPerSm) rmsnorm_cluster_kernel(const RmsArgs a) {
     using E = RmsElem<T>;
     dsb::Ctx c;
     dsb::ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
@@ -120,11 +155,12 @@ __global__ void __launch_bounds__(kThreadsRms, 3) rmsnorm_cluster_kernel(const R
     const uint32_t slice = a.slice_bytes, units = slice >> 4;   // 16-B units per row slice (<= 32 * UPL)
     const uint32_t slots = rms_slots_off(), woff = rms_w_off(N), stage0 = rms_stage_off(N, slice);
     const uint32_t stage_bytes = (uint32_t)kR * slice * (RES ? 2u : 1u);
-    const long long nst = a.stages;
-    const long long groups = (a.rows + kR - 1) / kR;
-    const long long step = (long long)num_clusters();
-    const long long first = (long long)cluster_id();
-    const long long iters = first < groups ? (groups - 1 - first) / step + 1 : 0;
+    const uint32_t nst = (uint32_t)a.stages;
+    // cluster q owns the contiguous rows [lo, hi) = [q*rows/C, (q+1)*rows/C): every cluster moves the same
+    // bytes (within one row), in groups of kR rows (the last one partial)
+    const long long nclu = (long long)num_clusters(), cq = (long long)cluster_id();
+    const long long lo = cq * a.rows / nclu, hi = (cq + 1) * a.rows / nclu;
+    const long long iters = (hi - lo + kR - 1) / kR;
     const size_t row_bytes = (size_t)a.hidden * sizeof(T);
     const size_t col_off = (size_t)c.rank * slice;
 
@@ -133,31 +169,32 @@ __global__ void __launch_bounds__(kThreadsRms, 3) rmsnorm_cluster_kernel(const R
             mbar_init(c.bar(kFull + s), 1);
             mbar_init(c.bar(kEmpty + s), kConsumers);
         }
+        mbar_init(c.bar(kWBar), 1);
         for (int s = 0; s < kSets; ++s) mbar_init(c.bar(kSum + s), 1);
         fence_mbar_init();
     }
-    {   // weight slice -> shared
-        const uint4* wsrc = reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(a.w) + col_off);
-        uint4* wdst = c.ptr<uint4>(woff);
-        for (uint32_t i = threadIdx.x; i < units; i += blockDim.x) wdst[i] = __ldg(wsrc + i);
-    }
-    __syncthreads();
-    cluster_sync();   // barriers of every CTA initialised before any remote store completes on them
+    __syncthreads();   // local barriers initialised: the producer may load at once
+    // Split cluster barrier: every thread arrives now (releasing its barrier inits cluster-wide); consumers
+    // wait before their first remote store, the producer only after it has issued its loads, so the first
+    // HBM reads overlap the cluster rendezvous.
+    cluster_arrive();
     c.deadline = globaltimer() + c.wait_limit;
 
     if (warp == kConsumers) {
         // ---------------------------------------------------------------- producer warp (lane 0)
         if (lane == 0) {
+            dsb::arm(c, kWBar, slice);   // weight slice -> shared, on its own barrier
+            bulk_load_g2s(c.sa + woff, static_cast<const unsigned char*>(a.w) + col_off, slice, c.bar(kWBar));
             const unsigned char* xb = static_cast<const unsigned char*>(a.x);
             const unsigned char* rb = static_cast<const unsigned char*>(a.res);
-            for (long long i = 0; i < iters; ++i) {
-                const int s = (int)(i % nst);
-                if (i >= nst) {   // the stage's previous group is normalised by every consumer warp
+            uint32_t s = 0;   // stage of group i
+            for (long long i = 0; i < iters; ++i, s = (s + 1 == nst) ? 0u : s + 1) {
+                if (i >= (long long)nst) {   // the stage's previous group is normalised by every consumer warp
                     c.deadline = globaltimer() + c.wait_limit;
-                    wait_one(c, kEmpty + s);
+                    wait_one(c, kEmpty + (int)s);
                 }
-                const long long r0 = (first + i * step) * kR;
-                const int nr = (int)min((long long)kR, a.rows - r0);
+                const long long r0 = lo + i * kR;
+                const int nr = (int)min((long long)kR, hi - r0);
                 const uint32_t dst = stage0 + (uint32_t)s * stage_bytes;
                 dsb::arm(c, kFull + s, (uint32_t)nr * slice * (RES ? 2u : 1u));
                 for (int r = 0; r < nr; ++r) {
@@ -169,75 +206,103 @@ __global__ void __launch_bounds__(kThreadsRms, 3) rmsnorm_cluster_kernel(const R
             }
         }
         __syncwarp();   // reconverge before the aligned cluster barrier
+        cluster_wait();
     } else {
         // ---------------------------------------------------------------- consumer warps
+        cluster_wait();   // every CTA's barriers initialised before any remote store completes on them
+        wait_one(c, kWBar);
         const uint4* wp = c.ptr<const uint4>(woff);
-        // h of row k of group i (slot of the stage), unit u, as floats
-        auto load_h = [&](long long i, int k, uint32_t u, float* f) {
-            const uint4* xs = c.ptr<const uint4>(stage0 + (uint32_t)(i % nst) * stage_bytes);
+        const float inv_hidden = 1.0f / (float)a.hidden;
+        constexpr int P = E::kPairs;
+        // this lane's weight units as fp32 pairs, held in registers when they fit in 16 of them
+        constexpr bool kWReg = UPL * P * 2 <= 16;
+        f2x wr[kWReg ? UPL : 1][P];
+        if constexpr (kWReg) {
+#pragma unroll
+            for (int q = 0; q < UPL; ++q) {
+                const uint32_t u = lane + 32u * q;
+                if (u < units) E::unpack(wp[u], wr[q]);
+            }
+        }
+        // h of row k of the group held in stage s, unit u, as fp32 pairs
+        auto load_h = [&](uint32_t s, int k, uint32_t u, f2x* f) {
+            const uint4* xs = c.ptr<const uint4>(stage0 + s * stage_bytes);
             const uint32_t idx = (warp * kRowsPerWarp + k) * units + u;
             E::unpack(xs[idx], f);
             if (RES) {
-                float r[E::kPer16];
+                f2x r[P];
                 E::unpack(xs[(size_t)kR * units + idx], r);
 #pragma unroll
-                for (int e = 0; e < E::kPer16; ++e) f[e] += r[e];
+                for (int e = 0; e < P; ++e) f[e] = f2_add(f[e], r[e]);
                 E::unpack(E::pack(f), f);   // h rounded to the element type (the pre-norm output)
             }
         };
-        // wait for group j's rows, reduce my rows' sums of squares and push them to every CTA
-        auto send = [&](long long j) {
-            wait_one(c, kFull + (int)(j % nst));
-            const long long row0 = (first + j * step) * kR + (long long)warp * kRowsPerWarp;
+        // wait for group j's rows (stage s), reduce my rows' sums of squares and push them to every CTA
+        auto send = [&](long long j, uint32_t s) {
+            wait_one(c, kFull + (int)s);
+            const long long row0 = lo + j * kR + (long long)warp * kRowsPerWarp;
             float ss[kRowsPerWarp];
 #pragma unroll
             for (int k = 0; k < kRowsPerWarp; ++k) {
-                ss[k] = 0.f;
-                if (row0 + k < a.rows) {
+                f2x acc = 0ull;   // (+0.0f, +0.0f)
+                if (row0 + k < hi) {
 #pragma unroll
                     for (int q = 0; q < UPL; ++q) {
                         const uint32_t u = lane + 32u * q;
                         if (u < units) {
-                            float f[E::kPer16];
-                            load_h(j, k, u, f);
+                            f2x f[P];
+                            load_h(s, k, u, f);
 #pragma unroll
-                            for (int e = 0; e < E::kPer16; ++e) ss[k] = fmaf(f[e], f[e], ss[k]);
+                            for (int e = 0; e < P; ++e) acc = f2_fma(f[e], f[e], acc);
                         }
                     }
                 }
+                const float2 a2 = f2_split(acc);
+                ss[k] = a2.x + a2.y;
 #pragma unroll
                 for (int off = 16; off > 0; off >>= 1) ss[k] += __shfl_xor_sync(0xffffffffu, ss[k], off);
             }
-            const int set = (int)(j % kSets);
+            const int set = (int)(j & (kSets - 1));
             if (threadIdx.x == 0) dsb::arm(c, kSum + set, (uint32_t)N * kR * 4u);
-            if (lane == 0) {
+            if (lane < (uint32_t)N) {   // lane q stores the pair into CTA q (the butterfly left it in every lane)
                 const uint32_t dst = slots + (((uint32_t)set * N + c.rank) * kR + warp * kRowsPerWarp) * 4u;
-                const uint32_t bar = c.bar(kSum + set);
-                for (uint32_t q = 0; q < (uint32_t)N; ++q) {
-                    const uint32_t rd = mapa(c.sa + dst, q), rbar = mapa(bar, q);
-                    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1,%2}, [%3];" ::
-                                     "r"(rd),
-                                 "f"(ss[0]), "f"(ss[1]), "r"(rbar)
-                                 : "memory");
-                }
+                const uint32_t rd = mapa(c.sa + dst, lane), rbar = mapa(c.bar(kSum + set), lane);
+                asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1,%2}, [%3];" ::"r"(rd),
+                             "f"(ss[0]), "f"(ss[1]), "r"(rbar)
+                             : "memory");
             }
         };
-        if (iters > 0) send(0);
+        const long long look = rms_lookahead((int)nst);
+        uint32_t s = 0, s_send = 0;   // stages of group i and of the next group to send
+        for (long long j = 0; j < look && j < iters; ++j) {
+            send(j, s_send);
+            s_send = (s_send + 1 == nst) ? 0u : s_send + 1;
+        }
         for (long long i = 0; i < iters; ++i) {
             c.deadline = globaltimer() + c.wait_limit;
-            if (i + 1 < iters) send(i + 1);   // one group ahead
-            const int set = (int)(i % kSets);
+            if (i + look < iters) {   // `look` groups ahead
+                send(i + look, s_send);
+                s_send = (s_send + 1 == nst) ? 0u : s_send + 1;
+            }
+            const int set = (int)(i & (kSets - 1));
             wait_one(c, kSum + set);
-            const long long row0 = (first + i * step) * kR + (long long)warp * kRowsPerWarp;
-            const float* sl = c.ptr<const float>(slots + (uint32_t)set * N * kR * 4u);
+            const long long row0 = lo + i * kR + (long long)warp * kRowsPerWarp;
+            // the N partials of my two rows: lane q < N loads CTA q's pair, a butterfly over N lanes sums them
+            float2 part = make_float2(0.f, 0.f);
+            if (lane < (uint32_t)N)
+                part = *c.ptr<const float2>(slots + (((uint32_t)set * N + lane) * kR + warp * kRowsPerWarp) * 4u);
+#pragma unroll
+            for (int off = N / 2; off > 0; off >>= 1) {
+                part.x += __shfl_xor_sync(0xffffffffu, part.x, off);
+                part.y += __shfl_xor_sync(0xffffffffu, part.y, off);
+            }
+            const float tot2[kRowsPerWarp] = {__shfl_sync(0xffffffffu, part.x, 0), __shfl_sync(0xffffffffu, part.y, 0)};
 #pragma unroll
             for (int k = 0; k < kRowsPerWarp; ++k) {
                 const long long row = row0 + k;
-                float tot = 0.f;
-#pragma unroll
-                for (int q = 0; q < N; ++q) tot += sl[q * kR + warp * kRowsPerWarp + k];
-                const float scale = rsqrtf(tot / (float)a.hidden + a.eps);
-                if (row >= a.rows) continue;
+                const float scale = rsqrtf(fmaf(tot2[k], inv_hidden, a.eps));
+                const f2x scale2 = f2_make(scale, scale);
+                if (row >= hi) continue;
                 uint4* yo = reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.y) + (size_t)row * row_bytes + col_off);
                 uint4* po = RES && a.pre != nullptr
                                 ? reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.pre) + (size_t)row * row_bytes +
@@ -247,18 +312,25 @@ __global__ void __launch_bounds__(kThreadsRms, 3) rmsnorm_cluster_kernel(const R
                 for (int q = 0; q < UPL; ++q) {
                     const uint32_t u = lane + 32u * q;
                     if (u < units) {
-                        float f[E::kPer16], w[E::kPer16];
-                        load_h(i, k, u, f);
+                        f2x f[P];
+                        load_h(s, k, u, f);
                         if (RES && po != nullptr) __stcs(po + u, E::pack(f));
-                        E::unpack(wp[u], w);
+                        if constexpr (kWReg) {
 #pragma unroll
-                        for (int e = 0; e < E::kPer16; ++e) f[e] = f[e] * scale * w[e];
+                            for (int e = 0; e < P; ++e) f[e] = f2_mul(f2_mul(f[e], scale2), wr[q][e]);
+                        } else {
+                            f2x w[P];
+                            E::unpack(wp[u], w);
+#pragma unroll
+                            for (int e = 0; e < P; ++e) f[e] = f2_mul(f2_mul(f[e], scale2), w[e]);
+                        }
                         __stcs(yo + u, E::pack(f));
                     }
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(c.bar(kEmpty + (int)(i % nst)));   // stage free for the producer
+            if (lane == 0) mbar_arrive(c.bar(kEmpty + (int)s));   // stage free for the producer
+            s = (s + 1 == nst) ? 0u : s + 1;
         }
     }
     dsb::finish(c);   // no CTA leaves while a peer may still store into its slots
@@ -316,9 +388,15 @@ dsmem_status rms_launch(int dtype, const void* x, const void* res, const void* w
     const bool has_res = res != nullptr;
     const uint32_t units = (uint32_t)(slice / 16);
     const int upl = units <= 32 ? 1 : units <= 64 ? 2 : 4;
-    // the deepest ring (at most kStages, at least 2) that fits the per-CTA shared-memory limit
+    // Ring depth: the deepest (<= kStages) that still lets kCtasPerSm CTAs share an SM (228 KiB of shared
+    // memory, 1 KiB reserved per CTA), else the deepest that fits one CTA; at least 2.
+    auto per_sm = [&](int st) { return (int)(kSmemPerSm / (rms_smem(n, (uint32_t)slice, has_res, st) + 1024u)); };
     int stages = kStages;
-    while (stages > 2 && rms_smem(n, (uint32_t)slice, has_res, stages) > dsb::kSmemLimit) --stages;
+    while (stages > 2 && per_sm(stages) < kCtasPerSm) --stages;
+    if (per_sm(stages) < kCtasPerSm) {
+        stages = kStages;
+        while (stages > 2 && rms_smem(n, (uint32_t)slice, has_res, stages) > dsb::kSmemLimit) --stages;
+    }
     const uint32_t smem = rms_smem(n, (uint32_t)slice, has_res, stages);
     if (smem > dsb::kSmemLimit) return DSMEM_ERR_SMEM_LIMIT;
     const void* fn = dtype == DSMEM_BF16
@@ -417,3 +495,4 @@ dsmem_status dsmem_rmsnorm_check(int device, unsigned* error_bits) {
 }
 
 }  // extern "C"
+
