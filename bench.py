@@ -37,6 +37,9 @@ CLUSTER_N = 8
 PAYLOAD = 65536           # bytes per CTA (f32: M = 16384)
 BATCH_BYTES = 2 << 30     # input bytes per GPU per step
 HBM_FALLBACK_GBS = 6650.0
+# kernels the library launches for a batch (more than one cluster problem) with its pipelined drivers on
+KERNEL_NAMES = {"TWO_SHOT_PUSH": "two_shot_pipelined_kernel<AR_TwoShotPipelined<{n},float,Sum>>",
+                "RS_PUSH_GLOBAL_AG": "two_shot_pipelined_kernel<AR_RsPushGlobalAgPipelined<{n},float,Sum>>"}
 
 
 def parse():
@@ -314,7 +317,8 @@ def run_ours(args, rank, world, local):
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                 "peak_source": peak_src, "algorithmic_bytes_per_launch": algo_bytes,
-                "kernel": f"batch_kernel<AR_{resolved.name}<8,float,Sum>>"}
+                "kernel": KERNEL_NAMES.get(resolved.name, f"batch_kernel<AR_{resolved.name}<{n},float,Sum>>")
+                .format(n=n)}
 
     # end to end through the public API, host buffers: H2D of the step's input, launch, D2H of its output
     hin = torch.empty(tin.numel(), dtype=torch.float32, pin_memory=True)
