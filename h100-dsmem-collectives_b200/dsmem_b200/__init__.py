@@ -166,6 +166,20 @@ def lib():
         "dsmem_ceiling_dsmem_bw": (c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double),
                                            ctypes.POINTER(c_ll), ctypes.POINTER(c_int)]),
         "dsmem_version": (ctypes.c_char_p, []),
+        "dsmem_tp_alloc": (c_int, [c_size, ctypes.POINTER(c_vp), c_vp]),
+        "dsmem_tp_open": (c_int, [c_vp, c_int, c_int, c_vp]),
+        "dsmem_tp_buffers": (c_int, [c_vp, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), ctypes.POINTER(c_size)]),
+        "dsmem_tp_allreduce_rmsnorm": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, ctypes.c_float, c_ll, c_int, c_int,
+                                               c_vp, c_vp]),
+        "dsmem_tp_check": (c_int, [c_vp, ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_uint)]),
+        "dsmem_tp_close": (c_int, [c_vp]),
+        "dsmem_tp_emulate": (c_int, [c_int, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), c_int, c_vp, c_vp,
+                                     ctypes.c_float, c_ll, c_int, c_int, c_vp]),
+        "dsmem_nccl_unique_id": (c_int, [c_vp]),
+        "dsmem_nccl_comm_init": (c_int, [c_int, c_int, c_vp, ctypes.POINTER(c_vp)]),
+        "dsmem_nccl_comm_destroy": (c_int, [c_vp]),
+        "dsmem_tp_allreduce_rmsnorm_nccl": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, ctypes.c_float, c_ll, c_int, c_int,
+                                                    c_vp, c_vp, c_vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -352,6 +366,26 @@ def rmsnorm_check(device=0):
     _ok(lib().dsmem_rmsnorm_check(int(device), ctypes.byref(bits)), "dsmem_rmsnorm_check")
     if bits.value & 1:
         raise DsmemError(Status.TIMEOUT, "rmsnorm")
+
+
+def tp_emulate(xs, ys, w, eps=1e-6, cluster_size=8, residual=None, stream=None):
+    """The tensor-parallel AllReduce+RMSNorm kernel for len(xs) ranks emulated in one launch on one GPU:
+    every ys[k] = RMSNorm(sum(xs) (+ residual)) * w. bf16 CUDA tensors [rows, hidden]."""
+    import torch
+
+    tp = len(xs)
+    if len(ys) != tp or tp == 0:
+        raise ValueError("xs and ys must have one tensor per rank")
+    rows, hidden = xs[0].shape
+    for t in list(xs) + list(ys) + [w] + ([residual] if residual is not None else []):
+        if t.dtype != torch.bfloat16 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError("bf16 contiguous CUDA tensors expected")
+    xa = (ctypes.c_void_p * tp)(*[x.data_ptr() for x in xs])
+    ya = (ctypes.c_void_p * tp)(*[y.data_ptr() for y in ys])
+    s = stream if stream is not None else torch.cuda.current_stream(xs[0].device).cuda_stream
+    _ok(lib().dsmem_tp_emulate(tp, xa, ya, int(Dtype.BF16), residual.data_ptr() if residual is not None else None,
+                               w.data_ptr(), float(eps), rows, hidden, int(cluster_size), ctypes.c_void_p(s or None)),
+        f"dsmem_tp_emulate(tp={tp}, {rows}x{hidden}, cluster {cluster_size})")
 
 
 def dsmem_bandwidth_point(mode, cluster_size, passes, reps=5, ctas_per_sm=1):

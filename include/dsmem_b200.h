@@ -232,6 +232,57 @@ dsmem_status dsmem_allreduce_two_shot_noalloc(dsmem_dtype dtype, int cluster_siz
                                               const void* in, void* out, int num_clusters, unsigned* status_out,
                                               dsmem_stream_t stream);
 
+/*
+ * Tensor-parallel AllReduce + RMSNorm across the GPUs of one node (one process per
+ * GPU). y = RMSNorm(sum over ranks of x_rank (+ residual)) * w on every rank, bf16, fp32 sum and
+ * statistics. Replaces the AllReduce + RMSNorm pipeline of
+ * kernels/rmsnorm_lamport__fused_allreduce_rmsnorm__hpcops.cu:37-197 (which the reference declares but
+ * never ran, roofline/.../hpcops_rmsnorm_lamport.yaml:35-50) with one fused kernel per rank over NVLink
+ * peer memory: reduce-scatter by rows with peer loads, the cluster RMSNorm of the owned rows (DSMEM
+ * partial-sum push), all-gather by peer stores. Set-up, per rank:
+ *   dsmem_tp_alloc   allocate this rank's buffer (signals + x region + y region, capacity bytes each) and
+ *                    return its CUDA IPC handle (DSMEM_TP_HANDLE_BYTES) to share with the other ranks;
+ *   dsmem_tp_open    map every rank's buffer (handles: tp handles in rank order);
+ *   dsmem_tp_buffers the x and y regions: a producer may write x there and a consumer read y there, which
+ *                    saves the copies that dsmem_tp_allreduce_rmsnorm makes for other pointers.
+ * dsmem_tp_allreduce_rmsnorm: x (NULL: already in the x region) [rows x hidden]; residual (nullable) and
+ * w local; y (NULL: leave in the y region). Every rank calls it with the same shape, in the same order;
+ * cross-GPU waits are bounded (2 s) and report DSMEM_ERR_TIMEOUT through dsmem_tp_check.
+ * Shapes: hidden a multiple of 8 * cluster_size, at most 2 KiB of a row per CTA; rows*hidden*2 <= capacity
+ * (else DSMEM_ERR_SCRATCH_LIMIT). tp in {1, 2, 4, 8}.
+ */
+#define DSMEM_TP_HANDLE_BYTES 64
+typedef struct dsmem_tp_ctx* dsmem_tp_t;
+dsmem_status dsmem_tp_alloc(size_t capacity_bytes, dsmem_tp_t* ctx, void* ipc_handle);
+dsmem_status dsmem_tp_open(dsmem_tp_t ctx, int rank, int tp, const void* handles);
+dsmem_status dsmem_tp_buffers(dsmem_tp_t ctx, void** x, void** y, size_t* capacity_bytes);
+dsmem_status dsmem_tp_allreduce_rmsnorm(dsmem_tp_t ctx, dsmem_dtype dtype, const void* x, const void* residual,
+                                        const void* w, float eps, long long rows, int hidden, int cluster_size,
+                                        void* y, dsmem_stream_t stream);
+/* Read and clear the context's device error words (synchronous): TIMEOUT / BOUNDS / OK; detail as in
+ * dsmem_last_error_detail (barrier 0x70 + r: entry wait for rank r; 0x78 + r: exit wait). */
+dsmem_status dsmem_tp_check(dsmem_tp_t ctx, unsigned* error_bits, unsigned* detail);
+dsmem_status dsmem_tp_close(dsmem_tp_t ctx);
+/* The same kernel for `tp` ranks emulated in one launch on one GPU (xs, ys: tp local buffers each; every
+ * row computed once and written to all tp y buffers; no flags). For single-GPU parity tests. */
+dsmem_status dsmem_tp_emulate(int tp, const void* const* xs, void* const* ys, dsmem_dtype dtype, const void* residual,
+                              const void* w, float eps, long long rows, int hidden, int cluster_size,
+                              dsmem_stream_t stream);
+
+/*
+ * The NCCL composition (the baseline of the fused kernel, and the configs[4] pipeline as the reference
+ * describes it): ncclAllReduce(bf16, sum) of x into `sum`, then dsmem_rmsnorm(_residual)_launch of sum.
+ * comm is an ncclComm_t; NCCL is resolved at run time from the process (libnccl.so.2). The helpers make a
+ * communicator for callers without one (uid: 128 bytes, an ncclUniqueId, shared by the caller).
+ */
+typedef void* dsmem_nccl_comm_t;
+dsmem_status dsmem_nccl_unique_id(void* uid);
+dsmem_status dsmem_nccl_comm_init(int world, int rank, const void* uid, dsmem_nccl_comm_t* comm);
+dsmem_status dsmem_nccl_comm_destroy(dsmem_nccl_comm_t comm);
+dsmem_status dsmem_tp_allreduce_rmsnorm_nccl(dsmem_nccl_comm_t comm, dsmem_dtype dtype, const void* x,
+                                             const void* residual, const void* w, float eps, long long rows,
+                                             int hidden, int cluster_size, void* sum, void* y, dsmem_stream_t stream);
+
 /* Library version string. */
 const char* dsmem_version(void);
 

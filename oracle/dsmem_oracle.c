@@ -228,6 +228,22 @@ void orc_rmsnorm(int dtype, size_t rows, size_t hidden, const void* x, const voi
     }
 }
 
+void orc_tp_rmsnorm(int dtype, size_t ranks, size_t rows, size_t hidden, const void* const* xs, const void* res,
+                    const void* w, double eps, double* y) {
+    for (size_t r = 0; r < rows; ++r) {
+        double ss = 0.0;
+        for (size_t i = 0; i < hidden; ++i) {
+            double h = 0.0;
+            for (size_t k = 0; k < ranks; ++k) h += load_elem(dtype, xs[k], r * hidden + i);
+            if (res) h += load_elem(dtype, res, r * hidden + i);
+            y[r * hidden + i] = h;
+            ss += h * h;
+        }
+        const double scale = 1.0 / sqrt(ss / (double)hidden + eps);
+        for (size_t i = 0; i < hidden; ++i) y[r * hidden + i] *= scale * load_elem(dtype, w, i);
+    }
+}
+
 void orc_sum_ranks(int dtype, size_t ranks, size_t n, const void* const* xs, double* out) {
     for (size_t i = 0; i < n; ++i) {
         double s = 0.0;

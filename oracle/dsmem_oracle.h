@@ -74,6 +74,11 @@ long long orc_check(int dtype, size_t n, const void* out, const double* ref, int
 void orc_rmsnorm(int dtype, size_t rows, size_t hidden, const void* x, const void* res, const void* w, double eps,
                  double* y, double* pre);
 
+/* Tensor-parallel AllReduce + RMSNorm oracle: h = sum over ranks of xs[k] (+ res), in double, then the
+ * RMSNorm above (clusterfusion_rmsnorm.py:65) of h; xs: `ranks` arrays [rows][hidden]; y in double. */
+void orc_tp_rmsnorm(int dtype, size_t ranks, size_t rows, size_t hidden, const void* const* xs, const void* res,
+                    const void* w, double eps, double* y);
+
 /* Sum of `ranks` arrays of bf16/f32 (TP all-reduce input), in double. */
 void orc_sum_ranks(int dtype, size_t ranks, size_t n, const void* const* xs, double* out);
 

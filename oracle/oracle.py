@@ -42,6 +42,7 @@ def lib():
         L.orc_check.restype = ctypes.c_longlong
         L.orc_rmsnorm.argtypes = [i, sz, sz, vp, vp, vp, d, vp, vp]
         L.orc_sum_ranks.argtypes = [i, sz, sz, ctypes.POINTER(vp), vp]
+        L.orc_tp_rmsnorm.argtypes = [i, sz, sz, sz, ctypes.POINTER(vp), vp, vp, d, vp]
         L.orc_mt64_seed.argtypes = [vp, u64]
         L.orc_mt64_next.argtypes = [vp]
         L.orc_mt64_next.restype = u64
@@ -131,6 +132,17 @@ def sum_ranks(dtype, xs):
     out = np.empty(xs[0].size, np.float64)
     lib().orc_sum_ranks(dtype, len(xs), xs[0].size, arr, _p(out))
     return out
+
+
+def tp_rmsnorm(dtype, xs, w, eps, res=None):
+    """y (double) = RMSNorm(sum of the ranks' xs (+ res)) * w; xs: list of [rows, hidden] arrays."""
+    xs = [np.ascontiguousarray(x) for x in xs]
+    rows, hidden = xs[0].shape
+    arr = (ctypes.c_void_p * len(xs))(*[x.ctypes.data for x in xs])
+    y = np.empty((rows, hidden), np.float64)
+    lib().orc_tp_rmsnorm(dtype, len(xs), rows, hidden, arr, _p(np.ascontiguousarray(res)) if res is not None else None,
+                         _p(np.ascontiguousarray(w)), eps, _p(y))
+    return y
 
 
 def bf16_to_f32(u16):

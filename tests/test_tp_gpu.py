@@ -1,0 +1,138 @@
+"""Tensor-parallel AllReduce + RMSNorm kernel against the CPU oracle.
+
+Single GPU: the kernel for TP ranks emulated in one launch (dsmem_tp_emulate: all ranks' x and y buffers
+local, every row computed once and stored into every rank's y). Two or more GPUs: the real path, one
+process per GPU with CUDA-IPC-mapped buffers (skipped when the box has one GPU).
+Oracle: oracle.tp_rmsnorm (h = sum over ranks (+ residual) in double, then clusterfusion_rmsnorm.py:65).
+Tolerance |got - ref| <= 1e-2 * (1 + |ref|) (bf16 output); every rank's y must be bit-identical.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+import dsmem_b200 as D  # noqa: E402
+
+RTOL = 1e-2
+
+
+def _bf16(torch, host):
+    return torch.from_numpy(host.view(np.int16).copy()).view(torch.bfloat16).cuda()
+
+
+def _np(t):
+    import torch
+
+    return t.cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def _inputs(orc, tp, rows, hidden, seed, residual):
+    xs = [orc.normal(1, rows * hidden, seed + r, 0.0, 1.0).reshape(rows, hidden) for r in range(tp)]
+    w = orc.normal(1, hidden, seed + 100, 1.0, 0.02)
+    res = orc.normal(1, rows * hidden, seed + 200, 0.0, 1.0).reshape(rows, hidden) if residual else None
+    return xs, w, res
+
+
+@pytest.mark.parametrize("tp", (1, 2, 4, 8))
+def test_tp_emulated_matches_oracle(cuda, orc, tp):
+    torch = cuda
+    failures = []
+    for n, rows, hidden, residual in ((8, 64, 8192, False), (8, 17, 8192, True), (16, 33, 8192, False),
+                                      (4, 5, 4096, True), (8, 1, 8192, False), (2, 40, 1024, False)):
+        xs, w, res = _inputs(orc, tp, rows, hidden, seed=rows + tp, residual=residual)
+        txs = [_bf16(torch, x) for x in xs]
+        tys = [torch.full((rows, hidden), float("nan"), dtype=torch.bfloat16, device="cuda") for _ in range(tp)]
+        D.tp_emulate(txs, tys, _bf16(torch, w), 1e-6, cluster_size=n,
+                     residual=_bf16(torch, res) if residual else None)
+        torch.cuda.synchronize()
+        ref = orc.tp_rmsnorm(1, xs, w, 1e-6, res)
+        got = [_np(y) for y in tys]
+        for k in range(1, tp):
+            if not np.array_equal(got[k], got[0]):
+                failures.append(f"n={n} rows={rows}: rank {k}'s y differs from rank 0's")
+        bad, _, mr = orc.check(1, got[0].reshape(-1), ref.reshape(-1), 1, RTOL)
+        if bad:
+            failures.append(f"n={n} rows={rows} hidden={hidden} res={residual}: {bad} beyond tol (max rel {mr})")
+    assert not failures, "\n".join(failures)
+
+
+def test_tp_rejects_bad_shapes(cuda):
+    torch = cuda
+    x = torch.zeros(4, 1000, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(1000, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(D.DsmemError) as e:
+        D.tp_emulate([x, x.clone()], [x.clone(), x.clone()], w, cluster_size=8)   # 1000 not a multiple of 64
+    assert e.value.status == D.Status.ILLEGAL_CONFIG
+    x = torch.zeros(4, 65536, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(65536, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(D.DsmemError) as e:
+        D.tp_emulate([x], [x.clone()], w, cluster_size=8)                           # 8 KiB per CTA slice
+    assert e.value.status == D.Status.ILLEGAL_CONFIG
+
+
+# ----------------------------------------------------------------------------- real multi-GPU path
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, rows, hidden, n, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from dsmem_b200 import tp as T
+    from oracle import oracle as orc
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        xs, w, res = _inputs(orc, world, rows, hidden, seed=7, residual=True)
+        ctx = T.TPContext(T.tp_bytes(rows, hidden))
+        x = _bf16(torch, xs[rank])
+        tw, tr = _bf16(torch, w), _bf16(torch, res)
+        y = torch.empty_like(x)
+        for _ in range(3):   # repeated calls exercise the epoch flags and buffer reuse
+            ctx.allreduce_rmsnorm(x, tw, 1e-6, residual=tr, out=y, cluster_size=n)
+        torch.cuda.synchronize()
+        ctx.check()
+        comm = T.NcclComm()
+        ysum, y2 = torch.empty_like(x), torch.empty_like(x)
+        comm.allreduce_rmsnorm(x, tw, ysum, y2, 1e-6, residual=tr, cluster_size=n)
+        torch.cuda.synchronize()
+        D.rmsnorm_check()
+        np.save(os.path.join(out_dir, f"y{rank}.npy"), _np(y))
+        np.save(os.path.join(out_dir, f"nccl{rank}.npy"), _np(y2))
+        dist.barrier()
+        comm.close()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", (2, 4, 8))
+def test_tp_multi_gpu(cuda, orc, tmp_path, world):
+    torch = cuda
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    rows, hidden, n = 64, 8192, 8
+    mp.start_processes(_rank_main, args=(world, _free_port(), rows, hidden, n, str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    xs, w, res = _inputs(orc, world, rows, hidden, seed=7, residual=True)
+    ref = orc.tp_rmsnorm(1, xs, w, 1e-6, res)
+    ys = [np.load(tmp_path / f"y{r}.npy") for r in range(world)]
+    for r in range(1, world):
+        assert np.array_equal(ys[r], ys[0]), f"rank {r}'s y differs from rank 0's"
+    bad, _, mr = orc.check(1, ys[0].reshape(-1), ref.reshape(-1), 1, RTOL)
+    assert bad == 0, f"fused: {bad} beyond tol (max rel {mr})"
+    for r in range(world):
+        bad, _, mr = orc.check(1, np.load(tmp_path / f"nccl{r}.npy").reshape(-1), ref.reshape(-1), 1, RTOL)
+        assert bad == 0, f"nccl composition rank {r}: {bad} beyond tol (max rel {mr})"
