@@ -17,9 +17,10 @@
 //   * all-gather: the normalised rows are stored into the y buffer of every rank (peer stores), so each
 //     row crosses NVLink once per destination, as in a ring-optimal AllReduce (2(TP-1)/TP of the tensor
 //     per rank), with the RMSNorm fused between the two halves.
-// Cross-GPU ordering: at entry CTA 0 writes the call's epoch into every peer's start flag (release,
-// system scope) and every CTA waits for all peers' start flags (their x is complete: it was written
-// before their launch); at exit the last CTA of the grid (an atomic counter) publishes the epoch into
+// Cross-GPU ordering: at entry CTA 0 writes the call's epoch (a per-rank device counter of completed
+// calls, plus one; no host state, so the call can be captured in a CUDA graph) into every peer's start
+// flag (release, system scope) and every CTA waits for all peers' start flags (their x is complete: it
+// was written before their launch); at exit the last CTA of the grid (an atomic counter) publishes the epoch into
 // every peer's end flag after all CTAs' peer stores, then waits for all peers' end flags, so when the
 // kernel ends this rank's y is complete and no peer still reads its x. Every wait is bounded.
 #include <cuda_runtime.h>
@@ -27,6 +28,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <map>
 #include <mutex>
 
 #include "../../include/dsmem_b200.h"
@@ -47,8 +49,8 @@ constexpr int kSets = 4;                        // partial-sum slot sets (2 are 
 constexpr uint32_t kSlots = 128;                // slot sets start after the barrier area
 constexpr size_t kSignalBytes = 4096;           // per-rank signal region at the start of its buffer
 // signal words (u32): start flag per source rank at 0, end flag per source rank at 32, the grid's
-// arrival counter at 64, error words at 96..99
-constexpr int kSigStart = 0, kSigEnd = 32, kSigCounter = 64, kSigErr = 96;
+// arrival counter at 64, the epoch of the last completed call at 65, error words at 96..99
+constexpr int kSigStart = 0, kSigEnd = 32, kSigCounter = 64, kSigEpoch = 65, kSigErr = 96;
 
 struct TpArgs {
     const uint4* x[kMaxTp];   // x buffer of every rank (this rank's own at [rank])
@@ -64,7 +66,6 @@ struct TpArgs {
     uint32_t slice_bytes;
     uint32_t smem_bytes;
     int rank;
-    unsigned epoch;
     int emulate;              // 1: one launch computes every row for TP local buffers, no flags
 };
 
@@ -94,7 +95,7 @@ __device__ __forceinline__ bool wait_flag(dsb::Ctx& c, const unsigned* flag, uns
 }
 
 template <int N, int TP, int UPL>
-__global__ void __launch_bounds__(kThreadsTp, 2) tp_allreduce_rmsnorm_kernel(const TpArgs a) {
+__global__ void __launch_bounds__(kThreadsTp, (UPL >= 4 ? 1 : 2)) tp_allreduce_rmsnorm_kernel(const TpArgs a) {
     constexpr int P = RmsElem<__nv_bfloat16>::kPairs;
     using E = RmsElem<__nv_bfloat16>;
     dsb::Ctx c;
@@ -108,14 +109,18 @@ __global__ void __launch_bounds__(kThreadsTp, 2) tp_allreduce_rmsnorm_kernel(con
         for (int s = 0; s < kSets; ++s) mbar_init(c.bar(s), 1);
         fence_mbar_init();
     }
-    // ---- cross-GPU entry: every peer has launched, so its x (written before its launch) is complete
+    // ---- cross-GPU entry: every peer has launched, so its x (written before its launch) is complete.
+    // The call's epoch is one past the last completed call's, kept in device memory (the last CTA of a
+    // call stores it), so the kernel can sit in a CUDA graph: every rank makes the same sequence of calls.
+    unsigned epoch = 0;
     if (!a.emulate) {
+        epoch = ld_acquire_sys(a.sig[a.rank] + kSigEpoch) + 1u;
         if (blockIdx.x == 0 && threadIdx.x < TP && (int)threadIdx.x != a.rank) {
             fence_sys();
-            st_release_sys(a.sig[threadIdx.x] + kSigStart + a.rank, a.epoch);
+            st_release_sys(a.sig[threadIdx.x] + kSigStart + a.rank, epoch);
         }
         if (threadIdx.x < TP && (int)threadIdx.x != a.rank)
-            wait_flag(c, a.sig[a.rank] + kSigStart + threadIdx.x, a.epoch, 0x70 + (int)threadIdx.x);
+            wait_flag(c, a.sig[a.rank] + kSigStart + threadIdx.x, epoch, 0x70 + (int)threadIdx.x);
     }
     __syncthreads();
     cluster_sync();   // every CTA's slot barriers initialised before any remote store completes on them
@@ -143,39 +148,64 @@ __global__ void __launch_bounds__(kThreadsTp, 2) tp_allreduce_rmsnorm_kernel(con
         const long long row0 = lo + i * kR + (long long)warp * kRowsPerWarp;
         uint4 h[kRowsPerWarp][UPL];
         float ss[kRowsPerWarp];
+        bool ok[kRowsPerWarp][UPL];
+        long long idx[kRowsPerWarp][UPL];
 #pragma unroll
-        for (int k = 0; k < kRowsPerWarp; ++k) {
-            f2x sacc = 0ull;
-            const long long row = row0 + k;
+        for (int k = 0; k < kRowsPerWarp; ++k)
 #pragma unroll
             for (int q = 0; q < UPL; ++q) {
                 const uint32_t u = lane + 32u * q;
-                h[k][q] = make_uint4(0u, 0u, 0u, 0u);
-                if (row < hi && u < units) {
-                    const long long idx = row * row_u4 + col_u4 + u;
-                    uint4 v[TP];
+                ok[k][q] = row0 + k < hi && u < units;
+                idx[k][q] = (row0 + k) * row_u4 + col_u4 + u;
+            }
+        // Sum over the ranks in rank order. The group's loads from PB ranks at a time are all issued before
+        // any is used, so a lane keeps PB * 2 * UPL 16-byte peer loads in flight.
+        constexpr int PB_MAX = UPL >= 4 ? 1 : (UPL == 2 ? 2 : 4);
+        constexpr int PB = TP < PB_MAX ? TP : PB_MAX;   // a divisor of TP: ranks p0 + pp stay below TP
+        static_assert(TP % PB == 0, "rank batches must tile the TP ranks");
+        f2x acc[kRowsPerWarp][UPL][P];
 #pragma unroll
-                    for (int p = 0; p < TP; ++p) v[p] = a.x[p][idx];   // all ranks' loads in flight
-                    f2x acc[P];
-                    E::unpack(v[0], acc);
+        for (int p0 = 0; p0 < TP; p0 += PB) {
+            uint4 v[PB][kRowsPerWarp][UPL];
 #pragma unroll
-                    for (int p = 1; p < TP; ++p) {
-                        f2x t[P];
-                        E::unpack(v[p], t);
+            for (int pp = 0; pp < PB; ++pp)
 #pragma unroll
-                        for (int e = 0; e < P; ++e) acc[e] = f2_add(acc[e], t[e]);
+                for (int k = 0; k < kRowsPerWarp; ++k)
+#pragma unroll
+                    for (int q = 0; q < UPL; ++q)
+                        v[pp][k][q] = ok[k][q] ? a.x[p0 + pp][idx[k][q]] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int pp = 0; pp < PB; ++pp)
+#pragma unroll
+                for (int k = 0; k < kRowsPerWarp; ++k)
+#pragma unroll
+                    for (int q = 0; q < UPL; ++q) {
+                        if (p0 + pp == 0) {
+                            E::unpack(v[pp][k][q], acc[k][q]);
+                        } else {
+                            f2x t[P];
+                            E::unpack(v[pp][k][q], t);
+#pragma unroll
+                            for (int e = 0; e < P; ++e) acc[k][q][e] = f2_add(acc[k][q][e], t[e]);
+                        }
                     }
-                    if (a.res != nullptr) {
-                        f2x t[P];
-                        E::unpack(a.res[idx], t);
+        }
 #pragma unroll
-                        for (int e = 0; e < P; ++e) acc[e] = f2_add(acc[e], t[e]);
-                    }
-                    h[k][q] = E::pack(acc);   // h rounded to bf16, as the unfused AllReduce would give it
-                    E::unpack(h[k][q], acc);
+        for (int k = 0; k < kRowsPerWarp; ++k) {
+            f2x sacc = 0ull;
 #pragma unroll
-                    for (int e = 0; e < P; ++e) sacc = f2_fma(acc[e], acc[e], sacc);
+            for (int q = 0; q < UPL; ++q) {
+                if (a.res != nullptr && ok[k][q]) {
+                    f2x t[P];
+                    E::unpack(a.res[idx[k][q]], t);
+#pragma unroll
+                    for (int e = 0; e < P; ++e) acc[k][q][e] = f2_add(acc[k][q][e], t[e]);
                 }
+                h[k][q] = E::pack(acc[k][q]);   // h rounded to bf16, as the unfused AllReduce would give it
+                f2x hf[P];
+                E::unpack(h[k][q], hf);
+#pragma unroll
+                for (int e = 0; e < P; ++e) sacc = f2_fma(hf[e], hf[e], sacc);   // zero where !ok
             }
             const float2 s2 = f2_split(sacc);
             ss[k] = s2.x + s2.y;
@@ -226,9 +256,8 @@ __global__ void __launch_bounds__(kThreadsTp, 2) tp_allreduce_rmsnorm_kernel(con
                         for (int e = 0; e < P; ++e) f[e] = f2_mul(f2_mul(f[e], scale2), wv[e]);
                     }
                     const uint4 yv = E::pack(f);
-                    const long long idx = row * row_u4 + col_u4 + u;
 #pragma unroll
-                    for (int p = 0; p < TP; ++p) a.y[p][idx] = yv;   // all-gather: every rank's y
+                    for (int p = 0; p < TP; ++p) a.y[p][idx[k][q]] = yv;   // all-gather: every rank's y
                 }
             }
         }
@@ -244,9 +273,10 @@ __global__ void __launch_bounds__(kThreadsTp, 2) tp_allreduce_rmsnorm_kernel(con
                 fence_sys();
                 *counter = 0u;   // for the next call (stream-ordered after this kernel)
                 for (int t = 0; t < TP; ++t)
-                    if (t != a.rank) st_release_sys(a.sig[t] + kSigEnd + a.rank, a.epoch);
+                    if (t != a.rank) st_release_sys(a.sig[t] + kSigEnd + a.rank, epoch);
                 for (int t = 0; t < TP; ++t)
-                    if (t != a.rank) wait_flag(c, a.sig[a.rank] + kSigEnd + t, a.epoch, 0x78 + t);
+                    if (t != a.rank) wait_flag(c, a.sig[a.rank] + kSigEnd + t, epoch, 0x78 + t);
+                a.sig[a.rank][kSigEpoch] = epoch;   // read by the next call's CTAs (stream-ordered)
             }
         }
     }
@@ -288,7 +318,7 @@ std::mutex g_tp_mu;
 
 // Shape checks and launch of the kernel for `tp` ranks (emulate: all buffers local, one launch).
 dsmem_status tp_launch(const void* const* xs, void* const* ys, unsigned* const* sigs, unsigned* err, int tp,
-                       int rank, unsigned epoch, int emulate, dsmem_dtype dtype, const void* residual,
+                       int rank, int emulate, dsmem_dtype dtype, const void* residual,
                        const void* w, float eps, long long rows, int hidden, int cluster_size,
                        cudaStream_t stream) {
     if (dtype != DSMEM_BF16) return DSMEM_ERR_ILLEGAL_CONFIG;
@@ -321,15 +351,24 @@ dsmem_status tp_launch(const void* const* xs, void* const* ys, unsigned* const* 
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int resident = 0;
+    int resident = 0, dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return DSMEM_ERR_CUDA;
     {
+        // kernel attributes and the occupancy query once per (kernel, device): they cost more than a launch
+        static std::map<std::pair<const void*, int>, int> occupancy;
         std::lock_guard<std::mutex> lock(g_tp_mu);
-        if (n > 8 && cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-            return DSMEM_ERR_CUDA;
-        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return DSMEM_ERR_CUDA;
-        cfg.gridDim = dim3((unsigned)n, 1, 1);
-        if (cudaOccupancyMaxActiveClusters(&resident, fn, &cfg) != cudaSuccess) return DSMEM_ERR_CUDA;
+        auto it = occupancy.find({fn, dev});
+        if (it != occupancy.end()) {
+            resident = it->second;
+        } else {
+            if (n > 8 && cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+                return DSMEM_ERR_CUDA;
+            if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+                return DSMEM_ERR_CUDA;
+            cfg.gridDim = dim3((unsigned)n, 1, 1);
+            if (cudaOccupancyMaxActiveClusters(&resident, fn, &cfg) != cudaSuccess) return DSMEM_ERR_CUDA;
+            occupancy[{fn, dev}] = resident;
+        }
     }
     if (resident < 1) return DSMEM_ERR_SMEM_LIMIT;
     // every CTA must be resident (the exit counter is passed by all of them); at least one cluster even
@@ -353,7 +392,6 @@ dsmem_status tp_launch(const void* const* xs, void* const* ys, unsigned* const* 
     a.slice_bytes = slice;
     a.smem_bytes = smem;
     a.rank = rank;
-    a.epoch = epoch;
     a.emulate = emulate;
     void* args[] = {&a};
     return cudaLaunchKernelExC(&cfg, fn, args) == cudaSuccess ? DSMEM_OK : DSMEM_ERR_CUDA;
@@ -369,8 +407,6 @@ struct dsmem_tp_ctx {
     size_t capacity = 0;             // bytes of each of the x and y regions
     unsigned char* base = nullptr;   // this rank's buffer: [signals 4 KiB][x][y]
     unsigned char* peer[kMaxTp] = {};
-    unsigned epoch = 0;
-    unsigned* emu_err = nullptr;     // error words of the single-GPU emulation
 };
 
 extern "C" {
@@ -450,9 +486,8 @@ dsmem_status dsmem_tp_allreduce_rmsnorm(dsmem_tp_t c, dsmem_dtype dtype, const v
         sigs[p] = reinterpret_cast<unsigned*>(c->peer[p]);
     }
     const dsmem_status st = tp_launch(xs, ys, sigs, reinterpret_cast<unsigned*>(c->base) + kSigErr, c->tp, c->rank,
-                                      c->epoch + 1, 0, dtype, residual, w, eps, rows, hidden, cluster_size, s);
+                                      0, dtype, residual, w, eps, rows, hidden, cluster_size, s);
     if (st != DSMEM_OK) return st;
-    ++c->epoch;
     if (y != nullptr && y != yb && bytes && cudaMemcpyAsync(y, yb, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
         return DSMEM_ERR_CUDA;
     return DSMEM_OK;
@@ -472,7 +507,7 @@ dsmem_status dsmem_tp_emulate(int tp, const void* const* xs, void* const* ys, ds
             cudaMemset(err[dev], 0, 4 * sizeof(unsigned));
         }
     }
-    return tp_launch(xs, ys, nullptr, err[dev], tp, 0, 0, 1, dtype, residual, w, eps, rows, hidden, cluster_size,
+    return tp_launch(xs, ys, nullptr, err[dev], tp, 0, 1, dtype, residual, w, eps, rows, hidden, cluster_size,
                      reinterpret_cast<cudaStream_t>(stream));
 }
 

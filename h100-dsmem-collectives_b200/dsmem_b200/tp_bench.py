@@ -1,0 +1,134 @@
+"""Timing of the tensor-parallel AllReduce + RMSNorm on the GPUs of one node.
+
+    torchrun --nnodes 1 --nproc-per-node 2 --master-addr 127.0.0.1 -m dsmem_b200.tp_bench
+
+(run from the package directory, or with it on PYTHONPATH). Per rank: bf16 x [T x 8192] ~ N(0,1) with
+seed + rank, residual and w ~ N(1, 0.02), eps 1e-6, cluster 8, T in {1, 64, 1024, 8192}. For each T:
+  fused      dsmem_tp_allreduce_rmsnorm with x already in the context's x region and y left in its y
+             region (the zero-copy use: a producer writes x there, a consumer reads y there);
+  fused_api  the same call from ordinary tensors (copies x in and y out on the stream);
+  nccl       the composition: ncclAllReduce (bf16 sum) then the cluster RMSNorm (dsmem_tp_allreduce_rmsnorm_nccl).
+Each figure is the median over rounds of the mean over `reps` calls captured in one CUDA graph (so the
+host's launch overhead is not timed), CUDA events on the replay stream, max over ranks. NVLink roofline: each rank must receive (TP-1)/TP of the tensor and send
+(TP-1)/TP of it, so the bound is (TP-1)/TP * T*H*2 bytes / 770 GB/s (measured peer-copy bandwidth per
+direction on this pool); frac = that time / measured time.
+"""
+from __future__ import annotations
+
+import json
+import statistics
+
+NVLINK_GBS = 770.0
+HIDDEN = 8192
+TOKENS = (1, 64, 1024, 8192)
+
+
+def run(tokens=TOKENS, hidden=HIDDEN, cluster=8, reps=20, rounds=5, warmup=5):
+    import torch
+    import torch.distributed as dist
+
+    from . import rmsnorm_check
+    from . import tp as T
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    tmax = max(tokens)
+    ctx = T.TPContext(T.tp_bytes(tmax, hidden))
+    comm = T.NcclComm()
+    w = (1 + 0.02 * torch.randn(hidden, device=dev, generator=gen)).to(torch.bfloat16)
+    out = {}
+    try:
+        for t in tokens:
+            x = torch.randn(t, hidden, device=dev, generator=gen).to(torch.bfloat16)
+            res = torch.randn(t, hidden, device=dev, generator=gen).to(torch.bfloat16)
+            y = torch.empty_like(x)
+            xb, yb = ctx.buffers(t, hidden)
+            xb.copy_(x)
+            sum_buf = torch.empty_like(x)
+            cases = {
+                "fused": lambda: _zero_copy(ctx, w, res, t, hidden, cluster),
+                "fused_api": lambda: ctx.allreduce_rmsnorm(x, w, 1e-6, residual=res, out=y, cluster_size=cluster),
+                "nccl": lambda: comm.allreduce_rmsnorm(x, w, sum_buf, y, 1e-6, residual=res, cluster_size=cluster),
+            }
+            row = {}
+            for name, fn in cases.items():
+                stream = torch.cuda.Stream()
+                with torch.cuda.stream(stream):
+                    for _ in range(warmup):
+                        fn()
+                torch.cuda.synchronize()
+                dist.barrier()
+                # `reps` calls captured in one CUDA graph, so host launch overhead stays out of the figure
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    for _ in range(reps):
+                        fn()
+                torch.cuda.synchronize()
+                dist.barrier()
+                vals = []
+                for _ in range(rounds):
+                    with torch.cuda.stream(stream):
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record()
+                        graph.replay()
+                        e1.record()
+                    torch.cuda.synchronize()
+                    vals.append(e0.elapsed_time(e1) * 1e3 / reps)
+                del graph
+                us = torch.tensor([statistics.median(vals)], device=dev)
+                dist.all_reduce(us, op=dist.ReduceOp.MAX)
+                us = us.item()
+                size = t * hidden * 2
+                bound_us = (world - 1) / world * size / (NVLINK_GBS * 1e9) * 1e6
+                row[name] = {"us": round(us, 2), "algbw_GBps": round(size / (us * 1e-6) / 1e9, 1),
+                             "busbw_GBps": round(size / (us * 1e-6) / 1e9 * 2 * (world - 1) / world, 1),
+                             "nvlink_frac": round(bound_us / us, 4) if world > 1 else None}
+            ctx.check()
+            rmsnorm_check()
+            out[str(t)] = row
+            dist.barrier()
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.close()
+        ctx.close()
+    return {"tp": world, "hidden": hidden, "cluster_size": cluster, "dtype": "bf16", "nvlink_peak_GBps": NVLINK_GBS,
+            "tokens": out}
+
+
+def _zero_copy(ctx, w, res, t, hidden, cluster):
+    """The fused call with x already in the x region and y left in the y region."""
+    import ctypes
+
+    import torch
+
+    from . import Dtype, _ok, lib
+
+    _ok(lib().dsmem_tp_allreduce_rmsnorm(ctx._ctx, int(Dtype.BF16), None, res.data_ptr(), w.data_ptr(), 1e-6, t,
+                                         hidden, int(cluster), None,
+                                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream or None)),
+        "dsmem_tp_allreduce_rmsnorm")
+
+
+def main():
+    import datetime
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    try:
+        res = run()
+        if dist.get_rank() == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
