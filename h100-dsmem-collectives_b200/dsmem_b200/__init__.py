@@ -117,6 +117,17 @@ EXTENSIONS = {
 }
 
 
+class DecoderParams(ctypes.Structure):
+    """dsmem_decoder_params of include/dsmem_b200.h."""
+    _fields_ = [("batch", ctypes.c_int), ("hidden", ctypes.c_int), ("heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("ffn", ctypes.c_int), ("seq_len", ctypes.c_longlong), ("cache_capacity", ctypes.c_longlong),
+                ("cluster_size", ctypes.c_int), ("eps", ctypes.c_float)] + \
+               [(k, ctypes.c_void_p) for k in ("inp", "res", "w_rms", "wqkv", "wo", "w_post", "wgu", "wd", "kcache",
+                                               "vcache", "cos", "sin", "workspace")] + \
+               [("workspace_bytes", ctypes.c_size_t)] + \
+               [(k, ctypes.c_void_p) for k in ("out", "h_out", "o_out", "k_new", "v_new")]
+
+
 class DsmemError(RuntimeError):
     def __init__(self, status, what=""):
         self.status = Status(status)
@@ -175,6 +186,9 @@ def lib():
         "dsmem_tp_close": (c_int, [c_vp]),
         "dsmem_tp_emulate": (c_int, [c_int, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), c_int, c_vp, c_vp,
                                      ctypes.c_float, c_ll, c_int, c_int, c_vp]),
+        "dsmem_decoder_workspace_bytes": (c_size, [c_int, c_int, c_int]),
+        "dsmem_decoder_layer_launch": (c_int, [ctypes.POINTER(DecoderParams), c_vp]),
+        "dsmem_decoder_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
         "dsmem_nccl_unique_id": (c_int, [c_vp]),
         "dsmem_nccl_comm_init": (c_int, [c_int, c_int, c_vp, ctypes.POINTER(c_vp)]),
         "dsmem_nccl_comm_destroy": (c_int, [c_vp]),
@@ -366,6 +380,49 @@ def rmsnorm_check(device=0):
     _ok(lib().dsmem_rmsnorm_check(int(device), ctypes.byref(bits)), "dsmem_rmsnorm_check")
     if bits.value & 1:
         raise DsmemError(Status.TIMEOUT, "rmsnorm")
+
+
+def decoder_layer(inp, res, w_rms, wqkv, wo, w_post, wgu, wd, kcache, vcache, cos, sin, seq_len, eps=1e-5,
+                  cluster_size=8, out=None, h_out=None, o_out=None, k_new=None, v_new=None, workspace=None,
+                  stream=None):
+    """One decode step of the Llama-2-7B-shaped layer (dsmem_decoder_layer_launch). bf16 CUDA tensors:
+    inp, res [B, hidden]; weights in nn.Linear layout; kcache / vcache [B, cap, heads, 128] with seq_len
+    valid tokens (the step's k, v are stored at index seq_len); cos / sin fp32 [128]. Returns (out, h_out)."""
+    import torch
+
+    B, hidden = inp.shape
+    heads, head_dim = kcache.shape[2], kcache.shape[3]
+    ffn = wd.shape[1]
+    out = torch.empty_like(inp) if out is None else out
+    h_out = torch.empty_like(inp) if h_out is None else h_out
+    need = lib().dsmem_decoder_workspace_bytes(B, hidden, ffn)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=inp.device)
+    p = DecoderParams(batch=B, hidden=hidden, heads=heads, head_dim=head_dim, ffn=ffn, seq_len=int(seq_len),
+                      cache_capacity=kcache.shape[1], cluster_size=int(cluster_size), eps=float(eps))
+    for k, t in (("inp", inp), ("res", res), ("w_rms", w_rms), ("wqkv", wqkv), ("wo", wo), ("w_post", w_post),
+                 ("wgu", wgu), ("wd", wd), ("kcache", kcache), ("vcache", vcache), ("cos", cos), ("sin", sin),
+                 ("workspace", workspace), ("out", out), ("h_out", h_out), ("o_out", o_out), ("k_new", k_new),
+                 ("v_new", v_new)):
+        if t is not None:
+            if not t.is_cuda or not t.is_contiguous():
+                raise ValueError(f"{k} must be a contiguous CUDA tensor")
+            setattr(p, k, t.data_ptr())
+    p.workspace_bytes = workspace.numel() * workspace.element_size()
+    s = stream if stream is not None else torch.cuda.current_stream(inp.device).cuda_stream
+    _ok(lib().dsmem_decoder_layer_launch(ctypes.byref(p), ctypes.c_void_p(s or None)),
+        f"dsmem_decoder_layer_launch(B={B}, hidden={hidden}, ffn={ffn}, S={seq_len}, cluster {cluster_size})")
+    return out, h_out
+
+
+def decoder_check(device=0):
+    """Raise DsmemError(TIMEOUT/BOUNDS) if a decoder kernel's device-side check fired since the last call."""
+    bits = ctypes.c_uint(0)
+    _ok(lib().dsmem_decoder_check(int(device), ctypes.byref(bits)), "dsmem_decoder_check")
+    if bits.value & 1:
+        raise DsmemError(Status.TIMEOUT, "decoder")
+    if bits.value & 2:
+        raise DsmemError(Status.BOUNDS, "decoder")
 
 
 def tp_emulate(xs, ys, w, eps=1e-6, cluster_size=8, residual=None, stream=None):

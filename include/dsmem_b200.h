@@ -283,6 +283,40 @@ dsmem_status dsmem_tp_allreduce_rmsnorm_nccl(dsmem_nccl_comm_t comm, dsmem_dtype
                                              const void* residual, const void* w, float eps, long long rows,
                                              int hidden, int cluster_size, void* sum, void* y, dsmem_stream_t stream);
 
+/*
+ * Llama-2-7B-shaped decoder layer, one decode step. Replaces the fused layer of
+ * kernels/fused_decoder_layer__llama2_7b__clusterfusion.cu:291-922 (ClusterFusion's
+ * llama_decoder_layer_sglang: fp16, batch 1, attention block only) with the whole layer for a batch of
+ * 1..16 sequences, bf16, and the maths of roofline/harness/workloads/clusterfusion_llama2_7b_decoder.py:160-180:
+ *   x = inp + res; xn = RMSNorm(x) w_rms; q, k, v = xn Wqkv^T (rows q | k | v, head-major); NEOX RoPE on q
+ *   and k with the given cos/sin [head_dim] (fp32); k, v stored at token index seq_len of the caches;
+ *   a = softmax(q K^T / sqrt(head_dim)) V over seq_len + 1 tokens; o = a Wo^T; h = x + o;
+ *   hn = RMSNorm(h) w_post; out = (SiLU(hn Wg^T) * hn Wu^T) Wd^T with Wgu = [Wg; Wu] ([2 ffn][hidden]).
+ * Shapes: head_dim 128, hidden = heads * 128, ffn a multiple of 64 and of 32 * cluster_size, cluster_size
+ * 4 or 8 (the CTAs of a cluster split each projection's K dimension and each sequence-head's keys).
+ * Caches [batch][cache_capacity][heads][head_dim] bf16, seq_len < cache_capacity. All tensors bf16
+ * except cos/sin; weights in nn.Linear layout [out][in]. Outputs: out [batch][hidden] (layer output),
+ * h_out [batch][hidden] (the residual stream after attention), o_out (nullable, the attention-block
+ * output), k_new / v_new (nullable, [batch][heads][head_dim]). The caller owns a workspace of
+ * dsmem_decoder_workspace_bytes(batch, hidden, ffn) bytes. Seven stream-ordered launches; asynchronous.
+ */
+typedef struct {
+    int batch, hidden, heads, head_dim, ffn;
+    long long seq_len, cache_capacity;
+    int cluster_size;
+    float eps;
+    const void *inp, *res, *w_rms, *wqkv, *wo, *w_post, *wgu, *wd;
+    void *kcache, *vcache;
+    const float *cos, *sin;
+    void* workspace;
+    size_t workspace_bytes;
+    void *out, *h_out, *o_out, *k_new, *v_new;
+} dsmem_decoder_params;
+size_t dsmem_decoder_workspace_bytes(int batch, int hidden, int ffn);
+dsmem_status dsmem_decoder_layer_launch(const dsmem_decoder_params* params, dsmem_stream_t stream);
+/* Read and clear the decoder kernels' device error word of `device` (synchronous). */
+dsmem_status dsmem_decoder_check(int device, unsigned* error_bits);
+
 /* Library version string. */
 const char* dsmem_version(void);
 

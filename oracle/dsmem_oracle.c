@@ -8,6 +8,7 @@
 #include "dsmem_oracle.h"
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 /* ----------------------------------------------------------------- mt19937_64 */
@@ -250,4 +251,101 @@ void orc_sum_ranks(int dtype, size_t ranks, size_t n, const void* const* xs, dou
         for (size_t r = 0; r < ranks; ++r) s += load_elem(dtype, xs[r], i);
         out[i] = s;
     }
+}
+
+/* ------------------------------------------------------------------- decoder layer */
+static double bfd(const uint16_t* a, size_t i) { return (double)orc_bf16_to_f32(a[i]); }
+
+static void rms_row(const double* x, const uint16_t* w, size_t n, double eps, double* y) {
+    double ss = 0.0;
+    for (size_t i = 0; i < n; ++i) ss += x[i] * x[i];
+    const double sc = 1.0 / sqrt(ss / (double)n + eps);
+    for (size_t i = 0; i < n; ++i) y[i] = x[i] * sc * bfd(w, i);
+}
+
+/* y[f] = sum_k x[k] W[f][k] for f in [0, nout) (W bf16 [nout][nin], nn.Linear layout) */
+static void linear(const double* x, const uint16_t* W, size_t nout, size_t nin, double* y) {
+    for (size_t f = 0; f < nout; ++f) {
+        const uint16_t* row = W + f * nin;
+        double acc = 0.0;
+        for (size_t k = 0; k < nin; ++k) acc += x[k] * (double)orc_bf16_to_f32(row[k]);
+        y[f] = acc;
+    }
+}
+
+void orc_decoder_layer(int batch, int hidden, int heads, int head_dim, int ffn, long long seq_len, long long cap,
+                       const uint16_t* inp, const uint16_t* res, const uint16_t* w_rms, const uint16_t* wqkv,
+                       const uint16_t* wo, const uint16_t* w_post, const uint16_t* wgu, const uint16_t* wd,
+                       const uint16_t* kc, const uint16_t* vc, const float* cosv, const float* sinv, double eps,
+                       double* out, double* h_out, double* o_out, double* k_new, double* v_new) {
+    const size_t hid = (size_t)hidden, D = (size_t)head_dim, H = (size_t)heads, F = (size_t)ffn, half = D / 2;
+    double* x = (double*)malloc(hid * sizeof(double));
+    double* xn = (double*)malloc(hid * sizeof(double));
+    double* qkv = (double*)malloc(3 * hid * sizeof(double));
+    double* a = (double*)malloc(hid * sizeof(double));
+    double* o = (double*)malloc(hid * sizeof(double));
+    double* hn = (double*)malloc(hid * sizeof(double));
+    double* gu = (double*)malloc(2 * F * sizeof(double));
+    double* act = (double*)malloc(F * sizeof(double));
+    double* logit = (double*)malloc(((size_t)seq_len + 1) * sizeof(double));
+    for (int b = 0; b < batch; ++b) {
+        const size_t rb = (size_t)b * hid;
+        for (size_t i = 0; i < hid; ++i) x[i] = bfd(inp, rb + i) + bfd(res, rb + i);
+        rms_row(x, w_rms, hid, eps, xn);
+        linear(xn, wqkv, 3 * hid, hid, qkv);
+        for (int part = 0; part < 2; ++part)   /* NEOX RoPE: x*cos + cat(-x[half:], x[:half])*sin */
+            for (size_t hh = 0; hh < H; ++hh) {
+                double* v = qkv + (size_t)part * hid + hh * D;
+                double r[512];
+                for (size_t i = 0; i < D; ++i) {
+                    const double rot = i < half ? -v[i + half] : v[i - half];
+                    r[i] = v[i] * (double)cosv[i] + rot * (double)sinv[i];
+                }
+                memcpy(v, r, D * sizeof(double));
+            }
+        const double* q = qkv;
+        const double* kn = qkv + hid;
+        const double* vn = qkv + 2 * hid;
+        for (size_t i = 0; i < hid; ++i) {
+            if (k_new) k_new[rb + i] = kn[i];
+            if (v_new) v_new[rb + i] = vn[i];
+        }
+        const double scale = 1.0 / sqrt((double)D);
+        for (size_t hh = 0; hh < H; ++hh) {
+            double mx = -1e300;
+            for (long long s = 0; s <= seq_len; ++s) {
+                double dot = 0.0;
+                for (size_t d = 0; d < D; ++d) {
+                    const double kv = s < seq_len ? bfd(kc, (((size_t)b * cap + s) * H + hh) * D + d) : kn[hh * D + d];
+                    dot += q[hh * D + d] * kv;
+                }
+                logit[s] = dot * scale;
+                if (logit[s] > mx) mx = logit[s];
+            }
+            double den = 0.0;
+            for (long long s = 0; s <= seq_len; ++s) {
+                logit[s] = exp(logit[s] - mx);
+                den += logit[s];
+            }
+            for (size_t d = 0; d < D; ++d) {
+                double num = 0.0;
+                for (long long s = 0; s <= seq_len; ++s) {
+                    const double vv = s < seq_len ? bfd(vc, (((size_t)b * cap + s) * H + hh) * D + d) : vn[hh * D + d];
+                    num += logit[s] * vv;
+                }
+                a[hh * D + d] = num / den;
+            }
+        }
+        linear(a, wo, hid, hid, o);
+        for (size_t i = 0; i < hid; ++i) {
+            if (o_out) o_out[rb + i] = o[i];
+            x[i] += o[i];   /* h */
+            if (h_out) h_out[rb + i] = x[i];
+        }
+        rms_row(x, w_post, hid, eps, hn);
+        linear(hn, wgu, 2 * F, hid, gu);
+        for (size_t j = 0; j < F; ++j) act[j] = gu[j] / (1.0 + exp(-gu[j])) * gu[F + j];
+        linear(act, wd, hid, F, out + rb);
+    }
+    free(x); free(xn); free(qkv); free(a); free(o); free(hn); free(gu); free(act); free(logit);
 }

@@ -79,6 +79,16 @@ void orc_rmsnorm(int dtype, size_t rows, size_t hidden, const void* x, const voi
 void orc_tp_rmsnorm(int dtype, size_t ranks, size_t rows, size_t hidden, const void* const* xs, const void* res,
                     const void* w, double eps, double* y);
 
+/* Decoder layer oracle (clusterfusion_llama2_7b_decoder.py:160-180, reference_fp32 with the FFN tail) in
+ * double: bf16 inputs and weights, no intermediate rounding. Caches [batch][cap][heads][head_dim] with
+ * seq_len valid tokens; the new k, v are the step's own (RoPE on q and k with cos/sin [head_dim]).
+ * Outputs [batch][hidden] (k_new / v_new [batch][heads*head_dim]; any output pointer but out may be NULL). */
+void orc_decoder_layer(int batch, int hidden, int heads, int head_dim, int ffn, long long seq_len, long long cap,
+                       const uint16_t* inp, const uint16_t* res, const uint16_t* w_rms, const uint16_t* wqkv,
+                       const uint16_t* wo, const uint16_t* w_post, const uint16_t* wgu, const uint16_t* wd,
+                       const uint16_t* kc, const uint16_t* vc, const float* cosv, const float* sinv, double eps,
+                       double* out, double* h_out, double* o_out, double* k_new, double* v_new);
+
 /* Sum of `ranks` arrays of bf16/f32 (TP all-reduce input), in double. */
 void orc_sum_ranks(int dtype, size_t ranks, size_t n, const void* const* xs, double* out);
 

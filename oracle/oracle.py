@@ -43,6 +43,8 @@ def lib():
         L.orc_rmsnorm.argtypes = [i, sz, sz, vp, vp, vp, d, vp, vp]
         L.orc_sum_ranks.argtypes = [i, sz, sz, ctypes.POINTER(vp), vp]
         L.orc_tp_rmsnorm.argtypes = [i, sz, sz, sz, ctypes.POINTER(vp), vp, vp, d, vp]
+        ll = ctypes.c_longlong
+        L.orc_decoder_layer.argtypes = [i, i, i, i, i, ll, ll] + [vp] * 10 + [vp, vp, d] + [vp] * 5
         L.orc_mt64_seed.argtypes = [vp, u64]
         L.orc_mt64_next.argtypes = [vp]
         L.orc_mt64_next.restype = u64
@@ -143,6 +145,20 @@ def tp_rmsnorm(dtype, xs, w, eps, res=None):
     lib().orc_tp_rmsnorm(dtype, len(xs), rows, hidden, arr, _p(np.ascontiguousarray(res)) if res is not None else None,
                          _p(np.ascontiguousarray(w)), eps, _p(y))
     return y
+
+
+def decoder_layer(inp, res, w_rms, wqkv, wo, w_post, wgu, wd, kc, vc, cos, sin, seq_len, eps, heads, head_dim=128):
+    """Decoder-layer oracle (double): bf16 bit arrays in; returns dict of out, h, o, k_new, v_new (float64
+    [batch, hidden]). kc / vc: [batch, cap, heads, head_dim] with seq_len valid tokens."""
+    batch, hidden = inp.shape
+    ffn = wd.shape[1]
+    cap = kc.shape[1]
+    arrs = [np.ascontiguousarray(a) for a in (inp, res, w_rms, wqkv, wo, w_post, wgu, wd, kc, vc)]
+    cs = [np.ascontiguousarray(a, dtype=np.float32) for a in (cos, sin)]
+    outs = {k: np.empty((batch, hidden), np.float64) for k in ("out", "h", "o", "k_new", "v_new")}
+    lib().orc_decoder_layer(batch, hidden, heads, head_dim, ffn, seq_len, cap, *[_p(a) for a in arrs],
+                            *[_p(c) for c in cs], eps, *[_p(outs[k]) for k in ("out", "h", "o", "k_new", "v_new")])
+    return outs
 
 
 def bf16_to_f32(u16):
