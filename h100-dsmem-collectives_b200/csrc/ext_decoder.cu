@@ -15,9 +15,10 @@
 //      within a 32-wide block is permuted identically on both operands); the N partial tiles meet by
 //      DSMEM loads (reduce-scatter by feature pairs (i, i+64)), whose owner applies RoPE and writes q
 //      (fp32) and the new k, v into the cache;
-//   3. decode attention: one cluster per (sequence, head), the cluster's CTAs split the keys, groups of
-//      4 lanes own one key at a time (32 dims a lane), online softmax in base 2, then the partial
-//      (max, sum, acc) of the 64 groups meet in shared memory and the N CTAs' in DSMEM;
+//   3. decode attention: one cluster per (sequence, head), the cluster's CTAs split the keys and stream
+//      them through a 4-stage shared-memory ring of 32-key K/V tiles (16-byte cp.async); groups of 8
+//      lanes take one key of a tile at a time (16 dims a lane), online softmax in base 2; then the
+//      partial (max, sum, acc) of the 32 groups meet in shared memory and the N CTAs' in DSMEM;
 //   4. O projection (as 2) with the epilogue h = x + o;
 //   5. cluster RMSNorm of h;
 //   6. gate/up projection (as 2; a tile holds gate rows j and up rows j of the same 64 j) with the
@@ -46,7 +47,7 @@ using bf16 = __nv_bfloat16;
 constexpr int kHeadDim = 128;
 constexpr int kTile = 128;           // output features per cluster tile
 constexpr int kProjThreads = 256;    // 8 warps x 16 feature rows
-constexpr int kAttnThreads = 256;    // 64 groups of 4 lanes
+constexpr int kAttnThreads = 256;    // 32 groups of 8 lanes
 constexpr uint32_t kArea = 128;      // barrier area / finish flag at the start of the dynamic window
 
 enum Epi : int { kEpiQKV = 0, kEpiO = 1, kEpiGateUp = 2, kEpiDown = 3 };
@@ -134,15 +135,38 @@ __global__ void __launch_bounds__(kProjThreads) proj_kernel(const ProjArgs a) {
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
     const uint2* fr = frag + lane;
-#pragma unroll 4
-    for (int kb = 0; kb < nkb; ++kb) {
-        const uint4 A0 = ld_stream(w0 + 4 * kb), A1 = ld_stream(w1 + 4 * kb);
+    // weights for kU k-blocks at a time, the next batch's loads issued before this batch's MMAs, so a lane
+    // keeps 2 * kU (up to 4 * kU) 16-byte loads in flight
+    constexpr int kU = 4;
+    uint4 cur0[kU], cur1[kU], nxt0[kU], nxt1[kU];
+    auto fetch = [&](uint4* d0, uint4* d1, int kb0) {
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-            const uint2 b0 = fr[((kb * 2 + 0) * NT + j) * 32];
-            const uint2 b1 = fr[((kb * 2 + 1) * NT + j) * 32];
-            mma_bf16(acc[j], A0.x, A1.x, A0.y, A1.y, b0.x, b0.y);
-            mma_bf16(acc[j], A0.z, A1.z, A0.w, A1.w, b1.x, b1.y);
+        for (int u = 0; u < kU; ++u)
+            if (kb0 + u < nkb) {
+                d0[u] = ld_stream(w0 + 4 * (kb0 + u));
+                d1[u] = ld_stream(w1 + 4 * (kb0 + u));
+            }
+    };
+    fetch(cur0, cur1, 0);
+    for (int kb0 = 0; kb0 < nkb; kb0 += kU) {
+        if (kb0 + kU < nkb) fetch(nxt0, nxt1, kb0 + kU);
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int kb = kb0 + u;
+            if (kb < nkb) {
+#pragma unroll
+                for (int j = 0; j < NT; ++j) {
+                    const uint2 b0 = fr[((kb * 2 + 0) * NT + j) * 32];
+                    const uint2 b1 = fr[((kb * 2 + 1) * NT + j) * 32];
+                    mma_bf16(acc[j], cur0[u].x, cur1[u].x, cur0[u].y, cur1[u].y, b0.x, b0.y);
+                    mma_bf16(acc[j], cur0[u].z, cur1[u].z, cur0[u].w, cur1[u].w, b1.x, b1.y);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            cur0[u] = nxt0[u];
+            cur1[u] = nxt1[u];
         }
     }
 #pragma unroll
@@ -221,89 +245,141 @@ struct AttnArgs {
     unsigned* err;
 };
 
-// One cluster = one (sequence, head); CTA r of N takes keys [r*L/N, (r+1)*L/N).
+constexpr int kKeyTile = 32;                       // keys per shared-memory tile
+constexpr int kAttnStages = 4;                     // tiles in flight
+constexpr uint32_t kTileBytes = kKeyTile * kHeadDim * 2u;   // one K (or V) tile, 8 KiB
+constexpr int kAttnGroups = kAttnThreads / 8;      // 32 groups of 8 lanes, one key each per step
+// shared memory: [kArea) flag | stages x (K tile, V tile) | group partials (m, l, acc[128]) | CTA partial
+constexpr uint32_t kAttnStageOff = kArea;
+constexpr uint32_t kAttnGroupOff = kAttnStageOff + kAttnStages * 2u * kTileBytes;
+constexpr uint32_t kAttnCtaOff = kAttnGroupOff + (uint32_t)kAttnGroups * (2 + kHeadDim) * 4u;
+constexpr uint32_t kAttnSmem = kAttnCtaOff + (2 + kHeadDim) * 4u;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int K>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(K) : "memory");
+}
+
+// One cluster = one (sequence, head); CTA r of N takes keys [r*L/N, (r+1)*L/N). The CTA streams its keys
+// through kAttnStages shared-memory tiles of 32 keys (16-byte cp.async, so the loads of several tiles are
+// in flight while one is consumed); 32 groups of 8 lanes each take one key of a tile per step, a lane owning
+// 16 of the 128 dimensions; online softmax in base 2. Then the 32 groups' (max, sum, acc) meet in shared
+// memory and the N CTAs' in DSMEM.
 template <int N>
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
     dsb::Ctx c;
     dsb::ctx_init(c, a.smem_bytes, a.err, 1000000000ull);
     dsb::flag_init(c);
     const int cid = (int)cluster_id(), b = cid / a.H, head = cid % a.H;
-    const int lane = threadIdx.x & 31, j = lane & 3, grp = threadIdx.x >> 2;
-    constexpr int kGroups = kAttnThreads / 4;
+    const int lane = threadIdx.x & 31, sub = lane & 7, grp = threadIdx.x >> 3;
+    const unsigned gmask = 0xFFu << (lane & 24);   // the 8 lanes of this group
     const long long lo = (long long)c.rank * a.L / N, hi = (long long)(c.rank + 1) * a.L / N;
-    float qv[32];
-    {
-        const float* qp = a.q + ((size_t)b * a.H + head) * kHeadDim + 32 * j;
+    const int tiles = (int)((hi - lo + kKeyTile - 1) / kKeyTile);
+    const size_t tok_stride = (size_t)a.H * kHeadDim;   // elements between consecutive keys
+    const bf16* kbase = a.kc + (size_t)b * a.cap * tok_stride + (size_t)head * kHeadDim;
+    const bf16* vbase = a.vc + (size_t)b * a.cap * tok_stride + (size_t)head * kHeadDim;
+    // tile t: 32 keys x 256 B for K and for V = 1024 16-byte chunks, 4 per thread
+    auto issue = [&](int t) {
+        const int st = t % kAttnStages;
+        const uint32_t kdst = c.sa + kAttnStageOff + (uint32_t)st * 2u * kTileBytes;
 #pragma unroll
-        for (int d = 0; d < 32; ++d) qv[d] = qp[d] * a.scale_log2;
+        for (int u = 0; u < 2; ++u) {
+            const int chunk = threadIdx.x + u * kAttnThreads;   // 0..511: key = chunk / 16, piece = chunk % 16
+            const int key = chunk >> 4, piece = chunk & 15;
+            const long long s = lo + (long long)t * kKeyTile + key;
+            if (s < hi) {
+                const size_t off = (size_t)s * tok_stride + (size_t)piece * 8;
+                cp_async16(kdst + (uint32_t)chunk * 16u, kbase + off);
+                cp_async16(kdst + kTileBytes + (uint32_t)chunk * 16u, vbase + off);
+            }
+        }
+    };
+#pragma unroll
+    for (int t = 0; t < kAttnStages - 1; ++t) {
+        if (t < tiles) issue(t);
+        cp_async_commit();
     }
-    float m = -INFINITY, l = 0.f, acc[32];
+    f2x q2[8];   // this lane's 16 query dimensions, pre-scaled for exp2
+    {
+        const float* qp = a.q + ((size_t)b * a.H + head) * kHeadDim + 16 * sub;
 #pragma unroll
-    for (int d = 0; d < 32; ++d) acc[d] = 0.f;
-    const size_t tok_stride = (size_t)a.H * kHeadDim;
-    const bf16* kbase = a.kc + ((size_t)b * a.cap) * tok_stride + (size_t)head * kHeadDim + 32 * j;
-    const bf16* vbase = a.vc + ((size_t)b * a.cap) * tok_stride + (size_t)head * kHeadDim + 32 * j;
-    for (long long s = lo + grp; s < hi; s += kGroups) {
-        const uint4* kp = reinterpret_cast<const uint4*>(kbase + (size_t)s * tok_stride);
-        const uint4* vp = reinterpret_cast<const uint4*>(vbase + (size_t)s * tok_stride);
-        uint4 kv[4], vv[4];
+        for (int e = 0; e < 8; ++e) q2[e] = f2_make(qp[2 * e] * a.scale_log2, qp[2 * e + 1] * a.scale_log2);
+    }
+    float m = -INFINITY, l = 0.f;
+    f2x acc[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) kv[u] = ld_stream(kp + u);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) vv[u] = ld_stream(vp + u);
+    for (int e = 0; e < 8; ++e) acc[e] = 0ull;
+    for (int t = 0; t < tiles; ++t) {
+        if (t + kAttnStages - 1 < tiles) issue(t + kAttnStages - 1);
+        cp_async_commit();
+        cp_async_wait<kAttnStages - 1>();   // tile t landed (this thread's copies)
+        __syncthreads();                      // ... and every thread's
+        const unsigned char* kt = c.ptr<const unsigned char>(kAttnStageOff + (uint32_t)(t % kAttnStages) * 2u * kTileBytes);
+        const unsigned char* vt = kt + kTileBytes;
+        const long long s = lo + (long long)t * kKeyTile + grp;   // this group's key in the tile
+        const bool valid = s < hi;
+        const uint4* kr = reinterpret_cast<const uint4*>(kt + grp * 256 + sub * 32);
+        const uint4* vr = reinterpret_cast<const uint4*>(vt + grp * 256 + sub * 32);
         f2x dot2 = 0ull;
+        if (valid) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            f2x kf[4];
-            RmsElem<bf16>::unpack(kv[u], kf);
+            for (int u = 0; u < 2; ++u) {
+                f2x kf[4];
+                RmsElem<bf16>::unpack(kr[u], kf);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) dot2 = f2_fma(kf[e], f2_make(qv[8 * u + 2 * e], qv[8 * u + 2 * e + 1]), dot2);
+                for (int e = 0; e < 4; ++e) dot2 = f2_fma(kf[e], q2[4 * u + e], dot2);
+            }
         }
         const float2 d2 = f2_split(dot2);
         float logit = d2.x + d2.y;
-        // the 4 lanes of this group take the same keys; other groups of the warp may have left the loop,
-        // so the shuffles name this group's lanes only
-        const unsigned gmask = 0xFu << (lane & 28);
         logit += __shfl_xor_sync(gmask, logit, 1);
         logit += __shfl_xor_sync(gmask, logit, 2);
-        const float mn = fmaxf(m, logit);
-        const float corr = exp2f(m - mn), p = exp2f(logit - mn);
-        l = l * corr + p;
-        m = mn;
+        logit += __shfl_xor_sync(gmask, logit, 4);
+        if (valid) {
+            const float mn = fmaxf(m, logit);
+            const float corr = exp2f(m - mn), p = exp2f(logit - mn);
+            l = l * corr + p;
+            m = mn;
+            const f2x c2 = f2_make(corr, corr), p2 = f2_make(p, p);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            f2x vf[4];
-            RmsElem<bf16>::unpack(vv[u], vf);
+            for (int u = 0; u < 2; ++u) {
+                f2x vf[4];
+                RmsElem<bf16>::unpack(vr[u], vf);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 v2 = f2_split(vf[e]);
-                acc[8 * u + 2 * e] = fmaf(acc[8 * u + 2 * e], corr, p * v2.x);
-                acc[8 * u + 2 * e + 1] = fmaf(acc[8 * u + 2 * e + 1], corr, p * v2.y);
+                for (int e = 0; e < 4; ++e) acc[4 * u + e] = f2_fma(acc[4 * u + e], c2, f2_mul(p2, vf[e]));
             }
         }
+        __syncthreads();   // the stage is free for the tile issued next iteration
     }
-    // the 64 groups of this CTA: (max, sum, acc) in shared memory, combined per dimension
-    float* gm = c.ptr<float>(kArea);                       // [64]
-    float* gl = gm + kGroups;                              // [64]
-    float* gacc = gl + kGroups;                            // [64][128]
-    float* cta = gacc + kGroups * kHeadDim;                // [2 + 128]: M, L, A[128] of this CTA
-    if (j == 0) {
-        gm[grp] = m;
-        gl[grp] = l;
+    cp_async_wait<0>();
+    // the 32 groups of this CTA: (max, sum, acc) in shared memory, combined per dimension
+    float* gst = c.ptr<float>(kAttnGroupOff);   // per group: m, l, acc[128]
+    float* cta = c.ptr<float>(kAttnCtaOff);     // M, L, A[128] of this CTA
+    if (sub == 0) {
+        gst[grp * (2 + kHeadDim)] = m;
+        gst[grp * (2 + kHeadDim) + 1] = l;
     }
 #pragma unroll
-    for (int d = 0; d < 32; ++d) gacc[grp * kHeadDim + 32 * j + d] = acc[d];
+    for (int e = 0; e < 8; ++e) {
+        const float2 v = f2_split(acc[e]);
+        gst[grp * (2 + kHeadDim) + 2 + 16 * sub + 2 * e] = v.x;
+        gst[grp * (2 + kHeadDim) + 2 + 16 * sub + 2 * e + 1] = v.y;
+    }
     __syncthreads();
     if (threadIdx.x < kHeadDim) {
         const int d = threadIdx.x;
         float M = -INFINITY;
-        for (int g2 = 0; g2 < kGroups; ++g2) M = fmaxf(M, gm[g2]);
+        for (int g2 = 0; g2 < kAttnGroups; ++g2) M = fmaxf(M, gst[g2 * (2 + kHeadDim)]);
         float Ls = 0.f, A = 0.f;
         if (M != -INFINITY)
-            for (int g2 = 0; g2 < kGroups; ++g2) {
-                const float f = exp2f(gm[g2] - M);   // 0 for a group without keys (-inf)
-                Ls += gl[g2] * f;
-                A += gacc[g2 * kHeadDim + d] * f;
+            for (int g2 = 0; g2 < kAttnGroups; ++g2) {
+                const float f = exp2f(gst[g2 * (2 + kHeadDim)] - M);   // 0 for a group without keys (-inf)
+                Ls += gst[g2 * (2 + kHeadDim) + 1] * f;
+                A += gst[g2 * (2 + kHeadDim) + 2 + d] * f;
             }
         cta[2 + d] = A;
         if (d == 0) {
@@ -312,7 +388,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
         }
     }
     cluster_sync();   // every CTA's (M, L, A) visible
-    const uint32_t cta_sa = c.sa + kArea + (uint32_t)(2 * kGroups + kGroups * kHeadDim) * 4u;
+    const uint32_t cta_sa = c.sa + kAttnCtaOff;
     const int dpr = kHeadDim / N;   // dims finished by this CTA
     if (threadIdx.x < dpr) {
         const int d = (int)c.rank * dpr + threadIdx.x;
@@ -464,7 +540,7 @@ dsmem_status dsmem_decoder_layer_launch(const dsmem_decoder_params* p, dsmem_str
         t.L = p->seq_len + 1;
         t.H = H;
         t.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)kHeadDim));
-        t.smem_bytes = kArea + (uint32_t)(2 * 64 + 64 * kHeadDim + 2 + kHeadDim) * 4u;
+        t.smem_bytes = kAttnSmem;
         t.err = err;
         const void* fn = n == 4 ? reinterpret_cast<const void*>(&attn_kernel<4>)
                                 : reinterpret_cast<const void*>(&attn_kernel<8>);

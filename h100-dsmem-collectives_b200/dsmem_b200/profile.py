@@ -5,6 +5,7 @@ kernel, and exits; sized so a full-section capture of one to three launches ends
 (inputs above the 126 MB L2, a few hundred MB on the device at most).
   allreduce   batch AllReduce through the C ABI (--alg, --cluster, --payload, --problems, --dtype)
   rmsnorm     cluster-fused RMSNorm (--rows, --hidden, --cluster)
+  decoder     one Llama-2-7B decoder-layer step (--batch, --cluster; 4096 cached tokens): its seven launches
 """
 import argparse
 import pathlib
@@ -19,7 +20,8 @@ import dsmem_b200 as D  # noqa: E402
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=["allreduce", "rmsnorm"], default="allreduce")
+    ap.add_argument("--case", choices=["allreduce", "rmsnorm", "decoder"], default="allreduce")
+    ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--alg", default="two_shot_push")
     ap.add_argument("--cluster", type=int, default=8)
     ap.add_argument("--payload", type=int, default=65536)
@@ -48,6 +50,17 @@ def main(argv=None):
         for _ in range(args.warmup + args.launches):
             D.collective(D.Op.ALLREDUCE, alg, tin, tout, n, p)
         D.check()
+    elif args.case == "decoder":
+        hid, heads, ffn, S, B = 4096, 32, 11008, 4096, args.batch
+        nrm = lambda *s, std=0.02, mean=0.0: (mean + std * torch.randn(*s, device="cuda")).to(torch.bfloat16)  # noqa: E731
+        w = [nrm(hid, mean=1.0), nrm(3 * hid, hid), nrm(hid, hid), nrm(hid, mean=1.0), nrm(2 * ffn, hid), nrm(hid, ffn)]
+        kc, vc = nrm(B, S + 1, heads, 128, std=1.0), nrm(B, S + 1, heads, 128, std=1.0)
+        inp, res = nrm(B, hid, std=1.0), nrm(B, hid, std=1.0)
+        cos, sin = torch.ones(128, device="cuda"), torch.zeros(128, device="cuda")
+        for _ in range(args.warmup + args.launches):
+            D.decoder_layer(inp, res, *w, kc, vc, cos, sin, S, eps=1e-5, cluster_size=args.cluster)
+        torch.cuda.synchronize()
+        D.decoder_check()
     else:
         x = torch.randn(args.rows, args.hidden, device="cuda").to(torch.bfloat16)
         w = (1 + 0.02 * torch.randn(args.hidden, device="cuda")).to(torch.bfloat16)
