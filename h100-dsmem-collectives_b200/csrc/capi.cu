@@ -1,5 +1,6 @@
 // capi.cu -- implementation of include/dsmem_b200.h: registry lookup, legality, persistent launch.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 
 #include <algorithm>
 #include <cstdio>
@@ -105,9 +106,12 @@ struct DeviceState {
     int optin = 0;
 };
 
+// AUTO table key. regime 0 = one cluster per launch (picked by latency), 1 = batches (by throughput).
 struct TuneKey {
-    int op, n, dtype;
-    bool operator<(const TuneKey& o) const { return std::tie(op, n, dtype) < std::tie(o.op, o.n, o.dtype); }
+    int op, n, dtype, regime;
+    bool operator<(const TuneKey& o) const {
+        return std::tie(op, n, dtype, regime) < std::tie(o.op, o.n, o.dtype, o.regime);
+    }
 };
 
 struct State {
@@ -115,7 +119,8 @@ struct State {
     Registry reg;
     std::mutex mu;
     std::map<int, DeviceState> dev;
-    std::map<TuneKey, std::map<uint64_t, int>> tune;   // (op, N, dtype) -> {bytes -> alg}
+    std::map<TuneKey, std::map<uint64_t, int>> tune;   // (op, N, dtype, regime) -> {bytes -> alg}
+    std::once_flag default_table_once;                  // the measured table shipped beside the library
     unsigned long long wait_limit_ns = 1000000000ull;
     bool pipelined = true;        // batches use a pipelined driver where one exists
     uint64_t unit_bytes = 16384;  // pipelined drivers: largest sub-vector per CTA
@@ -175,13 +180,74 @@ dsmem_status classify(const KernelEntry* e, uint32_t m, uint64_t* smem) {
     return DSMEM_OK;
 }
 
-int resolve_auto(int op, int dtype, int n, size_t bytes) {
+// One line per entry: "op cluster_size bytes_per_cta dtype alg [single|batch]" ('#' comments).
+dsmem_status parse_table(const char* path, std::map<TuneKey, std::map<uint64_t, int>>& table) {
+    std::ifstream f(path);
+    if (!f) return DSMEM_ERR_INVALID_ARGUMENT;
+    std::string line;
+    while (std::getline(f, line)) {
+        if (line.empty() || line[0] == '#') continue;
+        std::istringstream is(line);
+        std::string ops, dts, algs, regs;
+        int n = 0;
+        unsigned long long bytes = 0;
+        if (!(is >> ops >> n >> bytes >> dts >> algs)) return DSMEM_ERR_INVALID_ARGUMENT;
+        int regime = 0;
+        if (is >> regs) {
+            if (regs == "batch") regime = 1;
+            else if (regs != "single") return DSMEM_ERR_INVALID_ARGUMENT;
+        }
+        int op = -1, dt = -1, alg = -1;
+        for (int i = 0; i < 4; ++i)
+            if (ops == kOpNames[i]) op = i;
+        for (int i = 0; i < 3; ++i)
+            if (dts == kDtypeNames[i]) dt = i;
+        for (int i = 1; i < DSMEM_ALG_COUNT; ++i)
+            if (algs == kAlgNames[i]) alg = i;
+        if (op < 0 || dt < 0 || alg < 0 || !valid_enums(op, alg, dt, n)) return DSMEM_ERR_INVALID_ARGUMENT;
+        if (find(op, alg, dt, n) == nullptr) return DSMEM_ERR_INVALID_ARGUMENT;
+        table[TuneKey{op, n, dt, regime}][bytes] = alg;
+    }
+    return DSMEM_OK;
+}
+
+// The measured table shipped with the library (<package>/autotune_b200.tsv, found next to lib/), loaded
+// once on the first AUTO resolution; the environment variable DSMEM_AUTOTUNE_TABLE names another file
+// (empty: none). A missing or malformed file leaves the built-in order.
+void load_default_table() {
+    std::call_once(st().default_table_once, [] {
+        std::string path;
+        if (const char* env = std::getenv("DSMEM_AUTOTUNE_TABLE")) {
+            path = env;
+        } else {
+            Dl_info info{};
+            if (dladdr(reinterpret_cast<void*>(&dsmem_version), &info) == 0 || info.dli_fname == nullptr) return;
+            std::string lib = info.dli_fname;
+            const size_t a = lib.rfind('/');
+            if (a == std::string::npos) return;
+            const std::string libdir = lib.substr(0, a);
+            const size_t b = libdir.rfind('/');
+            path = (b == std::string::npos ? std::string(".") : libdir.substr(0, b)) + "/autotune_b200.tsv";
+        }
+        if (path.empty()) return;
+        std::map<TuneKey, std::map<uint64_t, int>> table;
+        if (parse_table(path.c_str(), table) != DSMEM_OK) return;
+        std::lock_guard<std::mutex> lock(st().mu);
+        st().tune.swap(table);
+    });
+}
+
+int resolve_auto(int op, int dtype, int n, size_t bytes, int regime = 0) {
+    load_default_table();
     State& s = st();
     const uint32_t m = msg_elems(op, dtype, n, bytes);
     {
         std::lock_guard<std::mutex> g(s.mu);
-        auto it = s.tune.find(TuneKey{op, n, dtype});
-        if (it != s.tune.end() && !it->second.empty()) {
+        // the measured table of this regime, then of the other one: the entry of the largest measured
+        // payload <= bytes whose algorithm is legal here
+        for (int r : {regime, 1 - regime}) {
+            auto it = s.tune.find(TuneKey{op, n, dtype, r});
+            if (it == s.tune.end() || it->second.empty()) continue;
             auto jt = it->second.upper_bound((uint64_t)bytes);
             if (jt != it->second.begin()) {
                 --jt;
@@ -282,9 +348,9 @@ uint32_t pipeline_units(const KernelEntry* e, uint32_t m) {
 }
 
 dsmem_status prepare(int op, int alg, int dtype, int n, size_t bytes, const KernelEntry** entry, uint32_t* m_out,
-                     uint64_t* smem_out) {
+                     uint64_t* smem_out, int regime = 0) {
     if (!valid_enums(op, alg, dtype, n)) return DSMEM_ERR_INVALID_ARGUMENT;
-    if (alg == DSMEM_ALG_AUTO) alg = resolve_auto(op, dtype, n, bytes);
+    if (alg == DSMEM_ALG_AUTO) alg = resolve_auto(op, dtype, n, bytes, regime);
     if (alg == DSMEM_ALG_AUTO) return DSMEM_ERR_ILLEGAL_CONFIG;
     const KernelEntry* e = find(op, alg, dtype, n);
     const uint32_t m = msg_elems(op, dtype, n, bytes);
@@ -340,7 +406,7 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
     const KernelEntry* e = nullptr;
     uint32_t m = 0;
     uint64_t smem = 0;
-    dsmem_status s = prepare(op, alg, dtype, cluster_size, bytes_per_cta, &e, &m, &smem);
+    dsmem_status s = prepare(op, alg, dtype, cluster_size, bytes_per_cta, &e, &m, &smem, num_clusters > 1 ? 1 : 0);
     if (s != DSMEM_OK) return s;
     if (num_clusters < 0 || in == nullptr || out == nullptr) return DSMEM_ERR_INVALID_ARGUMENT;
     if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15u) return DSMEM_ERR_INVALID_ARGUMENT;
@@ -431,28 +497,10 @@ dsmem_status dsmem_max_active_clusters(dsmem_op op, dsmem_alg alg, dsmem_dtype d
 
 dsmem_status dsmem_autotune_table_load(const char* path) {
     if (path == nullptr) return DSMEM_ERR_INVALID_ARGUMENT;
-    std::ifstream f(path);
-    if (!f) return DSMEM_ERR_INVALID_ARGUMENT;
+    std::call_once(st().default_table_once, [] {});   // an explicit table replaces the default one for good
     std::map<TuneKey, std::map<uint64_t, int>> table;
-    std::string line;
-    while (std::getline(f, line)) {
-        if (line.empty() || line[0] == '#') continue;
-        std::istringstream is(line);
-        std::string ops, dts, algs;
-        int n = 0;
-        unsigned long long bytes = 0;
-        if (!(is >> ops >> n >> bytes >> dts >> algs)) return DSMEM_ERR_INVALID_ARGUMENT;
-        int op = -1, dt = -1, alg = -1;
-        for (int i = 0; i < 4; ++i)
-            if (ops == kOpNames[i]) op = i;
-        for (int i = 0; i < 3; ++i)
-            if (dts == kDtypeNames[i]) dt = i;
-        for (int i = 1; i < DSMEM_ALG_COUNT; ++i)
-            if (algs == kAlgNames[i]) alg = i;
-        if (op < 0 || dt < 0 || alg < 0 || !valid_enums(op, alg, dt, n)) return DSMEM_ERR_INVALID_ARGUMENT;
-        if (find(op, alg, dt, n) == nullptr) return DSMEM_ERR_INVALID_ARGUMENT;
-        table[TuneKey{op, n, dt}][bytes] = alg;
-    }
+    const dsmem_status s = parse_table(path, table);
+    if (s != DSMEM_OK) return s;
     std::lock_guard<std::mutex> lock(st().mu);
     st().tune.swap(table);
     return DSMEM_OK;
@@ -461,6 +509,12 @@ dsmem_status dsmem_autotune_table_load(const char* path) {
 dsmem_alg dsmem_autotune_pick(dsmem_op op, dsmem_dtype dtype, int cluster_size, size_t bytes_per_cta) {
     if (!valid_enums(op, 0, dtype, cluster_size)) return DSMEM_ALG_AUTO;
     return (dsmem_alg)resolve_auto(op, dtype, cluster_size, bytes_per_cta);
+}
+
+dsmem_alg dsmem_autotune_pick_ex(dsmem_op op, dsmem_dtype dtype, int cluster_size, size_t bytes_per_cta,
+                                 long long num_clusters) {
+    if (!valid_enums(op, 0, dtype, cluster_size)) return DSMEM_ALG_AUTO;
+    return (dsmem_alg)resolve_auto(op, dtype, cluster_size, bytes_per_cta, num_clusters > 1 ? 1 : 0);
 }
 
 dsmem_status dsmem_last_error_detail(int device, unsigned* error_bits, unsigned* detail, unsigned* cluster) {

@@ -155,6 +155,7 @@ def lib():
         "dsmem_max_active_clusters": (c_int, [c_int, c_int, c_int, c_int, c_size, ctypes.POINTER(c_int)]),
         "dsmem_autotune_table_load": (c_int, [ctypes.c_char_p]),
         "dsmem_autotune_pick": (c_int, [c_int, c_int, c_int, c_size]),
+        "dsmem_autotune_pick_ex": (c_int, [c_int, c_int, c_int, c_size, c_ll]),
         "dsmem_last_error": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
         "dsmem_last_error_detail": (c_int, [c_int] + [ctypes.POINTER(ctypes.c_uint)] * 3),
         "dsmem_check": (c_int, [c_vp]),
@@ -310,8 +311,10 @@ def autotune_load(path):
     _ok(lib().dsmem_autotune_table_load(str(path).encode()), f"dsmem_autotune_table_load({path})")
 
 
-def autotune_pick(op, dtype, cluster_size, bytes_per_cta):
-    return Alg(lib().dsmem_autotune_pick(int(op), int(dtype), int(cluster_size), int(bytes_per_cta)))
+def autotune_pick(op, dtype, cluster_size, bytes_per_cta, num_clusters=1):
+    """The algorithm AUTO runs for a launch of num_clusters problems (measured table, then built-in order)."""
+    return Alg(lib().dsmem_autotune_pick_ex(int(op), int(dtype), int(cluster_size), int(bytes_per_cta),
+                                            int(num_clusters)))
 
 
 def file_stem(op, alg):

@@ -1,0 +1,132 @@
+"""Catalogue sweep on one B200 and the measured AUTO table.
+
+    python -m dsmem_b200.sweep [--out-table autotune_b200.tsv] [--out-json sweep.json] [--dtype f32]
+
+For every op x algorithm x cluster size N in {2, 4, 8, 16} x bytes per CTA P in {256 B .. 128 KiB, 192 KiB}
+(the reference sweep's grid, driver.py:156-163) that is legal, two figures:
+  single   one cluster per launch, as the reference harness runs it (collectives/harness/main.cu): the
+           in-kernel span max(stamp[1]) - min(stamp[0]) over the N CTAs (%globaltimer), median of
+           `--reps` launches; algbw = P / span, busbw = algbw * the op's bus factor (perf_report.py:99-100:
+           AllReduce 2(N-1)/N, the others (N-1)/N);
+  batch    a grid-filled batch of independent problems (enough for four full waves of resident clusters and
+           at least 64 MiB of input), CUDA events over `--batch-reps` launches; algbw = problems * P / time.
+The AUTO table (one line per (op, N, P, dtype, regime) with the fastest algorithm) is the input of
+dsmem_autotune_table_load; regime `single` picks by span, `batch` by batch throughput.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+
+from . import (CATALOGUE, CLUSTER_SIZES, EXTENSIONS, STAMPS_PER_RANK, Alg, Dtype, DsmemError, Op, Status, check,
+               collective, in_elems_per_rank, max_active_clusters, msg_elems, out_elems_per_rank, query)
+
+PAYLOADS = [256 << k for k in range(10)] + [196608]
+BUS = {Op.ALLREDUCE: lambda n: 2 * (n - 1) / n, Op.ALLGATHER: lambda n: (n - 1) / n,
+       Op.REDUCESCATTER: lambda n: (n - 1) / n, Op.ALLTOALL: lambda n: (n - 1) / n}
+OP_NAMES = {Op.ALLREDUCE: "allreduce", Op.ALLGATHER: "allgather", Op.REDUCESCATTER: "reducescatter",
+            Op.ALLTOALL: "alltoall"}
+DT_NAMES = {Dtype.F32: "f32", Dtype.BF16: "bf16", Dtype.I32: "i32"}
+ALG_NAMES = {a: a.name.lower() for a in Alg}
+
+
+def measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps):
+    m = msg_elems(op, n, p, dt)
+    per_in = n * in_elems_per_rank(op, n, m)
+    per_out = n * out_elems_per_rank(op, n, m)
+    tdt = {Dtype.F32: torch.float32, Dtype.BF16: torch.bfloat16, Dtype.I32: torch.int32}[dt]
+    esz = {Dtype.F32: 4, Dtype.BF16: 2, Dtype.I32: 4}[dt]
+    inp = buf_in[: per_in * esz].view(tdt)
+    out = buf_out[: per_out * esz].view(tdt)
+    # single: `reps` launches, each with its own stamp slice, read back once
+    st = stamps[: reps * n * STAMPS_PER_RANK].view(reps, n * STAMPS_PER_RANK)
+    for r in range(reps):
+        collective(op, alg, inp, out, n, p, num_clusters=1, stamps=st[r])
+    check()
+    s = st.view(reps, n, STAMPS_PER_RANK).cpu()
+    spans = (s[:, :, 1].max(dim=1).values - s[:, :, 0].min(dim=1).values).tolist()
+    span_ns = statistics.median(spans[min(5, reps // 4):])
+    # batch: four waves of resident clusters, at least 64 MiB of input, within the buffers
+    res = max_active_clusters(op, alg, dt, n, p)
+    problems = max(4 * res, (64 << 20) // (per_in * esz))
+    problems = min(problems, buf_in.numel() // (per_in * esz), buf_out.numel() // (per_out * esz))
+    inp = buf_in[: problems * per_in * esz].view(tdt)
+    out = buf_out[: problems * per_out * esz].view(tdt)
+    for _ in range(2):
+        collective(op, alg, inp, out, n, p, num_clusters=problems)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(batch_reps):
+        collective(op, alg, inp, out, n, p, num_clusters=problems)
+    e1.record()
+    torch.cuda.synchronize()
+    check()
+    ms = e0.elapsed_time(e1) / batch_reps
+    algbw_single = p / span_ns
+    return {"span_ns": round(span_ns, 1), "algbw_GBps": round(algbw_single, 3),
+            "busbw_GBps": round(algbw_single * BUS[op](n), 3), "batch_problems": problems,
+            "batch_ms": round(ms, 4), "batch_algbw_GBps": round(problems * p / (ms * 1e-3) / 1e9, 1)}
+
+
+def run(dtypes=(Dtype.F32,), reps=60, batch_reps=5, sizes=CLUSTER_SIZES, payloads=PAYLOADS):
+    import torch
+
+    torch.cuda.set_device(0)
+    buf_in = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    buf_out = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    buf_in.random_(0, 64)   # small positive bytes: finite floats, no overflow in int sums
+    stamps = torch.zeros(reps * 16 * STAMPS_PER_RANK, dtype=torch.int64, device="cuda")
+    algs = list(CATALOGUE) + list(EXTENSIONS)
+    results = []
+    for dt in dtypes:
+        for (op, alg) in algs:
+            for n in sizes:
+                for p in payloads:
+                    if query(op, alg, dt, n, p)[0] != Status.OK:
+                        continue
+                    try:
+                        r = measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps)
+                    except DsmemError as e:
+                        r = {"error": str(e)}
+                    r.update({"op": OP_NAMES[op], "alg": ALG_NAMES[alg], "n": n, "bytes": p, "dtype": DT_NAMES[dt]})
+                    results.append(r)
+    return results
+
+
+def table(results):
+    """Fastest algorithm per (op, N, P, dtype, regime)."""
+    best = {}
+    for r in results:
+        if "error" in r:
+            continue
+        for regime, key, better in (("single", "span_ns", lambda a, b: a < b),
+                                    ("batch", "batch_algbw_GBps", lambda a, b: a > b)):
+            k = (r["op"], r["n"], r["bytes"], r["dtype"], regime)
+            if k not in best or better(r[key], best[k][key]):
+                best[k] = r
+    lines = ["# op cluster_size bytes_per_cta dtype alg regime  (measured on B200 by dsmem_b200.sweep)"]
+    for (op, n, p, dt, regime), r in sorted(best.items()):
+        lines.append(f"{op} {n} {p} {dt} {r['alg']} {regime}")
+    return "\n".join(lines) + "\n"
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out-table", default="autotune_b200.tsv")
+    ap.add_argument("--out-json", default="sweep_b200.json")
+    ap.add_argument("--dtype", default="f32", choices=["f32", "bf16", "i32", "all"])
+    ap.add_argument("--reps", type=int, default=60)
+    args = ap.parse_args(argv)
+    dts = {"f32": (Dtype.F32,), "bf16": (Dtype.BF16,), "i32": (Dtype.I32,),
+           "all": (Dtype.F32, Dtype.BF16, Dtype.I32)}[args.dtype]
+    res = run(dts, reps=args.reps)
+    with open(args.out_json, "w") as f:
+        json.dump(res, f)
+    with open(args.out_table, "w") as f:
+        f.write(table(res))
+    print(f"{len(res)} configurations; table -> {args.out_table}; results -> {args.out_json}", flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -138,6 +138,14 @@ dsmem_status dsmem_max_active_clusters(dsmem_op op, dsmem_alg alg, dsmem_dtype d
 dsmem_status dsmem_autotune_table_load(const char* path);
 /* The algorithm AUTO resolves to (after legality) for this configuration. */
 dsmem_alg dsmem_autotune_pick(dsmem_op op, dsmem_dtype dtype, int cluster_size, size_t bytes_per_cta);
+/* The algorithm AUTO runs for a launch of num_clusters problems: the table's `batch` regime (throughput)
+ * when num_clusters > 1, its `single` regime (latency, the reference harness's one cluster per launch)
+ * otherwise, each falling back to the other and then to the built-in order. Table lines are
+ * "op cluster_size bytes_per_cta dtype alg [single|batch]" (default single); the table measured on B200
+ * (h100-dsmem-collectives_b200/autotune_b200.tsv, next to lib/) is loaded on first use unless
+ * DSMEM_AUTOTUNE_TABLE names another file (empty: none) or dsmem_autotune_table_load ran first. */
+dsmem_alg dsmem_autotune_pick_ex(dsmem_op op, dsmem_dtype dtype, int cluster_size, size_t bytes_per_cta,
+                                 long long num_clusters);
 
 /* Read and clear the device error word of `device` (synchronises that device). */
 dsmem_status dsmem_last_error(int device, unsigned* error_bits);

@@ -132,6 +132,9 @@ def test_legality_and_smem_match_reference_matrix(dsmem):
 
 def test_auto_defaults_and_table(dsmem, tmp_path):
     Op, Alg, Dt = dsmem.Op, dsmem.Alg, dsmem.Dtype
+    empty = tmp_path / "empty.txt"
+    empty.write_text("")
+    dsmem.autotune_load(empty)   # the built-in order alone (no measured table)
     assert dsmem.autotune_pick(Op.ALLREDUCE, Dt.F32, 8, 16384) == Alg.TWO_SHOT_PUSH
     # two-shot needs N | M with 16-B chunks; 64 B at N = 8 is not legal for it
     pick = dsmem.autotune_pick(Op.ALLREDUCE, Dt.F32, 8, 64)
@@ -149,9 +152,19 @@ def test_auto_defaults_and_table(dsmem, tmp_path):
         assert dsmem.autotune_pick(Op.ALLREDUCE, Dt.F32, 8, 128) != Alg.AUTO
         # an entry whose algorithm is illegal at that size falls back to the defaults
         assert dsmem.autotune_pick(Op.ALLREDUCE, Dt.BF16, 8, 4096) == Alg.TWO_SHOT_PUSH
+        # regimes: a `batch` line serves batches; one cluster per launch keeps the `single` line
+        table.write_text("allreduce 8 256 f32 ring single\nallreduce 8 256 f32 rabenseifner batch\n")
+        dsmem.autotune_load(table)
+        assert dsmem.autotune_pick(Op.ALLREDUCE, Dt.F32, 8, 4096, num_clusters=1) == Alg.RING
+        assert dsmem.autotune_pick(Op.ALLREDUCE, Dt.F32, 8, 4096, num_clusters=64) == Alg.RABENSEIFNER
+        table.write_text("allreduce 8 256 f32 ring batch\n")   # no `single` line: the batch one serves
+        dsmem.autotune_load(table)
+        assert dsmem.autotune_pick(Op.ALLREDUCE, Dt.F32, 8, 4096, num_clusters=1) == Alg.RING
+        bad = tmp_path / "bad_regime.txt"
+        bad.write_text("allreduce 8 256 f32 ring sometimes\n")
+        with pytest.raises(dsmem.DsmemError):
+            dsmem.autotune_load(bad)
     finally:
-        empty = tmp_path / "empty.txt"
-        empty.write_text("")
         dsmem.autotune_load(empty)
     bad = tmp_path / "bad.txt"
     bad.write_text("allreduce 8 256 f32 no_such_alg\n")
@@ -170,3 +183,26 @@ def test_invalid_arguments(dsmem):
     with pytest.raises(dsmem.DsmemError) as e:
         dsmem.launch(dsmem.Op.ALLREDUCE, dsmem.Alg.RING, dsmem.Dtype.F32, 8, 4096, 16, 32, 1)
     assert e.value.status == dsmem.Status.INVALID_ARGUMENT or e.value.status == dsmem.Status.CUDA
+
+
+def test_shipped_autotune_table_parses(dsmem, tmp_path):
+    """The table measured on B200 and shipped next to lib/ loads, and every entry names a legal algorithm."""
+    path = dsmem.PKG_DIR / "autotune_b200.tsv"
+    if not path.exists():
+        pytest.skip("no measured table shipped")
+    dsmem.autotune_load(path)
+    try:
+        lines = [ln.split() for ln in path.read_text().splitlines() if ln.strip() and not ln.startswith("#")]
+        assert lines
+        ops = {"allreduce": dsmem.Op.ALLREDUCE, "allgather": dsmem.Op.ALLGATHER,
+               "reducescatter": dsmem.Op.REDUCESCATTER, "alltoall": dsmem.Op.ALLTOALL}
+        dts = {"f32": dsmem.Dtype.F32, "bf16": dsmem.Dtype.BF16, "i32": dsmem.Dtype.I32}
+        for op, n, p, dt, alg, regime in lines:
+            a = dsmem.Alg[alg.upper()]
+            assert dsmem.query(ops[op], a, dts[dt], int(n), int(p))[0] == dsmem.Status.OK
+            got = dsmem.autotune_pick(ops[op], dts[dt], int(n), int(p), num_clusters=64 if regime == "batch" else 1)
+            assert got == a
+    finally:
+        empty = tmp_path / "empty.txt"
+        empty.write_text("")
+        dsmem.autotune_load(empty)
