@@ -237,6 +237,18 @@ void load_default_table() {
     });
 }
 
+uint32_t pipeline_units(const KernelEntry* e, uint32_t m);
+
+// classify() OK, or a payload above the one-piece limit that the pipelined driver runs in fitting units.
+// Caller holds st().mu.
+bool launchable(const KernelEntry* e, uint32_t m) {
+    const dsmem_status s = classify(e, m, nullptr);
+    if (s == DSMEM_OK) return true;
+    if (s != DSMEM_ERR_SMEM_LIMIT || e->fn_pipe == nullptr || !st().pipelined) return false;
+    const uint32_t sub = pipeline_units(e, m);
+    return sub != 0 && e->smem_pipe(m / sub) <= dsb::kSmemLimit;
+}
+
 int resolve_auto(int op, int dtype, int n, size_t bytes, int regime = 0) {
     load_default_table();
     State& s = st();
@@ -252,7 +264,8 @@ int resolve_auto(int op, int dtype, int n, size_t bytes, int regime = 0) {
             if (jt != it->second.begin()) {
                 --jt;
                 const KernelEntry* e = find(op, jt->second, dtype, n);
-                if (classify(e, m, nullptr) == DSMEM_OK) return jt->second;
+                if (e != nullptr && (regime == 1 ? launchable(e, m) : classify(e, m, nullptr) == DSMEM_OK))
+                    return jt->second;
             }
         }
     }
@@ -347,15 +360,27 @@ uint32_t pipeline_units(const KernelEntry* e, uint32_t m) {
     return 0;
 }
 
+// Legality of a launch. A payload whose one-piece buffers exceed the shared-memory limit (the reference's
+// SKIP:smem) still runs when the algorithm has a pipelined driver whose sub-vector units fit: *pipe_only is
+// then set and the launch must take that driver (dsmem_query keeps the reference's classification).
 dsmem_status prepare(int op, int alg, int dtype, int n, size_t bytes, const KernelEntry** entry, uint32_t* m_out,
-                     uint64_t* smem_out, int regime = 0) {
+                     uint64_t* smem_out, int regime = 0, bool* pipe_only = nullptr) {
     if (!valid_enums(op, alg, dtype, n)) return DSMEM_ERR_INVALID_ARGUMENT;
     if (alg == DSMEM_ALG_AUTO) alg = resolve_auto(op, dtype, n, bytes, regime);
     if (alg == DSMEM_ALG_AUTO) return DSMEM_ERR_ILLEGAL_CONFIG;
     const KernelEntry* e = find(op, alg, dtype, n);
     const uint32_t m = msg_elems(op, dtype, n, bytes);
     uint64_t smem = 0;
-    const dsmem_status s = classify(e, m, &smem);
+    dsmem_status s = classify(e, m, &smem);
+    if (pipe_only) *pipe_only = false;
+    if (s == DSMEM_ERR_SMEM_LIMIT && pipe_only != nullptr && e->fn_pipe != nullptr) {
+        std::lock_guard<std::mutex> lock(st().mu);
+        const uint32_t sub = st().pipelined ? pipeline_units(e, m) : 0u;
+        if (sub && e->smem_pipe(m / sub) <= dsb::kSmemLimit) {
+            *pipe_only = true;
+            s = DSMEM_OK;
+        }
+    }
     if (s != DSMEM_OK) return s;
     *entry = e;
     *m_out = m;
@@ -406,7 +431,9 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
     const KernelEntry* e = nullptr;
     uint32_t m = 0;
     uint64_t smem = 0;
-    dsmem_status s = prepare(op, alg, dtype, cluster_size, bytes_per_cta, &e, &m, &smem, num_clusters > 1 ? 1 : 0);
+    bool pipe_only = false;
+    dsmem_status s = prepare(op, alg, dtype, cluster_size, bytes_per_cta, &e, &m, &smem, num_clusters > 1 ? 1 : 0,
+                             &pipe_only);
     if (s != DSMEM_OK) return s;
     if (num_clusters < 0 || in == nullptr || out == nullptr) return DSMEM_ERR_INVALID_ARGUMENT;
     if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15u) return DSMEM_ERR_INVALID_ARGUMENT;
@@ -420,10 +447,11 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
         State& g = st();
         std::lock_guard<std::mutex> lock(g.mu);
         DeviceState& d = device_state(dev);
-        if (smem > (uint64_t)d.optin) return DSMEM_ERR_SMEM_LIMIT;
-        // batches use the pipelined driver when the algorithm has one and its shared memory fits
+        if (!pipe_only && smem > (uint64_t)d.optin) return DSMEM_ERR_SMEM_LIMIT;
+        // batches use the pipelined driver when the algorithm has one and its shared memory fits (and so
+        // does any payload too large for the one-piece kernel)
         a.sub = 1;
-        if (g.pipelined && num_clusters > 1 && e->fn_pipe != nullptr) {
+        if (g.pipelined && (num_clusters > 1 || pipe_only) && e->fn_pipe != nullptr) {
             const uint32_t sub = pipeline_units(e, m);
             const uint64_t sp = sub ? e->smem_pipe(m / sub) : 0;
             if (sub && sp <= dsb::kSmemLimit && sp <= (uint64_t)d.optin) {
@@ -432,6 +460,7 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
                 a.sub = sub;
             }
         }
+        if (fn == e->fn && pipe_only) return DSMEM_ERR_SMEM_LIMIT;
         if (ensure_attrs(d, fn, e->n, smem) != cudaSuccess) return DSMEM_ERR_CUDA;
         if (occupancy(d, fn, e->n, smem, &resident) != cudaSuccess) return DSMEM_ERR_CUDA;
         if (resident < 1) return DSMEM_ERR_SMEM_LIMIT;   // the cluster cannot be placed (main.cu:221)

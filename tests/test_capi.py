@@ -197,9 +197,13 @@ def test_shipped_autotune_table_parses(dsmem, tmp_path):
         ops = {"allreduce": dsmem.Op.ALLREDUCE, "allgather": dsmem.Op.ALLGATHER,
                "reducescatter": dsmem.Op.REDUCESCATTER, "alltoall": dsmem.Op.ALLTOALL}
         dts = {"f32": dsmem.Dtype.F32, "bf16": dsmem.Dtype.BF16, "i32": dsmem.Dtype.I32}
+        pipelined = (dsmem.Alg.TWO_SHOT_PUSH, dsmem.Alg.RS_PUSH_GLOBAL_AG)
+        by_name = {dsmem.lib().dsmem_alg_name(int(x)).decode(): x for x in dsmem.Alg}
         for op, n, p, dt, alg, regime in lines:
-            a = dsmem.Alg[alg.upper()]
-            assert dsmem.query(ops[op], a, dts[dt], int(n), int(p))[0] == dsmem.Status.OK
+            a = by_name[alg]
+            st = dsmem.query(ops[op], a, dts[dt], int(n), int(p))[0]
+            # payloads above the one-piece limit run on the pipelined driver (batches)
+            assert st == dsmem.Status.OK or (st == dsmem.Status.SMEM_LIMIT and a in pipelined and regime == "batch")
             got = dsmem.autotune_pick(ops[op], dts[dt], int(n), int(p), num_clusters=64 if regime == "batch" else 1)
             assert got == a
     finally:
