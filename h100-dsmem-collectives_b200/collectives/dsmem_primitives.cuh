@@ -212,9 +212,13 @@ __device__ __forceinline__ bool mbar_try_wait_parity_suspend(uint32_t bar, uint3
 }
 // Wait until the phase completes or %globaltimer passes `deadline_ns`; false on time-out. Each probe may
 // suspend the thread for up to 100 us, so the limit is honoured to within that.
-constexpr uint32_t kWaitSuspendNs = 100000u;
+#ifndef DSMEM_WAIT_SUSPEND_NS
+#define DSMEM_WAIT_SUSPEND_NS 100000u
+#endif
+constexpr uint32_t kWaitSuspendNs = DSMEM_WAIT_SUSPEND_NS;   // 0: probe without a suspend hint
 __device__ __forceinline__ bool mbar_wait_parity_until(uint32_t bar, uint32_t parity, unsigned long long deadline_ns) {
-    while (!mbar_try_wait_parity_suspend(bar, parity, kWaitSuspendNs)) {
+    while (kWaitSuspendNs != 0u ? !mbar_try_wait_parity_suspend(bar, parity, kWaitSuspendNs)
+                                : !mbar_try_wait_parity(bar, parity)) {
         if (globaltimer() > deadline_ns) return false;
     }
     return true;

@@ -18,8 +18,8 @@
 //     warp writes the warp's 2 partials into slot[set][b][warp*2..] of CTA q with one st.async, whose
 //     bytes complete on that CTA's mbarrier of the set (armed for N*R*4 bytes), so there is no release
 //     fence and no cluster barrier per group;
-//   * the exchange runs at most L = 1 group ahead (rms_lookahead): a warp sends group i+1's partials
-//     before it waits for group i's sums if group i+1's rows have landed, else right after normalising i. A writer sends group g after it received everyone's
+//   * the exchange runs up to L = 1 group ahead (rms_lookahead): before it waits for group i's sums a
+//     warp sends group i+1's partials if its rows have landed, else right after normalising i. A writer sends group g after it received everyone's
 //     partials of g-L-1, so an owner may still be reading any set of groups g-L-1 .. g+L-1 when g's
 //     partials arrive: slot sets rotate over kSets >= 2L+2 groups, so g's set is none of those;
 //   * outputs leave with 16-byte streaming stores; the weight slice sits in registers when it fits.
@@ -52,8 +52,9 @@ constexpr uint32_t kSmemPerSm = 233472;             // 228 KiB of shared memory 
 // end-of-kernel flag word at byte 120)
 constexpr int kFull = 0, kEmpty = kStages, kWBar = 2 * kStages, kSum = 16;
 static_assert(8 * kWBar < (int)dsb::kFlagOff && kSum * 8 > (int)dsb::kFlagOff, "barriers overlap the flag word");
-// partial sums are sent at most `lookahead` groups ahead of the group being normalised. One group hides
-// the exchange round trip; a deeper lookahead makes the first group wait for later groups' loads.
+// partial sums are sent at most `lookahead` groups ahead of the group being normalised (only for groups
+// whose rows have landed, so the first group never waits for later loads). Measured: 1 is best; 3 delays
+// every group's stores by the partials of the groups ahead (config 3: 21.9 us against 18.5 us).
 __host__ __device__ constexpr int rms_lookahead(int) { return 1; }
 static_assert(kSets >= 2 * rms_lookahead(kStages) + 2, "slot sets must cover 2 * lookahead + 2 groups");
 
@@ -211,6 +212,7 @@ __global__ void __launch_bounds__(kThreadsRms, kCtasPerSm) rmsnorm_cluster_kerne
                              : "memory");
             }
         };
+        constexpr long long kLook = rms_lookahead(kStages);
         uint32_t s = 0, s_send = 0;   // stages of group i and of the next group to send
         long long sent = 0;            // groups whose partials this warp has sent
         auto send_next = [&]() {
@@ -220,13 +222,14 @@ __global__ void __launch_bounds__(kThreadsRms, kCtasPerSm) rmsnorm_cluster_kerne
         if (iters > 0) send_next();
         for (long long i = 0; i < iters; ++i) {
             c.deadline = globaltimer() + c.wait_limit;
-            // Group i+1's partials go out before group i is normalised when its rows have already landed
-            // (the exchange then runs rms_lookahead() = 1 group ahead), else right after: a group never
-            // waits for a later group's load (which matters while the first loads stream in).
-            if (sent == i + 1 && sent < iters) {
+            // The partials of groups i+1 .. i+L (L = rms_lookahead) whose rows have already landed go out
+            // before group i is normalised, so their exchanges overlap this group's work; group i+1's goes
+            // out right after it at the latest. No group waits for a later group's load.
+            while (sent < iters && sent <= i + kLook) {
                 const int fb = kFull + (int)s_send;
                 const bool ready = __shfl_sync(0xffffffffu, mbar_try_wait_parity(c.bar(fb), (c.phase >> fb) & 1u), 0);
-                if (ready) send_next();
+                if (!ready) break;
+                send_next();
             }
             const int set = (int)(i & (kSets - 1));
             wait_one(c, kSum + set);
