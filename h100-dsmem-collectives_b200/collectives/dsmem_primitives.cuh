@@ -281,6 +281,19 @@ __device__ __forceinline__ void bulk_load_g2s(uint32_t dst, const void* src, uin
         "l"(src), "r"(bytes), "r"(bar)
         : "memory");
 }
+// Tiled TMA load of one box of a 3-D tensor map (global -> this CTA's shared memory, no multicast),
+// completing on a local mbarrier. `tmap` is the generic address of a __grid_constant__ CUtensorMap;
+// x * element size must be a multiple of 16 bytes. Box elements outside the tensor read as zero and
+// still count toward the transaction bytes.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int x, int y, int z, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
 // Bulk copy this CTA's shared memory -> global, tracked by the issuing thread's bulk groups.
 __device__ __forceinline__ void bulk_store_s2g(void* dst, uint32_t src, uint32_t bytes) {
     asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)

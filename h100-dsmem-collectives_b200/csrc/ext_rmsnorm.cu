@@ -6,23 +6,27 @@
 //     [b*H/N, (b+1)*H/N), partial sum of squares by warp shuffles, cluster AllReduce of one float;
 //   kernels/rmsnorm_lamport__fused_allreduce_rmsnorm__hpcops.cu:37-197   h = x + residual written back,
 //     replicated-push scalar AllReduce (one store into slot[b] of every CTA) (:153-169).
-// B200 design (one launch, persistent clusters of N CTAs; per CTA 8 consumer warps + 1 producer warp):
-//   * cluster q of C owns the contiguous rows [q*rows/C, (q+1)*rows/C), taken in groups of R = 16 (two per
-//     consumer warp; the last group partial); CTA b owns the column slice b of every row;
-//   * the producer warp streams the weight slice and each group's R row slices (and residual slices) with
-//     one-CTA bulk copies (cp.async.bulk, no multicast) into a ring of 2..4 shared-memory stages (as many
-//     as fit; full/empty mbarriers); a stage is released only after its rows are normalised, so x is read
-//     from shared memory twice and never held in registers. The producer starts loading before the
-//     cluster rendezvous (split arrive/wait), which only the remote stores need;
-//   * the per-row partial sums of squares meet in the hpc-ops replicated push: lane q < N of each consumer
-//     warp writes the warp's 2 partials into slot[set][b][warp*2..] of CTA q with one st.async, whose
-//     bytes complete on that CTA's mbarrier of the set (armed for N*R*4 bytes), so there is no release
-//     fence and no cluster barrier per group;
-//   * the exchange runs up to L = 1 group ahead (rms_lookahead): before it waits for group i's sums a
-//     warp sends group i+1's partials if its rows have landed, else right after normalising i. A writer sends group g after it received everyone's
-//     partials of g-L-1, so an owner may still be reading any set of groups g-L-1 .. g+L-1 when g's
-//     partials arrive: slot sets rotate over kSets >= 2L+2 groups, so g's set is none of those;
+// B200 design (one launch, persistent clusters of N CTAs; per CTA 1 producer warp, 4 sum warps and 8
+// normalising warps):
+//   * cluster q of C owns the contiguous groups [q*G/C, (q+1)*G/C) of R = 16 rows (G = ceil(rows/R); only
+//     the tensor's last group is partial); CTA b owns the column slice b of every row;
+//   * the producer warp streams the weight slice (one bulk copy) and each group's R row slices (and residual
+//     slices) as ONE tiled TMA load per operand: a 3-D tensor map {chunk, chunks per row, rows} whose box
+//     is the CTA's slice of 16 rows (no multicast; rows past the tensor read as zeros). Loads go into a
+//     ring of 2..12 shared-memory stages (as many as fit two CTAs per SM; full/empty mbarriers), at most
+//     kAhead groups beyond the last one landed; a stage is released only after its rows are normalised, so
+//     x is read from HBM once and from shared memory twice, never held in registers. The cluster
+//     rendezvous (split arrive/wait) starts before the first load and completes under the loads;
+//   * sum warp v computes the partial sums of squares of rows 4v..4v+3 of a group as soon as its stage has
+//     landed and meets the peers' partials in the hpc-ops replicated push: lane q < N writes the 4 partials
+//     into slot[set][b][4v..] of CTA q with one st.async, whose bytes complete on that CTA's mbarrier of the
+//     set (armed for N*R*4 bytes), so there is no release fence and no cluster barrier per group;
+//   * normalising warp w waits for the set's barrier, sums the N partials of rows 2w, 2w+1 (lane-parallel
+//     loads, butterfly), scales, multiplies by the weight and writes the rows. The sum warps run up to the
+//     ring depth ahead, so the exchange of later groups overlaps this group's stores; slot sets rotate over
+//     a power of two >= 2 * stages of sets (the reuse argument is at kMaxSets);
 //   * outputs leave with 16-byte streaming stores; the weight slice sits in registers when it fits.
+#include <cuda.h>   // CUtensorMap (the encoder is reached through the runtime's driver entry point)
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -38,27 +42,43 @@ namespace {
 using namespace dsmem;
 using namespace dsb2;
 
-constexpr int kConsumers = 8;                       // consumer warps
-constexpr int kThreadsRms = (kConsumers + 1) * 32;  // + one producer warp
-constexpr int kRowsPerWarp = 2;                     // one st.async.v2 / float2 of partials per warp
-static_assert(kRowsPerWarp == 2, "the partial exchange moves float2 pairs");
-constexpr int kR = kConsumers * kRowsPerWarp;       // rows per group
-constexpr int kStages = 4;                          // most stages (barrier ids); a launch uses 2..4
-constexpr int kSets = 8;                            // partial-sum slot sets (see the header comment)
+// Warp roles: kNormWarps normalise (2 rows of a 16-row group each), kSsWarps compute the rows' sums of
+// squares and push them to the cluster (4 rows each), one producer warp streams the rows in. The sum
+// warps run ahead of the normalising warps, so a group's exchange overlaps the previous group's stores.
+constexpr int kNormWarps = 8;
+constexpr int kSsWarps = 4;
+constexpr int kConsumers = kNormWarps;              // arrivals that free a stage
+constexpr int kProducerWarp = kNormWarps + kSsWarps;
+constexpr int kThreadsRms = (kProducerWarp + 1) * 32;
+constexpr int kRowsPerWarp = 2;                     // rows a normalising warp owns in a group
+constexpr int kRowsPerSs = 4;                       // rows a sum warp owns in a group (one st.async.v4)
+constexpr int kR = kNormWarps * kRowsPerWarp;       // rows per group
+static_assert(kR == kSsWarps * kRowsPerSs, "both roles cover the group");
+constexpr int kMaxStages = 12;                      // most ring stages (barrier ids); a launch uses 2..12
+constexpr int kAhead = 2;                           // groups in flight beyond the last one landed (<= 2 stages)
+constexpr int kMaxSets = 32;                        // most partial-sum slot sets (a power of two >= 2 * stages)
 constexpr int kMaxUnitsPerLane = 4;                 // 16-byte units of a row slice per lane (<= 2 KiB)
-constexpr int kCtasPerSm = 3;                       // occupancy target (registers capped to fit it)
+constexpr int kCtasPerSm = 2;                       // occupancy target (registers capped to fit it)
 constexpr uint32_t kSmemPerSm = 233472;             // 228 KiB of shared memory per SM
-// barrier ids: full[s] 0..3, empty[s] 4..7, weight 8, sum[set] 16..23 (id 15 would overlap the
-// end-of-kernel flag word at byte 120)
-constexpr int kFull = 0, kEmpty = kStages, kWBar = 2 * kStages, kSum = 16;
-static_assert(8 * kWBar < (int)dsb::kFlagOff && kSum * 8 > (int)dsb::kFlagOff, "barriers overlap the flag word");
-// partial sums are sent at most `lookahead` groups ahead of the group being normalised (only for groups
-// whose rows have landed, so the first group never waits for later loads). Measured: 1 is best; 3 delays
-// every group's stores by the partials of the groups ahead (config 3: 21.9 us against 18.5 us).
-__host__ __device__ constexpr int rms_lookahead(int) { return 1; }
-static_assert(kSets >= 2 * rms_lookahead(kStages) + 2, "slot sets must cover 2 * lookahead + 2 groups");
+// barrier ids (8 bytes each, [0, 512) of shared memory): full[s] 0..11, weight 12, empty[s] 16..27,
+// sum[set] 32..63; id 15 holds the end-of-kernel flag word (byte 120)
+constexpr int kFull = 0, kWBar = kMaxStages, kEmpty = 16, kSum = 32;
+constexpr uint32_t kBarBytes = 8u * (kSum + kMaxSets);
+static_assert(8 * kWBar < (int)dsb::kFlagOff && kEmpty * 8 > (int)dsb::kFlagOff && kEmpty + kMaxStages <= kSum,
+              "barrier ids overlap");
+// Slot-set reuse: CTA b's sum warps send group g only after b's stage for g was loaded, i.e. after b's
+// normalising warps finished group g - stages, which needed every peer's partials of g - stages. A peer q's
+// sum warps sent g - stages only after q's stage for it was loaded, i.e. after q's normalising warps finished
+// g - 2 stages (and q's sum barrier of that group completed). So when g's partials reach q, q may still read
+// the sets of groups g - 2 stages + 1 .. g - 1 only, and 2 * stages sets keep g's set out of them.
+static_assert(kMaxSets >= 2 * kMaxStages, "slot sets must cover 2 * stages groups");
 
 struct RmsArgs {
+    // 3-D views of x and of the residual: {chunk elements, chunks per row, rows}; one box = 16 rows of one
+    // CTA's column slice, so a group's rows arrive with one TMA load per operand
+    alignas(64) CUtensorMap tmx;
+    alignas(64) CUtensorMap tmr;
+    int chunks_per_slice;   // box extent along the chunk dimension
     const void* x;
     const void* res;     // nullable
     const void* w;
@@ -71,103 +91,116 @@ struct RmsArgs {
     float eps;
     uint32_t slice_bytes;   // bytes of one row slice of one CTA
     uint32_t smem_bytes;
-    int stages;             // shared-memory stages of the row ring (2..kStages)
+    int stages;             // shared-memory stages of the row ring (2..kMaxStages)
+    int sets;               // partial-sum slot sets: a power of two >= 2 * stages
 };
 
-// Shared-memory layout: [0,256) barriers | slots kSets x N x R floats | w slice | stages x R x slice (x2 with residual)
-__host__ __device__ constexpr uint32_t rms_slots_off() { return 256u; }
-__host__ __device__ constexpr uint32_t rms_w_off(int n) { return rms_slots_off() + (uint32_t)kSets * n * kR * 4u; }
-__host__ __device__ constexpr uint32_t rms_stage_off(int n, uint32_t slice) { return rms_w_off(n) + slice; }
-__host__ __device__ constexpr uint32_t rms_smem(int n, uint32_t slice, bool residual, int stages) {
-    return rms_stage_off(n, slice) + (uint32_t)stages * kR * slice * (residual ? 2u : 1u);
+// Shared-memory layout: [0,512) barriers | slots sets x N x R floats | w slice | stages x R x slice (x2 with residual)
+__host__ __device__ constexpr uint32_t rms_slots_off() { return kBarBytes; }
+__host__ __device__ constexpr uint32_t rms_w_off(int n, int sets) { return rms_slots_off() + (uint32_t)sets * n * kR * 4u; }
+__host__ __device__ constexpr uint32_t rms_stage_off(int n, int sets, uint32_t slice) {
+    return rms_w_off(n, sets) + ((slice + 127u) & ~127u);   // stages start 128-byte aligned (TMA destination)
+}
+__host__ __device__ constexpr uint32_t rms_smem(int n, uint32_t slice, bool residual, int stages, int sets) {
+    return rms_stage_off(n, sets, slice) + (uint32_t)stages * kR * slice * (residual ? 2u : 1u);
+}
+__host__ __device__ constexpr int rms_sets(int stages) {
+    int s = 2;
+    while (s < 2 * stages) s *= 2;
+    return s;
 }
 
-// Bounded wait on barrier i by one thread (its own phase bookkeeping in c.phase).
-__device__ __forceinline__ void wait_one(dsb::Ctx& c, int i) { dsb::wait(c, i); }
+// Bounded wait by one thread for barrier i to finish the phase of parity `par` (the phases follow from the
+// group index, so the kernel keeps no per-barrier phase word).
+__device__ __forceinline__ void wait_par(dsb::Ctx& c, int i, uint32_t par) {
+    if (c.dead) return;
+    if (mbar_try_wait_parity(c.bar(i), par)) return;
+    if (!mbar_wait_parity_until(c.bar(i), par, c.deadline)) {
+        c.dead = true;
+        if ((threadIdx.x & 31) == 0) dsb::report_timeout(c, i);
+    }
+}
 
 template <int N, typename T, bool RES, int UPL>
-__global__ void __launch_bounds__(kThreadsRms, kCtasPerSm) rmsnorm_cluster_kernel(const RmsArgs a) {
+__global__ void __launch_bounds__(kThreadsRms, kCtasPerSm) rmsnorm_cluster_kernel(const __grid_constant__ RmsArgs a) {
     using E = RmsElem<T>;
     dsb::Ctx c;
     dsb::ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
     dsb::flag_init(c);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t slice = a.slice_bytes, units = slice >> 4;   // 16-B units per row slice (<= 32 * UPL)
-    const uint32_t slots = rms_slots_off(), woff = rms_w_off(N), stage0 = rms_stage_off(N, slice);
+    const uint32_t nsets = (uint32_t)a.sets;
+    const uint32_t slots = rms_slots_off(), woff = rms_w_off(N, a.sets), stage0 = rms_stage_off(N, a.sets, slice);
     const uint32_t stage_bytes = (uint32_t)kR * slice * (RES ? 2u : 1u);
     const uint32_t nst = (uint32_t)a.stages;
-    // cluster q owns the contiguous rows [lo, hi) = [q*rows/C, (q+1)*rows/C): every cluster moves the same
-    // bytes (within one row), in groups of kR rows (the last one partial)
+    // cluster q owns the contiguous groups [q*G/C, (q+1)*G/C) of kR rows (G = ceil(rows / kR)); only the
+    // tensor's last group is partial, and its rows past the end arrive as zeros
     const long long nclu = (long long)num_clusters(), cq = (long long)cluster_id();
-    const long long lo = cq * a.rows / nclu, hi = (cq + 1) * a.rows / nclu;
-    const long long iters = (hi - lo + kR - 1) / kR;
+    const long long groups = (a.rows + kR - 1) / kR;
+    const long long g_lo = cq * groups / nclu, g_hi = (cq + 1) * groups / nclu;
+    const long long lo = g_lo * kR, hi = min(g_hi * kR, a.rows);
+    const long long iters = g_hi - g_lo;
     const size_t row_bytes = (size_t)a.hidden * sizeof(T);
     const size_t col_off = (size_t)c.rank * slice;
 
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(c.bar(kFull + s), 1);
-            mbar_init(c.bar(kEmpty + s), kConsumers);
-        }
+    const int cy = (int)c.rank * a.chunks_per_slice;   // this CTA's first chunk of a row
+    // Issue group i's loads into stage s: whole boxes (rows past the tensor included) on full[s].
+    auto load_group = [&](long long i, uint32_t s) {
+        const int r0 = (int)(lo + i * kR);
+        const uint32_t dst = stage0 + s * stage_bytes;
+        dsb::arm(c, kFull + (int)s, stage_bytes);
+        tma_load_3d(c.sa + dst, &a.tmx, 0, cy, r0, c.bar(kFull + (int)s));
+        if (RES) tma_load_3d(c.sa + dst + (uint32_t)kR * slice, &a.tmr, 0, cy, r0, c.bar(kFull + (int)s));
+    };
+    if (threadIdx.x == kProducerWarp * 32) {   // the barriers the loads complete on
+        for (uint32_t s = 0; s < nst; ++s) mbar_init(c.bar(kFull + (int)s), 1);
         mbar_init(c.bar(kWBar), 1);
-        for (int s = 0; s < kSets; ++s) mbar_init(c.bar(kSum + s), 1);
+        fence_mbar_init();
+        prefetch_tmap(&a.tmx);
+        if (RES) prefetch_tmap(&a.tmr);
+    } else if (warp == 0) {   // lane l initialises empty[l] and sum[l] (in parallel)
+        if (lane < nst) mbar_init(c.bar(kEmpty + (int)lane), kConsumers);
+        if (lane < nsets) mbar_init(c.bar(kSum + (int)lane), 1);
         fence_mbar_init();
     }
-    __syncthreads();   // local barriers initialised: the producer may load at once
+    __syncthreads();   // every local barrier initialised
     // Split cluster barrier: every thread arrives now (releasing its barrier inits cluster-wide); consumers
-    // wait before their first remote store, the producer only after it has issued its loads, so the first
-    // HBM reads overlap the cluster rendezvous.
+    // wait before their first remote store, the producer only after its loop, so the HBM reads overlap the
+    // cluster rendezvous. The arrivals go out before the first bulk load: arriving after the loads were
+    // issued held the cluster's rendezvous back until most of the loaded bytes had come in (about 5 us at
+    // 4096 x 4096 bf16 on B200).
     cluster_arrive();
     c.deadline = globaltimer() + c.wait_limit;
 
-    if (warp == kConsumers) {
+    if (warp == kProducerWarp) {
         // ---------------------------------------------------------------- producer warp (lane 0)
         if (lane == 0) {
             dsb::arm(c, kWBar, slice);   // weight slice -> shared, on its own barrier
             bulk_load_g2s(c.sa + woff, static_cast<const unsigned char*>(a.w) + col_off, slice, c.bar(kWBar));
-            const unsigned char* xb = static_cast<const unsigned char*>(a.x);
-            const unsigned char* rb = static_cast<const unsigned char*>(a.res);
-            uint32_t s = 0;   // stage of group i
-            for (long long i = 0; i < iters; ++i, s = (s + 1 == nst) ? 0u : s + 1) {
-                if (i >= (long long)nst) {   // the stage's previous group is normalised by every consumer warp
-                    c.deadline = globaltimer() + c.wait_limit;
-                    wait_one(c, kEmpty + (int)s);
+            // Group i goes out once group i - kAhead has landed (fewer bytes queued per CTA: the first groups
+            // of every CTA arrive sooner and closer together) and its stage's previous group is normalised.
+            uint32_t s = 0, round = 0;   // group i = round * nst + s
+            uint32_t sa = 0, pa = 0;     // stage and full-phase parity of group i - kAhead
+            for (long long i = 0; i < iters; ++i) {
+                c.deadline = globaltimer() + c.wait_limit;
+                if (i >= kAhead) {
+                    wait_par(c, kFull + (int)sa, pa);
+                    if (++sa == nst) sa = 0, pa ^= 1u;
                 }
-                const long long r0 = lo + i * kR;
-                const int nr = (int)min((long long)kR, hi - r0);
-                const uint32_t dst = stage0 + (uint32_t)s * stage_bytes;
-                dsb::arm(c, kFull + s, (uint32_t)nr * slice * (RES ? 2u : 1u));
-                for (int r = 0; r < nr; ++r) {
-                    const size_t src = (size_t)(r0 + r) * row_bytes + col_off;
-                    bulk_load_g2s(c.sa + dst + (uint32_t)r * slice, xb + src, slice, c.bar(kFull + s));
-                    if (RES)
-                        bulk_load_g2s(c.sa + dst + ((uint32_t)kR + r) * slice, rb + src, slice, c.bar(kFull + s));
-                }
+                if (round > 0) wait_par(c, kEmpty + (int)s, (round - 1u) & 1u);
+                load_group(i, s);
+                if (++s == nst) s = 0, ++round;
             }
         }
         __syncwarp();   // reconverge before the aligned cluster barrier
         cluster_wait();
     } else {
-        // ---------------------------------------------------------------- consumer warps
         cluster_wait();   // every CTA's barriers initialised before any remote store completes on them
-        wait_one(c, kWBar);
-        const uint4* wp = c.ptr<const uint4>(woff);
-        const float inv_hidden = 1.0f / (float)a.hidden;
         constexpr int P = E::kPairs;
-        // this lane's weight units as fp32 pairs, held in registers when they fit in 16 of them
-        constexpr bool kWReg = UPL * P * 2 <= 16;
-        f2x wr[kWReg ? UPL : 1][P];
-        if constexpr (kWReg) {
-#pragma unroll
-            for (int q = 0; q < UPL; ++q) {
-                const uint32_t u = lane + 32u * q;
-                if (u < units) E::unpack(wp[u], wr[q]);
-            }
-        }
-        // h of row k of the group held in stage s, unit u, as fp32 pairs
-        auto load_h = [&](uint32_t s, int k, uint32_t u, f2x* f) {
+        // h of row `row` (within the group) held in stage s, unit u, as fp32 pairs
+        auto load_h = [&](uint32_t s, int row, uint32_t u, f2x* f) {
             const uint4* xs = c.ptr<const uint4>(stage0 + s * stage_bytes);
-            const uint32_t idx = (warp * kRowsPerWarp + k) * units + u;
+            const uint32_t idx = (uint32_t)row * units + u;
             E::unpack(xs[idx], f);
             if (RES) {
                 f2x r[P];
@@ -177,108 +210,118 @@ __global__ void __launch_bounds__(kThreadsRms, kCtasPerSm) rmsnorm_cluster_kerne
                 E::unpack(E::pack(f), f);   // h rounded to the element type (the pre-norm output)
             }
         };
-        // wait for group j's rows (stage s), reduce my rows' sums of squares and push them to every CTA
-        auto send = [&](long long j, uint32_t s) {
-            wait_one(c, kFull + (int)s);
-            const long long row0 = lo + j * kR + (long long)warp * kRowsPerWarp;
-            float ss[kRowsPerWarp];
+        if (warp >= kNormWarps) {
+            // ------------------------------------------------------------ sum warps: rows 4v..4v+3
+            const uint32_t v = warp - kNormWarps;
+            uint32_t s = 0, ph = 0, set = 0;   // stage, its full parity, slot set of group j
+            for (long long j = 0; j < iters; ++j) {
+                c.deadline = globaltimer() + c.wait_limit;
+                wait_par(c, kFull + (int)s, ph);
+                const long long row0 = lo + j * kR + (long long)v * kRowsPerSs;
+                float ss[kRowsPerSs];
 #pragma unroll
-            for (int k = 0; k < kRowsPerWarp; ++k) {
-                f2x acc = 0ull;   // (+0.0f, +0.0f)
-                if (row0 + k < hi) {
+                for (int k = 0; k < kRowsPerSs; ++k) {
+                    f2x acc = 0ull;
+                    if (row0 + k < hi) {
+#pragma unroll
+                        for (int q = 0; q < UPL; ++q) {
+                            const uint32_t u = lane + 32u * q;
+                            if (u < units) {
+                                f2x f[P];
+                                load_h(s, (int)(v * kRowsPerSs) + k, u, f);
+#pragma unroll
+                                for (int e = 0; e < P; ++e) acc = f2_fma(f[e], f[e], acc);
+                            }
+                        }
+                    }
+                    const float2 a2 = f2_split(acc);
+                    ss[k] = a2.x + a2.y;
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                    for (int k = 0; k < kRowsPerSs; ++k) ss[k] += __shfl_xor_sync(0xffffffffu, ss[k], off);
+                if (v == 0 && lane == 0) dsb::arm(c, kSum + (int)set, (uint32_t)N * kR * 4u);
+                if (lane < (uint32_t)N) {   // lane q stores the 4 partials into CTA q
+                    const uint32_t dst = slots + ((set * N + c.rank) * kR + v * kRowsPerSs) * 4u;
+                    const uint32_t rd = mapa(c.sa + dst, lane), rbar = mapa(c.bar(kSum + (int)set), lane);
+                    asm volatile(
+                        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1,%2,%3,%4}, [%5];" ::"r"(rd),
+                        "f"(ss[0]), "f"(ss[1]), "f"(ss[2]), "f"(ss[3]), "r"(rbar)
+                        : "memory");
+                }
+                if (++s == nst) s = 0, ph ^= 1u;
+                if (++set == nsets) set = 0;
+            }
+        } else {
+            // ------------------------------------------------------------ normalising warps: rows 2w, 2w+1
+            wait_par(c, kWBar, 0);
+            const uint4* wp = c.ptr<const uint4>(woff);
+            const float inv_hidden = 1.0f / (float)a.hidden;
+            // this lane's weight units as fp32 pairs, held in registers when they fit in 16 of them
+            constexpr bool kWReg = UPL * P * 2 <= 16;
+            f2x wr[kWReg ? UPL : 1][P];
+            if constexpr (kWReg) {
+#pragma unroll
+                for (int q = 0; q < UPL; ++q) {
+                    const uint32_t u = lane + 32u * q;
+                    if (u < units) E::unpack(wp[u], wr[q]);
+                }
+            }
+            uint32_t s = 0, ph = 0, set = 0, sph = 0;   // stage and its full parity, slot set and its parity
+            for (long long i = 0; i < iters; ++i) {
+                c.deadline = globaltimer() + c.wait_limit;
+                wait_par(c, kSum + (int)set, sph);
+                wait_par(c, kFull + (int)s, ph);   // completed already (the own sum warps waited on it); makes
+                                                   // the bulk-copied rows visible to this warp
+                const long long row0 = lo + i * kR + (long long)warp * kRowsPerWarp;
+                // the N partials of my two rows: lane q < N loads CTA q's pair, a butterfly over N lanes sums them
+                float2 part = make_float2(0.f, 0.f);
+                if (lane < (uint32_t)N)
+                    part = *c.ptr<const float2>(slots + ((set * N + lane) * kR + warp * kRowsPerWarp) * 4u);
+#pragma unroll
+                for (int off = N / 2; off > 0; off >>= 1) {
+                    part.x += __shfl_xor_sync(0xffffffffu, part.x, off);
+                    part.y += __shfl_xor_sync(0xffffffffu, part.y, off);
+                }
+                const float tot2[kRowsPerWarp] = {__shfl_sync(0xffffffffu, part.x, 0),
+                                                  __shfl_sync(0xffffffffu, part.y, 0)};
+#pragma unroll
+                for (int k = 0; k < kRowsPerWarp; ++k) {
+                    const long long row = row0 + k;
+                    const float scale = rsqrtf(fmaf(tot2[k], inv_hidden, a.eps));
+                    const f2x scale2 = f2_make(scale, scale);
+                    if (row >= hi) continue;
+                    uint4* yo = reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.y) + (size_t)row * row_bytes + col_off);
+                    uint4* po = RES && a.pre != nullptr
+                                    ? reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.pre) +
+                                                               (size_t)row * row_bytes + col_off)
+                                    : nullptr;
 #pragma unroll
                     for (int q = 0; q < UPL; ++q) {
                         const uint32_t u = lane + 32u * q;
                         if (u < units) {
                             f2x f[P];
-                            load_h(s, k, u, f);
+                            load_h(s, (int)(warp * kRowsPerWarp) + k, u, f);
+                            if (RES && po != nullptr) __stcs(po + u, E::pack(f));
+                            if constexpr (kWReg) {
 #pragma unroll
-                            for (int e = 0; e < P; ++e) acc = f2_fma(f[e], f[e], acc);
+                                for (int e = 0; e < P; ++e) f[e] = f2_mul(f2_mul(f[e], scale2), wr[q][e]);
+                            } else {
+                                f2x w[P];
+                                E::unpack(wp[u], w);
+#pragma unroll
+                                for (int e = 0; e < P; ++e) f[e] = f2_mul(f2_mul(f[e], scale2), w[e]);
+                            }
+                            __stcs(yo + u, E::pack(f));
                         }
                     }
                 }
-                const float2 a2 = f2_split(acc);
-                ss[k] = a2.x + a2.y;
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) ss[k] += __shfl_xor_sync(0xffffffffu, ss[k], off);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(c.bar(kEmpty + (int)s));   // stage free for the producer
+                if (++s == nst) s = 0, ph ^= 1u;
+                if (++set == nsets) set = 0, sph ^= 1u;
             }
-            const int set = (int)(j & (kSets - 1));
-            if (threadIdx.x == 0) dsb::arm(c, kSum + set, (uint32_t)N * kR * 4u);
-            if (lane < (uint32_t)N) {   // lane q stores the pair into CTA q (the butterfly left it in every lane)
-                const uint32_t dst = slots + (((uint32_t)set * N + c.rank) * kR + warp * kRowsPerWarp) * 4u;
-                const uint32_t rd = mapa(c.sa + dst, lane), rbar = mapa(c.bar(kSum + set), lane);
-                asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1,%2}, [%3];" ::"r"(rd),
-                             "f"(ss[0]), "f"(ss[1]), "r"(rbar)
-                             : "memory");
-            }
-        };
-        constexpr long long kLook = rms_lookahead(kStages);
-        uint32_t s = 0, s_send = 0;   // stages of group i and of the next group to send
-        long long sent = 0;            // groups whose partials this warp has sent
-        auto send_next = [&]() {
-            send(sent++, s_send);
-            s_send = (s_send + 1 == nst) ? 0u : s_send + 1;
-        };
-        if (iters > 0) send_next();
-        for (long long i = 0; i < iters; ++i) {
-            c.deadline = globaltimer() + c.wait_limit;
-            // The partials of groups i+1 .. i+L (L = rms_lookahead) whose rows have already landed go out
-            // before group i is normalised, so their exchanges overlap this group's work; group i+1's goes
-            // out right after it at the latest. No group waits for a later group's load.
-            while (sent < iters && sent <= i + kLook) {
-                const int fb = kFull + (int)s_send;
-                const bool ready = __shfl_sync(0xffffffffu, mbar_try_wait_parity(c.bar(fb), (c.phase >> fb) & 1u), 0);
-                if (!ready) break;
-                send_next();
-            }
-            const int set = (int)(i & (kSets - 1));
-            wait_one(c, kSum + set);
-            const long long row0 = lo + i * kR + (long long)warp * kRowsPerWarp;
-            // the N partials of my two rows: lane q < N loads CTA q's pair, a butterfly over N lanes sums them
-            float2 part = make_float2(0.f, 0.f);
-            if (lane < (uint32_t)N)
-                part = *c.ptr<const float2>(slots + (((uint32_t)set * N + lane) * kR + warp * kRowsPerWarp) * 4u);
-#pragma unroll
-            for (int off = N / 2; off > 0; off >>= 1) {
-                part.x += __shfl_xor_sync(0xffffffffu, part.x, off);
-                part.y += __shfl_xor_sync(0xffffffffu, part.y, off);
-            }
-            const float tot2[kRowsPerWarp] = {__shfl_sync(0xffffffffu, part.x, 0), __shfl_sync(0xffffffffu, part.y, 0)};
-#pragma unroll
-            for (int k = 0; k < kRowsPerWarp; ++k) {
-                const long long row = row0 + k;
-                const float scale = rsqrtf(fmaf(tot2[k], inv_hidden, a.eps));
-                const f2x scale2 = f2_make(scale, scale);
-                if (row >= hi) continue;
-                uint4* yo = reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.y) + (size_t)row * row_bytes + col_off);
-                uint4* po = RES && a.pre != nullptr
-                                ? reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.pre) + (size_t)row * row_bytes +
-                                                           col_off)
-                                : nullptr;
-#pragma unroll
-                for (int q = 0; q < UPL; ++q) {
-                    const uint32_t u = lane + 32u * q;
-                    if (u < units) {
-                        f2x f[P];
-                        load_h(s, k, u, f);
-                        if (RES && po != nullptr) __stcs(po + u, E::pack(f));
-                        if constexpr (kWReg) {
-#pragma unroll
-                            for (int e = 0; e < P; ++e) f[e] = f2_mul(f2_mul(f[e], scale2), wr[q][e]);
-                        } else {
-                            f2x w[P];
-                            E::unpack(wp[u], w);
-#pragma unroll
-                            for (int e = 0; e < P; ++e) f[e] = f2_mul(f2_mul(f[e], scale2), w[e]);
-                        }
-                        __stcs(yo + u, E::pack(f));
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(c.bar(kEmpty + (int)s));   // stage free for the producer
-            s = (s + 1 == nst) ? 0u : s + 1;
-            if (sent == i + 1 && sent < iters) send_next();
         }
     }
     dsb::finish(c);   // no CTA leaves while a peer may still store into its slots
@@ -295,6 +338,36 @@ struct RmsKey {
 std::mutex g_mu;
 std::map<RmsKey, int> g_occ;
 unsigned* g_err[64] = {};
+
+// cuTensorMapEncodeTiled, reached through the runtime (no link against the driver library)
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// 3-D tiled view of a [rows x hidden] row-major tensor: {ce, hidden/ce, rows}, box {ce, cps, kR}.
+bool encode_rows(CUtensorMap* m, const void* base, bool bf16, long long rows, int hidden, int ce, int cps) {
+    const EncodeTiledFn enc = encode_fn();
+    if (enc == nullptr) return false;
+    const cuuint64_t eb = bf16 ? 2 : 4;
+    const cuuint64_t dims[3] = {(cuuint64_t)ce, (cuuint64_t)(hidden / ce), (cuuint64_t)rows};
+    const cuuint64_t strides[2] = {(cuuint64_t)ce * eb, (cuuint64_t)hidden * eb};
+    const cuuint32_t box[3] = {(cuuint32_t)ce, (cuuint32_t)cps, (cuuint32_t)kR};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base),
+               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 template <int N, typename T, bool RES>
 const void* rms_fn(int upl) {
@@ -333,19 +406,28 @@ dsmem_status rms_launch(int dtype, const void* x, const void* res, const void* w
                          reinterpret_cast<uintptr_t>(res) | reinterpret_cast<uintptr_t>(pre);
     if (al & 15u) return DSMEM_ERR_INVALID_ARGUMENT;
     if (rows == 0) return DSMEM_OK;
+    if (rows > 0x7fffffffLL) return DSMEM_ERR_INVALID_ARGUMENT;   // TMA row coordinates are 32-bit
     const bool has_res = res != nullptr;
+    // TMA chunk: the widest divisor of the slice's elements within the 256-element box limit whose bytes are
+    // a multiple of 16 (16 bytes always qualifies: the slice is a multiple of 16 bytes)
+    const int slice_elems = (int)(slice / eb);
+    int ce = std::min(slice_elems, 256);
+    while (slice_elems % ce != 0 || ((size_t)ce * eb) % 16 != 0) --ce;
+    const int cps = slice_elems / ce;
     const uint32_t units = (uint32_t)(slice / 16);
     const int upl = units <= 32 ? 1 : units <= 64 ? 2 : 4;
-    // Ring depth: the deepest (<= kStages) that still lets kCtasPerSm CTAs share an SM (228 KiB of shared
+    // Ring depth: the deepest (<= kMaxStages) that still lets kCtasPerSm CTAs share an SM (228 KiB of shared
     // memory, 1 KiB reserved per CTA), else the deepest that fits one CTA; at least 2.
-    auto per_sm = [&](int st) { return (int)(kSmemPerSm / (rms_smem(n, (uint32_t)slice, has_res, st) + 1024u)); };
-    int stages = kStages;
+    auto bytes = [&](int st) { return rms_smem(n, (uint32_t)slice, has_res, st, rms_sets(st)); };
+    auto per_sm = [&](int st) { return (int)(kSmemPerSm / (bytes(st) + 1024u)); };
+    int stages = kMaxStages;
     while (stages > 2 && per_sm(stages) < kCtasPerSm) --stages;
     if (per_sm(stages) < kCtasPerSm) {
-        stages = kStages;
-        while (stages > 2 && rms_smem(n, (uint32_t)slice, has_res, stages) > dsb::kSmemLimit) --stages;
+        stages = kMaxStages;
+        while (stages > 2 && bytes(stages) > dsb::kSmemLimit) --stages;
     }
-    const uint32_t smem = rms_smem(n, (uint32_t)slice, has_res, stages);
+    const int sets = rms_sets(stages);
+    const uint32_t smem = bytes(stages);
     if (smem > dsb::kSmemLimit) return DSMEM_ERR_SMEM_LIMIT;
     const void* fn = dtype == DSMEM_BF16
                          ? (has_res ? pick<__nv_bfloat16, true>(n, upl) : pick<__nv_bfloat16, false>(n, upl))
@@ -394,6 +476,9 @@ dsmem_status rms_launch(int dtype, const void* x, const void* res, const void* w
     long long clusters = std::min<long long>(groups, resident);
     if (max_clusters > 0) clusters = std::min<long long>(clusters, max_clusters);
     cfg.gridDim = dim3((unsigned)(clusters * n), 1, 1);
+    if (!encode_rows(&a.tmx, x, dtype == DSMEM_BF16, rows, hidden, ce, cps)) return DSMEM_ERR_CUDA;
+    if (has_res && !encode_rows(&a.tmr, res, dtype == DSMEM_BF16, rows, hidden, ce, cps)) return DSMEM_ERR_CUDA;
+    a.chunks_per_slice = cps;
     a.x = x;
     a.res = res;
     a.w = w;
@@ -406,6 +491,7 @@ dsmem_status rms_launch(int dtype, const void* x, const void* res, const void* w
     a.slice_bytes = (uint32_t)slice;
     a.smem_bytes = smem;
     a.stages = stages;
+    a.sets = sets;
     void* args[] = {&a};
     return cudaLaunchKernelExC(&cfg, fn, args) == cudaSuccess ? DSMEM_OK : DSMEM_ERR_CUDA;
 }
