@@ -215,33 +215,51 @@ def rmsnorm_config3(torch, D, hbm_peak, reps=50):
     """bf16 [4096 x 4096] ~ N(0,1), w ~ N(1, 0.02), eps 1e-6, cluster 8 per row.
     The 64 MiB of traffic fits the 126 MB L2, so every launch must start from cold rows (the reference's
     flush_l2: true, roofline/workloads/clusterfusion_rmsnorm.yaml:42): launches rotate over four (x, y)
-    pairs, 256 MiB in all."""
+    pairs, 256 MiB in all. The `reps` launches are captured once in a CUDA graph and replayed: a ~15 us
+    kernel launched one call at a time from Python is bound by the host's launch rate, not by the GPU."""
     T, H, n = 4096, 4096, 8
     g = torch.Generator(device="cuda")
     g.manual_seed(0)
     # four (x, y) pairs, 256 MiB in all, used in rotation: each launch reads rows that left the L2 two
-    # launches ago, so no flush kernel is needed and launches run back to back on the stream (single-launch
-    # event intervals are too coarse for a ~15 us kernel on this driver)
+    # launches ago, so no flush kernel is needed and launches run back to back on the stream
     xs = [torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16) for _ in range(4)]
     ys = [torch.empty_like(xs[0]) for _ in range(4)]
     w = (1 + 0.02 * torch.randn(H, device="cuda", generator=g)).to(torch.bfloat16)
     for i in range(8):
         D.rmsnorm(xs[i % 4], w, 1e-6, cluster_size=n, out=ys[i % 4])
-    times = []
-    for _ in range(5):
-        torch.cuda._sleep(200_000)   # the host enqueues the first launches while the stream is busy
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
+    torch.cuda.synchronize()
+
+    def timed(run):
+        times = []
+        for _ in range(5):
+            torch.cuda._sleep(200_000)   # the host enqueues while the stream is busy
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            run()
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1) / reps)
+        return statistics.median(times)
+
+    def stream_loop():
         for i in range(reps):
             D.rmsnorm(xs[i % 4], w, 1e-6, cluster_size=n, out=ys[i % 4])
-        e1.record()
-        torch.cuda.synchronize()
-        times.append(e0.elapsed_time(e1) / reps)
+
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        stream_loop()
+    graph.replay()
+    torch.cuda.synchronize()
+    ms = timed(graph.replay)
+    ms_stream = timed(stream_loop)
     D.rmsnorm_check()
-    ms = statistics.median(times)
+    del graph
     algo = 2 * T * H * 2 + 2 * H   # read x, write y, read w (clusterfusion_rmsnorm.yaml:14 at bf16)
     gbs = algo / (ms * 1e-3) / 1e9
-    return {"workload": "rmsnorm bf16 4096x4096 cluster8, cold L2 (4 rotating buffer pairs, 256 MiB)", "kernel_us_median": round(ms * 1e3, 3),
+    return {"workload": "rmsnorm bf16 4096x4096 cluster8, cold L2 (4 rotating buffer pairs, 256 MiB)",
+            "kernel_us_median": round(ms * 1e3, 3), "timing": f"CUDA graph of {reps} back-to-back launches",
+            "stream_launch_us_median": round(ms_stream * 1e3, 3),
             "rows_per_s": round(T / (ms * 1e-3), 1), "hbm_GBps": round(gbs, 1),
             "hbm_frac": round(gbs / hbm_peak, 4), "algorithmic_bytes": algo, "reps": reps,
             "h100_reference_us": {"clusterfusion_cluster2_fp16_64x8192": 3.78}}

@@ -76,6 +76,19 @@ def test_rmsnorm_residual(cuda, orc, n):
         run(cuda, orc, dt, 129, 2048 if dt == D.Dtype.BF16 else 1024, n, residual=True, seed=3)
 
 
+@pytest.mark.parametrize("n,hidden,rows", ((2, 1024, 16 * 1000 + 5), (8, 4096, 8192 + 3), (16, 4096, 5000)))
+def test_rmsnorm_many_groups_per_cluster(cuda, orc, n, hidden, rows):
+    """Many 16-row groups per cluster (interleaved over the clusters, the last one partial), launched
+    three times in a row; a skipped group would keep the NaN the output starts with."""
+    for seed in (11, 12, 13):
+        run(cuda, orc, D.Dtype.BF16, rows, hidden, n, seed=seed)
+
+
+def test_rmsnorm_many_groups_residual(cuda, orc):
+    run(cuda, orc, D.Dtype.BF16, 9001, 2048, 8, residual=True, seed=13)
+    run(cuda, orc, D.Dtype.F32, 9001, 1024, 4, residual=True, seed=14)
+
+
 def test_rmsnorm_tp_shape(cuda, orc):
     """The hidden size of BASELINE config 5 (8192, bf16) at cluster 8 (2 KiB per CTA row slice)."""
     run(cuda, orc, D.Dtype.BF16, 64, 8192, 8, seed=5)
