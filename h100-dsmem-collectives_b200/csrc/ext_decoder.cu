@@ -9,12 +9,13 @@
 // B200 design: seven stream-ordered launches, every stage HBM-bound (weights read once per step, the KV
 // cache once per sequence):
 //   1. cluster RMSNorm of x = inp + res (ext_rmsnorm.cu: x and xn written once);
-//   2. QKV projection: one cluster per 128-feature tile, the cluster's N CTAs split K; each warp streams
-//      16 weight rows with 16-byte loads straight into mma.sync m16n8k16 A fragments (bf16, fp32
-//      accumulate; the activation K-slice sits in shared memory in fragment order, so the k order
-//      within a 32-wide block is permuted identically on both operands); the N partial tiles meet by
-//      DSMEM loads (reduce-scatter by feature pairs (i, i+64)), whose owner applies RoPE and writes q
-//      (fp32) and the new k, v into the cache;
+//   2. QKV projection on the tcgen05 tensor cores: persistent clusters, each with up to 8 tiles of 128
+//      output features; the cluster's N CTAs split K. Per CTA a TMA producer streams 128-row weight chunks
+//      (128-byte swizzle) through a 64 KiB ring, one thread issues tcgen05.mma kind::f16 (M = 128 weight
+//      rows, N = 16 batch rows, K = 16; fp32 accumulators in TMEM, 16 columns per tile), and four warps
+//      read the accumulators back (tcgen05.ld) into partial tiles; the N partial tiles meet by DSMEM loads
+//      (reduce-scatter by feature pairs (i, i+64)), whose owner applies RoPE and writes q (fp32) and the
+//      new k, v into the cache;
 //   3. decode attention: one cluster per (sequence, head), the cluster's CTAs split the keys and stream
 //      them through a 4-stage shared-memory ring of 32-key K/V tiles (16-byte cp.async); groups of 8
 //      lanes take one key of a tile at a time (16 dims a lane), online softmax in base 2; then the
@@ -24,8 +25,6 @@
 //   6. gate/up projection (as 2; a tile holds gate rows j and up rows j of the same 64 j) with the
 //      epilogue SiLU(gate) * up;
 //   7. down projection (as 2).
-// Tensor cores run through the legacy mma.sync path (the B operand is only 8-16 tokens wide, so the
-// projections stay HBM-bound on it).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -33,10 +32,12 @@
 #include <cmath>
 #include <map>
 #include <mutex>
+#include <tuple>
 
 #include "../../include/dsmem_b200.h"
 #include "../collectives/dsmem_b200_algos.cuh"
 #include "f32x2.cuh"
+#include "tmap.cuh"
 
 namespace {
 
@@ -46,13 +47,21 @@ using bf16 = __nv_bfloat16;
 
 constexpr int kHeadDim = 128;
 constexpr int kTile = 128;           // output features per cluster tile
-constexpr int kProjThreads = 256;    // 8 warps x 16 feature rows
 constexpr int kAttnThreads = 256;    // 32 groups of 8 lanes
 constexpr uint32_t kArea = 128;      // barrier area / finish flag at the start of the dynamic window
 
 enum Epi : int { kEpiQKV = 0, kEpiO = 1, kEpiGateUp = 2, kEpiDown = 3 };
 
 struct ProjArgs {
+    // tcgen05 path: the weight tile as {K, rows, 2 halves} (box {32, 64, 2}: one 32-wide K chunk of the
+    // tile's two 64-row halves) and the activations as {K, B} (box {32, 16}: rows past B read as zero),
+    // both with the 64-byte swizzle of the UMMA K-major operand layout
+    alignas(64) CUtensorMap tmw;
+    alignas(64) CUtensorMap tma;
+    int w_row0_step;      // first weight row of tile t = t * w_row0_step (the second half follows by map)
+    int tiles;            // 128-feature tiles of the projection
+    int chunk;            // K chunk width: 64 (128-byte swizzle) or 32 (64-byte swizzle) elements
+    uint32_t tmem_cols;   // TMEM columns each CTA allocates (a power of two >= 32, 16 per tile)
     const bf16* W;        // [rows][K] (nn.Linear layout)
     const bf16* act;      // [B][K]
     int K;
@@ -77,159 +86,246 @@ struct ProjArgs {
     unsigned* err;
 };
 
-__device__ __forceinline__ void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-
+// Epilogue of one feature pair (i, i + 64) of tile `tile` for batch row n: lo, hi are the cluster sums.
 template <int EPI>
-__device__ __forceinline__ long long weight_row(int tile, int lrow, int ffn) {
-    if constexpr (EPI == kEpiGateUp) return lrow < 64 ? 64LL * tile + lrow : (long long)ffn + 64LL * tile + (lrow - 64);
-    return (long long)kTile * tile + lrow;
+__device__ __forceinline__ void proj_epilogue(const ProjArgs& a, int tile, int i, int n, float lo, float hi) {
+    if constexpr (EPI == kEpiQKV) {
+        const int which = tile / a.H, head = tile % a.H;   // 0 q, 1 k, 2 v
+        float o0 = lo, o1 = hi;
+        if (which < 2) {   // NEOX rotation of the pair (i, i+64)
+            o0 = lo * a.cosv[i] - hi * a.sinv[i];
+            o1 = hi * a.cosv[i + 64] + lo * a.sinv[i + 64];
+        }
+        const size_t hd = ((size_t)n * a.H + head) * kHeadDim;
+        if (which == 0) {
+            a.q[hd + i] = o0;
+            a.q[hd + i + 64] = o1;
+        } else {
+            bf16* cache = which == 1 ? a.kc : a.vc;
+            bf16* fresh = which == 1 ? a.knew : a.vnew;
+            const size_t ci = (((size_t)n * a.cap + a.S) * a.H + head) * kHeadDim;
+            cache[ci + i] = __float2bfloat16_rn(o0);
+            cache[ci + i + 64] = __float2bfloat16_rn(o1);
+            if (fresh != nullptr) {
+                fresh[hd + i] = __float2bfloat16_rn(o0);
+                fresh[hd + i + 64] = __float2bfloat16_rn(o1);
+            }
+        }
+    } else if constexpr (EPI == kEpiO) {
+        const size_t f = (size_t)kTile * tile + i, row = (size_t)n * a.out_ld;
+        const float x0 = __bfloat162float(a.x[row + f]), x1 = __bfloat162float(a.x[row + f + 64]);
+        a.h_out[row + f] = __float2bfloat16_rn(x0 + lo);
+        a.h_out[row + f + 64] = __float2bfloat16_rn(x1 + hi);
+        if (a.o_out != nullptr) {
+            a.o_out[row + f] = __float2bfloat16_rn(lo);
+            a.o_out[row + f + 64] = __float2bfloat16_rn(hi);
+        }
+    } else if constexpr (EPI == kEpiGateUp) {
+        const float silu = lo / (1.0f + expf(-lo));
+        a.out[(size_t)n * a.out_ld + 64 * tile + i] = __float2bfloat16_rn(silu * hi);
+    } else {
+        const size_t f = (size_t)kTile * tile + i, row = (size_t)n * a.out_ld;
+        a.out[row + f] = __float2bfloat16_rn(lo);
+        a.out[row + f + 64] = __float2bfloat16_rn(hi);
+    }
 }
 
-// One cluster = one 128-feature tile; CTA `rank` of the cluster reduces K-slice `rank`.
-template <int EPI, int N, int NT>
-__global__ void __launch_bounds__(kProjThreads) proj_kernel(const ProjArgs a) {
+// --------------------------------------------------------------------------------------------------
+// tcgen05 projection: persistent clusters; cluster q takes the 128-feature tiles q, q + C, q + 2C, ..
+// (at most kTcMaxTiles), CTA `rank` reduces its share of K (whole chunks, split as evenly as they allow)
+// for every one of them on the 5th-generation tensor cores. Per CTA, 4 warps:
+//   warp 0 lane 0  loads the activation K-slice once (one TMA load per K chunk, 16 rows: rows past B read
+//                  as zero), then streams the weight rows of all its tiles, K chunks of 128 rows (one TMA
+//                  load per chunk), through a 64 KiB ring without a break between tiles;
+//   warp 1         allocates TMEM (16 fp32 columns per tile); its lane 0 issues, per chunk, tcgen05.mma
+//                  kind::f16 (M = 128 weight rows, N = 16 activation rows, K = 16 per instruction; bf16 in,
+//                  fp32 accumulate into the tile's TMEM columns) and frees the stage with tcgen05.commit;
+//   warps 0-3      after the last MMA, read every tile's 128 x 16 accumulator back (tcgen05.ld 32x32b, one
+//                  TMEM lane quarter per warp) into partial tiles in the (now idle) ring; then one cluster
+//                  barrier, then per tile the reduce-scatter by feature pairs (i, i + 64) over the cluster
+//                  (DSMEM loads, rank order) and the projection's epilogue (proj_epilogue).
+// Operands are K-major with the swizzle that matches the chunk's row length: 64-element chunks (128-byte
+// rows, 128-byte swizzle, 1024-byte 8-row atoms) when they divide K, else 32-element chunks (64-byte
+// rows and swizzle); TMA writes exactly these layouts, and K step k of a chunk starts 32 * k bytes in.
+// Measured on B200 (Llama-2-7B layer, batch 1, ncu): a 64 KiB ring beat 96 KiB, and 128-byte rows beat
+// 64-byte rows by about 10 % (fewer, longer DRAM bursts per weight row).
+constexpr int kTcThreads = 128;
+constexpr int kTcMaxStages = 12;                          // barrier ids reserved for ring stages
+constexpr uint32_t kTcRing = 64u * 1024u;                 // weight ring bytes (measured best: 96 KiB was slower)
+constexpr int kTcMaxTiles = 8;                            // partial tiles (8 KiB each) reuse the ring
+constexpr uint32_t kTcPart = 128u * 16u * 4u;
+constexpr uint32_t kTcArea = 256;   // barriers: full 0..11, act 12, done 13, TMEM word 14, empty 16..27
+constexpr int kTcFull = 0, kTcAct = 12, kTcDone = 13, kTcEmpty = 16;
+constexpr uint32_t kTcTmemWord = 112;
+static_assert(8 * (kTcDone + 2) <= (int)dsb::kFlagOff && 8 * kTcEmpty > (int)dsb::kFlagOff &&
+                  8 * (kTcEmpty + kTcMaxStages) <= (int)kTcArea && kTcMaxTiles <= 8,
+              "barrier ids overlap the flag word");
+static_assert(kTcMaxTiles * kTcPart <= kTcRing, "the partial tiles fit in the ring");
+static_assert(kTcRing / (128u * 32u * 2u) <= (uint32_t)kTcMaxStages, "ring stages have barrier ids");
+// K chunk of `cw` (64 or 32) elements: 128 weight rows of cw * 2 bytes, 16 activation rows of cw * 2 bytes.
+__host__ __device__ constexpr uint32_t tc_chunk_w(int cw) { return 128u * (uint32_t)cw * 2u; }
+__host__ __device__ constexpr uint32_t tc_chunk_a(int cw) { return 16u * (uint32_t)cw * 2u; }
+__host__ __device__ constexpr uint32_t tc_smem(int chunks, int cw) {
+    return kTcArea + 1024u + (uint32_t)chunks * tc_chunk_a(cw) + kTcRing;
+}
+
+// UMMA shared-memory descriptor of a K-major operand whose rows are `row_bytes` (128 or 64) long with the
+// matching swizzle: 8-row atoms 8 * row_bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_kmajor(uint32_t saddr, uint32_t row_bytes) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu)                // start address (16-byte units)
+           | ((uint64_t)1u << 16)                            // leading byte offset (unused by swizzled K-major)
+           | ((uint64_t)((8u * row_bytes) >> 4) << 32)       // stride byte offset between 8-row atoms
+           | ((uint64_t)1u << 46)                            // descriptor version of sm_100
+           | ((uint64_t)(row_bytes == 128u ? 2u : 4u) << 61);   // layout: 128- or 64-byte swizzle
+}
+// Instruction descriptor, kind::f16: D fp32, A and B bf16, both K-major, N = 16, M = 128.
+constexpr uint32_t kTcIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(kTcIdesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Bounded wait by one thread for barrier i to finish the phase of parity `par`.
+__device__ __forceinline__ void tc_wait(dsb::Ctx& c, int i, uint32_t par) {
+    if (c.dead) return;
+    if (mbar_try_wait_parity(c.bar(i), par)) return;
+    if (!mbar_wait_parity_until(c.bar(i), par, c.deadline)) {
+        c.dead = true;
+        dsb::report_timeout(c, i);
+    }
+}
+
+template <int EPI, int N>
+__global__ void __launch_bounds__(kTcThreads) proj_tc_kernel(const __grid_constant__ ProjArgs a) {
     dsb::Ctx c;
     dsb::ctx_init(c, a.smem_bytes, a.err, 1000000000ull);
     dsb::flag_init(c);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int tile = (int)cluster_id();
-    const int Kc = a.K / N, k0 = (int)c.rank * Kc, nkb = Kc / 32;
-    uint2* frag = c.ptr<uint2>(kArea);                              // B fragments of the K-slice
-    const uint32_t frag_bytes = (uint32_t)nkb * 2u * NT * 32u * 8u;
-    float* part = c.ptr<float>(kArea + frag_bytes);                // [128][8*NT] partial tile
-    constexpr int NB = 8 * NT;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = (int)cluster_id(), C = (int)num_clusters();
+    const int nt = a.tiles > q ? min(kTcMaxTiles, (a.tiles - q + C - 1) / C) : 0;   // this cluster's tiles
+    // this CTA's K chunks: the K / cw chunks split as evenly as whole chunks allow
+    const int cw = a.chunk, tch = a.K / cw;
+    const int ch0 = (int)c.rank * tch / N, nch = ((int)c.rank + 1) * tch / N - ch0;
+    const uint32_t cwb = tc_chunk_w(cw), cab = tc_chunk_a(cw), rowb = (uint32_t)cw * 2u;
+    const uint32_t act0 = ((c.sa + kTcArea + 1023u) & ~1023u) - c.sa;   // 1024-aligned (swizzle atoms)
+    const uint32_t ring0 = act0 + (uint32_t)((tch + N - 1) / N) * cab;  // 1024-aligned as well
+    const int nst = (int)(kTcRing / cwb);
+    constexpr int NB = 16;
 
-    // 1. the activation K-slice in fragment order: entry ((kb*2 + s)*NT + j)*32 + lane holds, for batch
-    //    row n = lane/4 + 8j, the 4 elements k0 + 32kb + 8(lane%4) + 4s .. +3 (zeros past B)
-    for (int e = threadIdx.x; e < nkb * 2 * NT * 32; e += blockDim.x) {
-        const int l = e & 31, rest = e >> 5, j = rest % NT, s = (rest / NT) & 1, kb = rest / NT / 2;
-        const int n = (l >> 2) + 8 * j;
-        const int k = k0 + kb * 32 + 8 * (l & 3) + 4 * s;
-        uint2 v = make_uint2(0u, 0u);
-        if (n < a.B) v = *reinterpret_cast<const uint2*>(a.act + (size_t)n * a.K + k);
-        frag[e] = v;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < nst; ++s) {
+            mbar_init(c.bar(kTcFull + s), 1);
+            mbar_init(c.bar(kTcEmpty + s), 1);
+        }
+        mbar_init(c.bar(kTcAct), 1);
+        mbar_init(c.bar(kTcDone), 1);
+        fence_mbar_init();
+        prefetch_tmap(&a.tmw);
+        prefetch_tmap(&a.tma);
     }
+    if (warp == 1) {   // TMEM: 16 fp32 columns per tile
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(c.sa + kTcTmemWord),
+                     "r"(a.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *c.ptr<volatile uint32_t>(kTcTmemWord);
+    c.deadline = globaltimer() + c.wait_limit;
 
-    // 2. this warp's 16 rows: lane (g, t) streams 16 B of rows g and g+8 per 32-wide k block; the k
-    //    order inside a block is permuted the same way for A (here) and B (the fragments above)
-    const int lrow0 = warp * 16 + g, lrow1 = lrow0 + 8;
-    const uint4* w0 = reinterpret_cast<const uint4*>(a.W + weight_row<EPI>(tile, lrow0, a.ffn) * a.K + k0) + t;
-    const uint4* w1 = reinterpret_cast<const uint4*>(a.W + weight_row<EPI>(tile, lrow1, a.ffn) * a.K + k0) + t;
-    float acc[NT][4];
-#pragma unroll
-    for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    const uint2* fr = frag + lane;
-    // weights for kU k-blocks at a time, the next batch's loads issued before this batch's MMAs, so a lane
-    // keeps 2 * kU (up to 4 * kU) 16-byte loads in flight
-    constexpr int kU = 4;
-    uint4 cur0[kU], cur1[kU], nxt0[kU], nxt1[kU];
-    auto fetch = [&](uint4* d0, uint4* d1, int kb0) {
-#pragma unroll
-        for (int u = 0; u < kU; ++u)
-            if (kb0 + u < nkb) {
-                d0[u] = ld_stream(w0 + 4 * (kb0 + u));
-                d1[u] = ld_stream(w1 + 4 * (kb0 + u));
-            }
-    };
-    fetch(cur0, cur1, 0);
-    for (int kb0 = 0; kb0 < nkb; kb0 += kU) {
-        if (kb0 + kU < nkb) fetch(nxt0, nxt1, kb0 + kU);
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const int kb = kb0 + u;
-            if (kb < nkb) {
-#pragma unroll
-                for (int j = 0; j < NT; ++j) {
-                    const uint2 b0 = fr[((kb * 2 + 0) * NT + j) * 32];
-                    const uint2 b1 = fr[((kb * 2 + 1) * NT + j) * 32];
-                    mma_bf16(acc[j], cur0[u].x, cur1[u].x, cur0[u].y, cur1[u].y, b0.x, b0.y);
-                    mma_bf16(acc[j], cur0[u].z, cur1[u].z, cur0[u].w, cur1[u].w, b1.x, b1.y);
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        dsb::arm(c, kTcAct, (uint32_t)nch * cab);
+        for (int i = 0; i < nch; ++i)
+            tma_load_2d(c.sa + act0 + (uint32_t)i * cab, &a.tma, (ch0 + i) * cw, 0, c.bar(kTcAct));
+        int g = 0;   // chunk index over all tiles: stage g % nst
+        for (int j = 0; j < nt && !c.dead; ++j) {
+            const int y0 = (q + j * C) * a.w_row0_step;
+            for (int i = 0; i < nch; ++i, ++g) {
+                const int s = g % nst;
+                if (g >= nst) {
+                    c.deadline = globaltimer() + c.wait_limit;
+                    tc_wait(c, kTcEmpty + s, (uint32_t)((g / nst - 1) & 1));
                 }
+                if (c.dead) break;
+                dsb::arm(c, kTcFull + s, cwb);
+                tma_load_3d(c.sa + ring0 + (uint32_t)s * cwb, &a.tmw, (ch0 + i) * cw, y0, 0, c.bar(kTcFull + s));
             }
         }
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            cur0[u] = nxt0[u];
-            cur1[u] = nxt1[u];
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------------------------ MMA issuer
+        tc_wait(c, kTcAct, 0u);
+        int g = 0;
+        for (int j = 0; j < nt && !c.dead; ++j) {
+            const uint32_t d = tmem + 16u * (uint32_t)j;   // the tile's accumulator columns
+            for (int i = 0; i < nch; ++i, ++g) {
+                const int s = g % nst;
+                c.deadline = globaltimer() + c.wait_limit;
+                tc_wait(c, kTcFull + s, (uint32_t)((g / nst) & 1));
+                if (c.dead) break;
+                tc_fence_after();
+                const uint32_t wa = c.sa + ring0 + (uint32_t)s * cwb, aa = c.sa + act0 + (uint32_t)i * cab;
+                for (int k = 0; k < cw / 16; ++k)   // K steps of 16 elements = 32 bytes into the swizzled rows
+                    umma_bf16(d, umma_desc_kmajor(wa + 32u * k, rowb), umma_desc_kmajor(aa + 32u * k, rowb),
+                              (i | k) != 0 ? 1u : 0u);
+                umma_commit(c.bar(kTcEmpty + s));   // the stage is free once these MMAs have read it
+            }
         }
+        umma_commit(c.bar(kTcDone));   // every MMA of this thread complete -> accumulators final
     }
-#pragma unroll
-    for (int j = 0; j < NT; ++j) {   // D fragment: (row g, cols 2t, 2t+1), (row g+8, cols 2t, 2t+1)
-        part[lrow0 * NB + 8 * j + 2 * t] = acc[j][0];
-        part[lrow0 * NB + 8 * j + 2 * t + 1] = acc[j][1];
-        part[lrow1 * NB + 8 * j + 2 * t] = acc[j][2];
-        part[lrow1 * NB + 8 * j + 2 * t + 1] = acc[j][3];
-    }
-    cluster_sync();   // every CTA's partial tile is complete and visible
+    __syncwarp();
 
-    // 3. reduce-scatter by feature pairs (i, i+64) over the cluster (rank order), then the epilogue
+    // ---------------------------------------------------------------------- accumulators -> partial tiles
+    c.deadline = globaltimer() + c.wait_limit;
+    tc_wait(c, kTcDone, 0u);
+    tc_fence_after();
+    const int row = 32 * warp + lane;   // TMEM lane = weight row of the tile = output feature
+    for (int j = 0; j < nt; ++j) {
+        uint32_t r[16];
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(tmem + ((uint32_t)(32 * warp) << 16) + 16u * (uint32_t)j));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        float* part = c.ptr<float>(ring0 + (uint32_t)j * kTcPart);
+#pragma unroll
+        // a CTA without K chunks (K < N chunks) issued no MMA: its partial sums are zero
+        for (int e = 0; e < 16; ++e) part[row * NB + e] = (c.dead || nch == 0) ? 0.f : __uint_as_float(r[e]);
+    }
+    tc_fence_before();
+    cluster_sync();   // every CTA's partial tiles complete and visible; every TMEM read done
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols) : "memory");
+
+    // ---------------------------------------------------------------------- reduce-scatter + epilogue
     const int npairs = 64 / N;
-    const uint32_t part_sa = c.sa + kArea + frag_bytes;
-    for (int e = threadIdx.x; e < npairs * a.B; e += blockDim.x) {
-        const int i = (int)c.rank * npairs + e / a.B, n = e % a.B;
-        float lo = 0.f, hi = 0.f;
+    for (int j = 0; j < nt; ++j) {
+        const uint32_t part_sa = c.sa + ring0 + (uint32_t)j * kTcPart;
+        for (int e = threadIdx.x; e < npairs * a.B; e += blockDim.x) {
+            const int i = (int)c.rank * npairs + e / a.B, n = e % a.B;
+            float lo = 0.f, hi = 0.f;
 #pragma unroll
-        for (int r = 0; r < N; ++r) {
-            lo += ld_cluster_f32(mapa(part_sa + (uint32_t)(i * NB + n) * 4u, (uint32_t)r));
-            hi += ld_cluster_f32(mapa(part_sa + (uint32_t)((i + 64) * NB + n) * 4u, (uint32_t)r));
-        }
-        if constexpr (EPI == kEpiQKV) {
-            const int which = tile / a.H, head = tile % a.H;   // 0 q, 1 k, 2 v
-            float o0 = lo, o1 = hi;
-            if (which < 2) {   // NEOX rotation of the pair (i, i+64)
-                o0 = lo * a.cosv[i] - hi * a.sinv[i];
-                o1 = hi * a.cosv[i + 64] + lo * a.sinv[i + 64];
+            for (int r = 0; r < N; ++r) {
+                lo += ld_cluster_f32(mapa(part_sa + (uint32_t)(i * NB + n) * 4u, (uint32_t)r));
+                hi += ld_cluster_f32(mapa(part_sa + (uint32_t)((i + 64) * NB + n) * 4u, (uint32_t)r));
             }
-            const size_t hd = ((size_t)n * a.H + head) * kHeadDim;
-            if (which == 0) {
-                a.q[hd + i] = o0;
-                a.q[hd + i + 64] = o1;
-            } else {
-                bf16* cache = which == 1 ? a.kc : a.vc;
-                bf16* fresh = which == 1 ? a.knew : a.vnew;
-                const size_t ci = (((size_t)n * a.cap + a.S) * a.H + head) * kHeadDim;
-                cache[ci + i] = __float2bfloat16_rn(o0);
-                cache[ci + i + 64] = __float2bfloat16_rn(o1);
-                if (fresh != nullptr) {
-                    fresh[hd + i] = __float2bfloat16_rn(o0);
-                    fresh[hd + i + 64] = __float2bfloat16_rn(o1);
-                }
-            }
-        } else if constexpr (EPI == kEpiO) {
-            const size_t f = (size_t)kTile * tile + i, row = (size_t)n * a.out_ld;
-            const float x0 = __bfloat162float(a.x[row + f]), x1 = __bfloat162float(a.x[row + f + 64]);
-            a.h_out[row + f] = __float2bfloat16_rn(x0 + lo);
-            a.h_out[row + f + 64] = __float2bfloat16_rn(x1 + hi);
-            if (a.o_out != nullptr) {
-                a.o_out[row + f] = __float2bfloat16_rn(lo);
-                a.o_out[row + f + 64] = __float2bfloat16_rn(hi);
-            }
-        } else if constexpr (EPI == kEpiGateUp) {
-            const float silu = lo / (1.0f + expf(-lo));
-            a.out[(size_t)n * a.out_ld + 64 * tile + i] = __float2bfloat16_rn(silu * hi);
-        } else {
-            const size_t f = (size_t)kTile * tile + i, row = (size_t)n * a.out_ld;
-            a.out[row + f] = __float2bfloat16_rn(lo);
-            a.out[row + f + 64] = __float2bfloat16_rn(hi);
+            proj_epilogue<EPI>(a, q + j * C, i, n, lo, hi);
         }
     }
-    dsb::finish(c);   // peers have finished reading my partial tile
+    dsb::finish(c);   // peers have finished reading my partial tiles
 }
 
 struct AttnArgs {
@@ -414,22 +510,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
 std::mutex g_dec_mu;
 unsigned* g_dec_err[64] = {};
 
-template <int EPI, int N>
-const void* proj_fn(int nt) {
-    return nt == 1 ? reinterpret_cast<const void*>(&proj_kernel<EPI, N, 1>)
-                   : reinterpret_cast<const void*>(&proj_kernel<EPI, N, 2>);
-}
-template <int EPI>
-const void* proj_fn_n(int n, int nt) {
-    return n == 4 ? proj_fn<EPI, 4>(nt) : proj_fn<EPI, 8>(nt);
-}
-
-cudaError_t launch_cluster(const void* fn, int n, long long clusters, uint32_t smem, cudaStream_t s, void* arg) {
+cudaError_t launch_cluster(const void* fn, int n, long long clusters, uint32_t smem, cudaStream_t s, void* arg,
+                           int threads) {
     {
         std::lock_guard<std::mutex> lock(g_dec_mu);
         static std::map<std::pair<const void*, uint32_t>, bool> done;
         if (!done[{fn, smem}]) {
             cudaError_t r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (r != cudaSuccess) return r;
+            r = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
             if (r != cudaSuccess) return r;
             done[{fn, smem}] = true;
         }
@@ -441,7 +530,7 @@ cudaError_t launch_cluster(const void* fn, int n, long long clusters, uint32_t s
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3((unsigned)(clusters * n), 1, 1);
-    cfg.blockDim = dim3(kProjThreads, 1, 1);
+    cfg.blockDim = dim3((unsigned)threads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cfg.attrs = attr;
@@ -450,16 +539,95 @@ cudaError_t launch_cluster(const void* fn, int n, long long clusters, uint32_t s
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-dsmem_status proj(int epi, int n, ProjArgs& a, long long tiles, cudaStream_t s) {
-    const int nt = a.B <= 8 ? 1 : 2;
-    const int nkb = a.K / n / 32;
-    a.smem_bytes = kArea + (uint32_t)nkb * 2u * nt * 32u * 8u + (uint32_t)kTile * 8u * nt * 4u;
+// Same block shape as the tcgen05 projection kernels and no TMEM: the occupancy query runs on it, because
+// the query counts one CTA per SM for kernels that allocate TMEM (it cannot see how many columns they take),
+// while two of these CTAs (at most 2 x 128 of the SM's 512 columns) share an SM.
+__global__ void __launch_bounds__(kTcThreads) tc_occupancy_probe() {}
+
+// Co-resident clusters of a tcgen05 projection kernel of `smem` bytes (cached per cluster size, device and
+// shared memory).
+cudaError_t tc_resident(const void* /*fn*/, int n, uint32_t smem, int* out) {
+    const void* fn = reinterpret_cast<const void*>(&tc_occupancy_probe);
+    int dev = 0;
+    cudaError_t r = cudaGetDevice(&dev);
+    if (r != cudaSuccess) return r;
+    std::lock_guard<std::mutex> lock(g_dec_mu);
+    static std::map<std::tuple<int, int, uint32_t>, int> cache;
+    auto key = std::make_tuple(n, dev, smem);
+    auto it = cache.find(key);
+    if (it != cache.end()) return (*out = it->second), cudaSuccess;
+    if ((r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess) return r;
+    // the largest shared-memory carveout, so that two CTAs share an SM (the default carveout fits one)
+    if ((r = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared)) !=
+        cudaSuccess)
+        return r;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)n;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)n, 1, 1);
+    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int res = 0;
+    if ((r = cudaOccupancyMaxActiveClusters(&res, fn, &cfg)) != cudaSuccess) return r;
+    cache[key] = res;
+    *out = res;
+    return cudaSuccess;
+}
+
+template <int EPI>
+const void* proj_tc_fn(int n) {
+    return n == 4 ? reinterpret_cast<const void*>(&proj_tc_kernel<EPI, 4>)
+                  : reinterpret_cast<const void*>(&proj_tc_kernel<EPI, 8>);
+}
+
+// Projection of a.act [B][K] by the weight rows of `tiles` 128-feature tiles on the tcgen05 kernel.
+// w_rows: rows of a.W; the tile's second 64 rows follow its first 64 by `half_rows` rows (64, or ffn for
+// the gate/up tiles, whose first half is gate rows and second half up rows), and tile t starts at row
+// t * row_step.
+dsmem_status proj(int epi, int n, ProjArgs& a, long long tiles, cudaStream_t s, long long w_rows, long long half_rows,
+                  int row_step) {
+    const cuuint64_t K = (cuuint64_t)a.K;
+    // K chunks of 64 elements (128-byte rows, 128-byte swizzle) when they divide K, else 32 (64-byte)
+    const int cw = a.K % 64 == 0 ? 64 : 32;
+    const CUtensorMapSwizzle sw = cw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    {   // weights: {K, rows reachable from a tile's first half, 2 halves}, box {cw, 64, 2}
+        const cuuint64_t dims[3] = {K, (cuuint64_t)(w_rows - half_rows), 2};
+        const cuuint64_t strides[2] = {K * 2, (cuuint64_t)half_rows * K * 2};
+        const cuuint32_t box[3] = {(cuuint32_t)cw, 64, 2};
+        if (!dsb_tmap::encode(&a.tmw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.W, dims, strides, box, sw))
+            return DSMEM_ERR_CUDA;
+    }
+    {   // activations: {K, B}, box {cw, 16}
+        const cuuint64_t dims[2] = {K, (cuuint64_t)a.B};
+        const cuuint64_t strides[1] = {K * 2};
+        const cuuint32_t box[2] = {(cuuint32_t)cw, 16};
+        if (!dsb_tmap::encode(&a.tma, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.act, dims, strides, box, sw))
+            return DSMEM_ERR_CUDA;
+    }
+    a.chunk = cw;
+    a.w_row0_step = row_step;
+    a.tiles = (int)tiles;
+    a.smem_bytes = tc_smem((a.K / cw + n - 1) / n, cw);
     if (a.smem_bytes > dsb::kSmemLimit) return DSMEM_ERR_SMEM_LIMIT;
-    const void* fn = epi == kEpiQKV ? proj_fn_n<kEpiQKV>(n, nt)
-                   : epi == kEpiO ? proj_fn_n<kEpiO>(n, nt)
-                   : epi == kEpiGateUp ? proj_fn_n<kEpiGateUp>(n, nt)
-                                       : proj_fn_n<kEpiDown>(n, nt);
-    return launch_cluster(fn, n, tiles, a.smem_bytes, s, &a) == cudaSuccess ? DSMEM_OK : DSMEM_ERR_CUDA;
+    const void* fn = epi == kEpiQKV ? proj_tc_fn<kEpiQKV>(n)
+                   : epi == kEpiO ? proj_tc_fn<kEpiO>(n)
+                   : epi == kEpiGateUp ? proj_tc_fn<kEpiGateUp>(n)
+                                       : proj_tc_fn<kEpiDown>(n);
+    // persistent clusters: as many as are co-resident, each with at most kTcMaxTiles tiles
+    int resident = 0;
+    if (tc_resident(fn, n, a.smem_bytes, &resident) != cudaSuccess || resident < 1) return DSMEM_ERR_CUDA;
+    const long long clusters = std::max<long long>(std::min<long long>(tiles, resident),
+                                                   (tiles + kTcMaxTiles - 1) / kTcMaxTiles);
+    const long long per = (tiles + clusters - 1) / clusters;
+    uint32_t cols = 32;
+    while (cols < 16u * (uint32_t)per) cols *= 2;
+    a.tmem_cols = cols;
+    return launch_cluster(fn, n, clusters, a.smem_bytes, s, &a, kTcThreads) == cudaSuccess ? DSMEM_OK : DSMEM_ERR_CUDA;
 }
 
 }  // namespace
@@ -528,7 +696,7 @@ dsmem_status dsmem_decoder_layer_launch(const dsmem_decoder_params* p, dsmem_str
     a.cosv = p->cos;
     a.sinv = p->sin;
     a.err = err;
-    if ((st = proj(kEpiQKV, n, a, 3LL * hid / kTile, s)) != DSMEM_OK) return st;
+    if ((st = proj(kEpiQKV, n, a, 3LL * hid / kTile, s, 3LL * hid, 64, kTile)) != DSMEM_OK) return st;
     // 3. attention over the S cached tokens and the new one
     {
         AttnArgs t{};
@@ -544,7 +712,7 @@ dsmem_status dsmem_decoder_layer_launch(const dsmem_decoder_params* p, dsmem_str
         t.err = err;
         const void* fn = n == 4 ? reinterpret_cast<const void*>(&attn_kernel<4>)
                                 : reinterpret_cast<const void*>(&attn_kernel<8>);
-        if (launch_cluster(fn, n, (long long)B * H, t.smem_bytes, s, &t) != cudaSuccess) return DSMEM_ERR_CUDA;
+        if (launch_cluster(fn, n, (long long)B * H, t.smem_bytes, s, &t, kAttnThreads) != cudaSuccess) return DSMEM_ERR_CUDA;
     }
     // 4. o = a Wo^T, h = x + o
     a = ProjArgs{};
@@ -557,7 +725,7 @@ dsmem_status dsmem_decoder_layer_launch(const dsmem_decoder_params* p, dsmem_str
     a.h_out = static_cast<bf16*>(p->h_out);
     a.out_ld = hid;
     a.err = err;
-    if ((st = proj(kEpiO, n, a, hid / kTile, s)) != DSMEM_OK) return st;
+    if ((st = proj(kEpiO, n, a, hid / kTile, s, hid, 64, kTile)) != DSMEM_OK) return st;
     // 5. hn = RMSNorm(h) w_post
     st = dsmem_rmsnorm_launch(DSMEM_BF16, p->h_out, p->w_post, p->eps, B, hid, 8, hn, stream);
     if (st != DSMEM_OK) return st;
@@ -571,7 +739,7 @@ dsmem_status dsmem_decoder_layer_launch(const dsmem_decoder_params* p, dsmem_str
     a.out = act;
     a.out_ld = ffn;
     a.err = err;
-    if ((st = proj(kEpiGateUp, n, a, ffn / 64, s)) != DSMEM_OK) return st;
+    if ((st = proj(kEpiGateUp, n, a, ffn / 64, s, 2LL * ffn, ffn, 64)) != DSMEM_OK) return st;
     // 7. out = act Wd^T
     a = ProjArgs{};
     a.W = static_cast<const bf16*>(p->wd);
@@ -581,7 +749,7 @@ dsmem_status dsmem_decoder_layer_launch(const dsmem_decoder_params* p, dsmem_str
     a.out = static_cast<bf16*>(p->out);
     a.out_ld = hid;
     a.err = err;
-    return proj(kEpiDown, n, a, hid / kTile, s);
+    return proj(kEpiDown, n, a, hid / kTile, s, hid, 64, kTile);
 }
 
 dsmem_status dsmem_decoder_check(int device, unsigned* error_bits) {

@@ -26,7 +26,6 @@
 //     ring depth ahead, so the exchange of later groups overlaps this group's stores; slot sets rotate over
 //     a power of two >= 2 * stages of sets (the reuse argument is at kMaxSets);
 //   * outputs leave with 16-byte streaming stores; the weight slice sits in registers when it fits.
-#include <cuda.h>   // CUtensorMap (the encoder is reached through the runtime's driver entry point)
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -36,6 +35,7 @@
 #include "../../include/dsmem_b200.h"
 #include "../collectives/dsmem_b200_algos.cuh"
 #include "f32x2.cuh"
+#include "tmap.cuh"
 
 namespace {
 
@@ -341,34 +341,14 @@ std::mutex g_mu;
 std::map<RmsKey, int> g_occ;
 unsigned* g_err[64] = {};
 
-// cuTensorMapEncodeTiled, reached through the runtime (no link against the driver library)
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            p = nullptr;
-        return reinterpret_cast<EncodeTiledFn>(p);
-    }();
-    return fn;
-}
-
 // 3-D tiled view of a [rows x hidden] row-major tensor: {ce, hidden/ce, rows}, box {ce, cps, kR}.
 bool encode_rows(CUtensorMap* m, const void* base, bool bf16, long long rows, int hidden, int ce, int cps) {
-    const EncodeTiledFn enc = encode_fn();
-    if (enc == nullptr) return false;
     const cuuint64_t eb = bf16 ? 2 : 4;
     const cuuint64_t dims[3] = {(cuuint64_t)ce, (cuuint64_t)(hidden / ce), (cuuint64_t)rows};
     const cuuint64_t strides[2] = {(cuuint64_t)ce * eb, (cuuint64_t)hidden * eb};
     const cuuint32_t box[3] = {(cuuint32_t)ce, (cuuint32_t)cps, (cuuint32_t)kR};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    return enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base),
-               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return dsb_tmap::encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base,
+                            dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 template <int N, typename T, bool RES>
