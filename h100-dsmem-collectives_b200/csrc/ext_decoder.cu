@@ -6,10 +6,11 @@
 //   x = inp + res; xn = RMSNorm(x) w_rms; qkv = xn Wqkv^T; q, k = NEOX RoPE(q, k); append k, v to the cache;
 //   a = softmax(q K^T / sqrt(D)) V over the cache and the new token; o = a Wo^T; h = x + o;
 //   hn = RMSNorm(h) w_post; out = (SiLU(hn Wg^T) * hn Wu^T) Wd^T.
-// B200 design: seven stream-ordered launches, every stage HBM-bound (weights read once per step, the KV
+// B200 design: five stream-ordered launches, every stage HBM-bound (weights read once per step, the KV
 // cache once per sequence):
-//   1. cluster RMSNorm of x = inp + res (ext_rmsnorm.cu: x and xn written once);
-//   2. QKV projection on the tcgen05 tensor cores: persistent clusters, each with up to 8 tiles of 128
+//   1-2. QKV projection on the tcgen05 tensor cores, with the RMSNorm of x = inp + res fused into its
+//      prologue (each CTA normalises its K-slice of the batch rows: partial sums of squares meet over
+//      the cluster in DSMEM; cluster 0 writes x for the residual): persistent clusters, each with up to 8 tiles of 128
 //      output features; the cluster's N CTAs split K. Per CTA a TMA producer streams 128-row weight chunks
 //      (128-byte swizzle) through a 64 KiB ring, one thread issues tcgen05.mma kind::f16 (M = 128 weight
 //      rows, N = 16 batch rows, K = 16; fp32 accumulators in TMEM, 16 columns per tile), and four warps
@@ -21,9 +22,8 @@
 //      lanes take one key of a tile at a time (16 dims a lane), online softmax in base 2; then the
 //      partial (max, sum, acc) of the 32 groups meet in shared memory and the N CTAs' in DSMEM;
 //   4. O projection (as 2) with the epilogue h = x + o;
-//   5. cluster RMSNorm of h;
-//   6. gate/up projection (as 2; a tile holds gate rows j and up rows j of the same 64 j) with the
-//      epilogue SiLU(gate) * up;
+//   5-6. gate/up projection (as 2, with the RMSNorm of h fused into its prologue; a tile holds gate rows
+//      j and up rows j of the same 64 j) with the epilogue SiLU(gate) * up;
 //   7. down projection (as 2).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -61,6 +61,14 @@ struct ProjArgs {
     int w_row0_step;      // first weight row of tile t = t * w_row0_step (the second half follows by map)
     int tiles;            // 128-feature tiles of the projection
     int chunk;            // K chunk width: 64 (128-byte swizzle) or 32 (64-byte swizzle) elements
+    // Fused RMSNorm prologue (nrm_x != nullptr): the activations are RMSNorm(h) * nrm_w with
+    // h = nrm_x (+ nrm_res) rounded to bf16, over the K = hidden features of each row; cluster 0 also
+    // writes h to nrm_h when given. act / tma are then unused.
+    const bf16* nrm_x;
+    const bf16* nrm_res;
+    const bf16* nrm_w;
+    bf16* nrm_h;
+    float nrm_eps;
     uint32_t tmem_cols;   // TMEM columns each CTA allocates (a power of two >= 32, 16 per tile)
     const bf16* W;        // [rows][K] (nn.Linear layout)
     const bf16* act;      // [B][K]
@@ -154,9 +162,13 @@ constexpr int kTcMaxStages = 12;                          // barrier ids reserve
 constexpr uint32_t kTcRing = 64u * 1024u;                 // weight ring bytes (measured best: 96 KiB was slower)
 constexpr int kTcMaxTiles = 8;                            // partial tiles (8 KiB each) reuse the ring
 constexpr uint32_t kTcPart = 128u * 16u * 4u;
-constexpr uint32_t kTcArea = 256;   // barriers: full 0..11, act 12, done 13, TMEM word 14, empty 16..27
+constexpr uint32_t kTcArea = 1024;  // barriers: full 0..11, act 12, done 13, TMEM word 14, empty 16..27,
+                                    // partial sums 28; bytes [256, 768): the fused RMSNorm's partial sums of
+                                    // squares [N][16], [768, 832): its row scales
 constexpr int kTcFull = 0, kTcAct = 12, kTcDone = 13, kTcEmpty = 16;
 constexpr uint32_t kTcTmemWord = 112;
+constexpr uint32_t kTcSsq = 256, kTcScl = 768;
+constexpr int kTcSsqBar = 28;
 static_assert(8 * (kTcDone + 2) <= (int)dsb::kFlagOff && 8 * kTcEmpty > (int)dsb::kFlagOff &&
                   8 * (kTcEmpty + kTcMaxStages) <= (int)kTcArea && kTcMaxTiles <= 8,
               "barrier ids overlap the flag word");
@@ -228,9 +240,11 @@ __global__ void __launch_bounds__(kTcThreads) proj_tc_kernel(const __grid_consta
         }
         mbar_init(c.bar(kTcAct), 1);
         mbar_init(c.bar(kTcDone), 1);
+        mbar_init(c.bar(kTcSsqBar), 1);
+        if (a.nrm_x != nullptr) dsb::arm(c, kTcSsqBar, (uint32_t)N * (uint32_t)a.B * 4u);   // every peer's partials
         fence_mbar_init();
         prefetch_tmap(&a.tmw);
-        prefetch_tmap(&a.tma);
+        if (a.nrm_x == nullptr) prefetch_tmap(&a.tma);
     }
     if (warp == 1) {   // TMEM: 16 fp32 columns per tile
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(c.sa + kTcTmemWord),
@@ -244,28 +258,132 @@ __global__ void __launch_bounds__(kTcThreads) proj_tc_kernel(const __grid_consta
     const uint32_t tmem = *c.ptr<volatile uint32_t>(kTcTmemWord);
     c.deadline = globaltimer() + c.wait_limit;
 
-    if (warp == 0 && lane == 0) {
-        // ------------------------------------------------------------------ TMA producer
-        dsb::arm(c, kTcAct, (uint32_t)nch * cab);
-        for (int i = 0; i < nch; ++i)
-            tma_load_2d(c.sa + act0 + (uint32_t)i * cab, &a.tma, (ch0 + i) * cw, 0, c.bar(kTcAct));
-        int g = 0;   // chunk index over all tiles: stage g % nst
-        for (int j = 0; j < nt && !c.dead; ++j) {
-            const int y0 = (q + j * C) * a.w_row0_step;
-            for (int i = 0; i < nch; ++i, ++g) {
-                const int s = g % nst;
-                if (g >= nst) {
-                    c.deadline = globaltimer() + c.wait_limit;
-                    tc_wait(c, kTcEmpty + s, (uint32_t)((g / nst - 1) & 1));
+    const bool fused = a.nrm_x != nullptr;
+    const int total = nt * nch;   // weight chunks of this CTA over all its tiles: chunk g = tile g / nch
+    // Issue weight chunk g into its stage (after the stage's previous chunk was consumed). Producer lane.
+    auto issue = [&](int g) {
+        const int s = g % nst, j = g / nch, i = g % nch;
+        if (g >= nst) {
+            c.deadline = globaltimer() + c.wait_limit;
+            tc_wait(c, kTcEmpty + s, (uint32_t)((g / nst - 1) & 1));
+        }
+        if (c.dead) return;
+        dsb::arm(c, kTcFull + s, cwb);
+        tma_load_3d(c.sa + ring0 + (uint32_t)s * cwb, &a.tmw, (ch0 + i) * cw, (q + j * C) * a.w_row0_step, 0,
+                    c.bar(kTcFull + s));
+    };
+    int g_issued = 0;
+    if (fused) {
+        // ------------------------------------------------------------------ fused RMSNorm prologue
+        // Every thread arrives at the cluster barrier before any bulk load is issued (an arrive issued after
+        // them waits for their bytes), then the first ring's worth of weight chunks goes out, so the loads
+        // overlap the prologue; the partial sums travel by st.async onto each peer's barrier.
+        cluster_arrive();
+        if (warp == 0 && lane == 0)
+            for (; g_issued < min(nst, total); ++g_issued) issue(g_issued);
+        const int k0 = ch0 * cw, kl = nch * cw, units = kl / 8;   // this CTA's K range, 8-element units
+        // h of unit u of row r: 8 bf16 values, x (+ res) rounded to bf16
+        auto load_h = [&](int r, int u, f2x* f) {
+            const size_t off = (size_t)r * a.K + k0 + 8 * u;
+            RmsElem<bf16>::unpack(*reinterpret_cast<const uint4*>(a.nrm_x + off), f);
+            if (a.nrm_res != nullptr) {
+                f2x rr[4];
+                RmsElem<bf16>::unpack(*reinterpret_cast<const uint4*>(a.nrm_res + off), rr);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) f[e] = f2_add(f[e], rr[e]);
+                RmsElem<bf16>::unpack(RmsElem<bf16>::pack(f), f);
+            }
+        };
+        // pass 1: h of every (row, unit) into its swizzled place in the operand (rows past B zero), and
+        // each row's partial sum of squares over this CTA's K range
+        const uint32_t sw_mask = cw == 64 ? 7u : 3u;
+        auto slot = [&](int r, int u) {   // shared-memory offset of unit u of row r in the operand
+            const int i = u / (cw / 8), uc = u % (cw / 8);
+            const uint32_t swz = (uint32_t)uc ^ (cw == 64 ? ((uint32_t)r & sw_mask) : (((uint32_t)r >> 1) & sw_mask));
+            return act0 + (uint32_t)i * cab + (uint32_t)r * rowb + 16u * swz;
+        };
+        // the weight units of pass 2 (units tid and tid + 128), loaded now so their latency overlaps pass 1
+        uint4 wreg[2];
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+            const int u = threadIdx.x + h2 * kTcThreads;
+            wreg[h2] = u < units ? *reinterpret_cast<const uint4*>(a.nrm_w + k0 + 8 * u) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        float part_ss[4];   // this warp's rows w, w + 4, w + 8, w + 12
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+            const int r = warp + 4 * rr;
+            f2x acc = 0ull;
+#pragma unroll 2
+            for (int u = lane; u < units; u += 32) {
+                uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                if (r < a.B) {
+                    f2x f[4];
+                    load_h(r, u, f);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc = f2_fma(f[e], f[e], acc);
+                    v = RmsElem<bf16>::pack(f);
+                    if (q == 0 && a.nrm_h != nullptr) *reinterpret_cast<uint4*>(a.nrm_h + (size_t)r * a.K + k0 + 8 * u) = v;
                 }
-                if (c.dead) break;
-                dsb::arm(c, kTcFull + s, cwb);
-                tma_load_3d(c.sa + ring0 + (uint32_t)s * cwb, &a.tmw, (ch0 + i) * cw, y0, 0, c.bar(kTcFull + s));
+                *c.ptr<uint4>(slot(r, u)) = v;
+            }
+            const float2 a2 = f2_split(acc);
+            float v = a2.x + a2.y;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            part_ss[rr] = v;
+        }
+        cluster_wait();   // every peer's barriers initialised (and its arrive released them)
+        // lane p < N sends this warp's row partials into slot [rank][r] of CTA p
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+            const int r = warp + 4 * rr;
+            if (r < a.B && lane < N) {
+                const uint32_t dst = mapa(c.sa + kTcSsq + 4u * ((uint32_t)c.rank * 16u + (uint32_t)r), (uint32_t)lane);
+                asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(dst),
+                             "r"(__float_as_uint(part_ss[rr])), "r"(mapa(c.bar(kTcSsqBar), (uint32_t)lane))
+                             : "memory");
             }
         }
+        c.deadline = globaltimer() + c.wait_limit;
+        tc_wait(c, kTcSsqBar, 0u);   // every peer's partials of every row
+        float* scl = c.ptr<float>(kTcScl);
+        if (threadIdx.x < a.B) {
+            const float* ssq = c.ptr<const float>(kTcSsq);
+            float t = 0.f;
+            for (int p2 = 0; p2 < N; ++p2) t += ssq[p2 * 16 + threadIdx.x];   // rank order
+            scl[threadIdx.x] = rsqrtf(fmaf(t, 1.0f / (float)a.K, a.nrm_eps));
+        }
+        __syncthreads();
+        // pass 2: y = (h * scale) * w in place, w of a unit shared by the rows
+        for (int u = threadIdx.x, h2 = 0; u < units; u += kTcThreads, ++h2) {
+            f2x w[4];
+            RmsElem<bf16>::unpack(h2 < 2 ? wreg[h2 & 1] : *reinterpret_cast<const uint4*>(a.nrm_w + k0 + 8 * u), w);
+            for (int r = 0; r < a.B; ++r) {
+                uint4* pv = c.ptr<uint4>(slot(r, u));
+                f2x f[4];
+                RmsElem<bf16>::unpack(*pv, f);
+                const f2x scale2 = f2_make(scl[r], scl[r]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) f[e] = f2_mul(f2_mul(f[e], scale2), w[e]);
+                *pv = RmsElem<bf16>::pack(f);
+            }
+        }
+        fence_proxy_async_smem();   // the operand is read by tcgen05.mma (async proxy)
+        __syncthreads();
+    }
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------------ TMA producer
+        if (!fused) {
+            dsb::arm(c, kTcAct, (uint32_t)nch * cab);
+            for (int i = 0; i < nch; ++i)
+                tma_load_2d(c.sa + act0 + (uint32_t)i * cab, &a.tma, (ch0 + i) * cw, 0, c.bar(kTcAct));
+        }
+        for (int g = g_issued; g < total && !c.dead; ++g) issue(g);
     } else if (warp == 1 && lane == 0) {
         // ------------------------------------------------------------------ MMA issuer
-        tc_wait(c, kTcAct, 0u);
+        if (!fused) tc_wait(c, kTcAct, 0u);
         int g = 0;
         for (int j = 0; j < nt && !c.dead; ++j) {
             const uint32_t d = tmem + 16u * (uint32_t)j;   // the tile's accumulator columns
@@ -602,7 +720,7 @@ dsmem_status proj(int epi, int n, ProjArgs& a, long long tiles, cudaStream_t s, 
         if (!dsb_tmap::encode(&a.tmw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.W, dims, strides, box, sw))
             return DSMEM_ERR_CUDA;
     }
-    {   // activations: {K, B}, box {cw, 16}
+    if (a.nrm_x == nullptr) {   // activations: {K, B}, box {cw, 16} (else the kernel computes them)
         const cuuint64_t dims[2] = {K, (cuuint64_t)a.B};
         const cuuint64_t strides[1] = {K * 2};
         const cuuint32_t box[2] = {(cuuint32_t)cw, 16};
@@ -636,7 +754,8 @@ extern "C" {
 
 size_t dsmem_decoder_workspace_bytes(int batch, int hidden, int ffn) {
     const size_t bh = (size_t)std::max(batch, 0) * (size_t)std::max(hidden, 0);
-    // x, xn, a, hn (bf16), q (fp32), act (bf16 [B][ffn]); each region 256-B aligned
+    // x, (spare), a, (spare) (bf16 [B][hidden]), q (fp32), act (bf16 [B][ffn]); each region 256-B aligned
+    // (the two spare regions held the normalised rows before the RMSNorms moved into the projections)
     auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
     return 4 * al(bh * 2) + al(bh * 4) + al((size_t)std::max(batch, 0) * (size_t)std::max(ffn, 0) * 2);
 }
@@ -669,20 +788,19 @@ dsmem_status dsmem_decoder_layer_launch(const dsmem_decoder_params* p, dsmem_str
     const size_t bh = (size_t)B * hid;
     unsigned char* ws = static_cast<unsigned char*>(p->workspace);
     bf16* x = reinterpret_cast<bf16*>(ws);
-    bf16* xn = reinterpret_cast<bf16*>(ws + al(bh * 2));
     bf16* att = reinterpret_cast<bf16*>(ws + 2 * al(bh * 2));
-    bf16* hn = reinterpret_cast<bf16*>(ws + 3 * al(bh * 2));
     float* q = reinterpret_cast<float*>(ws + 4 * al(bh * 2));
     bf16* act = reinterpret_cast<bf16*>(ws + 4 * al(bh * 2) + al(bh * 4));
     dsmem_status st;
 
-    // 1. x = inp + res, xn = RMSNorm(x) w_rms
-    st = dsmem_rmsnorm_residual_launch(DSMEM_BF16, p->inp, p->res, p->w_rms, p->eps, B, hid, 8, x, xn, stream);
-    if (st != DSMEM_OK) return st;
-    // 2. QKV + RoPE + cache append
+    // 1-2. x = inp + res, xn = RMSNorm(x) w_rms (fused prologue; cluster 0 writes x), QKV + RoPE + cache append
     ProjArgs a{};
     a.W = static_cast<const bf16*>(p->wqkv);
-    a.act = xn;
+    a.nrm_x = static_cast<const bf16*>(p->inp);
+    a.nrm_res = static_cast<const bf16*>(p->res);
+    a.nrm_w = static_cast<const bf16*>(p->w_rms);
+    a.nrm_h = x;
+    a.nrm_eps = p->eps;
     a.K = hid;
     a.B = B;
     a.H = H;
@@ -726,13 +844,12 @@ dsmem_status dsmem_decoder_layer_launch(const dsmem_decoder_params* p, dsmem_str
     a.out_ld = hid;
     a.err = err;
     if ((st = proj(kEpiO, n, a, hid / kTile, s, hid, 64, kTile)) != DSMEM_OK) return st;
-    // 5. hn = RMSNorm(h) w_post
-    st = dsmem_rmsnorm_launch(DSMEM_BF16, p->h_out, p->w_post, p->eps, B, hid, 8, hn, stream);
-    if (st != DSMEM_OK) return st;
-    // 6. act = SiLU(hn Wg^T) * (hn Wu^T)
+    // 5-6. hn = RMSNorm(h) w_post (fused prologue), act = SiLU(hn Wg^T) * (hn Wu^T)
     a = ProjArgs{};
     a.W = static_cast<const bf16*>(p->wgu);
-    a.act = hn;
+    a.nrm_x = static_cast<const bf16*>(p->h_out);
+    a.nrm_w = static_cast<const bf16*>(p->w_post);
+    a.nrm_eps = p->eps;
     a.K = hid;
     a.B = B;
     a.ffn = ffn;

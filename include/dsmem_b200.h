@@ -306,7 +306,7 @@ dsmem_status dsmem_tp_allreduce_rmsnorm_nccl(dsmem_nccl_comm_t comm, dsmem_dtype
  * except cos/sin; weights in nn.Linear layout [out][in]. Outputs: out [batch][hidden] (layer output),
  * h_out [batch][hidden] (the residual stream after attention), o_out (nullable, the attention-block
  * output), k_new / v_new (nullable, [batch][heads][head_dim]). The caller owns a workspace of
- * dsmem_decoder_workspace_bytes(batch, hidden, ffn) bytes. Seven stream-ordered launches; asynchronous.
+ * dsmem_decoder_workspace_bytes(batch, hidden, ffn) bytes. Five stream-ordered launches; asynchronous.
  */
 typedef struct {
     int batch, hidden, heads, head_dim, ffn;
