@@ -334,6 +334,98 @@ struct AR_RecursiveDoubling {
     }
 };
 
+// ---- mbarrier-credit ("DSMEM-native") variants: the reference's deferred design (per-round buffers and
+// barriers instead of a barrier.cluster per round, collectives/ROADMAP.md:38-45). B200 extensions: same
+// schedules and the same arithmetic (operands added in the same order) as the barrier-per-round originals.
+// Every round's bytes land in a buffer and on an mbarrier of their own (each used once per problem, between
+// the batch driver's entry and exit cluster barriers), and a CTA forwards only what it has itself received
+// or reduced, so a round waits for its one incoming copy and nothing else. No buffer that a bulk copy may
+// still be reading is written again within the problem.
+
+// Ring AllReduce (allreduce__ring__nccl.cu:25-60 schedule): reduce-scatter rounds s = 0..N-2 push chunk
+// (b - s) into slot s of CTA b+1, which adds it into its chunk (b - s - 1); all-gather rounds push the
+// owned chunk (b + 1), then each received chunk, into slot s of the all-gather area of CTA b+1. Barriers
+// 0..N-2 count the reduce-scatter rounds, N-1..2N-3 the all-gather rounds (so N <= 8).
+template <int N_, typename T_, class Op_>
+struct AR_RingCredit {
+    DSB_TRAITS(AllReduce, 2 * (N_ - 1))
+    __host__ __device__ static constexpr bool legal(uint32_t M) {
+        return N_ <= 8 && M % N_ == 0 && mult16((M / N_) * B);
+    }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) {
+        return kD0 + 1ull * M * B + 2ull * (N_ - 1) * (M / N_) * B;
+    }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t CB = (M / N_) * B, rs0 = kD0 + M * B, ag0 = rs0 + (N_ - 1) * CB, next = (c.rank + 1) % N_;
+        if (threadIdx.x == 0)
+            for (int k = 0; k < 2 * (N_ - 1); ++k) arm(c, k, CB);
+        int round = 0;
+        for (int s = 0; s < N_ - 1; ++s, ++round) {
+            const uint32_t send_c = (c.rank + N_ - s) % N_, recv_c = (c.rank + 2 * N_ - s - 1) % N_;
+            if (threadIdx.x == 0) push<N_>(c, next, rs0 + s * CB, kD0 + send_c * CB, CB, s);
+            wait(c, s);
+            reduce2<T, Op>(c, kD0 + recv_c * CB, kD0 + recv_c * CB, rs0 + s * CB, CB);
+            fence_proxy_async_smem();
+            __syncthreads();   // the reduced chunk is whole before thread 0 pushes it on
+            c.st.round(round);
+        }
+        for (int s = 0; s < N_ - 1; ++s, ++round) {
+            const uint32_t src = s == 0 ? kD0 + ((c.rank + 1) % N_) * CB : ag0 + (s - 1) * CB;
+            if (threadIdx.x == 0) push<N_>(c, next, ag0 + s * CB, src, CB, N_ - 1 + s);
+            wait(c, N_ - 1 + s);
+            c.st.round(round);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        const uint32_t C = M / N_, CB = C * B, ag0 = kD0 + M * B + (N_ - 1) * CB;
+        const uint32_t own = (c.rank + 1) % N_;
+        s2g(c, g + own * C, kD0 + own * CB, CB);
+        for (int s = 0; s < N_ - 1; ++s) s2g(c, g + ((c.rank + N_ - s) % N_) * C, ag0 + s * CB, CB);
+    }
+};
+
+// Recursive-doubling AllReduce (allreduce__recursive_doubling__clusterfusion.cu:27-52 schedule): round k
+// pushes the running vector to CTA b + 2^k into its buffer k, which then holds buffer k + running vector
+// and becomes the running vector pushed in round k + 1. log2 N buffers and barriers.
+template <int N_, typename T_, class Op_>
+struct AR_RecursiveDoublingCredit {
+    DSB_TRAITS(AllReduce, ilog2(N_))
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && N_ >= 2 && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) {
+        return kD0 + (1ull + ilog2(N_)) * M * B;
+    }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        constexpr int L = ilog2(N_);
+        const uint32_t MB = M * B;
+        if (threadIdx.x == 0)
+            for (int k = 0; k < L; ++k) arm(c, k, MB);
+        uint32_t cur = kD0;
+        for (int k = 0; k < L; ++k) {
+            const uint32_t buf = kD0 + (uint32_t)(k + 1) * MB;
+            if (threadIdx.x == 0) push<N_>(c, (c.rank + (1u << k)) % N_, buf, cur, MB, k);
+            wait(c, k);
+            reduce2<T, Op>(c, buf, cur, buf, MB);   // the reference's order: running vector + received
+            fence_proxy_async_smem();
+            __syncthreads();   // the new running vector is whole before thread 0 pushes it
+            cur = buf;
+            c.st.round(k);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + (uint32_t)ilog2(N_) * M * B, M * B);
+    }
+};
+
 // allreduce__shift_accumulate_bulk__clusterfusion.cu:29-51 (as shipped: only N == 4 reduces correctly).
 // Rounds i = 1..N-2: push the running vector to (b+i) mod N, add what arrives from (b-i).
 template <int N_, typename T_, class Op_>

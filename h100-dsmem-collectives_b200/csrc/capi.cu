@@ -48,7 +48,9 @@ const char* const kAlgNames[DSMEM_ALG_COUNT] = {"auto",
                                                 "pairwise_exchange",
                                                 "pairwise_xor",
                                                 "shift",
-                                                "rs_push_global_ag"};
+                                                "rs_push_global_ag",
+                                                "ring_credit",
+                                                "recursive_doubling_credit"};
 const char* const kDtypeNames[] = {"f32", "bf16", "i32"};
 
 // (op, alg) -> reference file stem collectives/<op>__<alg>__<src>.cu

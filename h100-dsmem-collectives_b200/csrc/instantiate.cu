@@ -37,7 +37,7 @@ enum : int {
     kPullRsPushAg = 6, kRabenseifner = 7, kOneShotPull = 8, kTwoShotPush = 9, kReduceBcastBinomial = 10,
     kAtomicAllPush = 11, kMesh2D = 12, kDirectShift = 13, kBruck = 14, kDirectPull = 15,
     kGatherBcastBinomial = 16, kRecursiveHalving = 17, kDirectPush = 18, kPairwiseExchange = 19,
-    kPairwiseXor = 20, kShift = 21, kRsPushGlobalAg = 22
+    kPairwiseXor = 20, kShift = 21, kRsPushGlobalAg = 22, kRingCredit = 23, kRecursiveDoublingCredit = 24
 };
 
 template <template <int, typename, class> class A, int N>
@@ -95,6 +95,10 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<AR_ReduceBcastBinomial>(r, kReduceBcastBinomial);
     add_all_n<AR_AtomicAllPush>(r, kAtomicAllPush);
     add_all_n<AR_Mesh2D>(r, kMesh2D);
+    add<AR_RingCredit, 2>(r, kRingCredit);   // 2 (N - 1) barriers: N <= 8
+    add<AR_RingCredit, 4>(r, kRingCredit);
+    add<AR_RingCredit, 8>(r, kRingCredit);
+    add_all_n<AR_RecursiveDoublingCredit>(r, kRecursiveDoublingCredit);
 #elif DSB_OP == 1
     add_all_n<AG_RecursiveDoubling>(r, kRecursiveDoubling);
     add_all_n<AG_DirectShift>(r, kDirectShift);

@@ -53,6 +53,8 @@ class Alg(enum.IntEnum):
     PAIRWISE_XOR = 20
     SHIFT = 21
     RS_PUSH_GLOBAL_AG = 22   # B200 extension (no reference file): DSMEM reduce-scatter, all-gather via the outputs
+    RING_CREDIT = 23         # B200 extension: ring AllReduce, a buffer + mbarrier per round (N <= 8)
+    RECURSIVE_DOUBLING_CREDIT = 24   # B200 extension: recursive doubling, a buffer + mbarrier per round
 
 
 class Dtype(enum.IntEnum):
@@ -114,6 +116,8 @@ CATALOGUE = {
 # Algorithms of this build with no reference file (selectable, and candidates for AUTO).
 EXTENSIONS = {
     (Op.ALLREDUCE, Alg.RS_PUSH_GLOBAL_AG): "allreduce__rs_push_global_ag (B200 extension)",
+    (Op.ALLREDUCE, Alg.RING_CREDIT): "allreduce__ring_credit (B200 extension)",
+    (Op.ALLREDUCE, Alg.RECURSIVE_DOUBLING_CREDIT): "allreduce__recursive_doubling_credit (B200 extension)",
 }
 
 

@@ -84,7 +84,12 @@ typedef enum {
     /* B200 extension, no reference file: allreduce whose reduce-scatter shot (the two-shot's first) runs
      * over DSMEM and whose all-gather goes straight into the N output rows (half the SM-to-SM bytes). */
     DSMEM_ALG_RS_PUSH_GLOBAL_AG = 22,                 /* allreduce                               */
-    DSMEM_ALG_COUNT = 23
+    /* B200 extensions, no reference file: the ring (N <= 8) and recursive-doubling AllReduce schedules with
+     * a buffer and an mbarrier per round instead of a barrier.cluster per round (the "DSMEM-native"
+     * variants the reference defers, collectives/ROADMAP.md:38-45); same arithmetic as the originals. */
+    DSMEM_ALG_RING_CREDIT = 23,                       /* allreduce (N = 2, 4, 8)                 */
+    DSMEM_ALG_RECURSIVE_DOUBLING_CREDIT = 24,         /* allreduce                               */
+    DSMEM_ALG_COUNT = 25
 } dsmem_alg;
 
 /* ELEM_T of the reference (float | int, main.cu:99) plus bf16. */
