@@ -1,6 +1,7 @@
 """Catalogue sweep on one B200 and the measured AUTO table.
 
     python -m dsmem_b200.sweep [--out-table autotune_b200.tsv] [--out-json sweep.json] [--dtype f32]
+                               [--ops allreduce,...] [--merge old_table.tsv]
 
 For every op x algorithm x cluster size N in {2, 4, 8, 16} x bytes per CTA P in {256 B .. 128 KiB, 192 KiB}
 (the reference sweep's grid, driver.py:156-163) that is legal, two figures:
@@ -75,7 +76,7 @@ def measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps)
             "batch_ms": round(ms, 4), "batch_algbw_GBps": round(problems * n * p / (ms * 1e-3) / 1e9, 1)}
 
 
-def run(dtypes=(Dtype.F32,), reps=60, batch_reps=5, sizes=CLUSTER_SIZES, payloads=PAYLOADS):
+def run(dtypes=(Dtype.F32,), reps=60, batch_reps=5, sizes=CLUSTER_SIZES, payloads=PAYLOADS, ops=tuple(Op)):
     import torch
 
     torch.cuda.set_device(0)
@@ -83,7 +84,7 @@ def run(dtypes=(Dtype.F32,), reps=60, batch_reps=5, sizes=CLUSTER_SIZES, payload
     buf_out = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
     buf_in.random_(0, 64)   # small positive bytes: finite floats, no overflow in int sums
     stamps = torch.zeros(reps * 16 * STAMPS_PER_RANK, dtype=torch.int64, device="cuda")
-    algs = list(CATALOGUE) + list(EXTENSIONS)
+    algs = [k for k in list(CATALOGUE) + list(EXTENSIONS) if k[0] in ops]
     results = []
     for dt in dtypes:
         for (op, alg) in algs:
@@ -99,6 +100,17 @@ def run(dtypes=(Dtype.F32,), reps=60, batch_reps=5, sizes=CLUSTER_SIZES, payload
                     r.update({"op": OP_NAMES[op], "alg": ALG_NAMES[alg], "n": n, "bytes": p, "dtype": DT_NAMES[dt]})
                     results.append(r)
     return results
+
+
+def merge(old_text, new_text, results):
+    """The lines of `old_text` whose (op, dtype) the sweep `results` did not cover, then `new_text`'s."""
+    covered = {(r["op"], r["dtype"]) for r in results}
+    keep = [ln for ln in old_text.splitlines()
+            if ln.strip() and not ln.startswith("#") and (ln.split()[0], ln.split()[3]) not in covered]
+    new = [ln for ln in new_text.splitlines() if ln.strip() and not ln.startswith("#")]
+    head = "# op cluster_size bytes_per_cta dtype alg regime  (measured on B200 by dsmem_b200.sweep)"
+    key = lambda ln: (ln.split()[0], int(ln.split()[1]), int(ln.split()[2]), ln.split()[3], ln.split()[5])
+    return "\n".join([head] + sorted(keep + new, key=key)) + "\n"
 
 
 def table(results):
@@ -124,14 +136,22 @@ def main(argv=None):
     ap.add_argument("--out-json", default="sweep_b200.json")
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16", "i32", "all"])
     ap.add_argument("--reps", type=int, default=60)
+    ap.add_argument("--ops", default="all", help="comma list of allreduce,allgather,reducescatter,alltoall")
+    ap.add_argument("--merge", default=None, help="existing table: keep its lines for the (op, dtype) not swept")
     args = ap.parse_args(argv)
     dts = {"f32": (Dtype.F32,), "bf16": (Dtype.BF16,), "i32": (Dtype.I32,),
            "all": (Dtype.F32, Dtype.BF16, Dtype.I32)}[args.dtype]
-    res = run(dts, reps=args.reps)
+    by_name = {v: k for k, v in OP_NAMES.items()}
+    ops = tuple(Op) if args.ops == "all" else tuple(by_name[o] for o in args.ops.split(","))
+    res = run(dts, reps=args.reps, ops=ops)
     with open(args.out_json, "w") as f:
         json.dump(res, f)
+    text = table(res)
+    if args.merge:
+        with open(args.merge) as f:
+            text = merge(f.read(), text, res)
     with open(args.out_table, "w") as f:
-        f.write(table(res))
+        f.write(text)
     print(f"{len(res)} configurations; table -> {args.out_table}; results -> {args.out_json}", flush=True)
 
 
