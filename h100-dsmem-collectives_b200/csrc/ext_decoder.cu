@@ -17,10 +17,11 @@
 //      read the accumulators back (tcgen05.ld) into partial tiles; the N partial tiles meet by DSMEM loads
 //      (reduce-scatter by feature pairs (i, i+64)), whose owner applies RoPE and writes q (fp32) and the
 //      new k, v into the cache;
-//   3. decode attention: one cluster per (sequence, head), the cluster's CTAs split the keys and stream
-//      them through a 4-stage shared-memory ring of 32-key K/V tiles (16-byte cp.async); groups of 8
-//      lanes take one key of a tile at a time (16 dims a lane), online softmax in base 2; then the
-//      partial (max, sum, acc) of the 32 groups meet in shared memory and the N CTAs' in DSMEM;
+//   3. decode attention: one cluster per (sequence, head), the cluster's CTAs split the keys; a producer
+//      warp streams them as 64-token K and V tiles of the head (one TMA load each) through a 3-stage ring
+//      with full/empty mbarriers; groups of 8 lanes take two keys of a tile (16 dims a lane), online
+//      softmax in base 2; then the partial (max, sum, acc) of the 32 groups meet in shared memory and the
+//      N CTAs' in DSMEM;
 //   4. O projection (as 2) with the epilogue h = x + o;
 //   5-6. gate/up projection (as 2, with the RMSNorm of h fused into its prologue; a tile holds gate rows
 //      j and up rows j of the same 64 j) with the epilogue SiLU(gate) * up;
@@ -447,6 +448,9 @@ __global__ void __launch_bounds__(kTcThreads) proj_tc_kernel(const __grid_consta
 }
 
 struct AttnArgs {
+    // the K and V caches as {D, H, cap, B} (box {D, 1, kKeyTile, 1}: one head of kKeyTile consecutive tokens)
+    alignas(64) CUtensorMap tmk;
+    alignas(64) CUtensorMap tmv;
     const float* q;       // [B][H][D], RoPE applied
     const bf16* kc;       // [B][cap][H][D]
     const bf16* vc;
@@ -459,129 +463,136 @@ struct AttnArgs {
     unsigned* err;
 };
 
-constexpr int kKeyTile = 32;                       // keys per shared-memory tile
-constexpr int kAttnStages = 4;                     // tiles in flight
-constexpr uint32_t kTileBytes = kKeyTile * kHeadDim * 2u;   // one K (or V) tile, 8 KiB
-constexpr int kAttnGroups = kAttnThreads / 8;      // 32 groups of 8 lanes, one key each per step
-// shared memory: [kArea) flag | stages x (K tile, V tile) | group partials (m, l, acc[128]) | CTA partial
+constexpr int kKeyTile = 64;                       // keys per shared-memory tile (two per group)
+constexpr int kAttnStages = 3;                     // tiles in flight
+constexpr uint32_t kTileBytes = kKeyTile * kHeadDim * 2u;   // one K (or V) tile, 16 KiB
+constexpr int kAttnGroups = kAttnThreads / 8;      // 32 groups of 8 lanes, two keys each per tile
+constexpr int kAttnCompute = kAttnThreads / 32;    // compute warps; one more warp loads the tiles
+// shared memory: [kArea) barriers (full 0..2, empty 3..5) + flag | stages x (K tile, V tile) | group
+// partials (m, l, acc[128]) | CTA partial
 constexpr uint32_t kAttnStageOff = kArea;
 constexpr uint32_t kAttnGroupOff = kAttnStageOff + kAttnStages * 2u * kTileBytes;
 constexpr uint32_t kAttnCtaOff = kAttnGroupOff + (uint32_t)kAttnGroups * (2 + kHeadDim) * 4u;
 constexpr uint32_t kAttnSmem = kAttnCtaOff + (2 + kHeadDim) * 4u;
+constexpr int kAttnFull = 0, kAttnEmpty = kAttnStages;
+static_assert(8 * 2 * kAttnStages <= (int)dsb::kFlagOff, "barrier ids overlap the flag word");
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int K>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(K) : "memory");
-}
-
-// One cluster = one (sequence, head); CTA r of N takes keys [r*L/N, (r+1)*L/N). The CTA streams its keys
-// through kAttnStages shared-memory tiles of 32 keys (16-byte cp.async, so the loads of several tiles are
-// in flight while one is consumed); 32 groups of 8 lanes each take one key of a tile per step, a lane owning
-// 16 of the 128 dimensions; online softmax in base 2. Then the 32 groups' (max, sum, acc) meet in shared
-// memory and the N CTAs' in DSMEM.
+// One cluster = one (sequence, head); CTA r of N takes keys [r*L/N, (r+1)*L/N). A producer warp streams the
+// CTA's keys as tiles of 64 tokens of this head, one TMA load for K and one for V per tile (tokens past the
+// cache read as zero), through kAttnStages shared-memory stages with full/empty mbarriers; 32 groups of 8
+// lanes take two keys of a tile each, a lane owning 16 of the 128 dimensions; online softmax in base 2.
+// Then the 32 groups' (max, sum, acc) meet in shared memory and the N CTAs' in DSMEM.
 template <int N>
-__global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads + 32) attn_kernel(const __grid_constant__ AttnArgs a) {
     dsb::Ctx c;
     dsb::ctx_init(c, a.smem_bytes, a.err, 1000000000ull);
     dsb::flag_init(c);
     const int cid = (int)cluster_id(), b = cid / a.H, head = cid % a.H;
-    const int lane = threadIdx.x & 31, sub = lane & 7, grp = threadIdx.x >> 3;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane & 7, grp = threadIdx.x >> 3;
     const unsigned gmask = 0xFFu << (lane & 24);   // the 8 lanes of this group
     const long long lo = (long long)c.rank * a.L / N, hi = (long long)(c.rank + 1) * a.L / N;
     const int tiles = (int)((hi - lo + kKeyTile - 1) / kKeyTile);
-    const size_t tok_stride = (size_t)a.H * kHeadDim;   // elements between consecutive keys
-    const bf16* kbase = a.kc + (size_t)b * a.cap * tok_stride + (size_t)head * kHeadDim;
-    const bf16* vbase = a.vc + (size_t)b * a.cap * tok_stride + (size_t)head * kHeadDim;
-    // tile t: 32 keys x 256 B for K and for V = 1024 16-byte chunks, 4 per thread
-    auto issue = [&](int t) {
-        const int st = t % kAttnStages;
-        const uint32_t kdst = c.sa + kAttnStageOff + (uint32_t)st * 2u * kTileBytes;
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int chunk = threadIdx.x + u * kAttnThreads;   // 0..511: key = chunk / 16, piece = chunk % 16
-            const int key = chunk >> 4, piece = chunk & 15;
-            const long long s = lo + (long long)t * kKeyTile + key;
-            if (s < hi) {
-                const size_t off = (size_t)s * tok_stride + (size_t)piece * 8;
-                cp_async16(kdst + (uint32_t)chunk * 16u, kbase + off);
-                cp_async16(kdst + kTileBytes + (uint32_t)chunk * 16u, vbase + off);
-            }
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < kAttnStages; ++st) {
+            mbar_init(c.bar(kAttnFull + st), 1);
+            mbar_init(c.bar(kAttnEmpty + st), kAttnCompute);
         }
-    };
-#pragma unroll
-    for (int t = 0; t < kAttnStages - 1; ++t) {
-        if (t < tiles) issue(t);
-        cp_async_commit();
+        fence_mbar_init();
     }
-    f2x q2[8];   // this lane's 16 query dimensions, pre-scaled for exp2
-    {
-        const float* qp = a.q + ((size_t)b * a.H + head) * kHeadDim + 16 * sub;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) q2[e] = f2_make(qp[2 * e] * a.scale_log2, qp[2 * e + 1] * a.scale_log2);
-    }
+    __syncthreads();
+    c.deadline = globaltimer() + c.wait_limit;
     float m = -INFINITY, l = 0.f;
     f2x acc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0ull;
-    for (int t = 0; t < tiles; ++t) {
-        if (t + kAttnStages - 1 < tiles) issue(t + kAttnStages - 1);
-        cp_async_commit();
-        cp_async_wait<kAttnStages - 1>();   // tile t landed (this thread's copies)
-        __syncthreads();                      // ... and every thread's
-        const unsigned char* kt = c.ptr<const unsigned char>(kAttnStageOff + (uint32_t)(t % kAttnStages) * 2u * kTileBytes);
-        const unsigned char* vt = kt + kTileBytes;
-        const long long s = lo + (long long)t * kKeyTile + grp;   // this group's key in the tile
-        const bool valid = s < hi;
-        const uint4* kr = reinterpret_cast<const uint4*>(kt + grp * 256 + sub * 32);
-        const uint4* vr = reinterpret_cast<const uint4*>(vt + grp * 256 + sub * 32);
-        f2x dot2 = 0ull;
-        if (valid) {
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                f2x kf[4];
-                RmsElem<bf16>::unpack(kr[u], kf);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) dot2 = f2_fma(kf[e], q2[4 * u + e], dot2);
+    if (warp == kAttnCompute) {
+        // ------------------------------------------------------------------ producer warp (lane 0)
+        if (lane == 0) {
+            prefetch_tmap(&a.tmk);
+            prefetch_tmap(&a.tmv);
+            for (int t = 0; t < tiles; ++t) {
+                const int st = t % kAttnStages;
+                if (t >= kAttnStages) {
+                    c.deadline = globaltimer() + c.wait_limit;
+                    tc_wait(c, kAttnEmpty + st, (uint32_t)((t / kAttnStages - 1) & 1));
+                }
+                if (c.dead) break;
+                const uint32_t dst = c.sa + kAttnStageOff + (uint32_t)st * 2u * kTileBytes;
+                const int tok = (int)(lo + (long long)t * kKeyTile);
+                dsb::arm(c, kAttnFull + st, 2u * kTileBytes);
+                tma_load_4d(dst, &a.tmk, 0, head, tok, b, c.bar(kAttnFull + st));
+                tma_load_4d(dst + kTileBytes, &a.tmv, 0, head, tok, b, c.bar(kAttnFull + st));
             }
         }
-        const float2 d2 = f2_split(dot2);
-        float logit = d2.x + d2.y;
-        logit += __shfl_xor_sync(gmask, logit, 1);
-        logit += __shfl_xor_sync(gmask, logit, 2);
-        logit += __shfl_xor_sync(gmask, logit, 4);
-        if (valid) {
-            const float mn = fmaxf(m, logit);
-            const float corr = exp2f(m - mn), p = exp2f(logit - mn);
-            l = l * corr + p;
-            m = mn;
-            const f2x c2 = f2_make(corr, corr), p2 = f2_make(p, p);
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------------ compute warps
+        f2x q2[8];   // this lane's 16 query dimensions, pre-scaled for exp2
+        {
+            const float* qp = a.q + ((size_t)b * a.H + head) * kHeadDim + 16 * sub;
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                f2x vf[4];
-                RmsElem<bf16>::unpack(vr[u], vf);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[4 * u + e] = f2_fma(acc[4 * u + e], c2, f2_mul(p2, vf[e]));
-            }
+            for (int e = 0; e < 8; ++e) q2[e] = f2_make(qp[2 * e] * a.scale_log2, qp[2 * e + 1] * a.scale_log2);
         }
-        __syncthreads();   // the stage is free for the tile issued next iteration
+        for (int t = 0; t < tiles; ++t) {
+            const int st = t % kAttnStages;
+            c.deadline = globaltimer() + c.wait_limit;
+            tc_wait(c, kAttnFull + st, (uint32_t)((t / kAttnStages) & 1));
+            const unsigned char* kt = c.ptr<const unsigned char>(kAttnStageOff + (uint32_t)st * 2u * kTileBytes);
+            const unsigned char* vt = kt + kTileBytes;
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+                const int key = grp + h2 * kAttnGroups;   // this group's keys in the tile
+                const long long s = lo + (long long)t * kKeyTile + key;
+                const bool valid = s < hi;
+                const uint4* kr = reinterpret_cast<const uint4*>(kt + key * 256 + sub * 32);
+                const uint4* vr = reinterpret_cast<const uint4*>(vt + key * 256 + sub * 32);
+                f2x dot2 = 0ull;
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    f2x kf[4];
+                    RmsElem<bf16>::unpack(kr[u], kf);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) dot2 = f2_fma(kf[e], q2[4 * u + e], dot2);
+                }
+                const float2 d2 = f2_split(dot2);
+                float logit = d2.x + d2.y;
+                logit += __shfl_xor_sync(gmask, logit, 1);
+                logit += __shfl_xor_sync(gmask, logit, 2);
+                logit += __shfl_xor_sync(gmask, logit, 4);
+                if (valid) {
+                    const float mn = fmaxf(m, logit);
+                    const float corr = exp2f(m - mn), p = exp2f(logit - mn);
+                    l = l * corr + p;
+                    m = mn;
+                    const f2x c2 = f2_make(corr, corr), p2 = f2_make(p, p);
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        f2x vf[4];
+                        RmsElem<bf16>::unpack(vr[u], vf);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) acc[4 * u + e] = f2_fma(acc[4 * u + e], c2, f2_mul(p2, vf[e]));
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(c.bar(kAttnEmpty + st));   // this warp is done with the stage
+        }
     }
-    cp_async_wait<0>();
+    __syncthreads();
     // the 32 groups of this CTA: (max, sum, acc) in shared memory, combined per dimension
     float* gst = c.ptr<float>(kAttnGroupOff);   // per group: m, l, acc[128]
     float* cta = c.ptr<float>(kAttnCtaOff);     // M, L, A[128] of this CTA
-    if (sub == 0) {
-        gst[grp * (2 + kHeadDim)] = m;
-        gst[grp * (2 + kHeadDim) + 1] = l;
-    }
+    if (warp < kAttnCompute) {
+        if (sub == 0) {
+            gst[grp * (2 + kHeadDim)] = m;
+            gst[grp * (2 + kHeadDim) + 1] = l;
+        }
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        const float2 v = f2_split(acc[e]);
-        gst[grp * (2 + kHeadDim) + 2 + 16 * sub + 2 * e] = v.x;
-        gst[grp * (2 + kHeadDim) + 2 + 16 * sub + 2 * e + 1] = v.y;
+        for (int e = 0; e < 8; ++e) {
+            const float2 v = f2_split(acc[e]);
+            gst[grp * (2 + kHeadDim) + 2 + 16 * sub + 2 * e] = v.x;
+            gst[grp * (2 + kHeadDim) + 2 + 16 * sub + 2 * e + 1] = v.y;
+        }
     }
     __syncthreads();
     if (threadIdx.x < kHeadDim) {
@@ -827,10 +838,28 @@ dsmem_status dsmem_decoder_layer_launch(const dsmem_decoder_params* p, dsmem_str
         t.H = H;
         t.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)kHeadDim));
         t.smem_bytes = kAttnSmem;
+        {   // caches {D, H, cap, B}, box {D, 1, kKeyTile, 1}
+            const cuuint64_t dims[4] = {(cuuint64_t)kHeadDim, (cuuint64_t)H, (cuuint64_t)p->cache_capacity, (cuuint64_t)B};
+            const cuuint64_t strides[3] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)H * kHeadDim * 2,
+                                           (cuuint64_t)p->cache_capacity * H * kHeadDim * 2};
+            const cuuint32_t box[4] = {(cuuint32_t)kHeadDim, 1, (cuuint32_t)kKeyTile, 1};
+            if (!dsb_tmap::encode(&t.tmk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, p->kcache, dims, strides, box,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
+                !dsb_tmap::encode(&t.tmv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, p->vcache, dims, strides, box,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE))
+                return DSMEM_ERR_CUDA;
+        }
         t.err = err;
-        const void* fn = n == 4 ? reinterpret_cast<const void*>(&attn_kernel<4>)
-                                : reinterpret_cast<const void*>(&attn_kernel<8>);
-        if (launch_cluster(fn, n, (long long)B * H, t.smem_bytes, s, &t, kAttnThreads) != cudaSuccess) return DSMEM_ERR_CUDA;
+        // The attention's cluster size follows the number of (sequence, head) pairs, not the projections':
+        // few pairs need the keys of each split 8 ways to fill the GPU, many pairs stream longer key ranges
+        // per CTA with less merging (measured, Llama-2-7B at S = 4096: batch 1 -> 8, 4 and 16 -> 2).
+        const int pairs = B * H;
+        const int na = pairs <= 48 ? 8 : pairs <= 96 ? 4 : 2;
+        const void* fn = na == 2 ? reinterpret_cast<const void*>(&attn_kernel<2>)
+                       : na == 4 ? reinterpret_cast<const void*>(&attn_kernel<4>)
+                                 : reinterpret_cast<const void*>(&attn_kernel<8>);
+        if (launch_cluster(fn, na, (long long)B * H, t.smem_bytes, s, &t, kAttnThreads + 32) != cudaSuccess)
+            return DSMEM_ERR_CUDA;
     }
     // 4. o = a Wo^T, h = x + o
     a = ProjArgs{};
