@@ -34,7 +34,7 @@
 namespace dsb {
 using namespace dsmem;
 
-enum class OpKind : int { AllReduce = 0, AllGather = 1, ReduceScatter = 2, AllToAll = 3 };
+enum class OpKind : int { AllReduce = 0, AllGather = 1, ReduceScatter = 2, AllToAll = 3, Broadcast = 4 };
 
 constexpr uint32_t kBarArea = 128;
 constexpr uint32_t kD0 = kBarArea;
@@ -1674,11 +1674,15 @@ struct A2A_DirectPull {
 // --------------------------------------------------------------------------- element counts per rank
 template <class A>
 __host__ __device__ constexpr uint64_t in_elems_per_rank(uint32_t M) {
-    return (A::kOp == OpKind::AllReduce || A::kOp == OpKind::AllGather) ? (uint64_t)M : (uint64_t)A::kN * M;
+    return (A::kOp == OpKind::AllReduce || A::kOp == OpKind::AllGather || A::kOp == OpKind::Broadcast)
+               ? (uint64_t)M
+               : (uint64_t)A::kN * M;
 }
 template <class A>
 __host__ __device__ constexpr uint64_t out_elems_per_rank(uint32_t M) {
-    return (A::kOp == OpKind::AllReduce || A::kOp == OpKind::ReduceScatter) ? (uint64_t)M : (uint64_t)A::kN * M;
+    return (A::kOp == OpKind::AllReduce || A::kOp == OpKind::ReduceScatter || A::kOp == OpKind::Broadcast)
+               ? (uint64_t)M
+               : (uint64_t)A::kN * M;
 }
 
 // --------------------------------------------------------------------------- drivers
@@ -1744,6 +1748,98 @@ __global__ void __launch_bounds__(256) batch_kernel(const BatchArgs a) {
     }
     finish(c);
 }
+
+// ---- Broadcast from rank 0 (B200 extension: the rooted collectives the reference's roadmap lists as
+// candidates, collectives/ROADMAP.md:268-270; binomial, direct push and direct pull, no TMA multicast).
+// Per rank M elements in and out: out of every rank = in of rank 0 (the other ranks' inputs are unused).
+
+// Rank 0 pushes its vector into every peer (N-1 bulk copies, one round).
+template <int N_, typename T_, class Op_>
+struct BC_DirectPush {
+    DSB_TRAITS(Broadcast, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        if (c.rank == 0) {
+            g2s(c, kD0, g, M * B);
+            fence_proxy_async_smem();
+        }
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B;
+        if (c.rank == 0) {
+            if (threadIdx.x == 0)
+                for (uint32_t p = 1; p < (uint32_t)N_; ++p) push<N_>(c, p, kD0, kD0, MB, 0);
+        } else {
+            if (threadIdx.x == 0) arm(c, 0, MB);
+            wait(c, 0);
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// Every rank but 0 copies rank 0's vector into its own buffer with 16-byte remote loads (one round).
+template <int N_, typename T_, class Op_>
+struct BC_DirectPull {
+    DSB_TRAITS(Broadcast, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        if (c.rank == 0) g2s(c, kD0, g, M * B);
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        if (c.rank != 0) {
+            const uint32_t n = (M * B) >> 4, src = mapa(c.sa + kD0, 0u);
+            uint4* dst = c.ptr<uint4>(kD0);
+#pragma unroll 4
+            for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = ld_cluster_v4(src + 16u * i);
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// Binomial tree: in round k the ranks below 2^k (which hold the vector) push it to rank + 2^k. Rank r > 0
+// receives once, in round floor(log2 r), on its one barrier, then forwards it in the later rounds; no
+// cluster barrier between rounds. Any N.
+template <int N_, typename T_, class Op_>
+struct BC_Binomial {
+    DSB_TRAITS(Broadcast, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        if (c.rank == 0) {
+            g2s(c, kD0, g, M * B);
+            fence_proxy_async_smem();
+        }
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B;
+        int k0 = 0;   // first round in which this rank sends
+        if (c.rank != 0) {
+            if (threadIdx.x == 0) arm(c, 0, MB);
+            wait(c, 0);
+            k0 = ilog2((int)c.rank) + 1;
+        }
+        if (threadIdx.x == 0)
+            for (int k = k0; (1 << k) < N_; ++k) {
+                const uint32_t dst = c.rank + (1u << k);
+                if (dst < (uint32_t)N_) push<N_>(c, dst, kD0, kD0, MB, 0);
+            }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
 
 // -----------------------------------------------------------------------------------------------------
 // Pipelined persistent driver of the two-shot AllReduce (allreduce__two_shot_push__trtllm.cu:23-59) for

@@ -25,7 +25,7 @@ using dsb::Registry;
 
 constexpr int kThreads = 256;
 
-const char* const kOpNames[] = {"allreduce", "allgather", "reducescatter", "alltoall"};
+const char* const kOpNames[] = {"allreduce", "allgather", "reducescatter", "alltoall", "broadcast"};
 const char* const kAlgNames[DSMEM_ALG_COUNT] = {"auto",
                                                 "ring",
                                                 "recursive_doubling",
@@ -50,7 +50,8 @@ const char* const kAlgNames[DSMEM_ALG_COUNT] = {"auto",
                                                 "shift",
                                                 "rs_push_global_ag",
                                                 "ring_credit",
-                                                "recursive_doubling_credit"};
+                                                "recursive_doubling_credit",
+                                                "binomial"};
 const char* const kDtypeNames[] = {"f32", "bf16", "i32"};
 
 // (op, alg) -> reference file stem collectives/<op>__<alg>__<src>.cu
@@ -91,12 +92,13 @@ const Stem kStems[] = {
 };
 
 // Built-in AUTO order per op when no measured table entry applies: first legal candidate wins.
-const std::vector<int> kDefaultOrder[4] = {
+const std::vector<int> kDefaultOrder[5] = {
     {DSMEM_ALG_TWO_SHOT_PUSH, DSMEM_ALG_ONE_SHOT_PULL, DSMEM_ALG_RABENSEIFNER, DSMEM_ALG_RING,
      DSMEM_ALG_RECURSIVE_DOUBLING, DSMEM_ALG_PULL_REDUCE_SCATTER_PUSH_ALLGATHER},
     {DSMEM_ALG_DIRECT_PULL, DSMEM_ALG_DIRECT_REPLICATED_PUSH, DSMEM_ALG_BRUCK, DSMEM_ALG_RING},
     {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_DIRECT_PULL, DSMEM_ALG_RECURSIVE_HALVING, DSMEM_ALG_RING},
     {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_DIRECT_PULL, DSMEM_ALG_SHIFT, DSMEM_ALG_PAIRWISE_XOR},
+    {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_BINOMIAL, DSMEM_ALG_DIRECT_PULL},
 };
 
 constexpr size_t kErrWords = 4;
@@ -148,6 +150,9 @@ const Registry& registry() {
         dsb::register_op3_dt0(s.reg);
         dsb::register_op3_dt1(s.reg);
         dsb::register_op3_dt2(s.reg);
+        dsb::register_op4_dt0(s.reg);
+        dsb::register_op4_dt1(s.reg);
+        dsb::register_op4_dt2(s.reg);
     });
     return s.reg;
 }
@@ -162,14 +167,14 @@ int elem_bytes(int dtype) { return dtype == DSMEM_BF16 ? 2 : 4; }
 
 // Elements per rank block from the payload convention; 0 if P does not divide.
 uint32_t msg_elems(int op, int dtype, int n, size_t bytes) {
-    const size_t unit = (size_t)elem_bytes(dtype) * (op == DSMEM_OP_ALLREDUCE ? 1 : (size_t)n);
+    const size_t unit = (size_t)elem_bytes(dtype) * (op == DSMEM_OP_ALLREDUCE || op == DSMEM_OP_BROADCAST ? 1 : (size_t)n);
     if (bytes == 0 || bytes % unit != 0) return 0;
     const size_t m = bytes / unit;
     return m > 0xffffffffull ? 0u : (uint32_t)m;
 }
 
 bool valid_enums(int op, int alg, int dtype, int n) {
-    return op >= 0 && op <= 3 && alg >= 0 && alg < DSMEM_ALG_COUNT && dtype >= 0 && dtype <= 2 &&
+    return op >= 0 && op <= 4 && alg >= 0 && alg < DSMEM_ALG_COUNT && dtype >= 0 && dtype <= 2 &&
            (n == 2 || n == 4 || n == 8 || n == 16);
 }
 
@@ -200,7 +205,7 @@ dsmem_status parse_table(const char* path, std::map<TuneKey, std::map<uint64_t, 
             else if (regs != "single") return DSMEM_ERR_INVALID_ARGUMENT;
         }
         int op = -1, dt = -1, alg = -1;
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 5; ++i)
             if (ops == kOpNames[i]) op = i;
         for (int i = 0; i < 3; ++i)
             if (dts == kDtypeNames[i]) dt = i;
@@ -588,7 +593,7 @@ dsmem_status dsmem_check(dsmem_stream_t stream) {
     return DSMEM_OK;
 }
 
-const char* dsmem_op_name(dsmem_op op) { return (op >= 0 && op <= 3) ? kOpNames[op] : "?"; }
+const char* dsmem_op_name(dsmem_op op) { return (op >= 0 && op <= 4) ? kOpNames[op] : "?"; }
 const char* dsmem_alg_name(dsmem_alg alg) { return (alg >= 0 && alg < DSMEM_ALG_COUNT) ? kAlgNames[alg] : "?"; }
 const char* dsmem_dtype_name(dsmem_dtype dt) { return (dt >= 0 && dt <= 2) ? kDtypeNames[dt] : "?"; }
 

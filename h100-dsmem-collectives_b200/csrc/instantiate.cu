@@ -37,7 +37,8 @@ enum : int {
     kPullRsPushAg = 6, kRabenseifner = 7, kOneShotPull = 8, kTwoShotPush = 9, kReduceBcastBinomial = 10,
     kAtomicAllPush = 11, kMesh2D = 12, kDirectShift = 13, kBruck = 14, kDirectPull = 15,
     kGatherBcastBinomial = 16, kRecursiveHalving = 17, kDirectPush = 18, kPairwiseExchange = 19,
-    kPairwiseXor = 20, kShift = 21, kRsPushGlobalAg = 22, kRingCredit = 23, kRecursiveDoublingCredit = 24
+    kPairwiseXor = 20, kShift = 21, kRsPushGlobalAg = 22, kRingCredit = 23, kRecursiveDoublingCredit = 24,
+    kBinomial = 25
 };
 
 template <template <int, typename, class> class A, int N>
@@ -112,6 +113,10 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<RS_RecursiveHalving>(r, kRecursiveHalving);
     add_all_n<RS_DirectPush>(r, kDirectPush);
     add_all_n<RS_DirectPull>(r, kDirectPull);
+#elif DSB_OP == 4
+    add_all_n<BC_DirectPush>(r, kDirectPush);
+    add_all_n<BC_DirectPull>(r, kDirectPull);
+    add_all_n<BC_Binomial>(r, kBinomial);
 #else
     add<A2A_PairwiseExchange, 2>(r, kPairwiseExchange);
     add_all_n<A2A_DirectPush>(r, kDirectPush);

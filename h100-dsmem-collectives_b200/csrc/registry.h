@@ -35,5 +35,8 @@ void register_op2_dt2(Registry&);
 void register_op3_dt0(Registry&);
 void register_op3_dt1(Registry&);
 void register_op3_dt2(Registry&);
+void register_op4_dt0(Registry&);
+void register_op4_dt1(Registry&);
+void register_op4_dt2(Registry&);
 
 }  // namespace dsb

@@ -27,6 +27,7 @@ class Op(enum.IntEnum):
     ALLGATHER = 1
     REDUCESCATTER = 2
     ALLTOALL = 3
+    BROADCAST = 4   # B200 extension (no reference file): rank 0's vector to every rank
 
 
 class Alg(enum.IntEnum):
@@ -55,6 +56,7 @@ class Alg(enum.IntEnum):
     RS_PUSH_GLOBAL_AG = 22   # B200 extension (no reference file): DSMEM reduce-scatter, all-gather via the outputs
     RING_CREDIT = 23         # B200 extension: ring AllReduce, a buffer + mbarrier per round (N <= 8)
     RECURSIVE_DOUBLING_CREDIT = 24   # B200 extension: recursive doubling, a buffer + mbarrier per round
+    BINOMIAL = 25            # broadcast (B200 extension)
 
 
 class Dtype(enum.IntEnum):
@@ -118,6 +120,9 @@ EXTENSIONS = {
     (Op.ALLREDUCE, Alg.RS_PUSH_GLOBAL_AG): "allreduce__rs_push_global_ag (B200 extension)",
     (Op.ALLREDUCE, Alg.RING_CREDIT): "allreduce__ring_credit (B200 extension)",
     (Op.ALLREDUCE, Alg.RECURSIVE_DOUBLING_CREDIT): "allreduce__recursive_doubling_credit (B200 extension)",
+    (Op.BROADCAST, Alg.DIRECT_PUSH): "broadcast__direct_push (B200 extension)",
+    (Op.BROADCAST, Alg.DIRECT_PULL): "broadcast__direct_pull (B200 extension)",
+    (Op.BROADCAST, Alg.BINOMIAL): "broadcast__binomial (B200 extension)",
 }
 
 
@@ -223,7 +228,7 @@ def _ok(status, what):
 # ----------------------------------------------------------------------------------- layouts
 def msg_elems(op, n, bytes_per_cta, dtype):
     """M (elements per rank block) of payload P (nccl-tests convention, main.cu:97)."""
-    unit = ELEM_BYTES[Dtype(dtype)] * (1 if Op(op) == Op.ALLREDUCE else n)
+    unit = ELEM_BYTES[Dtype(dtype)] * (1 if Op(op) in (Op.ALLREDUCE, Op.BROADCAST) else n)
     if bytes_per_cta % unit:
         raise ValueError(f"payload {bytes_per_cta} B is not a multiple of {unit} B")
     return bytes_per_cta // unit
@@ -234,11 +239,11 @@ def payload_bytes(op, n, m, dtype):
 
 
 def in_elems_per_rank(op, n, m):
-    return m if Op(op) in (Op.ALLREDUCE, Op.ALLGATHER) else n * m
+    return m if Op(op) in (Op.ALLREDUCE, Op.ALLGATHER, Op.BROADCAST) else n * m
 
 
 def out_elems_per_rank(op, n, m):
-    return m if Op(op) in (Op.ALLREDUCE, Op.REDUCESCATTER) else n * m
+    return m if Op(op) in (Op.ALLREDUCE, Op.REDUCESCATTER, Op.BROADCAST) else n * m
 
 
 def algorithms(op):

@@ -26,9 +26,10 @@ from . import (CATALOGUE, CLUSTER_SIZES, EXTENSIONS, STAMPS_PER_RANK, Alg, Dtype
 
 PAYLOADS = [256 << k for k in range(10)] + [196608]
 BUS = {Op.ALLREDUCE: lambda n: 2 * (n - 1) / n, Op.ALLGATHER: lambda n: (n - 1) / n,
-       Op.REDUCESCATTER: lambda n: (n - 1) / n, Op.ALLTOALL: lambda n: (n - 1) / n}
+       Op.REDUCESCATTER: lambda n: (n - 1) / n, Op.ALLTOALL: lambda n: (n - 1) / n,
+       Op.BROADCAST: lambda n: 1.0}   # nccl-tests: broadcast busbw = algbw
 OP_NAMES = {Op.ALLREDUCE: "allreduce", Op.ALLGATHER: "allgather", Op.REDUCESCATTER: "reducescatter",
-            Op.ALLTOALL: "alltoall"}
+            Op.ALLTOALL: "alltoall", Op.BROADCAST: "broadcast"}
 DT_NAMES = {Dtype.F32: "f32", Dtype.BF16: "bf16", Dtype.I32: "i32"}
 ALG_NAMES = {a: (a.name.lower() if a != Alg.MESH_2D else "2d_mesh") for a in Alg}   # dsmem_alg_name()
 # algorithms with a pipelined driver: they also run payloads whose one-piece buffers exceed shared memory

@@ -53,7 +53,10 @@ typedef enum {
     DSMEM_OP_ALLREDUCE = 0,
     DSMEM_OP_ALLGATHER = 1,
     DSMEM_OP_REDUCESCATTER = 2,
-    DSMEM_OP_ALLTOALL = 3
+    DSMEM_OP_ALLTOALL = 3,
+    /* B200 extension, no reference file: broadcast of rank 0's vector (M elements per rank in and out;
+     * P = M * sizeof(T) as for allreduce), algorithms DIRECT_PUSH, DIRECT_PULL and BINOMIAL. */
+    DSMEM_OP_BROADCAST = 4
 } dsmem_op;
 
 /* The <alg> component of the reference file names collectives/<op>__<alg>__<src>.cu
@@ -89,7 +92,8 @@ typedef enum {
      * variants the reference defers, collectives/ROADMAP.md:38-45); same arithmetic as the originals. */
     DSMEM_ALG_RING_CREDIT = 23,                       /* allreduce (N = 2, 4, 8)                 */
     DSMEM_ALG_RECURSIVE_DOUBLING_CREDIT = 24,         /* allreduce                               */
-    DSMEM_ALG_COUNT = 25
+    DSMEM_ALG_BINOMIAL = 25,                          /* broadcast                               */
+    DSMEM_ALG_COUNT = 26
 } dsmem_alg;
 
 /* ELEM_T of the reference (float | int, main.cu:99) plus bf16. */

@@ -135,10 +135,10 @@ void orc_fill_normal(int dtype, void* buf, size_t n, uint64_t seed, double mean,
 
 /* ------------------------------------------------------------------ reference */
 size_t orc_in_elems(int op, int n, size_t m) {
-    return (op == ORC_ALLREDUCE || op == ORC_ALLGATHER) ? m : (size_t)n * m;
+    return (op == ORC_ALLREDUCE || op == ORC_ALLGATHER || op == ORC_BROADCAST) ? m : (size_t)n * m;
 }
 size_t orc_out_elems(int op, int n, size_t m) {
-    return (op == ORC_ALLREDUCE || op == ORC_REDUCESCATTER) ? m : (size_t)n * m;
+    return (op == ORC_ALLREDUCE || op == ORC_REDUCESCATTER || op == ORC_BROADCAST) ? m : (size_t)n * m;
 }
 
 /* main.cu:129-149, one problem per cluster c (offsets c*N*in_elems / c*N*out_elems). */
@@ -158,6 +158,8 @@ void orc_reference(int op, int dtype, int n, size_t m, long long clusters, const
                         for (int r = 0; r < n; ++r) s += load_elem(dtype, in, ib + (size_t)r * m + i);
                         ref[ob + (size_t)b * m + i] = s;
                     }
+                } else if (op == ORC_BROADCAST) {   /* every rank gets rank 0's vector */
+                    ref[ob + (size_t)b * m + i] = load_elem(dtype, in, ib + i);
                 } else if (op == ORC_ALLGATHER) {
                     for (int r = 0; r < n; ++r)
                         ref[ob + (size_t)b * n * m + (size_t)r * m + i] = load_elem(dtype, in, ib + (size_t)r * m + i);

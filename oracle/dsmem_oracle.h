@@ -24,7 +24,7 @@ extern "C" {
 #endif
 
 enum { ORC_F32 = 0, ORC_BF16 = 1, ORC_I32 = 2 };
-enum { ORC_ALLREDUCE = 0, ORC_ALLGATHER = 1, ORC_REDUCESCATTER = 2, ORC_ALLTOALL = 3 };
+enum { ORC_ALLREDUCE = 0, ORC_ALLGATHER = 1, ORC_REDUCESCATTER = 2, ORC_ALLTOALL = 3, ORC_BROADCAST = 4 };
 
 /* mt19937_64 (Matsumoto & Nishimura 2000), the engine of the reference's pattern B. */
 typedef struct {

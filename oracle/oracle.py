@@ -16,6 +16,7 @@ LIB = HERE / "_build" / "liboracle.so"
 
 F32, BF16, I32 = 0, 1, 2
 ALLREDUCE, ALLGATHER, REDUCESCATTER, ALLTOALL = 0, 1, 2, 3
+BROADCAST = 4   # B200 extension: rank 0's vector to every rank (no reference file)
 NP_DTYPE = {F32: np.float32, BF16: np.uint16, I32: np.int32}  # bf16 carried as raw uint16 bits
 
 _lib = None
@@ -63,11 +64,11 @@ def _p(a):
 
 
 def in_elems(op, n, m):
-    return m if op in (ALLREDUCE, ALLGATHER) else n * m
+    return m if op in (ALLREDUCE, ALLGATHER, BROADCAST) else n * m
 
 
 def out_elems(op, n, m):
-    return m if op in (ALLREDUCE, REDUCESCATTER) else n * m
+    return m if op in (ALLREDUCE, REDUCESCATTER, BROADCAST) else n * m
 
 
 def pattern_a(dtype, count):

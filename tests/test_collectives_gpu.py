@@ -68,7 +68,7 @@ def run_case(torch, orc, op, alg, n, dt, p, clusters, pattern, seed=0):
     D.check()
     got = _torch_to_np(tout, dt)
     ref = orc.reference(int(op), ORC_DT[dt], n, m, clusters, host)
-    exact = pattern == "A" or dt == D.Dtype.I32 or op in (D.Op.ALLGATHER, D.Op.ALLTOALL)
+    exact = pattern == "A" or dt == D.Dtype.I32 or op in (D.Op.ALLGATHER, D.Op.ALLTOALL, D.Op.BROADCAST)
     if exact:
         bad, ma, mr = orc.check(ORC_DT[dt], got, ref, 0)
         assert bad == 0, f"{bad} inexact elements (max abs {ma})"

@@ -63,3 +63,14 @@ def test_bf16_rounding_is_nearest_even(orc):
         assert orc.lib().orc_f32_to_bf16(float(v)) == int(b)
     # 1 + 2^-8 is a tie between 1 and 1 + 2^-7: rounds to the even mantissa (1.0)
     assert orc.bf16_to_f32(bits[1]) == 1.0
+
+
+def test_broadcast_reference_is_rank0_vector(orc):
+    """The broadcast restatement (B200 extension op 4): every rank's output is rank 0's input, per cluster."""
+    n, m, clusters = 4, 8, 3
+    inp = np.arange(clusters * n * m, dtype=np.int32)
+    ref = orc.reference(4, 2, n, m, clusters, inp)
+    for c in range(clusters):
+        for b in range(n):
+            got = ref[(c * n + b) * m:(c * n + b + 1) * m]
+            assert (got == inp[c * n * m:c * n * m + m]).all()
