@@ -195,7 +195,8 @@ def test_shipped_autotune_table_parses(dsmem, tmp_path):
         lines = [ln.split() for ln in path.read_text().splitlines() if ln.strip() and not ln.startswith("#")]
         assert lines
         ops = {"allreduce": dsmem.Op.ALLREDUCE, "allgather": dsmem.Op.ALLGATHER,
-               "reducescatter": dsmem.Op.REDUCESCATTER, "alltoall": dsmem.Op.ALLTOALL}
+               "reducescatter": dsmem.Op.REDUCESCATTER, "alltoall": dsmem.Op.ALLTOALL,
+               "broadcast": dsmem.Op.BROADCAST}
         dts = {"f32": dsmem.Dtype.F32, "bf16": dsmem.Dtype.BF16, "i32": dsmem.Dtype.I32}
         pipelined = (dsmem.Alg.TWO_SHOT_PUSH, dsmem.Alg.RS_PUSH_GLOBAL_AG)
         by_name = {dsmem.lib().dsmem_alg_name(int(x)).decode(): x for x in dsmem.Alg}
