@@ -1245,6 +1245,98 @@ struct AG_Bruck {
     }
 };
 
+// ---- mbarrier-credit AllGather variants (B200 extensions; see the AllReduce credit variants): the same
+// rounds, partners and messages as the originals, each round's bytes landing in slots written once per
+// problem and on a barrier of their own, so a round waits for its one incoming copy and there is no
+// barrier.cluster between rounds.
+
+// Ring (allgather__ring__nccl.cu:19-36 schedule): round s forwards slot (b - s) to the successor's same
+// slot, on barrier s. N - 1 barriers.
+template <int N_, typename T_, class Op_>
+struct AG_RingCredit {
+    DSB_TRAITS(AllGather, N_ - 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0 + c.rank * M * B, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, next = (c.rank + 1) % N_;
+        if (threadIdx.x == 0)
+            for (int s = 0; s < N_ - 1; ++s) arm(c, s, MB);
+        for (int s = 0; s < N_ - 1; ++s) {
+            const uint32_t slot = (c.rank + N_ - s) % N_;   // own data, then what round s - 1 brought
+            if (threadIdx.x == 0) push<N_>(c, next, kD0 + slot * MB, kD0 + slot * MB, MB, s);
+            wait(c, s);
+            c.st.round(s);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, N_ * M * B);
+    }
+};
+
+// Recursive doubling (allgather__recursive_doubling__clusterfusion.cu:22-42 schedule): round k pushes
+// D[0:2^k) to (b + 2^k)'s D[2^k:2^(k+1)) on barrier k; slot k ends holding rank (b - k) mod N.
+template <int N_, typename T_, class Op_>
+struct AG_RecursiveDoublingCredit {
+    DSB_TRAITS(AllGather, ilog2(N_))
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B;
+        if (threadIdx.x == 0)
+            for (int k = 0; (1 << k) < N_; ++k) arm(c, k, (1u << k) * MB);
+        for (int k = 0; (1 << k) < N_; ++k) {
+            const uint32_t bytes = (1u << k) * MB;
+            if (threadIdx.x == 0) push<N_>(c, (c.rank + (1u << k)) % N_, kD0 + bytes, kD0, bytes, k);
+            wait(c, k);
+            c.st.round(k);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        store_rotated<N_, -1>(c, g, M * B);
+    }
+};
+
+// Bruck (allgather__bruck__mpich.cu:22-41 schedule): round k (d = 2^k) sends the first min(d, N - d) slots
+// to (b - d) mod N, which stores them at slots [d, d + cnt), on barrier k. Any N.
+template <int N_, typename T_, class Op_>
+struct AG_BruckCredit {
+    DSB_TRAITS(AllGather, ilog2(N_ - 1) + 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B;
+        if (threadIdx.x == 0)
+            for (int k = 0; (1 << k) < N_; ++k) {
+                const uint32_t d = 1u << k, cnt = (d < N_ - d) ? d : N_ - d;
+                arm(c, k, cnt * MB);
+            }
+        for (int k = 0; (1 << k) < N_; ++k) {
+            const uint32_t d = 1u << k, cnt = (d < N_ - d) ? d : N_ - d;
+            if (threadIdx.x == 0) push<N_>(c, (c.rank + N_ - d) % N_, kD0 + d * MB, kD0, cnt * MB, k);
+            wait(c, k);
+            c.st.round(k);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        store_rotated<N_, +1>(c, g, M * B);
+    }
+};
+
 // allgather__direct_pull__generic.cu:17-33. Every CTA copies slot r straight out of CTA r's input
 // with 16-B ld.shared::cluster (own slot copied locally).
 template <int N_, typename T_, class Op_>

@@ -51,7 +51,8 @@ const char* const kAlgNames[DSMEM_ALG_COUNT] = {"auto",
                                                 "rs_push_global_ag",
                                                 "ring_credit",
                                                 "recursive_doubling_credit",
-                                                "binomial"};
+                                                "binomial",
+                                                "bruck_credit"};
 const char* const kDtypeNames[] = {"f32", "bf16", "i32"};
 
 // (op, alg) -> reference file stem collectives/<op>__<alg>__<src>.cu

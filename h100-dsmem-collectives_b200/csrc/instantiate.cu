@@ -38,7 +38,7 @@ enum : int {
     kAtomicAllPush = 11, kMesh2D = 12, kDirectShift = 13, kBruck = 14, kDirectPull = 15,
     kGatherBcastBinomial = 16, kRecursiveHalving = 17, kDirectPush = 18, kPairwiseExchange = 19,
     kPairwiseXor = 20, kShift = 21, kRsPushGlobalAg = 22, kRingCredit = 23, kRecursiveDoublingCredit = 24,
-    kBinomial = 25
+    kBinomial = 25, kBruckCredit = 26
 };
 
 template <template <int, typename, class> class A, int N>
@@ -108,6 +108,9 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<AG_Bruck>(r, kBruck);
     add_all_n<AG_DirectPull>(r, kDirectPull);
     add_all_n<AG_GatherBcastBinomial>(r, kGatherBcastBinomial);
+    add_all_n<AG_RingCredit>(r, kRingCredit);
+    add_all_n<AG_RecursiveDoublingCredit>(r, kRecursiveDoublingCredit);
+    add_all_n<AG_BruckCredit>(r, kBruckCredit);
 #elif DSB_OP == 2
     add_all_n<RS_Ring>(r, kRing);
     add_all_n<RS_RecursiveHalving>(r, kRecursiveHalving);

@@ -57,6 +57,7 @@ class Alg(enum.IntEnum):
     RING_CREDIT = 23         # B200 extension: ring AllReduce, a buffer + mbarrier per round (N <= 8)
     RECURSIVE_DOUBLING_CREDIT = 24   # B200 extension: recursive doubling, a buffer + mbarrier per round
     BINOMIAL = 25            # broadcast (B200 extension)
+    BRUCK_CREDIT = 26        # B200 extension: allgather Bruck, a buffer range + mbarrier per round
 
 
 class Dtype(enum.IntEnum):
@@ -120,6 +121,9 @@ EXTENSIONS = {
     (Op.ALLREDUCE, Alg.RS_PUSH_GLOBAL_AG): "allreduce__rs_push_global_ag (B200 extension)",
     (Op.ALLREDUCE, Alg.RING_CREDIT): "allreduce__ring_credit (B200 extension)",
     (Op.ALLREDUCE, Alg.RECURSIVE_DOUBLING_CREDIT): "allreduce__recursive_doubling_credit (B200 extension)",
+    (Op.ALLGATHER, Alg.RING_CREDIT): "allgather__ring_credit (B200 extension)",
+    (Op.ALLGATHER, Alg.RECURSIVE_DOUBLING_CREDIT): "allgather__recursive_doubling_credit (B200 extension)",
+    (Op.ALLGATHER, Alg.BRUCK_CREDIT): "allgather__bruck_credit (B200 extension)",
     (Op.BROADCAST, Alg.DIRECT_PUSH): "broadcast__direct_push (B200 extension)",
     (Op.BROADCAST, Alg.DIRECT_PULL): "broadcast__direct_pull (B200 extension)",
     (Op.BROADCAST, Alg.BINOMIAL): "broadcast__binomial (B200 extension)",
