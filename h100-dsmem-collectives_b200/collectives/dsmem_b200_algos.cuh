@@ -1484,6 +1484,79 @@ struct RS_RecursiveHalving {
     }
 };
 
+// ---- mbarrier-credit ReduceScatter variants (B200 extensions; see the AllReduce credit variants).
+
+// Ring (reducescatter__ring__nccl.cu:18-37 schedule): round s pushes the partial of chunk (b - s - 1) into
+// receive slot s of the successor, which adds it into its chunk (b - s - 2); chunk b completes on b.
+// N - 1 slots and barriers.
+template <int N_, typename T_, class Op_>
+struct RS_RingCredit {
+    DSB_TRAITS(ReduceScatter, N_ - 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + (2ull * N_ - 1) * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, N_ * M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, scr0 = kD0 + N_ * MB, next = (c.rank + 1) % N_;
+        if (threadIdx.x == 0)
+            for (int s = 0; s < N_ - 1; ++s) arm(c, s, MB);
+        for (int s = 0; s < N_ - 1; ++s) {
+            const uint32_t send_c = (c.rank + 2 * N_ - s - 1) % N_, recv_c = (c.rank + 2 * N_ - s - 2) % N_;
+            if (threadIdx.x == 0) push<N_>(c, next, scr0 + s * MB, kD0 + send_c * MB, MB, s);
+            wait(c, s);
+            reduce2<T, Op>(c, kD0 + recv_c * MB, kD0 + recv_c * MB, scr0 + s * MB, MB);
+            fence_proxy_async_smem();
+            __syncthreads();   // the reduced chunk is whole before thread 0 pushes it on
+            c.st.round(s);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + c.rank * M * B, M * B);
+    }
+};
+
+// Recursive halving (reducescatter__recursive_halving__mpich.cu:19-44 schedule): XOR partners d = N/2 .. 1,
+// the half sent in round k lands in the partner's scratch range k (N*M/2, N*M/4, .. elements) on barrier k.
+template <int N_, typename T_, class Op_>
+struct RS_RecursiveHalvingCredit {
+    DSB_TRAITS(ReduceScatter, ilog2(N_))
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && N_ >= 2 && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + (2ull * N_ - 1) * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, N_ * M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        if (threadIdx.x == 0) {
+            uint32_t len = N_ * M / 2;
+            for (int k = 0; k < ilog2(N_); ++k, len /= 2) arm(c, k, len * B);
+        }
+        uint32_t lo = 0, hi = N_ * M, scr = kD0 + N_ * M * B;
+        int k = 0;
+        for (int d = N_ / 2; d >= 1; d >>= 1, ++k) {
+            const uint32_t partner = c.rank ^ (uint32_t)d, mid = (lo + hi) / 2, len = hi - mid;
+            const bool upper = (c.rank & (uint32_t)d) != 0u;
+            const uint32_t send_lo = upper ? lo : mid, keep_lo = upper ? mid : lo;
+            if (threadIdx.x == 0) push<N_>(c, partner, scr, kD0 + send_lo * B, len * B, k);
+            wait(c, k);
+            reduce2<T, Op>(c, kD0 + keep_lo * B, kD0 + keep_lo * B, scr, len * B);
+            fence_proxy_async_smem();
+            __syncthreads();   // the kept half is reduced before thread 0 sends part of it on
+            lo = keep_lo;
+            hi = keep_lo + len;
+            scr += len * B;
+            c.st.round(k);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + c.rank * M * B, M * B);
+    }
+};
+
 // reducescatter__direct_push__generic.cu:19-40. N-1 bulk pushes of chunk j into slot[b] of CTA j,
 // one aggregate barrier, local reduction.
 template <int N_, typename T_, class Op_>

@@ -52,7 +52,8 @@ const char* const kAlgNames[DSMEM_ALG_COUNT] = {"auto",
                                                 "ring_credit",
                                                 "recursive_doubling_credit",
                                                 "binomial",
-                                                "bruck_credit"};
+                                                "bruck_credit",
+                                                "recursive_halving_credit"};
 const char* const kDtypeNames[] = {"f32", "bf16", "i32"};
 
 // (op, alg) -> reference file stem collectives/<op>__<alg>__<src>.cu

@@ -38,7 +38,7 @@ enum : int {
     kAtomicAllPush = 11, kMesh2D = 12, kDirectShift = 13, kBruck = 14, kDirectPull = 15,
     kGatherBcastBinomial = 16, kRecursiveHalving = 17, kDirectPush = 18, kPairwiseExchange = 19,
     kPairwiseXor = 20, kShift = 21, kRsPushGlobalAg = 22, kRingCredit = 23, kRecursiveDoublingCredit = 24,
-    kBinomial = 25, kBruckCredit = 26
+    kBinomial = 25, kBruckCredit = 26, kRecursiveHalvingCredit = 27
 };
 
 template <template <int, typename, class> class A, int N>
@@ -116,6 +116,8 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<RS_RecursiveHalving>(r, kRecursiveHalving);
     add_all_n<RS_DirectPush>(r, kDirectPush);
     add_all_n<RS_DirectPull>(r, kDirectPull);
+    add_all_n<RS_RingCredit>(r, kRingCredit);
+    add_all_n<RS_RecursiveHalvingCredit>(r, kRecursiveHalvingCredit);
 #elif DSB_OP == 4
     add_all_n<BC_DirectPush>(r, kDirectPush);
     add_all_n<BC_DirectPull>(r, kDirectPull);

@@ -58,6 +58,7 @@ class Alg(enum.IntEnum):
     RECURSIVE_DOUBLING_CREDIT = 24   # B200 extension: recursive doubling, a buffer + mbarrier per round
     BINOMIAL = 25            # broadcast (B200 extension)
     BRUCK_CREDIT = 26        # B200 extension: allgather Bruck, a buffer range + mbarrier per round
+    RECURSIVE_HALVING_CREDIT = 27   # B200 extension: reducescatter halving, a buffer + mbarrier per round
 
 
 class Dtype(enum.IntEnum):
@@ -124,6 +125,8 @@ EXTENSIONS = {
     (Op.ALLGATHER, Alg.RING_CREDIT): "allgather__ring_credit (B200 extension)",
     (Op.ALLGATHER, Alg.RECURSIVE_DOUBLING_CREDIT): "allgather__recursive_doubling_credit (B200 extension)",
     (Op.ALLGATHER, Alg.BRUCK_CREDIT): "allgather__bruck_credit (B200 extension)",
+    (Op.REDUCESCATTER, Alg.RING_CREDIT): "reducescatter__ring_credit (B200 extension)",
+    (Op.REDUCESCATTER, Alg.RECURSIVE_HALVING_CREDIT): "reducescatter__recursive_halving_credit (B200 extension)",
     (Op.BROADCAST, Alg.DIRECT_PUSH): "broadcast__direct_push (B200 extension)",
     (Op.BROADCAST, Alg.DIRECT_PULL): "broadcast__direct_pull (B200 extension)",
     (Op.BROADCAST, Alg.BINOMIAL): "broadcast__binomial (B200 extension)",

@@ -90,11 +90,12 @@ typedef enum {
     /* B200 extensions, no reference file: the ring (N <= 8) and recursive-doubling AllReduce schedules with
      * a buffer and an mbarrier per round instead of a barrier.cluster per round (the "DSMEM-native"
      * variants the reference defers, collectives/ROADMAP.md:38-45); same arithmetic as the originals. */
-    DSMEM_ALG_RING_CREDIT = 23,                       /* allreduce (N = 2, 4, 8), allgather      */
+    DSMEM_ALG_RING_CREDIT = 23,                       /* allreduce (N <= 8), allgather, reducescatter */
     DSMEM_ALG_RECURSIVE_DOUBLING_CREDIT = 24,         /* allreduce, allgather                    */
     DSMEM_ALG_BINOMIAL = 25,                          /* broadcast                               */
     DSMEM_ALG_BRUCK_CREDIT = 26,                      /* allgather (Bruck, a barrier per round)  */
-    DSMEM_ALG_COUNT = 27
+    DSMEM_ALG_RECURSIVE_HALVING_CREDIT = 27,          /* reducescatter                           */
+    DSMEM_ALG_COUNT = 28
 } dsmem_alg;
 
 /* ELEM_T of the reference (float | int, main.cu:99) plus bf16. */
