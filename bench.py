@@ -385,6 +385,8 @@ def run_ours(args, rank, world, local):
     if rank == 0 and not args.no_extras:
         extras["single_cluster"] = single_cluster_latency(torch, D)
         extras["rmsnorm"] = rmsnorm_config3(torch, D, hbm_peak)
+        # ceilings beyond DSMEM and HBM (tcgen05 MMA, L2, shared memory), 1 / slope over two work amounts
+        extras["ceilings_sm100"] = D.sm100_ceilings(reps=3)
 
     cpu = None
     if rank == 0 and world == 1:

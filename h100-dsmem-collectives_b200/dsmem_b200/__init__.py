@@ -191,6 +191,11 @@ def lib():
         "dsmem_rmsnorm_residual_launch": (c_int, [c_int, c_vp, c_vp, c_vp, ctypes.c_float, c_ll, c_int, c_int,
                                                   c_vp, c_vp, c_vp]),
         "dsmem_rmsnorm_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
+        "dsmem_ceiling_tcgen05": (c_int, [c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double),
+                                          ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_int)]),
+        "dsmem_ceiling_l2_bw": (c_int, [ctypes.c_longlong, c_int, c_int, ctypes.POINTER(ctypes.c_double),
+                                        ctypes.POINTER(ctypes.c_double)]),
+        "dsmem_ceiling_smem_bw": (c_int, [c_int, c_int, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]),
         "dsmem_ceiling_dsmem_bw": (c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double),
                                            ctypes.POINTER(c_ll), ctypes.POINTER(c_int)]),
         "dsmem_version": (ctypes.c_char_p, []),
@@ -482,6 +487,39 @@ def dsmem_bandwidth_peak(mode, cluster_size, passes=(4, 8, 16, 32), reps=5, ctas
     mx, my = sum(xs) / len(xs), sum(ys) / len(ys)
     slope = sum((x - mx) * (y - my) for x, y in zip(xs, ys)) / sum((x - mx) ** 2 for x in xs)
     return (1.0 / slope / 1e9 if slope > 0 else float("nan")), pts
+
+
+def _slope_rate(points):
+    """1 / slope of time (s) over work, least squares over (work, ms) points."""
+    xs = [w for (w, _) in points]
+    ys = [ms * 1e-3 for (_, ms) in points]
+    mx, my = sum(xs) / len(xs), sum(ys) / len(ys)
+    slope = sum((x - mx) * (y - my) for x, y in zip(xs, ys)) / sum((x - mx) ** 2 for x in xs)
+    return 1.0 / slope if slope > 0 else float("nan")
+
+
+def sm100_ceilings(reps=5):
+    """Ceilings beyond DSMEM and HBM (1 / slope): tcgen05 bf16 MMA TFLOP/s (M 128, N 256), L2 read GB/s
+    (64 MiB buffer) and shared-memory read GB/s, GPU-wide."""
+    out = {}
+    ms, work, ctas = ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
+    pts = []
+    for iters in (256, 1024):
+        _ok(lib().dsmem_ceiling_tcgen05(256, iters, reps, ctypes.byref(ms), ctypes.byref(work), ctypes.byref(ctas)),
+            "dsmem_ceiling_tcgen05")
+        pts.append((work.value, ms.value))
+    out["tcgen05_bf16_m128n256_TFLOPs"] = round(_slope_rate(pts) / 1e12, 1)
+    pts = []
+    for passes in (4, 16):
+        _ok(lib().dsmem_ceiling_l2_bw(64 << 20, passes, reps, ctypes.byref(ms), ctypes.byref(work)), "dsmem_ceiling_l2_bw")
+        pts.append((work.value, ms.value))
+    out["l2_read_GBps"] = round(_slope_rate(pts) / 1e9, 1)
+    pts = []
+    for passes in (64, 256):
+        _ok(lib().dsmem_ceiling_smem_bw(passes, reps, ctypes.byref(ms), ctypes.byref(work)), "dsmem_ceiling_smem_bw")
+        pts.append((work.value, ms.value))
+    out["smem_read_GBps"] = round(_slope_rate(pts) / 1e9, 1)
+    return out
 
 
 def version():

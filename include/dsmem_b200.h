@@ -229,6 +229,23 @@ dsmem_status dsmem_ceiling_dsmem_bw(int mode, int cluster_size, int ctas_per_sm,
                                     double* ms_median, long long* bytes_per_launch, int* clusters);
 
 /*
+ * Ceilings beyond DSMEM and HBM, for hierarchical rooflines (the reference's ceiling suite,
+ * roofline/harness/ceilings and roofline/docs/DESIGN.md:28-48, measures DSMEM and HBM on H100; these are
+ * sm_100a additions). Each returns the median event time of `reps` launches and the work of one launch;
+ * the caller fits 1 / slope over two or more work amounts.
+ *   dsmem_ceiling_tcgen05: one CTA per SM issues iters x 4 tcgen05.mma kind::f16 (M = 128, N = n in
+ *     {64, 128, 256}, K = 16, bf16 operands in shared memory, fp32 accumulator in TMEM); flops = 2*M*N*K
+ *     per instruction.
+ *   dsmem_ceiling_l2_bw: a full grid reads a `bytes` buffer (it should fit the L2) `passes` times with
+ *     16-byte L2 loads.
+ *   dsmem_ceiling_smem_bw: one CTA per SM (1024 threads) reads a 96 KiB shared-memory tile `passes` times.
+ */
+dsmem_status dsmem_ceiling_tcgen05(int n, int iters, int reps, double* ms_median, double* flops_per_launch,
+                                   int* ctas);
+dsmem_status dsmem_ceiling_l2_bw(long long bytes, int passes, int reps, double* ms_median, double* bytes_per_launch);
+dsmem_status dsmem_ceiling_smem_bw(int passes, int reps, double* ms_median, double* bytes_per_launch);
+
+/*
  * Batch two-shot AllReduce that allocates no device memory. No counterpart in the reference (whose
  * harness allocates every buffer itself); it exists for callers that cannot call cudaMalloc at this
  * point: code running while a stream is captured into a CUDA graph, frameworks whose caching allocator
