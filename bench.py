@@ -294,8 +294,9 @@ def run_ours(args, rank, world, local):
     n, p = CLUSTER_N, args.payload
     m = p // 4
     alg = D.Alg[args.alg.upper()] if args.alg.lower() != "auto" else D.Alg.AUTO
-    resolved = D.autotune_pick(D.Op.ALLREDUCE, D.Dtype.F32, n, p) if alg == D.Alg.AUTO else alg
     problems = BATCH_BYTES // (n * p)
+    # AUTO picks per launch shape: the batch regime of the table for a launch of `problems` clusters.
+    resolved = D.autotune_pick(D.Op.ALLREDUCE, D.Dtype.F32, n, p, problems) if alg == D.Alg.AUTO else alg
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
     tin = torch.rand(problems * n * m, device=dev, generator=g) * 2 - 1
