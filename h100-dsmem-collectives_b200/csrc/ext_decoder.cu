@@ -38,6 +38,7 @@
 #include "../../include/dsmem_b200.h"
 #include "../collectives/dsmem_b200_algos.cuh"
 #include "f32x2.cuh"
+#include "smem_attr.cuh"
 #include "tmap.cuh"
 
 namespace {
@@ -641,17 +642,9 @@ unsigned* g_dec_err[64] = {};
 
 cudaError_t launch_cluster(const void* fn, int n, long long clusters, uint32_t smem, cudaStream_t s, void* arg,
                            int threads) {
-    {
-        std::lock_guard<std::mutex> lock(g_dec_mu);
-        static std::map<std::pair<const void*, uint32_t>, bool> done;
-        if (!done[{fn, smem}]) {
-            cudaError_t r = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (r != cudaSuccess) return r;
-            r = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-            if (r != cudaSuccess) return r;
-            done[{fn, smem}] = true;
-        }
-    }
+    int dev = 0;
+    cudaError_t r = cudaGetDevice(&dev);
+    if (r != cudaSuccess || (r = dsb_attr::ensure_smem(fn, dev, smem)) != cudaSuccess) return r;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -35,6 +35,7 @@
 #include "../../include/dsmem_b200.h"
 #include "../collectives/dsmem_b200_algos.cuh"
 #include "f32x2.cuh"
+#include "smem_attr.cuh"
 #include "tmap.cuh"
 
 namespace {
@@ -435,16 +436,10 @@ dsmem_status rms_launch(int dtype, const void* x, const void* res, const void* w
             if (cudaMalloc(&g_err[dev], 4 * sizeof(unsigned)) != cudaSuccess) return DSMEM_ERR_CUDA;
             cudaMemset(g_err[dev], 0, 4 * sizeof(unsigned));
         }
+        if (dsb_attr::ensure_smem(fn, dev, smem, n > 8) != cudaSuccess) return DSMEM_ERR_CUDA;
         const RmsKey key{fn, dev, smem};
         auto it = g_occ.find(key);
         if (it == g_occ.end()) {
-            if (n > 8 && cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-                return DSMEM_ERR_CUDA;
-            if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-                return DSMEM_ERR_CUDA;
-            if (cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                     cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-                return DSMEM_ERR_CUDA;
             cfg.gridDim = dim3((unsigned)n, 1, 1);
             if (cudaOccupancyMaxActiveClusters(&resident, fn, &cfg) != cudaSuccess) return DSMEM_ERR_CUDA;
             g_occ[key] = resident;

@@ -30,10 +30,12 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <tuple>
 
 #include "../../include/dsmem_b200.h"
 #include "../collectives/dsmem_b200_algos.cuh"
 #include "f32x2.cuh"
+#include "smem_attr.cuh"
 
 namespace {
 
@@ -355,19 +357,16 @@ dsmem_status tp_launch(const void* const* xs, void* const* ys, unsigned* const* 
     if (cudaGetDevice(&dev) != cudaSuccess) return DSMEM_ERR_CUDA;
     {
         // kernel attributes and the occupancy query once per (kernel, device): they cost more than a launch
-        static std::map<std::pair<const void*, int>, int> occupancy;
+        static std::map<std::tuple<const void*, int, uint32_t>, int> occupancy;
         std::lock_guard<std::mutex> lock(g_tp_mu);
-        auto it = occupancy.find({fn, dev});
+        if (dsb_attr::ensure_smem(fn, dev, (uint32_t)smem, n > 8, false) != cudaSuccess) return DSMEM_ERR_CUDA;
+        auto it = occupancy.find({fn, dev, (uint32_t)smem});
         if (it != occupancy.end()) {
             resident = it->second;
         } else {
-            if (n > 8 && cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-                return DSMEM_ERR_CUDA;
-            if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-                return DSMEM_ERR_CUDA;
             cfg.gridDim = dim3((unsigned)n, 1, 1);
             if (cudaOccupancyMaxActiveClusters(&resident, fn, &cfg) != cudaSuccess) return DSMEM_ERR_CUDA;
-            occupancy[{fn, dev}] = resident;
+            occupancy[{fn, dev, (uint32_t)smem}] = resident;
         }
     }
     if (resident < 1) return DSMEM_ERR_SMEM_LIMIT;

@@ -191,6 +191,16 @@ def lib():
         "dsmem_rmsnorm_residual_launch": (c_int, [c_int, c_vp, c_vp, c_vp, ctypes.c_float, c_ll, c_int, c_int,
                                                   c_vp, c_vp, c_vp]),
         "dsmem_rmsnorm_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
+        "dsmem_rowwise_quant_launch": (c_int, [c_vp, c_vp, c_vp, c_ll, c_int, c_int, c_vp]),
+        "dsmem_lars_momentum_launch": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_int] + [ctypes.c_float] * 5
+                                       + [c_int, c_vp]),
+        "dsmem_layernorm_backward_launch": (c_int, [c_vp, c_vp, c_vp, c_vp, c_ll, c_int, ctypes.c_float, c_int, c_vp]),
+        "dsmem_pearson_backward_launch": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_ll, c_int, ctypes.c_float, c_int,
+                                                  c_vp]),
+        "dsmem_softmax_logits_backward_launch": (c_int, [c_vp, c_vp, c_vp, c_ll, c_int, c_int, c_vp]),
+        "dsmem_weighted_var_backward_launch": (c_int, [c_vp, c_vp, c_vp, c_vp, c_ll, c_int, ctypes.c_float, c_int,
+                                                       c_vp]),
+        "dsmem_rowwise_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
         "dsmem_ceiling_tcgen05": (c_int, [c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double),
                                           ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_int)]),
         "dsmem_ceiling_l2_bw": (c_int, [ctypes.c_longlong, c_int, c_int, ctypes.POINTER(ctypes.c_double),
@@ -404,6 +414,117 @@ def rmsnorm_check(device=0):
     _ok(lib().dsmem_rmsnorm_check(int(device), ctypes.byref(bits)), "dsmem_rmsnorm_check")
     if bits.value & 1:
         raise DsmemError(Status.TIMEOUT, "rmsnorm")
+
+
+# ----------------------------------------------------------------------------------- row-wise workloads
+# One cluster of cluster_size CTAs per row, one DSMEM exchange per row (dsmem_<name>_launch of
+# include/dsmem_b200.h); fp32 CUDA tensors [rows, cols], outputs allocated when not given.
+def _rw_prep(xs, outs, stream):
+    import torch
+
+    x0 = xs[0]
+    if x0.dim() != 2 or not x0.is_cuda:
+        raise ValueError("inputs must be CUDA [rows, cols] tensors")
+    for t in list(xs) + [o for o in outs if o is not None]:
+        if not t.is_cuda or not t.is_contiguous() or t.device != x0.device:
+            raise ValueError("row-wise tensors must be contiguous and on one CUDA device")
+    for t in xs:
+        if t.dtype != torch.float32:
+            raise ValueError("row-wise inputs are float32")
+    s = stream if stream is not None else torch.cuda.current_stream(x0.device).cuda_stream
+    return x0.shape[0], x0.shape[1], ctypes.c_void_p(s or None)
+
+
+def rowwise_quant(x, cluster_size=8, q=None, scales=None, stream=None):
+    """Row-wise int8 quantisation (rowwise_quant__reduction_reuse__credit.cu): returns (q int8, scales f32)."""
+    import torch
+
+    q = torch.empty(x.shape, dtype=torch.int8, device=x.device) if q is None else q
+    scales = torch.empty(x.shape[0], dtype=torch.float32, device=x.device) if scales is None else scales
+    rows, cols, s = _rw_prep([x], [q, scales], stream)
+    _ok(lib().dsmem_rowwise_quant_launch(x.data_ptr(), q.data_ptr(), scales.data_ptr(), rows, cols, int(cluster_size),
+                                         s), f"dsmem_rowwise_quant({rows}x{cols}, cluster {cluster_size})")
+    return q, scales
+
+
+def lars_momentum(weight, grad, momentum, cluster_size=8, momentum_coeff=0.9, weight_decay=0.01, lr=1.0e-3,
+                  trust_coeff=0.02, eps=1e-6, weight_out=None, momentum_out=None, stream=None):
+    """LARS momentum update (lars_momentum__reduction_reuse__credit.cu; defaults = its compiled-in constants):
+    returns (weight_out, momentum_out)."""
+    import torch
+
+    weight_out = torch.empty_like(weight) if weight_out is None else weight_out
+    momentum_out = torch.empty_like(weight) if momentum_out is None else momentum_out
+    rows, cols, s = _rw_prep([weight, grad, momentum], [weight_out, momentum_out], stream)
+    _ok(lib().dsmem_lars_momentum_launch(weight.data_ptr(), grad.data_ptr(), momentum.data_ptr(), weight_out.data_ptr(),
+                                         momentum_out.data_ptr(), rows, cols, float(momentum_coeff),
+                                         float(weight_decay), float(lr), float(trust_coeff), float(eps),
+                                         int(cluster_size), s),
+        f"dsmem_lars_momentum({rows}x{cols}, cluster {cluster_size})")
+    return weight_out, momentum_out
+
+
+def layernorm_backward(x, dy, gamma, eps=1e-5, cluster_size=8, dx=None, stream=None):
+    """dx of LayerNorm (layernorm_backward__reduction_reuse__credit.cu); gamma [cols]."""
+    import torch
+
+    dx = torch.empty_like(x) if dx is None else dx
+    rows, cols, s = _rw_prep([x, dy], [dx], stream)
+    if gamma.numel() != cols or gamma.dtype != torch.float32 or not gamma.is_contiguous():
+        raise ValueError("gamma must be a contiguous float32 [cols] tensor")
+    _ok(lib().dsmem_layernorm_backward_launch(x.data_ptr(), dy.data_ptr(), gamma.data_ptr(), dx.data_ptr(), rows,
+                                              cols, float(eps), int(cluster_size), s),
+        f"dsmem_layernorm_backward({rows}x{cols}, cluster {cluster_size})")
+    return dx
+
+
+def pearson_backward(x, y, grad, eps=1e-5, cluster_size=8, dx=None, dy=None, stream=None):
+    """(dx, dy) of the row-wise Pearson correlation (pearson_backward__reduction_reuse__credit.cu); grad [rows]."""
+    import torch
+
+    dx = torch.empty_like(x) if dx is None else dx
+    dy = torch.empty_like(x) if dy is None else dy
+    rows, cols, s = _rw_prep([x, y], [dx, dy], stream)
+    if grad.numel() != rows or grad.dtype != torch.float32 or not grad.is_contiguous():
+        raise ValueError("grad must be a contiguous float32 [rows] tensor")
+    _ok(lib().dsmem_pearson_backward_launch(x.data_ptr(), y.data_ptr(), grad.data_ptr(), dx.data_ptr(), dy.data_ptr(),
+                                            rows, cols, float(eps), int(cluster_size), s),
+        f"dsmem_pearson_backward({rows}x{cols}, cluster {cluster_size})")
+    return dx, dy
+
+
+def softmax_logits_backward(logits, dy, cluster_size=8, dx=None, stream=None):
+    """dx = p * (dy - sum(p * dy)), p = softmax(logits) per row (softmax_logits_backward__reduction_reuse__credit.cu)."""
+    import torch
+
+    dx = torch.empty_like(logits) if dx is None else dx
+    rows, cols, s = _rw_prep([logits, dy], [dx], stream)
+    _ok(lib().dsmem_softmax_logits_backward_launch(logits.data_ptr(), dy.data_ptr(), dx.data_ptr(), rows, cols,
+                                                   int(cluster_size), s),
+        f"dsmem_softmax_logits_backward({rows}x{cols}, cluster {cluster_size})")
+    return dx
+
+
+def weighted_var_backward(x, weights, dy, eps=1e-6, cluster_size=8, dx=None, stream=None):
+    """dx of the row-wise weighted variance (weighted_var_backward__reduction_reuse__credit.cu)."""
+    import torch
+
+    dx = torch.empty_like(x) if dx is None else dx
+    rows, cols, s = _rw_prep([x, weights, dy], [dx], stream)
+    _ok(lib().dsmem_weighted_var_backward_launch(x.data_ptr(), weights.data_ptr(), dy.data_ptr(), dx.data_ptr(), rows,
+                                                 cols, float(eps), int(cluster_size), s),
+        f"dsmem_weighted_var_backward({rows}x{cols}, cluster {cluster_size})")
+    return dx
+
+
+def rowwise_check(device=0):
+    """Raise DsmemError if a row-wise kernel's bounded wait gave up (TIMEOUT) or a copy failed its bounds check."""
+    bits = ctypes.c_uint(0)
+    _ok(lib().dsmem_rowwise_check(int(device), ctypes.byref(bits)), "dsmem_rowwise_check")
+    if bits.value & 1:
+        raise DsmemError(Status.TIMEOUT, "rowwise")
+    if bits.value:
+        raise DsmemError(Status.BOUNDS, "rowwise")
 
 
 def decoder_layer(inp, res, w_rms, wqkv, wo, w_post, wgu, wd, kcache, vcache, cos, sin, seq_len, eps=1e-5,

@@ -6,6 +6,7 @@ kernel, and exits; sized so a full-section capture of one to three launches ends
   allreduce   batch AllReduce through the C ABI (--alg, --cluster, --payload, --problems, --dtype)
   rmsnorm     cluster-fused RMSNorm (--rows, --hidden, --cluster)
   decoder     one Llama-2-7B decoder-layer step (--batch, --cluster; 4096 cached tokens): its seven launches
+  rowwise     a row-wise reduction-reuse kernel (--workload, --rows, --cols, --cluster; fp32, 5 + cols rows seed)
 """
 import argparse
 import pathlib
@@ -20,7 +21,9 @@ import dsmem_b200 as D  # noqa: E402
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=["allreduce", "rmsnorm", "decoder"], default="allreduce")
+    ap.add_argument("--case", choices=["allreduce", "rmsnorm", "decoder", "rowwise"], default="allreduce")
+    ap.add_argument("--workload", default="lars_momentum")
+    ap.add_argument("--cols", type=int, default=16384)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--alg", default="two_shot_push")
     ap.add_argument("--cluster", type=int, default=8)
@@ -50,6 +53,16 @@ def main(argv=None):
         for _ in range(args.warmup + args.launches):
             D.collective(D.Op.ALLREDUCE, alg, tin, tout, n, p)
         D.check()
+    elif args.case == "rowwise":
+        from dsmem_b200 import rowwise_bench as RB
+
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(5 + args.cols)
+        ins, outs = RB.make_set(torch, args.workload, args.rows, args.cols, gen)
+        for _ in range(args.warmup + args.launches):
+            RB.launch(args.workload, ins, outs, args.cluster)
+        torch.cuda.synchronize()
+        D.rowwise_check()
     elif args.case == "decoder":
         hid, heads, ffn, S, B = 4096, 32, 11008, 4096, args.batch
         nrm = lambda *s, std=0.02, mean=0.0: (mean + std * torch.randn(*s, device="cuda")).to(torch.bfloat16)  # noqa: E731

@@ -217,6 +217,50 @@ dsmem_status dsmem_rmsnorm_residual_launch(dsmem_dtype dtype, const void* x, con
 /* Read and clear the RMSNorm kernels' device error word of `device` (synchronous). */
 dsmem_status dsmem_rmsnorm_check(int device, unsigned* error_bits);
 
+/*
+ * Row-wise reduction-reuse workloads (fp32, [rows][cols] row-major): a cluster of `cluster_size` CTAs
+ * (1, 2, 4, 8, 16) per row, CTA b staging column slice b (ceil(cols / cluster_size) rounded up to 4
+ * elements) in shared memory, and ONE DSMEM exchange per row of a mergeable statistics record. Each
+ * replaces the clustered kernel of kernels/<name>__reduction_reuse__credit.cu, whose launch is one
+ * cluster of P CTAs per row (gridDim = rows * P, slice_elems = the column slice) and whose statistics
+ * take 1-3 replicated-push AllReduce stages of two cluster barriers each. Arrays 16-byte aligned with
+ * cols % 4 == 0 take bulk copies and vector stores; other shapes take per-element copies (same results).
+ * DSMEM_ERR_SMEM_LIMIT when one row slice of every input exceeds the 227 KiB per CTA (the reference
+ * declares the same shapes invalid). Device errors (bounded waits) are read by dsmem_rowwise_check.
+ */
+/* rowwise_quant__reduction_reuse__credit.cu:104-155 (cluster_quant_staged_kernel): amax = max |x| of the
+ * row, q = clamp(nearbyint(x * (127 / amax)), -127, 127) (0 for an all-zero row), scales[row] = amax / 127. */
+dsmem_status dsmem_rowwise_quant_launch(const float* x, int8_t* q, float* scales, long long rows, int cols,
+                                        int cluster_size, dsmem_stream_t stream);
+/* lars_momentum__reduction_reuse__credit.cu:126-185 (cluster_lars_staged_kernel): u = momentum_coeff * m +
+ * g + weight_decay * w, trust = trust_coeff * ||w|| / (||u|| + eps) over the row, w_out = w - lr * trust * u,
+ * m_out = u. The reference compiles in 0.9, 0.01, 1e-3, 0.02, 1e-6 (:29-33). */
+dsmem_status dsmem_lars_momentum_launch(const float* weight, const float* grad, const float* momentum,
+                                        float* weight_out, float* momentum_out, long long rows, int cols,
+                                        float momentum_coeff, float weight_decay, float lr, float trust_coeff,
+                                        float eps, int cluster_size, dsmem_stream_t stream);
+/* layernorm_backward__reduction_reuse__credit.cu:119-186 (cluster_bwd_staged_kernel): dx of LayerNorm
+ * given x, dy and gamma [cols] (mean and biased variance of x over the row; eps inside the rsqrt). */
+dsmem_status dsmem_layernorm_backward_launch(const float* x, const float* dy, const float* gamma, float* dx,
+                                             long long rows, int cols, float eps, int cluster_size,
+                                             dsmem_stream_t stream);
+/* pearson_backward__reduction_reuse__credit.cu:158-227 (cluster_bwd_staged_kernel): dx, dy of the Pearson
+ * correlation of rows x, y given the upstream gradient grad[rows]. */
+dsmem_status dsmem_pearson_backward_launch(const float* x, const float* y, const float* grad, float* dx, float* dy,
+                                           long long rows, int cols, float eps, int cluster_size,
+                                           dsmem_stream_t stream);
+/* softmax_logits_backward__reduction_reuse__credit.cu:164-237 (cluster_softmax_logits_bwd_staged_kernel):
+ * dx = p * (dy - sum(p * dy)) with p = softmax(logits) over the row. */
+dsmem_status dsmem_softmax_logits_backward_launch(const float* logits, const float* dy, float* dx, long long rows,
+                                                  int cols, int cluster_size, dsmem_stream_t stream);
+/* weighted_var_backward__reduction_reuse__credit.cu:135-221 (cluster_bwd_staged_kernel): dx of the weighted
+ * variance (non-negative weights; the reference compiles in eps = 1e-6, :29). */
+dsmem_status dsmem_weighted_var_backward_launch(const float* x, const float* weights, const float* dy, float* dx,
+                                                long long rows, int cols, float eps, int cluster_size,
+                                                dsmem_stream_t stream);
+/* Read and clear the row-wise kernels' device error word of `device` (synchronous). */
+dsmem_status dsmem_rowwise_check(int device, unsigned* error_bits);
+
 /* SM-to-SM bandwidth ceiling (the DSMEM roofline denominator). Replaces the reference's microbenchmark
  * roofline/harness/ceilings/src/dsmem_bw.cu:1-40 (ops `ld` and `tma_put`, ring +1, max active clusters,
  * 96 KiB per pass): mode 0 pull (ld.shared::cluster.v4), 1 push (cp.async.bulk) to the ring neighbour,

@@ -351,3 +351,151 @@ void orc_decoder_layer(int batch, int hidden, int heads, int head_dim, int ffn, 
     }
     free(x); free(xn); free(qkv); free(a); free(o); free(hn); free(gu); free(act); free(logit);
 }
+
+/* ----------------------------------------------------------------- row-wise reduction-reuse workloads */
+/* kernels/rowwise_quant__reduction_reuse__credit.cu:100-105 */
+int orc_quantize_i8(float value, float inv_scale) {
+    float q = nearbyintf(value * inv_scale);
+    q = fminf(127.0f, fmaxf(-127.0f, q));
+    return (int)(int8_t)q;
+}
+
+/* kernels/rowwise_quant__reduction_reuse__credit.cu:129-153 */
+void orc_rowwise_quant(size_t rows, size_t cols, const float* x, int8_t* q, float* scales) {
+    for (size_t r = 0; r < rows; ++r) {
+        const float* xr = x + r * cols;
+        float amax = 0.0f;
+        for (size_t i = 0; i < cols; ++i) amax = fmaxf(amax, fabsf(xr[i]));
+        const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+        scales[r] = amax / 127.0f;
+        for (size_t i = 0; i < cols; ++i) q[r * cols + i] = (int8_t)orc_quantize_i8(xr[i], inv);
+    }
+}
+
+/* kernels/lars_momentum__reduction_reuse__credit.cu:120-124 */
+double orc_lars_update(double w, double g, double m, double mu, double wd) { return mu * m + g + wd * w; }
+
+/* kernels/lars_momentum__reduction_reuse__credit.cu:160-184 */
+void orc_lars_momentum(size_t rows, size_t cols, const float* w, const float* g, const float* m, double mu,
+                       double wd, double lr, double eta, double eps, double* w_out, double* m_out) {
+    for (size_t r = 0; r < rows; ++r) {
+        const size_t b = r * cols;
+        double sw = 0.0, su = 0.0;
+        for (size_t i = 0; i < cols; ++i) {
+            const double u = orc_lars_update(w[b + i], g[b + i], m[b + i], mu, wd);
+            sw += (double)w[b + i] * w[b + i];
+            su += u * u;
+        }
+        const double step = lr * (eta * sqrt(sw) / (sqrt(su) + eps));
+        for (size_t i = 0; i < cols; ++i) {
+            const double u = orc_lars_update(w[b + i], g[b + i], m[b + i], mu, wd);
+            w_out[b + i] = w[b + i] - step * u;
+            m_out[b + i] = u;
+        }
+    }
+}
+
+/* kernels/layernorm_backward__reduction_reuse__credit.cu:146-185 */
+void orc_layernorm_backward(size_t rows, size_t cols, const float* x, const float* dy, const float* gamma,
+                            double eps, double* dx) {
+    for (size_t r = 0; r < rows; ++r) {
+        const size_t b = r * cols;
+        double sx = 0.0, sxx = 0.0;
+        for (size_t i = 0; i < cols; ++i) {
+            sx += x[b + i];
+            sxx += (double)x[b + i] * x[b + i];
+        }
+        const double mean = sx / (double)cols;
+        double var = sxx / (double)cols - mean * mean;
+        if (var < 0.0) var = 0.0;
+        const double inv_std = 1.0 / sqrt(var + eps);
+        double sg = 0.0, sgx = 0.0;
+        for (size_t i = 0; i < cols; ++i) {
+            const double xhat = (x[b + i] - mean) * inv_std, dyg = (double)dy[b + i] * gamma[i];
+            sg += dyg;
+            sgx += dyg * xhat;
+        }
+        const double mean_dyg = sg / (double)cols, mean_dyg_xhat = sgx / (double)cols;
+        for (size_t i = 0; i < cols; ++i) {
+            const double xhat = (x[b + i] - mean) * inv_std, dyg = (double)dy[b + i] * gamma[i];
+            dx[b + i] = (dyg - mean_dyg - xhat * mean_dyg_xhat) * inv_std;
+        }
+    }
+}
+
+/* kernels/pearson_backward__reduction_reuse__credit.cu:187-226 */
+void orc_pearson_backward(size_t rows, size_t cols, const float* x, const float* y, const float* grad, double eps,
+                          double* dx, double* dy) {
+    for (size_t r = 0; r < rows; ++r) {
+        const size_t b = r * cols;
+        double sx = 0.0, sy = 0.0, sxx = 0.0, syy = 0.0, sxy = 0.0;
+        for (size_t i = 0; i < cols; ++i) {
+            const double xv = x[b + i], yv = y[b + i];
+            sx += xv, sy += yv, sxx += xv * xv, syy += yv * yv, sxy += xv * yv;
+        }
+        const double mean_x = sx / (double)cols, mean_y = sy / (double)cols;
+        const double var_x = fmax(sxx - sx * mean_x, 0.0), var_y = fmax(syy - sy * mean_y, 0.0);
+        const double cov = sxy - sx * mean_y;
+        const double inv_x = 1.0 / sqrt(var_x + eps), inv_y = 1.0 / sqrt(var_y + eps);
+        const double inv_xy = inv_x * inv_y;
+        const double coeff_x = cov * inv_x * inv_x * inv_x * inv_y, coeff_y = cov * inv_x * inv_y * inv_y * inv_y;
+        const double g = grad[r];
+        for (size_t i = 0; i < cols; ++i) {
+            const double xc = x[b + i] - mean_x, yc = y[b + i] - mean_y;
+            dx[b + i] = g * (yc * inv_xy - xc * coeff_x);
+            dy[b + i] = g * (xc * inv_xy - yc * coeff_y);
+        }
+    }
+}
+
+/* kernels/softmax_logits_backward__reduction_reuse__credit.cu:199-236 */
+void orc_softmax_logits_backward(size_t rows, size_t cols, const float* z, const float* dy, double* dx) {
+    for (size_t r = 0; r < rows; ++r) {
+        const size_t b = r * cols;
+        double m = -INFINITY;
+        for (size_t i = 0; i < cols; ++i) m = fmax(m, z[b + i]);
+        double sum = 0.0;
+        for (size_t i = 0; i < cols; ++i) sum += exp(z[b + i] - m);
+        const double inv_sum = 1.0 / sum;
+        double dot = 0.0;
+        for (size_t i = 0; i < cols; ++i) dot += exp(z[b + i] - m) * inv_sum * dy[b + i];
+        for (size_t i = 0; i < cols; ++i) {
+            const double p = exp(z[b + i] - m) * inv_sum;
+            dx[b + i] = p * (dy[b + i] - dot);
+        }
+    }
+}
+
+/* kernels/weighted_var_backward__reduction_reuse__credit.cu:119-130 */
+double orc_wvar_backward_value(double value, double weight, double grad, double mean, double inv_sum_w,
+                               double inv_std, double sum_dy, double sum_dy_centered) {
+    const double centered = value - mean, inv_var = inv_std * inv_std;
+    return inv_std * (grad - weight * inv_sum_w * sum_dy - weight * centered * inv_var * inv_sum_w * sum_dy_centered);
+}
+
+/* kernels/weighted_var_backward__reduction_reuse__credit.cu:166-220 */
+void orc_weighted_var_backward(size_t rows, size_t cols, const float* x, const float* w, const float* dy,
+                               double eps, double* dx) {
+    for (size_t r = 0; r < rows; ++r) {
+        const size_t b = r * cols;
+        double sw = 0.0, swx = 0.0;
+        for (size_t i = 0; i < cols; ++i) {
+            sw += w[b + i];
+            swx += (double)w[b + i] * x[b + i];
+        }
+        const double inv_sum_w = 1.0 / (sw + eps), mean = swx * inv_sum_w;
+        double sv = 0.0;
+        for (size_t i = 0; i < cols; ++i) {
+            const double d = x[b + i] - mean;
+            sv += w[b + i] * d * d;
+        }
+        const double var = fmax(sv * inv_sum_w, 0.0), inv_std = 1.0 / sqrt(var + eps);
+        double sdy = 0.0, sdyc = 0.0;
+        for (size_t i = 0; i < cols; ++i) {
+            sdy += dy[b + i];
+            sdyc += dy[b + i] * (x[b + i] - mean);
+        }
+        for (size_t i = 0; i < cols; ++i)
+            dx[b + i] = orc_wvar_backward_value(x[b + i], w[b + i], dy[b + i], mean, inv_sum_w, inv_std, sdy, sdyc);
+    }
+}

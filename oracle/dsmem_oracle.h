@@ -92,6 +92,33 @@ void orc_decoder_layer(int batch, int hidden, int heads, int head_dim, int ffn, 
 /* Sum of `ranks` arrays of bf16/f32 (TP all-reduce input), in double. */
 void orc_sum_ranks(int dtype, size_t ranks, size_t n, const void* const* xs, double* out);
 
+/* Row-wise reduction-reuse workloads: the formulas of the clustered kernels of
+ * kernels/<name>__reduction_reuse__credit.cu over fp32 [rows][cols] inputs, row statistics accumulated in
+ * double in the reference's own stage order (one-pass variance where the reference uses it). */
+/* rowwise_quant :129-153 -- in fp32 exactly as the kernel computes it (max is order-free, so this is bit-exact):
+ * amax = max |x| (from 0, NaN ignored), inv = 127/amax (0 if amax == 0), q = clamp(nearbyint(x*inv), -127, 127),
+ * scale = amax/127. */
+void orc_rowwise_quant(size_t rows, size_t cols, const float* x, int8_t* q, float* scales);
+/* The element formula alone (quantize_to_i8, rowwise_quant :100-105). */
+int orc_quantize_i8(float value, float inv_scale);
+/* lars_momentum :160-184 (update_value :120-124). */
+void orc_lars_momentum(size_t rows, size_t cols, const float* w, const float* g, const float* m, double mu,
+                       double wd, double lr, double eta, double eps, double* w_out, double* m_out);
+double orc_lars_update(double w, double g, double m, double mu, double wd);
+/* layernorm_backward :146-185. */
+void orc_layernorm_backward(size_t rows, size_t cols, const float* x, const float* dy, const float* gamma,
+                            double eps, double* dx);
+/* pearson_backward :187-226. */
+void orc_pearson_backward(size_t rows, size_t cols, const float* x, const float* y, const float* grad, double eps,
+                          double* dx, double* dy);
+/* softmax_logits_backward :199-236. */
+void orc_softmax_logits_backward(size_t rows, size_t cols, const float* z, const float* dy, double* dx);
+/* weighted_var_backward :166-220 and its element formula backward_value :119-130. */
+void orc_weighted_var_backward(size_t rows, size_t cols, const float* x, const float* w, const float* dy,
+                               double eps, double* dx);
+double orc_wvar_backward_value(double value, double weight, double grad, double mean, double inv_sum_w,
+                               double inv_std, double sum_dy, double sum_dy_centered);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,18 @@ def lib():
         L.orc_uniform_real.restype = d
         L.orc_f32_to_bf16.argtypes = [ctypes.c_float]
         L.orc_f32_to_bf16.restype = ctypes.c_uint16
+        L.orc_rowwise_quant.argtypes = [sz, sz, vp, vp, vp]
+        L.orc_quantize_i8.argtypes = [ctypes.c_float, ctypes.c_float]
+        L.orc_quantize_i8.restype = i
+        L.orc_lars_momentum.argtypes = [sz, sz, vp, vp, vp, d, d, d, d, d, vp, vp]
+        L.orc_lars_update.argtypes = [d, d, d, d, d]
+        L.orc_lars_update.restype = d
+        L.orc_layernorm_backward.argtypes = [sz, sz, vp, vp, vp, d, vp]
+        L.orc_pearson_backward.argtypes = [sz, sz, vp, vp, vp, d, vp, vp]
+        L.orc_softmax_logits_backward.argtypes = [sz, sz, vp, vp, vp]
+        L.orc_weighted_var_backward.argtypes = [sz, sz, vp, vp, vp, d, vp]
+        L.orc_wvar_backward_value.argtypes = [d] * 8
+        L.orc_wvar_backward_value.restype = d
         _lib = L
     return _lib
 
@@ -160,6 +172,69 @@ def decoder_layer(inp, res, w_rms, wqkv, wo, w_post, wgu, wd, kc, vc, cos, sin, 
     lib().orc_decoder_layer(batch, hidden, heads, head_dim, ffn, seq_len, cap, *[_p(a) for a in arrs],
                             *[_p(c) for c in cs], eps, *[_p(outs[k]) for k in ("out", "h", "o", "k_new", "v_new")])
     return outs
+
+
+# ------------------------------------------------------------------ row-wise reduction-reuse workloads
+# The constants the reference kernels compile in (kernels/*__reduction_reuse__credit.cu), as float32 values.
+LARS_DEFAULTS = dict(mu=float(np.float32(0.9)), wd=float(np.float32(0.01)), lr=float(np.float32(1.0e-3)),
+                     eta=float(np.float32(0.02)), eps=float(np.float32(1e-6)))   # lars_momentum :29-33
+LN_BWD_EPS = float(np.float32(1e-5))     # layernorm_backward :29
+PEARSON_EPS = float(np.float32(1e-5))    # pearson_backward :29
+WVAR_EPS = float(np.float32(1.0e-6))     # weighted_var_backward :29
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def rowwise_quant(x):
+    """(q int8 [rows, cols], scales float32 [rows]), bit-exact fp32 restatement."""
+    x = _f32(x)
+    rows, cols = x.shape
+    q = np.empty((rows, cols), np.int8)
+    sc = np.empty(rows, np.float32)
+    lib().orc_rowwise_quant(rows, cols, _p(x), _p(q), _p(sc))
+    return q, sc
+
+
+def lars_momentum(w, g, m, mu, wd, lr, eta, eps):
+    w, g, m = _f32(w), _f32(g), _f32(m)
+    rows, cols = w.shape
+    wo, mo = np.empty((rows, cols)), np.empty((rows, cols))
+    lib().orc_lars_momentum(rows, cols, _p(w), _p(g), _p(m), mu, wd, lr, eta, eps, _p(wo), _p(mo))
+    return wo, mo
+
+
+def layernorm_backward(x, dy, gamma, eps):
+    x, dy, gamma = _f32(x), _f32(dy), _f32(gamma)
+    rows, cols = x.shape
+    dx = np.empty((rows, cols))
+    lib().orc_layernorm_backward(rows, cols, _p(x), _p(dy), _p(gamma), eps, _p(dx))
+    return dx
+
+
+def pearson_backward(x, y, grad, eps):
+    x, y, grad = _f32(x), _f32(y), _f32(grad)
+    rows, cols = x.shape
+    dx, dy = np.empty((rows, cols)), np.empty((rows, cols))
+    lib().orc_pearson_backward(rows, cols, _p(x), _p(y), _p(grad), eps, _p(dx), _p(dy))
+    return dx, dy
+
+
+def softmax_logits_backward(z, dy):
+    z, dy = _f32(z), _f32(dy)
+    rows, cols = z.shape
+    dx = np.empty((rows, cols))
+    lib().orc_softmax_logits_backward(rows, cols, _p(z), _p(dy), _p(dx))
+    return dx
+
+
+def weighted_var_backward(x, w, dy, eps):
+    x, w, dy = _f32(x), _f32(w), _f32(dy)
+    rows, cols = x.shape
+    dx = np.empty((rows, cols))
+    lib().orc_weighted_var_backward(rows, cols, _p(x), _p(w), _p(dy), eps, _p(dx))
+    return dx
 
 
 def bf16_to_f32(u16):

@@ -101,3 +101,10 @@ def test_rmsnorm_rejects_bad_shapes(cuda):
     with pytest.raises(D.DsmemError) as e:
         D.rmsnorm(x, w, cluster_size=8)
     assert e.value.status == D.Status.ILLEGAL_CONFIG
+
+
+def test_rmsnorm_launch_order_of_shapes(cuda, orc):
+    """One kernel (2 units per lane) with a larger, a smaller and again the larger shared-memory size: the
+    kernel's dynamic shared-memory opt-in only grows, so the third launch still fits."""
+    for hidden in (4096, 3072, 4096):
+        run(cuda, orc, D.Dtype.BF16, 40, hidden, 8, seed=hidden)
