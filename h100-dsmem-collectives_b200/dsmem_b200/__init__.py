@@ -201,6 +201,8 @@ def lib():
         "dsmem_weighted_var_backward_launch": (c_int, [c_vp, c_vp, c_vp, c_vp, c_ll, c_int, ctypes.c_float, c_int,
                                                        c_vp]),
         "dsmem_rowwise_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
+        "dsmem_topk_launch": (c_int, [c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp]),
+        "dsmem_topk_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
         "dsmem_ceiling_tcgen05": (c_int, [c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double),
                                           ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_int)]),
         "dsmem_ceiling_l2_bw": (c_int, [ctypes.c_longlong, c_int, c_int, ctypes.POINTER(ctypes.c_double),
@@ -525,6 +527,34 @@ def rowwise_check(device=0):
         raise DsmemError(Status.TIMEOUT, "rowwise")
     if bits.value:
         raise DsmemError(Status.BOUNDS, "rowwise")
+
+
+def topk(logits, k=2048, cluster_size=8, out=None, stream=None):
+    """Exact top-k indices of every row of fp32 logits [rows, n] (dsmem_topk_launch; hpc-ops'
+    topk_filtered_cluster8_exact_kernel). Returns int32 [rows, k], each row's indices in unspecified order."""
+    import torch
+
+    if logits.dim() != 2 or not logits.is_cuda or not logits.is_contiguous() or logits.dtype != torch.float32:
+        raise ValueError("logits must be a contiguous float32 CUDA [rows, n] tensor")
+    rows, n = logits.shape
+    if out is None:
+        out = torch.empty((rows, k), dtype=torch.int32, device=logits.device)
+    if out.dtype != torch.int32 or not out.is_contiguous() or out.shape != (rows, k):
+        raise ValueError("out must be a contiguous int32 [rows, k] tensor")
+    s = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
+    _ok(lib().dsmem_topk_launch(logits.data_ptr(), rows, n, int(k), out.data_ptr(), int(cluster_size),
+                                ctypes.c_void_p(s or None)), f"dsmem_topk({rows}x{n}, k {k}, cluster {cluster_size})")
+    return out
+
+
+def topk_check(device=0):
+    """Raise DsmemError if the top-k kernel's bounded wait gave up (TIMEOUT) or an output slot was out of range."""
+    bits = ctypes.c_uint(0)
+    _ok(lib().dsmem_topk_check(int(device), ctypes.byref(bits)), "dsmem_topk_check")
+    if bits.value & 1:
+        raise DsmemError(Status.TIMEOUT, "topk")
+    if bits.value:
+        raise DsmemError(Status.BOUNDS, "topk")
 
 
 def decoder_layer(inp, res, w_rms, wqkv, wo, w_post, wgu, wd, kcache, vcache, cos, sin, seq_len, eps=1e-5,

@@ -261,6 +261,21 @@ dsmem_status dsmem_weighted_var_backward_launch(const float* x, const float* wei
 /* Read and clear the row-wise kernels' device error word of `device` (synchronous). */
 dsmem_status dsmem_rowwise_check(int device, unsigned* error_bits);
 
+/*
+ * Exact top-k indices of every row of fp32 logits ([rows][n] row-major, 16-byte aligned base; any n): for
+ * each row the indices (0..n-1) of its k largest values, written to out_indices[row][0..k) in an unspecified
+ * order; among equal values at the cut, lower ranks' segments and lower indices are taken first. A cluster
+ * of cluster_size CTAs (2, 4, 8, 16) per row; each stages a contiguous segment of ceil(n / cluster_size)
+ * elements in shared memory (DSMEM_ERR_SMEM_LIMIT above about 200 KiB per segment); the radix select's
+ * 2048-bin histograms meet in a two-shot DSMEM AllReduce. Replaces topk_filtered_cluster8_exact_kernel of
+ * kernels/topk_filtered_cluster8__llm_sampling__hpcops.cu (hpc.topk(logits, ke, out, ...) with k = 2048 at
+ * cluster 8), generalised to any k <= n and cluster size. 1 <= k <= n.
+ */
+dsmem_status dsmem_topk_launch(const float* logits, long long rows, int n, int k, int32_t* out_indices,
+                               int cluster_size, dsmem_stream_t stream);
+/* Read and clear the top-k kernel's device error word of `device` (synchronous). */
+dsmem_status dsmem_topk_check(int device, unsigned* error_bits);
+
 /* SM-to-SM bandwidth ceiling (the DSMEM roofline denominator). Replaces the reference's microbenchmark
  * roofline/harness/ceilings/src/dsmem_bw.cu:1-40 (ops `ld` and `tma_put`, ring +1, max active clusters,
  * 96 KiB per pass): mode 0 pull (ld.shared::cluster.v4), 1 push (cp.async.bulk) to the ring neighbour,

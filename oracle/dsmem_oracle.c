@@ -499,3 +499,26 @@ void orc_weighted_var_backward(size_t rows, size_t cols, const float* x, const f
             dx[b + i] = orc_wvar_backward_value(x[b + i], w[b + i], dy[b + i], mean, inv_sum_w, inv_std, sdy, sdyc);
     }
 }
+
+/* ----------------------------------------------------------------- exact top-k values */
+/* Order of torch.topk (the reference test's validator, roofline/workloads/hpcops_topk_cluster8.yaml): larger
+ * first, NaN largest. Comparison on the order-preserving integer key of the float bits, with -0.0 == +0.0. */
+static uint32_t topk_key(float v) {
+    uint32_t b;
+    memcpy(&b, &v, 4);
+    if (v == 0.0f) b = 0u;   /* -0 and +0 are equal values */
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+static int topk_cmp_desc(const void* a, const void* b) {
+    const uint32_t ka = topk_key(*(const float*)a), kb = topk_key(*(const float*)b);
+    return ka < kb ? 1 : ka > kb ? -1 : 0;
+}
+void orc_topk_values(size_t rows, size_t n, size_t k, const float* x, float* vals) {
+    float* tmp = (float*)malloc(n * sizeof(float));
+    for (size_t r = 0; r < rows; ++r) {
+        memcpy(tmp, x + r * n, n * sizeof(float));
+        qsort(tmp, n, sizeof(float), topk_cmp_desc);
+        memcpy(vals + r * k, tmp, k * sizeof(float));
+    }
+    free(tmp);
+}

@@ -67,6 +67,7 @@ def lib():
         L.orc_weighted_var_backward.argtypes = [sz, sz, vp, vp, vp, d, vp]
         L.orc_wvar_backward_value.argtypes = [d] * 8
         L.orc_wvar_backward_value.restype = d
+        L.orc_topk_values.argtypes = [sz, sz, sz, vp, vp]
         _lib = L
     return _lib
 
@@ -235,6 +236,15 @@ def weighted_var_backward(x, w, dy, eps):
     dx = np.empty((rows, cols))
     lib().orc_weighted_var_backward(rows, cols, _p(x), _p(w), _p(dy), eps, _p(dx))
     return dx
+
+
+def topk_values(x, k):
+    """The k largest values of each row of x (float32 [rows, n]), sorted descending (torch.topk's order)."""
+    x = _f32(x)
+    rows, n = x.shape
+    vals = np.empty((rows, k), np.float32)
+    lib().orc_topk_values(rows, n, k, _p(x), _p(vals))
+    return vals
 
 
 def bf16_to_f32(u16):
