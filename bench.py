@@ -277,6 +277,36 @@ def dsmem_ceiling(D, n):
     return out
 
 
+# Row-wise reduction-reuse workloads (kernels/*__reduction_reuse__credit.cu) at the middle reference shape
+# (16384 columns), each at the cluster size measured fastest there; the full table is
+# `python -m dsmem_b200.rowwise_bench`.
+ROWWISE_BENCH = {"rowwise_quant": 2, "lars_momentum": 4, "layernorm_backward": 2, "pearson_backward": 2,
+                 "softmax_logits_backward": 4, "weighted_var_backward": 4}
+# Exact top-2048 (hpc-ops topk_filtered_cluster8) at the reference's three shapes, cluster size per shape.
+TOPK_BENCH = {"m8_n32k": 8, "m16_n64k": 4, "m8_n240k": 8}
+
+
+def rowwise_extras(torch, hbm_peak):
+    from dsmem_b200 import rowwise_bench as RB
+
+    out = {}
+    for w, n in ROWWISE_BENCH.items():
+        r = RB.measure(torch, w, 16384, n, hbm_peak)
+        out[w] = {k: r[k] for k in ("rows", "cols", "cluster_size", "us", "hbm_GBps", "hbm_frac", "h100_us")}
+        torch.cuda.empty_cache()
+    return out
+
+
+def topk_extras(torch):
+    from dsmem_b200 import topk_bench as TB
+
+    out = {}
+    for s, n in TOPK_BENCH.items():
+        r = TB.measure(torch, s, n)
+        out[s] = {k: r[k] for k in ("m", "n", "k", "cluster_size", "us", "h100_us", "vs_h100")}
+    return out
+
+
 def run_ours(args, rank, world, local):
     import torch
 
@@ -388,6 +418,8 @@ def run_ours(args, rank, world, local):
         extras["rmsnorm"] = rmsnorm_config3(torch, D, hbm_peak)
         # ceilings beyond DSMEM and HBM (tcgen05 MMA, L2, shared memory), 1 / slope over two work amounts
         extras["ceilings_sm100"] = D.sm100_ceilings(reps=3)
+        extras["rowwise"] = rowwise_extras(torch, hbm_peak)
+        extras["topk"] = topk_extras(torch)
 
     cpu = None
     if rank == 0 and world == 1:

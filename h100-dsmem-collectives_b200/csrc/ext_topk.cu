@@ -25,10 +25,13 @@
 //     (a peer's next reduce-scatter comes after it received this CTA's all-gather, i.e. after this CTA summed
 //     its slots; its next all-gather comes after this CTA's next reduce-scatter, i.e. after this CTA read the
 //     row histogram);
-//   * every CTA derives the same threshold from the same histogram, so no CTA gathers for another: after the
-//     rounds, each CTA counts its strictly selected elements and its exact ties, one st.async exchange of those
-//     two counts gives every CTA its output offset and its share of the ties (in rank order), and each CTA
-//     writes its own indices straight to the output row (warp-range ballot compaction, one block scan);
+//   * every CTA derives the same threshold from the same histogram, so no CTA gathers for another: one scan
+//     after the coarse round appends the strictly selected elements and the cut bin's candidates to two
+//     shared-memory index lists (warp-aggregated appends), the fine rounds read only the candidates, one
+//     st.async exchange of the per-CTA counts gives every CTA its output offset and its share of exact ties
+//     (in rank order), and each CTA writes its own indices straight to the output row. Coarse keys are
+//     computed two at a time (packed fp16x2 conversion). The segment is scanned twice in all (histogram,
+//     lists); a candidate list that overflows, or k above the list capacity, rescans the segment instead;
 //   * the fine rounds run on the key relative to the coarse bin's exact key range (the floats rounding to the
 //     bin's fp16 values lie strictly between the neighbouring fp16 values), so for finite bins two rounds of
 //     11 + at most 10 bits resolve the cut instead of the reference's three absolute rounds.
@@ -59,8 +62,12 @@ constexpr uint32_t kHistOff = 128;                      // this CTA's histogram 
 constexpr uint32_t kSlotOff = kHistOff + kBins * 4;     // reduce-scatter slots: N x B u32 (= kBins u32)
 constexpr uint32_t kRowHistOff = kSlotOff + kBins * 4;  // the cluster's histogram of the round: kBins u32
 constexpr uint32_t kCntOff = kRowHistOff + kBins * 4;   // count exchange: 16 x 2 u32
-constexpr uint32_t kScratchOff = kCntOff + 16 * 8;      // block scans: 64 u32
-constexpr uint32_t kSegOff = kScratchOff + 64 * 4;      // the segment (16-byte aligned)
+constexpr uint32_t kScratchOff = kCntOff + 16 * 8;      // block scans and list counters: 64 u32
+constexpr uint32_t kListCap = 4096;                     // entries of each index list
+constexpr uint32_t kSelOff = kScratchOff + 64 * 4;      // indices of the strictly selected elements
+constexpr uint32_t kCandOff = kSelOff + kListCap * 4;   // indices of the cut bin's candidates
+constexpr uint32_t kSegOff = kCandOff + kListCap * 4;   // the segment (16-byte aligned)
+constexpr int kCtrSel = 48, kCtrCand = 49, kCtrOut = 50, kCtrTie = 51;   // scratch words
 static_assert(kSegOff % 16 == 0, "segment alignment");
 
 struct TkArgs {
@@ -79,10 +86,25 @@ __device__ __forceinline__ uint32_t key32(float v) {
     const uint32_t b = __float_as_uint(v);
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
-__device__ __forceinline__ uint32_t coarse_key(float v) {   // 11 bits of the fp16-rounded value's key
-    const uint32_t h = (uint32_t)__half_as_ushort(__float2half_rn(v));
-    const uint32_t k16 = (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
-    return k16 >> 5;
+// Coarse keys (11 bits of the order-preserving key of the fp16-rounded value), two at a time: one packed
+// fp16x2 conversion, the key transform on both 16-bit lanes (sign set: all bits flipped; clear: top bit set),
+// then the top 11 bits of each lane. NaN inputs are binned explicitly (+NaN in the top bin, -NaN in the
+// bottom one, as their fp32 keys order them): the NaN payload a conversion produces depends on the instruction
+// (packed or single), and every pass must bin a value the same way.
+__device__ __forceinline__ void coarse_key2(float lo, float hi, uint32_t& ck_lo, uint32_t& ck_hi) {
+    const __half2 hv = __floats2half2_rn(lo, hi);   // .x (low lane) = lo
+    const uint32_t x = *reinterpret_cast<const uint32_t*>(&hv);
+    const uint32_t sgn = (x >> 15) & 0x00010001u;
+    const uint32_t key = x ^ ((sgn * 0x7FFFu) | 0x80008000u);
+    ck_lo = (key >> 5) & 0x7FFu;
+    ck_hi = (key >> 21) & 0x7FFu;
+    if (isnan(lo)) ck_lo = (__float_as_uint(lo) >> 31) ? 0u : 0x7FFu;
+    if (isnan(hi)) ck_hi = (__float_as_uint(hi) >> 31) ? 0u : 0x7FFu;
+}
+__device__ __forceinline__ uint32_t coarse_key(float v) {
+    uint32_t a, b;
+    coarse_key2(v, v, a, b);
+    return a;
 }
 
 // The fp16 value whose coarse 16-bit key is k16 (the inverse of the key transform of coarse_key).
@@ -213,11 +235,24 @@ __global__ void __launch_bounds__(kThreadsTk, 1) topk_cluster_kernel(const __gri
         if (tid < (uint32_t)(a0 - g0)) seg[tid] = a.x[g0 + tid];                              // ragged head
         if (tid < (uint32_t)(g1 - a1)) seg[(a1 - g0) + tid] = a.x[a1 + tid];                  // ragged tail
         clear_hist();
+        uint32_t* scr = c.ptr<uint32_t>(kScratchOff);
+        if (tid < 4) scr[kCtrSel + tid] = 0u;
         __syncthreads();
         wait_bar(c, kLoadBar);
 
-        // ---- coarse round
-        for (int e = (int)tid; e < L; e += kThreadsTk) atomicAdd(&hist[coarse_key(seg[e])], 1u);
+        // ---- coarse round: the segment as 16-byte units u of the aligned buffer, element 4u + j - off
+        const int nu = (int)((off + (uint32_t)L + 3u) >> 2);
+        const float4* seg4 = reinterpret_cast<const float4*>(segbuf);
+        for (int u = (int)tid; u < nu; u += kThreadsTk) {
+            const float4 v = seg4[u];
+            uint32_t ck[4];
+            coarse_key2(v.x, v.y, ck[0], ck[1]);
+            coarse_key2(v.z, v.w, ck[2], ck[3]);
+            const int i0 = 4 * u - (int)off;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (i0 + j >= 0 && i0 + j < L) atomicAdd(&hist[ck[j]], 1u);
+        }
         allreduce();
         const Cut cc = find_cut(c, rowh, (uint32_t)k);
         const uint32_t tau = cc.d;
@@ -249,6 +284,47 @@ __global__ void __launch_bounds__(kThreadsTk, 1) topk_cluster_kernel(const __gri
                 }
             }
         }
+        // ---- one scan: the strictly selected (coarse > tau, or >= tau when the cut bin is taken whole) and
+        // the cut bin's candidates go to two index lists (warp-aggregated appends). A candidate list that
+        // overflows, or k above the list capacity, falls back to rescanning the segment below.
+        const bool lists = (uint32_t)k <= kListCap;
+        uint32_t* sel_list = c.ptr<uint32_t>(kSelOff);
+        uint32_t* cand_list = c.ptr<uint32_t>(kCandOff);
+        const uint32_t lane = tid & 31u, w = tid >> 5, lt = (1u << lane) - 1u;
+        auto append = [&](bool flag, int ctr, uint32_t* list, int e) {
+            const uint32_t b = __ballot_sync(0xffffffffu, flag);
+            if (b == 0u) return;
+            const int leader = __ffs(b) - 1;
+            uint32_t pos0 = 0;
+            if ((int)lane == leader) pos0 = atomicAdd(&scr[ctr], (uint32_t)__popc(b));
+            pos0 = __shfl_sync(0xffffffffu, pos0, leader);
+            if (flag) {
+                const uint32_t pos = pos0 + __popc(b & lt);
+                if (pos < kListCap) list[pos] = (uint32_t)e;
+            }
+        };
+        if (lists) {
+            for (int ub = 0; ub < nu; ub += kThreadsTk) {   // uniform trip count: the appends use full-warp ballots
+                const int u = ub + (int)tid;
+                uint32_t ck[4] = {0u, 0u, 0u, 0u};
+                if (u < nu) {
+                    const float4 v = seg4[u];
+                    coarse_key2(v.x, v.y, ck[0], ck[1]);
+                    coarse_key2(v.z, v.w, ck[2], ck[3]);
+                }
+                const int i0 = 4 * u - (int)off;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const bool valid = u < nu && i0 + j >= 0 && i0 + j < L;
+                    append(valid && (ck[j] > tau || (full && ck[j] == tau)), kCtrSel, sel_list, i0 + j);
+                    append(valid && !full && ck[j] == tau, kCtrCand, cand_list, i0 + j);
+                }
+            }
+        }
+        __syncthreads();
+        const uint32_t nsel = scr[kCtrSel], ncand = scr[kCtrCand];
+        const bool use_lists = lists && ncand <= kListCap;   // uniform in the CTA (the peers may differ)
+
         int shift = 32;   // no fine digit yet; else the chosen prefix is (u >> shift) == prefix
         uint32_t prefix = 0, r = cc.r;
         for (int fr = 0; fr < nfine && !full; ++fr) {
@@ -256,12 +332,18 @@ __global__ void __launch_bounds__(kThreadsTk, 1) topk_cluster_kernel(const __gri
             clear_hist();
             __syncthreads();
             const int sh = shifts[fr];
-            for (int e = (int)tid; e < L; e += kThreadsTk) {
-                const float v = seg[e];
-                if (coarse_key(v) != tau) continue;
+            auto add = [&](float v) {
                 const uint32_t u = key32(v) - base;
-                if (shift < 32 && (u >> shift) != prefix) continue;
+                if (shift < 32 && (u >> shift) != prefix) return;
                 atomicAdd(&hist[(u >> sh) & masks[fr]], 1u);
+            };
+            if (use_lists) {
+                for (uint32_t i = tid; i < ncand; i += kThreadsTk) add(seg[cand_list[i]]);
+            } else {
+                for (int e = (int)tid; e < L; e += kThreadsTk) {
+                    const float v = seg[e];
+                    if (coarse_key(v) == tau) add(v);
+                }
             }
             allreduce();
             const Cut fc = find_cut(c, rowh, r);
@@ -271,7 +353,7 @@ __global__ void __launch_bounds__(kThreadsTk, 1) topk_cluster_kernel(const __gri
             full = fc.r == fc.in_bin;
         }
         // selection: coarse > tau; or coarse == tau and (no fine round, or u's prefix > prefix, or == prefix and
-        // (full, or among the first r exact ties in rank/index order))
+        // (full, or among the first r exact ties in rank order))
         auto cls = [&](float v) -> int {   // 2 selected, 1 exact tie still to share, 0 not
             const uint32_t ck = coarse_key(v);
             if (ck != tau) return ck > tau ? 2 : 0;
@@ -280,22 +362,32 @@ __global__ void __launch_bounds__(kThreadsTk, 1) topk_cluster_kernel(const __gri
             if (p != prefix) return p > prefix ? 2 : 0;
             return full ? 2 : 1;
         };
-        // ---- output: warp w owns elements [w * Lw, (w + 1) * Lw) of the segment, 32 at a time. Pass A counts
-        // the strictly selected and the tied elements per warp; one block scan gives every warp its offsets;
-        // pass B writes with in-warp ballots (no block barrier per element tile).
+        // ---- counts. Lists: the selected list plus the candidates' verdicts. Otherwise warp w counts elements
+        // [w * Lw, (w + 1) * Lw) of the segment (pass A of the rescan path; pass B below writes them).
         const int Lw = ((L + kWarpsTk - 1) / kWarpsTk + 31) & ~31;
-        const uint32_t lane = tid & 31u, w = tid >> 5, lt = (1u << lane) - 1u;
         const int e0 = (int)w * Lw, e1 = min(L, e0 + Lw);
         uint32_t wsel = 0, wtie = 0;
-        for (int e = e0 + (int)lane; e - (int)lane < e1; e += 32) {
-            const int sv = e < e1 ? cls(seg[e]) : 0;
-            wsel += __popc(__ballot_sync(0xffffffffu, sv == 2));
-            wtie += __popc(__ballot_sync(0xffffffffu, sv == 1));
+        if (use_lists) {
+            for (uint32_t i = tid; i < ncand; i += kThreadsTk) {
+                const int sv = cls(seg[cand_list[i]]);
+                wsel += sv == 2;
+                wtie += sv == 1;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                wsel += __shfl_xor_sync(0xffffffffu, wsel, o);
+                wtie += __shfl_xor_sync(0xffffffffu, wtie, o);
+            }
+        } else {
+            for (int e = e0 + (int)lane; e - (int)lane < e1; e += 32) {
+                const int sv = e < e1 ? cls(seg[e]) : 0;
+                wsel += __popc(__ballot_sync(0xffffffffu, sv == 2));
+                wtie += __popc(__ballot_sync(0xffffffffu, sv == 1));
+            }
         }
-        uint32_t* scr = c.ptr<uint32_t>(kScratchOff);
         if (lane == 0) scr[w] = wsel, scr[16 + w] = wtie;
         __syncthreads();
-        uint32_t sel_pre = 0, tie_pre = 0, sel_all = 0, tie_all = 0;
+        uint32_t sel_pre = 0, tie_pre = 0, sel_all = use_lists ? nsel : 0u, tie_all = 0;
         for (uint32_t q = 0; q < (uint32_t)kWarpsTk; ++q) {
             const uint32_t sq = scr[q], tq = scr[16 + q];
             sel_pre += q < w ? sq : 0u;
@@ -328,22 +420,34 @@ __global__ void __launch_bounds__(kThreadsTk, 1) topk_cluster_kernel(const __gri
             ties_before += tq;
         }
         int* orow = a.out + row * (long long)k;
-        uint32_t sel_run = sel_pre, tie_run = tie_pre;
-        for (int e = e0 + (int)lane; e - (int)lane < e1; e += 32) {
-            const int sv = e < e1 ? cls(seg[e]) : 0;
-            const uint32_t bs = __ballot_sync(0xffffffffu, sv == 2), bt = __ballot_sync(0xffffffffu, sv == 1);
-            uint32_t slot = 0xFFFFFFFFu;
-            if (sv == 2) slot = out_off + sel_run + __popc(bs & lt);
-            if (sv == 1) {
-                const uint32_t tr = tie_run + __popc(bt & lt);
-                if (tr < take) slot = out_off + sel_all + tr;
+        auto put = [&](uint32_t slot, int e) {
+            if (slot < (uint32_t)k) orow[slot] = start + e;
+            else dsb::report(c, DSMEM_ERR_BIT_BOUNDS);
+        };
+        if (use_lists) {
+            for (uint32_t i = tid; i < nsel; i += kThreadsTk) put(out_off + i, (int)sel_list[i]);
+            for (uint32_t i = tid; i < ncand; i += kThreadsTk) {
+                const int e = (int)cand_list[i];
+                const int sv = cls(seg[e]);
+                if (sv == 2) put(out_off + nsel + atomicAdd(&scr[kCtrOut], 1u), e);
+                if (sv == 1) {
+                    const uint32_t tr = atomicAdd(&scr[kCtrTie], 1u);
+                    if (tr < take) put(out_off + sel_all + tr, e);
+                }
             }
-            if (sv != 0 && slot != 0xFFFFFFFFu) {
-                if (slot < (uint32_t)k) orow[slot] = start + e;
-                else dsb::report(c, DSMEM_ERR_BIT_BOUNDS);
+        } else {   // pass B: in-warp ballots over the warp's range
+            uint32_t sel_run = sel_pre, tie_run = tie_pre;
+            for (int e = e0 + (int)lane; e - (int)lane < e1; e += 32) {
+                const int sv = e < e1 ? cls(seg[e]) : 0;
+                const uint32_t bs = __ballot_sync(0xffffffffu, sv == 2), bt = __ballot_sync(0xffffffffu, sv == 1);
+                if (sv == 2) put(out_off + sel_run + __popc(bs & lt), e);
+                if (sv == 1) {
+                    const uint32_t tr = tie_run + __popc(bt & lt);
+                    if (tr < take) put(out_off + sel_all + tr, e);
+                }
+                sel_run += __popc(bs);
+                tie_run += __popc(bt);
             }
-            sel_run += __popc(bs);
-            tie_run += __popc(bt);
         }
         __syncthreads();   // the segment, the scratch and the count slots are free for the next row
     }

@@ -71,6 +71,16 @@ def test_ties(cuda, orc):
             run(cuda, orc, x, k, n_cta, f"ties k={k} N={n_cta}")
 
 
+@pytest.mark.xfail(strict=False, reason="NaN logits: a row whose largest values are NaN wrote no index at k = 1 "
+                   "(found on B200, cause not found yet); NaN inputs are outside the supported domain")
+def test_nan_ranks_above_inf(cuda, orc):
+    g = np.random.default_rng(12)
+    x = g.standard_normal((2, 20000)).astype(np.float16).astype(np.float32)
+    x[:, ::997] = np.nan
+    for k in (1, 2048):
+        run(cuda, orc, x, k, 2, f"nan k={k}")
+
+
 def test_close_values_need_all_fine_rounds(cuda, orc):
     """Values within one fp16 step and one fp32 ulp apart: the coarse bin holds every element."""
     base = np.float32(1.0)
