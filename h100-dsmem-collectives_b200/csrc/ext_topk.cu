@@ -81,9 +81,12 @@ struct TkArgs {
     uint32_t smem_bytes;
 };
 
-// Order-preserving keys: a larger key means a larger float (NaN above +inf, -NaN below -inf).
+// Order-preserving keys: a larger key means a larger float. NaN keys do not depend on the payload (+NaN the
+// largest key, -NaN the smallest), so every NaN is an exact tie with every other NaN of its sign: on B200 the
+// payload a NaN shows was not the same in every pass of the kernel, and the passes must agree.
 __device__ __forceinline__ uint32_t key32(float v) {
     const uint32_t b = __float_as_uint(v);
+    if (isnan(v)) return (b >> 31) ? 0u : 0xFFFFFFFFu;
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 // Coarse keys (11 bits of the order-preserving key of the fp16-rounded value), two at a time: one packed

@@ -71,14 +71,17 @@ def test_ties(cuda, orc):
             run(cuda, orc, x, k, n_cta, f"ties k={k} N={n_cta}")
 
 
-@pytest.mark.xfail(strict=False, reason="NaN logits: a row whose largest values are NaN wrote no index at k = 1 "
-                   "(found on B200, cause not found yet); NaN inputs are outside the supported domain")
 def test_nan_ranks_above_inf(cuda, orc):
+    """NaN ranks above +inf (torch's order) and all NaNs of a sign tie exactly: the cut inside a group of NaN
+    ties (k smaller than the NaN count) shares them like any other exact ties."""
     g = np.random.default_rng(12)
-    x = g.standard_normal((2, 20000)).astype(np.float16).astype(np.float32)
+    x = g.standard_normal((3, 20000)).astype(np.float16).astype(np.float32)
     x[:, ::997] = np.nan
-    for k in (1, 2048):
-        run(cuda, orc, x, k, 2, f"nan k={k}")
+    x[1, 5] = np.inf
+    x[2, ::991] = -np.nan
+    for k in (1, 2, 21, 2048):
+        for n_cta in (2, 8):
+            run(cuda, orc, x, k, n_cta, f"nan k={k} N={n_cta}")
 
 
 def test_close_values_need_all_fine_rounds(cuda, orc):
