@@ -264,7 +264,8 @@ dsmem_status dsmem_rowwise_check(int device, unsigned* error_bits);
 /*
  * Exact top-k indices of every row of fp32 logits ([rows][n] row-major, 16-byte aligned base; any n): for
  * each row the indices (0..n-1) of its k largest values, written to out_indices[row][0..k) in an unspecified
- * order; among equal values at the cut, lower ranks' segments and lower indices are taken first. A cluster
+ * order; among equal values at the cut, lower ranks' segments are taken first (+NaN ranks above +inf, -NaN
+ * below -inf; all NaNs of a sign are equal). A cluster
  * of cluster_size CTAs (2, 4, 8, 16) per row; each stages a contiguous segment of ceil(n / cluster_size)
  * elements in shared memory (DSMEM_ERR_SMEM_LIMIT above about 200 KiB per segment); the radix select's
  * 2048-bin histograms meet in a two-shot DSMEM AllReduce. Replaces topk_filtered_cluster8_exact_kernel of

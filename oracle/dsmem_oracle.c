@@ -502,7 +502,8 @@ void orc_weighted_var_backward(size_t rows, size_t cols, const float* x, const f
 
 /* ----------------------------------------------------------------- exact top-k values */
 /* Order of torch.topk (the reference test's validator, roofline/workloads/hpcops_topk_cluster8.yaml): larger
- * first, NaN largest. Comparison on the order-preserving integer key of the float bits, with -0.0 == +0.0. */
+ * first, +NaN largest. Comparison on the order-preserving integer key of the float bits (-NaN smallest), with
+ * -0.0 == +0.0. */
 static uint32_t topk_key(float v) {
     uint32_t b;
     memcpy(&b, &v, 4);

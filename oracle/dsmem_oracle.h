@@ -119,7 +119,8 @@ void orc_weighted_var_backward(size_t rows, size_t cols, const float* x, const f
 double orc_wvar_backward_value(double value, double weight, double grad, double mean, double inv_sum_w,
                                double inv_std, double sum_dy, double sum_dy_centered);
 /* Exact top-k (hpc-ops topk_filtered, validated in its tests against torch.topk): the k largest values of each
- * row, sorted descending (NaN above +inf, as torch orders them), into vals[rows][k]. */
+ * row, sorted descending, into vals[rows][k]. +NaN ranks above +inf (torch's order); -NaN below -inf (the
+ * sign-respecting key order of the kernels' key transform; torch would rank it first as well). */
 void orc_topk_values(size_t rows, size_t n, size_t k, const float* x, float* vals);
 
 #ifdef __cplusplus
