@@ -202,6 +202,7 @@ def lib():
                                                        c_vp]),
         "dsmem_rowwise_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
         "dsmem_topk_launch": (c_int, [c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp]),
+        "dsmem_collective_host": (c_int, [c_int, c_int, c_int, c_int, c_size, c_vp, c_vp, c_ll, c_ll]),
         "dsmem_topk_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
         "dsmem_ceiling_tcgen05": (c_int, [c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double),
                                           ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_int)]),
@@ -682,6 +683,27 @@ def dtype_of(tensor):
     import torch
 
     return {torch.float32: Dtype.F32, torch.bfloat16: Dtype.BF16, torch.int32: Dtype.I32}[tensor.dtype]
+
+
+def collective_host(op, alg, inp, out, cluster_size, bytes_per_cta, num_clusters=None, chunk_clusters=0):
+    """The batched collective on HOST tensors (torch CPU, contiguous; page-locked for overlapped copies), synchronous
+    (dsmem_collective_host): copies in, the batch and copies out overlap in chunks on three streams."""
+    dt = dtype_of(inp)
+    if out.dtype != inp.dtype or inp.is_cuda or out.is_cuda:
+        raise ValueError("inp/out must be host (CPU) tensors of the same dtype")
+    if not (inp.is_contiguous() and out.is_contiguous()):
+        raise ValueError("inp/out must be contiguous")
+    m = msg_elems(op, cluster_size, bytes_per_cta, dt)
+    per_in = cluster_size * in_elems_per_rank(op, cluster_size, m)
+    per_out = cluster_size * out_elems_per_rank(op, cluster_size, m)
+    if num_clusters is None:
+        num_clusters = inp.numel() // per_in
+    if inp.numel() < num_clusters * per_in or out.numel() < num_clusters * per_out:
+        raise ValueError(f"tensors too small for {num_clusters} cluster problems")
+    _ok(lib().dsmem_collective_host(int(op), int(alg), int(dt), int(cluster_size), int(bytes_per_cta), inp.data_ptr(),
+                                    out.data_ptr(), int(num_clusters), int(chunk_clusters)),
+        f"dsmem_collective_host({Op(op).name}, {Alg(alg).name}, N={cluster_size}, P={bytes_per_cta})")
+    return out
 
 
 def collective(op, alg, inp, out, cluster_size, bytes_per_cta, num_clusters=None, stamps=None, smid=None,

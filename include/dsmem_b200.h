@@ -131,6 +131,16 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
                                         unsigned long long* stamps, unsigned* smid, int max_resident_clusters,
                                         dsmem_stream_t stream);
 
+/* The same batch on HOST buffers, synchronous: in and out are host memory (page-locked for overlap; pageable
+ * works, slower), laid out as for dsmem_collective_launch; on return out holds the results. The batch streams
+ * through double-buffered device staging in chunks of chunk_clusters problems (0: about 64 MiB per chunk):
+ * the host-to-device copy of chunk i+1, the collective on chunk i and the device-to-host copy of chunk i-1
+ * overlap on three streams. AUTO is resolved once for the whole batch. Device errors as dsmem_check. The
+ * host-side counterpart of the reference harness's reference() on host arrays (main.cu:129-149). */
+dsmem_status dsmem_collective_host(dsmem_op op, dsmem_alg alg, dsmem_dtype dtype, int cluster_size,
+                                   size_t bytes_per_cta, const void* host_in, void* host_out, long long num_clusters,
+                                   long long chunk_clusters);
+
 /* Static legality and shared-memory size of a configuration (the reference build matrix's
  * classification, driver.py:210-230, and the COLLECTIVE_SMEM_BYTES tag, main.cu:104-121).
  * legal = 1 if the configuration runs; smem_bytes = dynamic shared memory per CTA. */
