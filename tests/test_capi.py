@@ -211,3 +211,16 @@ def test_shipped_autotune_table_parses(dsmem, tmp_path):
         empty = tmp_path / "empty.txt"
         empty.write_text("")
         dsmem.autotune_load(empty)
+
+
+def test_capi_host_collective_argument_checks(dsmem):
+    """Host-side checks of dsmem_collective_host, which return before any device call."""
+    lib = dsmem.lib()
+    fake = ctypes.c_void_p(0x10000)
+    null = ctypes.c_void_p(None)
+    s, op, alg, dt = dsmem.Status, dsmem.Op, dsmem.Alg, dsmem.Dtype
+    assert lib.dsmem_collective_host(op.ALLREDUCE, alg.AUTO, dt.F32, 8, 65536, null, fake, 4, 0) == s.INVALID_ARGUMENT
+    assert lib.dsmem_collective_host(op.ALLREDUCE, alg.AUTO, dt.F32, 3, 65536, fake, fake, 4, 0) == s.INVALID_ARGUMENT
+    assert lib.dsmem_collective_host(op.ALLGATHER, alg.AUTO, dt.F32, 8, 100, fake, fake, 4, 0) == s.ILLEGAL_CONFIG
+    assert lib.dsmem_collective_host(op.ALLREDUCE, alg.AUTO, dt.F32, 8, 65536, fake, fake, -1, 0) == s.INVALID_ARGUMENT
+    assert lib.dsmem_collective_host(op.ALLREDUCE, alg.AUTO, dt.F32, 8, 65536, fake, fake, 0, 0) == s.OK

@@ -124,3 +124,4 @@ def test_capi_rowwise_argument_checks(dsmem):
     assert lib.dsmem_rowwise_quant_launch(null, fake, fake, 16, 4096, 8, null) == s.INVALID_ARGUMENT
     assert lib.dsmem_softmax_logits_backward_launch(fake, fake, fake, 16, 0, 8, null) == s.INVALID_ARGUMENT
     assert lib.dsmem_weighted_var_backward_launch(fake, fake, fake, fake, 0, 4096, 1e-6, 8, null) == s.OK
+
