@@ -365,7 +365,7 @@ __global__ void __launch_bounds__(kThreadsTk, 1) topk_cluster_kernel(const __gri
             if (p != prefix) return p > prefix ? 2 : 0;
             return full ? 2 : 1;
         };
-        // ---- counts. Lists: the selected list plus the candidates' verdicts. Otherwise warp w counts elements
+        // ---- counts. Lists: the selected list plus the candidates' classes. Otherwise warp w counts elements
         // [w * Lw, (w + 1) * Lw) of the segment (pass A of the rescan path; pass B below writes them).
         const int Lw = ((L + kWarpsTk - 1) / kWarpsTk + 31) & ~31;
         const int e0 = (int)w * Lw, e1 = min(L, e0 + Lw);
