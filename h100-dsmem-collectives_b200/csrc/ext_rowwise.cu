@@ -942,6 +942,30 @@ dsmem_status dsmem_weighted_var_backward_launch(const float* x, const float* wei
     return rw_launch<WWvarBwd>(a, arr, 4, rows, cols, cluster_size, reinterpret_cast<cudaStream_t>(stream));
 }
 
+dsmem_status dsmem_rowwise_query(int workload, int cols, int cluster_size, size_t* smem_bytes, int* rows_per_group,
+                                 int* stages, int* ahead) {
+    if (cols <= 0 || !(cluster_size == 1 || cluster_size == 2 || cluster_size == 4 || cluster_size == 8 ||
+                       cluster_size == 16))
+        return DSMEM_ERR_INVALID_ARGUMENT;
+    RwArgs a = blank();
+    dsmem_status s;
+    switch (workload) {
+        case 0: s = rw_plan<WQuant>(cols, cluster_size, a); break;
+        case 1: s = rw_plan<WLars>(cols, cluster_size, a); break;
+        case 2: s = rw_plan<WLnBwd>(cols, cluster_size, a); break;
+        case 3: s = rw_plan<WPearson>(cols, cluster_size, a); break;
+        case 4: s = rw_plan<WSoftmaxBwd>(cols, cluster_size, a); break;
+        case 5: s = rw_plan<WWvarBwd>(cols, cluster_size, a); break;
+        default: return DSMEM_ERR_INVALID_ARGUMENT;
+    }
+    if (s != DSMEM_OK) return s;
+    if (smem_bytes) *smem_bytes = a.smem_bytes;
+    if (rows_per_group) *rows_per_group = kWarps / a.tw;
+    if (stages) *stages = a.stages;
+    if (ahead) *ahead = a.ahead;
+    return DSMEM_OK;
+}
+
 dsmem_status dsmem_rowwise_check(int device, unsigned* error_bits) {
     unsigned v = 0;
     {

@@ -475,6 +475,15 @@ const void* tk_fn(int n) {
 
 extern "C" {
 
+dsmem_status dsmem_topk_query(int n, int cluster_size, size_t* smem_bytes) {
+    if (n <= 0 || tk_fn(cluster_size) == nullptr) return DSMEM_ERR_INVALID_ARGUMENT;
+    const int seg = ((n + cluster_size - 1) / cluster_size + 3) / 4 * 4;
+    const uint64_t smem = (uint64_t)kSegOff + ((uint64_t)seg + 4) * 4;   // + 3 elements of alignment offset
+    if (smem > dsb::kSmemLimit) return DSMEM_ERR_SMEM_LIMIT;
+    if (smem_bytes) *smem_bytes = (size_t)smem;
+    return DSMEM_OK;
+}
+
 dsmem_status dsmem_topk_launch(const float* logits, long long rows, int n, int k, int* out_indices, int cluster_size,
                                dsmem_stream_t stream) {
     if (logits == nullptr || out_indices == nullptr || rows < 0 || n <= 0 || k < 1 || k > n)
@@ -487,8 +496,9 @@ dsmem_status dsmem_topk_launch(const float* logits, long long rows, int n, int k
     if (rows == 0) return DSMEM_OK;
     const int N = cluster_size;
     const int seg = ((n + N - 1) / N + 3) / 4 * 4;
-    const uint64_t smem = (uint64_t)kSegOff + ((uint64_t)seg + 4) * 4;   // + 3 elements of alignment offset
-    if (smem > dsb::kSmemLimit) return DSMEM_ERR_SMEM_LIMIT;
+    size_t smem = 0;
+    const dsmem_status qs = dsmem_topk_query(n, N, &smem);
+    if (qs != DSMEM_OK) return qs;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return DSMEM_ERR_CUDA;
     cudaLaunchConfig_t cfg = {};

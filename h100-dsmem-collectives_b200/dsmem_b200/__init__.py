@@ -201,6 +201,9 @@ def lib():
         "dsmem_weighted_var_backward_launch": (c_int, [c_vp, c_vp, c_vp, c_vp, c_ll, c_int, ctypes.c_float, c_int,
                                                        c_vp]),
         "dsmem_rowwise_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
+        "dsmem_rowwise_query": (c_int, [c_int, c_int, c_int, ctypes.POINTER(c_size), ctypes.POINTER(c_int),
+                                        ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+        "dsmem_topk_query": (c_int, [c_int, c_int, ctypes.POINTER(c_size)]),
         "dsmem_topk_launch": (c_int, [c_vp, c_ll, c_int, c_int, c_vp, c_int, c_vp]),
         "dsmem_collective_host": (c_int, [c_int, c_int, c_int, c_int, c_size, c_vp, c_vp, c_ll, c_ll]),
         "dsmem_topk_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),

@@ -270,6 +270,11 @@ dsmem_status dsmem_weighted_var_backward_launch(const float* x, const float* wei
                                                 dsmem_stream_t stream);
 /* Read and clear the row-wise kernels' device error word of `device` (synchronous). */
 dsmem_status dsmem_rowwise_check(int device, unsigned* error_bits);
+/* Launch plan of a row-wise workload (0 quant, 1 LARS, 2 LayerNorm backward, 3 Pearson backward, 4 softmax
+ * backward, 5 weighted-variance backward) at `cols` columns: dynamic shared memory per CTA, rows per group,
+ * ring stages and groups of look-ahead; SMEM_LIMIT where the launch would return it. No device call. */
+dsmem_status dsmem_rowwise_query(int workload, int cols, int cluster_size, size_t* smem_bytes, int* rows_per_group,
+                                 int* stages, int* ahead);
 
 /*
  * Exact top-k indices of every row of fp32 logits ([rows][n] row-major, 16-byte aligned base; any n): for
@@ -286,6 +291,9 @@ dsmem_status dsmem_topk_launch(const float* logits, long long rows, int n, int k
                                int cluster_size, dsmem_stream_t stream);
 /* Read and clear the top-k kernel's device error word of `device` (synchronous). */
 dsmem_status dsmem_topk_check(int device, unsigned* error_bits);
+/* Dynamic shared memory per CTA of a top-k launch over rows of n (SMEM_LIMIT where the launch would return it).
+ * No device call. */
+dsmem_status dsmem_topk_query(int n, int cluster_size, size_t* smem_bytes);
 
 /* SM-to-SM bandwidth ceiling (the DSMEM roofline denominator). Replaces the reference's microbenchmark
  * roofline/harness/ceilings/src/dsmem_bw.cu:1-40 (ops `ld` and `tma_put`, ring +1, max active clusters,

@@ -224,3 +224,40 @@ def test_capi_host_collective_argument_checks(dsmem):
     assert lib.dsmem_collective_host(op.ALLGATHER, alg.AUTO, dt.F32, 8, 100, fake, fake, 4, 0) == s.ILLEGAL_CONFIG
     assert lib.dsmem_collective_host(op.ALLREDUCE, alg.AUTO, dt.F32, 8, 65536, fake, fake, -1, 0) == s.INVALID_ARGUMENT
     assert lib.dsmem_collective_host(op.ALLREDUCE, alg.AUTO, dt.F32, 8, 65536, fake, fake, 0, 0) == s.OK
+
+
+def test_rowwise_and_topk_plans_fit(dsmem):
+    """The row-wise and top-k launch planners (host logic, no device call): every planned launch fits the 227 KiB
+    of dynamic shared memory per CTA, has at least one ring stage and one look-ahead group at most, and returns
+    SMEM_LIMIT exactly where one row slice of every input (top-k: one segment) cannot fit."""
+    lib = dsmem.lib()
+    s = dsmem.Status
+    smem, rpg, stages, ahead = ctypes.c_size_t(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    # row slices resident per CTA: staged inputs (+ LayerNorm's gamma slice) for quant, LARS, LN, Pearson,
+    # softmax, weighted variance
+    n_inputs = [1, 3, 3, 2, 2, 3]
+    for wl in range(6):
+        for n in (1, 2, 4, 8, 16):
+            for cols in (1, 3, 5, 100, 1003, 4096, 16384, 40000, 65536, 131072):
+                st = lib.dsmem_rowwise_query(wl, cols, n, ctypes.byref(smem), ctypes.byref(rpg), ctypes.byref(stages),
+                                             ctypes.byref(ahead))
+                slice_bytes = (((cols + n - 1) // n + 3) // 4 * 4) * 4
+                if n_inputs[wl] * slice_bytes > 227 * 1024 - 1024:
+                    assert st == s.SMEM_LIMIT, (wl, n, cols, st)
+                    continue
+                assert st == s.OK, (wl, n, cols, st)
+                assert 0 < smem.value <= 232448
+                assert rpg.value in (1, 2, 4, 8) and 1 <= stages.value <= 8
+                assert ahead.value == min(1, stages.value - 1)
+    assert lib.dsmem_rowwise_query(6, 100, 8, None, None, None, None) == s.INVALID_ARGUMENT
+    assert lib.dsmem_rowwise_query(0, 100, 3, None, None, None, None) == s.INVALID_ARGUMENT
+    for n in (2, 4, 8, 16):
+        for length in (1, 7, 32768, 65536, 244650, 400000):
+            st = lib.dsmem_topk_query(length, n, ctypes.byref(smem))
+            if st == s.OK:
+                assert smem.value <= 232448
+            else:
+                assert st == s.SMEM_LIMIT and ((length + n - 1) // n) * 4 > 150 * 1024, (n, length)
+    assert lib.dsmem_topk_query(244650, 8, ctypes.byref(smem)) == s.OK            # the reference's m8_n240k
+    assert lib.dsmem_topk_query(244650, 4, ctypes.byref(smem)) == s.SMEM_LIMIT
+    assert lib.dsmem_topk_query(100, 3, ctypes.byref(smem)) == s.INVALID_ARGUMENT
