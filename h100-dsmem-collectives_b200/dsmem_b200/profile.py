@@ -7,6 +7,7 @@ kernel, and exits; sized so a full-section capture of one to three launches ends
   rmsnorm     cluster-fused RMSNorm (--rows, --hidden, --cluster)
   decoder     one Llama-2-7B decoder-layer step (--batch, --cluster; 4096 cached tokens): its seven launches
   rowwise     a row-wise reduction-reuse kernel (--workload, --rows, --cols, --cluster; fp32, 5 + cols rows seed)
+  topk        exact top-k (--rows, --cols as the row length n, --k, --cluster; randn rows)
 """
 import argparse
 import pathlib
@@ -21,7 +22,8 @@ import dsmem_b200 as D  # noqa: E402
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", choices=["allreduce", "rmsnorm", "decoder", "rowwise"], default="allreduce")
+    ap.add_argument("--case", choices=["allreduce", "rmsnorm", "decoder", "rowwise", "topk"], default="allreduce")
+    ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--workload", default="lars_momentum")
     ap.add_argument("--cols", type=int, default=16384)
     ap.add_argument("--batch", type=int, default=1)
@@ -63,6 +65,15 @@ def main(argv=None):
             RB.launch(args.workload, ins, outs, args.cluster)
         torch.cuda.synchronize()
         D.rowwise_check()
+    elif args.case == "topk":
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(args.rows * args.cols)
+        x = torch.randn(args.rows, args.cols, device="cuda", generator=gen)
+        out = torch.empty(args.rows, args.k, dtype=torch.int32, device="cuda")
+        for _ in range(args.warmup + args.launches):
+            D.topk(x, k=args.k, cluster_size=args.cluster, out=out)
+        torch.cuda.synchronize()
+        D.topk_check()
     elif args.case == "decoder":
         hid, heads, ffn, S, B = 4096, 32, 11008, 4096, args.batch
         nrm = lambda *s, std=0.02, mean=0.0: (mean + std * torch.randn(*s, device="cuda")).to(torch.bfloat16)  # noqa: E731
