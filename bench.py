@@ -436,8 +436,9 @@ def run_ours(args, rank, world, local):
         extras["rmsnorm"] = rmsnorm_config3(torch, D, hbm_peak)
         # ceilings beyond DSMEM and HBM (tcgen05 MMA, L2, shared memory), 1 / slope over two work amounts
         extras["ceilings_sm100"] = D.sm100_ceilings(reps=3)
-        extras["rowwise"] = rowwise_extras(torch, hbm_peak)
-        extras["topk"] = topk_extras(torch)
+        if world == 1:   # informative only: kept out of multi-GPU runs, where the other GPUs wait meanwhile
+            extras["rowwise"] = rowwise_extras(torch, hbm_peak)
+            extras["topk"] = topk_extras(torch)
 
     cpu = None
     if rank == 0 and world == 1:
