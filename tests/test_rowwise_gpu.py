@@ -144,3 +144,40 @@ def test_launch_order_of_shapes(cuda, orc):
         a = RC.inputs("softmax_logits_backward", 6, cols, cols)
         assert_match("softmax_logits_backward", ours(cuda, "softmax_logits_backward", a, 8),
                      RC.oracle_outputs(orc, "softmax_logits_backward", a), f"softmax 6x{cols}")
+
+
+@pytest.mark.parametrize("n", [2, 8])
+def test_edge_rows(cuda, orc, n):
+    """Rows whose slices are degenerate on some CTAs: constant rows (zero variance), zero weights over whole
+    slices (a zero-weight record in the merge), logits of -inf over whole slices (a -inf maximum in the merge)."""
+    rows, cols = 6, 4096
+    g = np.random.default_rng(40 + n)
+    a = RC.inputs("layernorm_backward", rows, cols, 9)
+    a["x"][0] = 0.5
+    a["x"][1, : cols // 2] = -1.25
+    assert_match("layernorm_backward", ours(cuda, "layernorm_backward", a, n),
+                 RC.oracle_outputs(orc, "layernorm_backward", a), f"LN edge rows N={n}")
+    a = RC.inputs("pearson_backward", rows, cols, 10)
+    a["x"][0] = 0.5
+    a["y"][1] = -2.0
+    assert_match("pearson_backward", ours(cuda, "pearson_backward", a, n),
+                 RC.oracle_outputs(orc, "pearson_backward", a), f"Pearson edge rows N={n}")
+    a = RC.inputs("weighted_var_backward", rows, cols, 11)
+    a["w"][0, : cols // 2] = 0.0
+    a["w"][1] = 0.0
+    a["x"][2] = 0.75
+    assert_match("weighted_var_backward", ours(cuda, "weighted_var_backward", a, n),
+                 RC.oracle_outputs(orc, "weighted_var_backward", a), f"wvar edge rows N={n}")
+    a = RC.inputs("softmax_logits_backward", rows, cols, 12)
+    a["z"][0, : cols // 2] = -np.inf
+    a["z"][1, cols // 4:] = -np.inf
+    a["z"][2] = 3.0
+    assert_match("softmax_logits_backward", ours(cuda, "softmax_logits_backward", a, n),
+                 RC.oracle_outputs(orc, "softmax_logits_backward", a), f"softmax edge rows N={n}")
+    a = RC.inputs("lars_momentum", rows, cols, 13)
+    a["w"][0] = 0.0
+    a["g"][1] = 0.0
+    a["m"][1] = 0.0
+    assert_match("lars_momentum", ours(cuda, "lars_momentum", a, n),
+                 RC.oracle_outputs(orc, "lars_momentum", a), f"LARS edge rows N={n}")
+    del g
