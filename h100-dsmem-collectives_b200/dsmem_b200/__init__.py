@@ -376,15 +376,24 @@ NOALLOC_MAX_PROBLEMS = 65536
 def allreduce_two_shot_noalloc(dtype, cluster_size, bytes_per_cta, in_ptr, out_ptr, num_clusters, stream=0,
                                want_status=True):
     """Two-shot batch AllReduce that allocates no device memory (dsmem_allreduce_two_shot_noalloc), for
-    callers that must not call cudaMalloc (stream capture in progress, a framework allocator that owns the
-    device memory). With want_status the call synchronises and returns the per-problem error bits (a list);
-    otherwise it returns None right after the launch."""
+    callers that cannot let a library allocate device memory (a framework allocator that has reserved the
+    GPU's memory, a fixed memory map). With want_status the call synchronises and returns the per-problem
+    error bits (a list); otherwise it returns None right after the launch (see noalloc_last_error)."""
     status = (ctypes.c_uint * max(1, num_clusters))() if want_status else None
     st = lib().dsmem_allreduce_two_shot_noalloc(int(dtype), int(cluster_size), int(bytes_per_cta),
                                                 ctypes.c_void_p(in_ptr), ctypes.c_void_p(out_ptr), int(num_clusters),
                                                 status, ctypes.c_void_p(stream or None))
     _ok(st, f"dsmem_allreduce_two_shot_noalloc(N={cluster_size}, P={bytes_per_cta}, clusters={num_clusters})")
     return list(status)[:num_clusters] if want_status else None
+
+
+def noalloc_last_error(stream=0):
+    """The device error bits of the previous allocation-free call on this device (a num_clusters = 0 call of
+    dsmem_allreduce_two_shot_noalloc: synchronises `stream`). Returns (status, bits) without raising."""
+    word = (ctypes.c_uint * 1)()
+    st = lib().dsmem_allreduce_two_shot_noalloc(int(Dtype.F32), 8, 16, None, None, 0, word,
+                                                ctypes.c_void_p(stream or None))
+    return Status(st), word[0]
 
 
 def rmsnorm(x, w, eps=1e-6, cluster_size=8, out=None, residual=None, pre_norm=None, stream=None):

@@ -325,21 +325,25 @@ dsmem_status dsmem_ceiling_smem_bw(int passes, int reps, double* ms_median, doub
 
 /*
  * Batch two-shot AllReduce that allocates no device memory. No counterpart in the reference (whose
- * harness allocates every buffer itself); it exists for callers that cannot call cudaMalloc at this
- * point: code running while a stream is captured into a CUDA graph, frameworks whose caching allocator
- * owns the device memory, callers with a fixed memory map. dsmem_collective_launch allocates a device
- * error word on its first call per device; this entry point instead keeps its scratch (error word + one
- * status word per cluster problem) in a fixed static device array of 4 * (64 + 65536) bytes, resident on
- * every GPU that loads the library until the process exits.
- *   Same result as dsmem_collective_launch(DSMEM_OP_ALLREDUCE, DSMEM_ALG_TWO_SHOT_PUSH, ...) on the same
- *   arguments (plain driver). num_clusters <= DSMEM_NOALLOC_MAX_PROBLEMS, else DSMEM_ERR_SCRATCH_LIMIT.
+ * harness allocates every buffer itself). dsmem_collective_launch allocates a device error word on its
+ * first call per device; some callers cannot let a library do that: a framework whose caching allocator
+ * has reserved the GPU's memory up front and accounts for every byte, or a program with a fixed memory map
+ * in which nothing is allocated after start-up. This entry point keeps its scratch (error word + one status
+ * word per cluster problem) in a fixed static device array of 4 * (64 + 65536) bytes, resident on every
+ * GPU that loads the library until the process exits.
+ *   Same result, bit for bit, as dsmem_collective_launch(DSMEM_OP_ALLREDUCE, DSMEM_ALG_TWO_SHOT_PUSH, ...)
+ *   on the same arguments with the plain driver (dsmem_set_pipelined(0)): same shots, same summation order.
+ *   num_clusters <= DSMEM_NOALLOC_MAX_PROBLEMS, else DSMEM_ERR_SCRATCH_LIMIT before anything is launched.
  *   status_out: host array of num_clusters words or NULL. If given, the call synchronises `stream`,
  *   copies each problem's error bits (DSMEM_ERRBIT_*) there and returns TIMEOUT/BOUNDS if any bit is set;
- *   if NULL the call returns after the launch and device-side errors are not reported.
- *   The first call on a device is its set-up: the CUDA runtime may load the library's device code (and
- *   with it the static array), and the entry point looks up the array's address and sets kernel
- *   attributes; make that first call before any stream capture. All calls share the array (cleared per
- *   call on `stream`); calls whose kernels overlap on the GPU race on it.
+ *   if NULL the call returns right after the launch.
+ *   num_clusters == 0 launches nothing; with status_out given, it synchronises `stream`, writes the previous
+ *   call's device error bits to status_out[0] and returns TIMEOUT/BOUNDS/OK from them (how a caller that
+ *   passed NULL learns of a device-side error).
+ *   The first call on a device is its set-up, made with that device current: it looks up the array's
+ *   device address and resolves all twelve kernels (3 dtypes x 4 cluster sizes), so the CUDA runtime loads
+ *   their code then and not on a later call; make that first call before any stream capture. All calls
+ *   share the array (cleared per call on `stream`); calls whose kernels overlap on the GPU race on it.
  */
 #define DSMEM_NOALLOC_MAX_PROBLEMS 65536
 dsmem_status dsmem_allreduce_two_shot_noalloc(dsmem_dtype dtype, int cluster_size, size_t bytes_per_cta,
