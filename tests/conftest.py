@@ -4,6 +4,8 @@ CPU tests (`-m "not gpu"`) cover the oracle against the reference's golden vecto
 C ABI (legality, names, tables) and that the library exports every declared symbol. GPU tests
 (`-m gpu`) are the parity tests proper and call the CUDA kernels through the C ABI.
 """
+import json
+import os
 import pathlib
 import subprocess
 import sys
@@ -55,3 +57,15 @@ def cuda():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch
+
+
+def reference_root():
+    """The reference checkout where it is mounted: $REF, else BASELINE.json's reference_path; None if absent.
+    Only CPU tests that build or read the reference's own sources use it (never a GPU test)."""
+    ref = os.environ.get("REF")
+    if not ref:
+        try:
+            ref = json.loads((ROOT / "BASELINE.json").read_text()).get("reference_path")
+        except (OSError, ValueError):
+            ref = None
+    return pathlib.Path(ref) if ref and pathlib.Path(ref).is_dir() else None

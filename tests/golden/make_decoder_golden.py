@@ -7,7 +7,8 @@ runs the function on the CPU at a small shape (2 heads x 16, hidden 32, FFN 48, 
 exactly representable in fp16 (the reference's dtype) and in bf16 (the oracle's), so both compute from identical
 values.
 
-    python tests/golden/make_decoder_golden.py      # needs the reference checkout (REF, default the mount)
+    python tests/golden/make_decoder_golden.py      # needs the reference checkout ($REF, else BASELINE.json's
+                                                    # reference_path)
 
 The fixture is committed; tests never need the reference at run time.
 """
@@ -20,7 +21,17 @@ import numpy as np
 
 HERE = pathlib.Path(__file__).resolve().parent
 OUT = HERE / "decoder_golden.npz"
-REF = pathlib.Path(os.environ.get("REF", "/root/reference"))
+
+def _reference_root():
+    import json
+
+    ref = os.environ.get("REF") or json.loads((HERE.parents[1] / "BASELINE.json").read_text()).get("reference_path")
+    if not ref or not pathlib.Path(ref).is_dir():
+        raise SystemExit("set REF to the reference checkout")
+    return pathlib.Path(ref)
+
+
+REF = _reference_root()
 
 
 def main():

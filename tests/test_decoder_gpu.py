@@ -6,7 +6,7 @@ the attention-block output o within max abs 2e-2, MAE 1e-3 and relative L2 1e-2;
 RoPE) and the layer output within relative L2 1e-2 and max abs 2e-2 * max|ref|. The kernel rounds the
 stage boundaries (x, xn, the attention output, h, hn, SiLU(gate)*up) to bf16; the oracle does not.
 Shapes: reduced (hidden 1024, 8 heads, ffn 2816, 300 cached tokens) at batch 1, 3, 16 and cluster 4 / 8,
-and the full Llama-2-7B layer (hidden 4096, 32 heads, ffn 11008, 4096 cached tokens) at batch 1.
+and the full Llama-2-7B layer (hidden 4096, 32 heads, ffn 11008, 4096 cached tokens) at batch 1, 4 and 16.
 """
 
 import numpy as np
@@ -86,8 +86,11 @@ def test_decoder_reduced_shape(cuda, orc, B, n):
     assert not fails, "\n".join(fails)
 
 
-def test_decoder_llama2_7b_batch1(cuda, orc):
-    fails = check(run_layer(cuda, orc, 1, 4096, 32, 11008, 4096, 4097, 8, seed=7))
+@pytest.mark.parametrize("B,n", [(1, 8), (4, 8), (16, 8), (16, 4)])
+def test_decoder_llama2_7b(cuda, orc, B, n):
+    """The full Llama-2-7B layer at configs[3]'s batches 1, 4 and 16 (batch 16's attention runs at cluster 2,
+    its (sequence, head) count being above 96), plus batch 16 with cluster-4 projections."""
+    fails = check(run_layer(cuda, orc, B, 4096, 32, 11008, 4096, 4097, n, seed=7 + B))
     assert not fails, "\n".join(fails)
 
 
