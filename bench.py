@@ -40,7 +40,7 @@ BATCH_BYTES = 2 << 30     # input bytes per GPU per step
 HBM_FALLBACK_GBS = 6650.0
 # kernels the library launches for a batch (more than one cluster problem) with its pipelined drivers on
 KERNEL_NAMES = {"TWO_SHOT_PUSH": "two_shot_pipelined_kernel<AR_TwoShotPipelined<{n},float,Sum>>",
-                "RS_PUSH_GLOBAL_AG": "two_shot_pipelined_kernel<AR_RsPushGlobalAgPipelined<{n},float,Sum>>"}
+                "RS_PUSH_GLOBAL_AG": "rs_global_ag_stream_kernel<AR_RsGlobalAgStream<{n},float,Sum>>"}
 
 
 def parse():

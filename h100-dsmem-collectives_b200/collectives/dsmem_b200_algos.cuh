@@ -1862,6 +1862,8 @@ struct BatchArgs {
     uint32_t M;                       // elements per rank block
     uint32_t smem_bytes;              // dynamic shared memory of the launch
     uint32_t sub;                     // pipelined drivers: units per problem (M / sub elements each)
+    uint32_t depth;                   // streamed drivers: stages of the ring (bounded by the window)
+    uint32_t lag;                     // streamed drivers: units of reduce-scatter in flight
 };
 
 __device__ __forceinline__ void ctx_init(Ctx& c, uint32_t smem_bytes, unsigned* err, unsigned long long limit) {
@@ -2024,21 +2026,6 @@ struct BC_Binomial {
 template <int N_, typename T_, class Op_>
 struct AR_TwoShotPipelined {
     DSB_TRAITS(AllReduce, 4)
-    static constexpr bool kGlobalAllGather = false;
-    __host__ __device__ static constexpr bool legal(uint32_t M) { return AR_TwoShotPush<N_, T_, Op_>::legal(M); }
-    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 3ull * M * B; }
-};
-
-// Pipelined batch driver of AR_RsPushGlobalAg (below): shot 1 exactly as the two-shot's; the all-gather
-// is replaced by bulk stores of the reduced chunk into all N ranks' output rows, so only the reduce-scatter
-// crosses the SM-to-SM network. Slot reuse, ordered by shot 2 in the two-shot, is ordered here by credits:
-// after its reduce, each CTA arrives on every peer's credit barrier (N-1 arrivals per unit), and a CTA
-// waits for the credits of unit k-1 before its shot 1 of unit k. The same credits tell it that its own
-// shot-1 copies of unit k-1 were received, i.e. finished reading the X buffer the next load refills.
-template <int N_, typename T_, class Op_>
-struct AR_RsPushGlobalAgPipelined {
-    DSB_TRAITS(AllReduce, 4)
-    static constexpr bool kGlobalAllGather = true;
     __host__ __device__ static constexpr bool legal(uint32_t M) { return AR_TwoShotPush<N_, T_, Op_>::legal(M); }
     __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 3ull * M * B; }
 };
@@ -2048,14 +2035,12 @@ __global__ void __launch_bounds__(256) two_shot_pipelined_kernel(const BatchArgs
     using T = typename A::T;
     using Op = typename A::Op;
     constexpr int N = A::kN;
-    constexpr bool kGlobalAG = A::kGlobalAllGather;
-    constexpr int kLoad0 = 0, kRS = 2, kAG = 3, kCredit = 3;   // barrier 3: shot 2, or the credits
+    constexpr int kLoad0 = 0, kRS = 2, kAG = 3;
     Ctx c;
     ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
     flag_init(c);
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 3; ++i) mbar_init(c.bar(i), 1);
-        mbar_init(c.bar(3), kGlobalAG ? N - 1 : 1);
+        for (int i = 0; i < 4; ++i) mbar_init(c.bar(i), 1);
         fence_mbar_init();
     }
     cluster_sync();   // every barrier of the cluster initialised before any remote push
@@ -2085,15 +2070,6 @@ __global__ void __launch_bounds__(256) two_shot_pipelined_kernel(const BatchArgs
         arm(c, kLoad0 + (int)xb, UB);
         bulk_load_g2s(c.sa + kD0 + xb * UB, in + off, UB, c.bar(kLoad0 + (int)xb));
     };
-    // thread 0: the N-1 credits of the previous unit (global all-gather only)
-    auto credit_wait = [&]() {
-        const uint32_t par = (c.phase >> kCredit) & 1u;
-        c.phase ^= 1u << kCredit;
-        if (!c.dead && !mbar_wait_parity_until(c.bar(kCredit), par, c.deadline)) {
-            c.dead = true;
-            report_timeout(c, kCredit);
-        }
-    };
     if (threadIdx.x == 0 && units > 0) load_unit(0, 0);
     for (long long k = 0; k < units; ++k) {
         const uint32_t x = (uint32_t)(k & 1), X = kD0 + x * UB, s = (uint32_t)(k % S);
@@ -2105,7 +2081,6 @@ __global__ void __launch_bounds__(256) two_shot_pipelined_kernel(const BatchArgs
         wait(c, kLoad0 + (int)x);   // my input for unit k is in X
         if (s == 0) c.st.mark(0);
         if (threadIdx.x == 0) {
-            if (kGlobalAG && k > 0) credit_wait();   // every peer consumed its slots of unit k-1
             // shot 1: chunk j of my input -> slot[b] of CTA j
             arm(c, kRS, (N - 1) * CB);
             for (uint32_t j = 1; j < (uint32_t)N; ++j) {
@@ -2135,51 +2110,209 @@ __global__ void __launch_bounds__(256) two_shot_pipelined_kernel(const BatchArgs
         fence_proxy_async_smem();
         __syncthreads();
         if (s + 1 == S) c.st.round(0);
-        if constexpr (kGlobalAG) {
-            if (threadIdx.x == 0) {
-                // credits: my slots of unit k are consumed (release orders the reduce's reads before them)
-                for (uint32_t j = 1; j < (uint32_t)N; ++j) mbar_arrive_remote(c.bar(kCredit), (c.rank + j) % N);
-                // all-gather through the outputs: my reduced chunk into row r of every rank of the problem
-                const uint64_t base = unit_off(k) - (uint64_t)c.rank * a.M + (uint64_t)c.rank * (CB / A::B);
-                for (uint32_t r = 0; r < (uint32_t)N; ++r) {
-                    const uint64_t off = base + (uint64_t)r * a.M;
-                    if (off + CB / A::B > total) {
-                        report(c, DSMEM_ERR_BIT_BOUNDS);
-                        continue;
-                    }
-                    bulk_store_s2g(out + off, c.sa + X + c.rank * CB, CB);
+        if (threadIdx.x == 0) {
+            // shot 2: my reduced chunk -> position b of every peer
+            arm(c, kAG, (N - 1) * CB);
+            for (uint32_t j = 1; j < (uint32_t)N; ++j) {
+                const uint32_t dst = (c.rank + j) % N;
+                push<N>(c, dst, X + c.rank * CB, X + c.rank * CB, CB, kAG);
+            }
+        }
+        wait(c, kAG);   // every reduced chunk is in X
+        if (s + 1 == S) {
+            c.st.round(1);
+            c.st.mark(1);
+        }
+        if (threadIdx.x == 0) {
+            bulk_store_s2g(out + unit_off(k), c.sa + X, UB);
+            bulk_commit();
+        }
+    }
+    if (threadIdx.x == 0) bulk_wait_all0();
+    finish(c);   // no CTA leaves while a peer may still push into it
+}
+
+// -----------------------------------------------------------------------------------------------------
+// Streamed batch driver of AR_RsPushGlobalAg (alg rs_push_global_ag; a B200 extension): the reduce-scatter
+// shot of the two-shot AllReduce (allreduce__two_shot_push__trtllm.cu:31-45) over the SM-to-SM network, and
+// the all-gather through the outputs, so (N-1)/N * P bytes per CTA cross the SM-to-SM network instead of the
+// two-shot's 2(N-1)/N * P. Warp-specialised and deeply pipelined:
+//   * warp 0, one thread (producer): streams the CTA's units (sub-vectors of U elements of its input rows)
+//     into a ring of D stages by one-CTA bulk copies global -> shared, D - L units ahead, and once a unit
+//     has landed pushes chunk j of it into stage slot (b - j - 1) mod N of CTA j (N - 1 bulk copies
+//     completing on CTA j's reduce-scatter barrier of the stage);
+//   * warps 1..W (consumers): for each unit, wait until their own input and the N - 1 partials of their
+//     chunk b have landed, sum the N partials in rank order 0..N-1 (the plain driver's order, so the result
+//     is the same bit for bit), and store the sum from registers straight into position b of all N output
+//     rows of the problem (16-byte streaming stores, no shared-memory round trip); then one consumer thread
+//     arrives on the stage's credit barrier of every peer and on the local `done` barrier.
+//   * A stage is reused for unit k + D only after the local consumers are done with unit k and all N - 1
+//     peers' credits for unit k have arrived: the peers have consumed the chunks this CTA pushed (so its
+//     bulk copies have finished reading the stage) and freed the slots it pushes into next. L units of
+//     reduce-scatter are in flight while D - L loads stream in; there is no cluster barrier per unit.
+//   * Before leaving, the producer drains the credits of the last D units, so no remote arrive or copy aimed
+//     at this CTA is in flight at exit.
+// Layout: mbarriers in a static array (4 per stage); dynamic window: stage s at kD0 + s * stage_bytes(U),
+// the unit's input (U elements) followed by N - 1 received partials of chunk b (U / N elements each).
+template <int N_, typename T_, class Op_>
+struct AR_RsGlobalAgStream {
+    DSB_TRAITS(AllReduce, 0)
+    static constexpr int kMaxDepth = 8;
+    static constexpr int kConsumerWarps = 4;
+    static constexpr int kThreads = 32 * (1 + kConsumerWarps);
+    __host__ __device__ static constexpr bool legal(uint32_t U) { return AR_TwoShotPush<N_, T_, Op_>::legal(U); }
+    __host__ __device__ static constexpr uint64_t stage_bytes(uint32_t U) {
+        return (uint64_t)U * B + (uint64_t)(N_ - 1) * (U / N_) * B;
+    }
+    // smallest launchable window (depth 2); the launcher grows the depth to what it asks for
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t U) { return kD0 + 2ull * stage_bytes(U); }
+};
+
+template <class A>
+__global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const BatchArgs a) {
+    using T = typename A::T;
+    using Op = typename A::Op;
+    constexpr int N = A::kN;
+    constexpr uint32_t kNC = 32u * A::kConsumerWarps;   // consumer threads
+    __shared__ __align__(8) unsigned long long bars[4 * A::kMaxDepth];
+    Ctx c;
+    ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
+    flag_init(c);
+    const uint32_t S = a.sub, U = a.M / S, UB = U * A::B, CB = UB / N, C = U / N, nl = CB >> 4;
+    const uint32_t stage = (uint32_t)A::stage_bytes(U);
+    const uint32_t D = min(min(a.depth, (a.smem_bytes - kD0) / stage), (uint32_t)A::kMaxDepth);
+    const uint32_t L = min(max(a.lag, 1u), D - 1u);   // units of reduce-scatter in flight
+    auto full = [&](uint32_t s) { return smem_u32(&bars[4 * s + 0]); };
+    auto rs = [&](uint32_t s) { return smem_u32(&bars[4 * s + 1]); };
+    auto credit = [&](uint32_t s) { return smem_u32(&bars[4 * s + 2]); };
+    auto done = [&](uint32_t s) { return smem_u32(&bars[4 * s + 3]); };
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < D; ++s) {
+            mbar_init(full(s), 1);
+            mbar_init(rs(s), 1);
+            mbar_init(credit(s), N - 1);
+            mbar_init(done(s), 1);
+        }
+        fence_mbar_init();
+    }
+    cluster_sync();   // every barrier of the cluster initialised before any remote push or arrive
+    const uint64_t total = (uint64_t)a.num_problems * N * a.M;   // elements of `in` and of `out`
+    const T* in = static_cast<const T*>(a.in);
+    T* out = static_cast<T*>(a.out);
+    const long long step = (long long)num_clusters();
+    const long long first = (long long)cluster_id();
+    const long long mine = first < a.num_problems ? (a.num_problems - 1 - first) / step + 1 : 0;
+    const long long units = mine * S;
+    auto problem_of = [&](long long k) { return first + (k / S) * step; };
+    // element offset of row r, sub-vector k % S, of unit k's problem
+    auto row_off = [&](long long k, uint32_t r) {
+        return ((uint64_t)problem_of(k) * N + r) * a.M + (uint64_t)(k % S) * U;
+    };
+    auto X = [&](uint32_t s) { return kD0 + s * stage; };
+    auto R = [&](uint32_t s) { return kD0 + s * stage + UB; };   // slot i at R + i * CB
+    // bounded wait on a static barrier; `ph` holds this thread's parity bit per stage
+    auto await = [&](uint32_t bar, uint32_t& ph, uint32_t s, int id) {
+        const uint32_t par = (ph >> s) & 1u;
+        ph ^= 1u << s;
+        if (c.dead || mbar_try_wait_parity(bar, par)) return;
+        if (!mbar_wait_parity_until(bar, par, c.deadline)) {
+            c.dead = true;
+            report_timeout(c, id);
+        }
+    };
+    if (threadIdx.x == 0 && units > 0) {
+        // ---------------------------------------------------------------- producer
+        uint32_t ph_full = 0, ph_credit = 0, ph_done = 0;
+        auto release = [&](long long j) {   // stage of unit j free: local consumers and every peer done
+            const uint32_t s = (uint32_t)(j % D);
+            await(done(s), ph_done, s, 3);
+            await(credit(s), ph_credit, s, 2);
+        };
+        auto issue_load = [&](long long k) {
+            const uint32_t s = (uint32_t)(k % D);
+            if (k >= (long long)D) release(k - D);
+            c.unit = (uint32_t)k;
+            const uint64_t off = row_off(k, c.rank);
+            if (off + U > total) {
+                report(c, DSMEM_ERR_BIT_BOUNDS);
+                return;
+            }
+            mbar_arrive_expect_tx(rs(s), (N - 1) * CB);   // the peers' partials of chunk b for unit k
+            mbar_arrive_expect_tx(full(s), UB);
+            bulk_load_g2s(c.sa + X(s), in + off, UB, full(s));
+        };
+        const long long ahead = (long long)(D - L);
+        for (long long k = 0; k < units && k < ahead; ++k) issue_load(k);
+        for (long long k = 0; k < units; ++k) {
+            const uint32_t s = (uint32_t)(k % D);
+            c.deadline = globaltimer() + c.wait_limit;
+            if (k % S == 0 && a.smid != nullptr) a.smid[(uint64_t)problem_of(k) * N + c.rank] = smid();
+            await(full(s), ph_full, s, 0);
+            for (uint32_t j = 1; j < (uint32_t)N; ++j) {
+                const uint32_t dst = (c.rank + j) % N, slot = (c.rank + N - dst - 1) % N;
+                const uint32_t to = R(s) + slot * CB, from = X(s) + dst * CB;
+                if (((to | from | CB) & 15u) != 0u || CB == 0u || to + CB > c.smem_bytes || from + CB > c.smem_bytes) {
+                    report(c, DSMEM_ERR_BIT_BOUNDS);
+                    continue;
                 }
-                bulk_commit();
+                bulk_push(dst, c.sa + to, c.sa + from, CB, rs(s));
             }
-            if (s + 1 == S) c.st.mark(1);
-        } else {
-            if (threadIdx.x == 0) {
-                // shot 2: my reduced chunk -> position b of every peer
-                arm(c, kAG, (N - 1) * CB);
-                for (uint32_t j = 1; j < (uint32_t)N; ++j) {
-                    const uint32_t dst = (c.rank + j) % N;
-                    push<N>(c, dst, X + c.rank * CB, X + c.rank * CB, CB, kAG);
+            if (k + ahead < units) issue_load(k + ahead);
+        }
+        c.deadline = globaltimer() + c.wait_limit;
+        for (long long j = units > (long long)D ? units - D : 0; j < units; ++j) release(j);
+    } else if (threadIdx.x >= 32) {
+        // ---------------------------------------------------------------- consumers
+        const uint32_t tc = threadIdx.x - 32;
+        uint32_t ph_full = 0, ph_rs = 0;
+        for (long long k = 0; k < units; ++k) {
+            const uint32_t s = (uint32_t)(k % D), sub = (uint32_t)(k % S);
+            c.unit = (uint32_t)k;
+            c.deadline = globaltimer() + c.wait_limit;
+            unsigned long long* st = a.stamps != nullptr && tc == 0
+                                         ? a.stamps + ((uint64_t)problem_of(k) * N + c.rank) * kStamps
+                                         : nullptr;
+            await(full(s), ph_full, s, 0);
+            if (st != nullptr && sub == 0) st[0] = globaltimer();
+            await(rs(s), ph_rs, s, 1);
+            if (st != nullptr && sub + 1 == S) st[2] = globaltimer();
+            const uint4* own = c.ptr<const uint4>(X(s) + c.rank * CB);
+            const uint4* slots = c.ptr<const uint4>(R(s));
+            uint4* rows[N];
+            bool ok = true;
+#pragma unroll
+            for (int r = 0; r < N; ++r) {
+                const uint64_t o = row_off(k, (uint32_t)r) + (uint64_t)c.rank * C;
+                ok = ok && o + C <= total;
+                rows[r] = reinterpret_cast<uint4*>(out + o);
+            }
+            if (!ok) {
+                if (tc == 0) report(c, DSMEM_ERR_BIT_BOUNDS);
+            } else {
+                for (uint32_t u = tc; u < nl; u += kNC) {
+                    uint4 v[N];
+#pragma unroll
+                    for (int r = 0; r < N; ++r)
+                        v[r] = r == (int)c.rank ? own[u] : slots[((r + N - (int)c.rank - 1) % N) * nl + u];
+                    auto acc = Pk<T, Op>::open(v[0]);
+#pragma unroll
+                    for (int r = 1; r < N; ++r) Pk<T, Op>::add(acc, v[r]);
+                    const uint4 res = Pk<T, Op>::close(acc);
+#pragma unroll
+                    for (int r = 0; r < N; ++r) __stcs(rows[r] + u, res);
                 }
             }
-            wait(c, kAG);   // every reduced chunk is in X
-            if (s + 1 == S) {
-                c.st.round(1);
-                c.st.mark(1);
-            }
-            if (threadIdx.x == 0) {
-                bulk_store_s2g(out + unit_off(k), c.sa + X, UB);
-                bulk_commit();
+            asm volatile("bar.sync 1, %0;" ::"r"(kNC) : "memory");   // every consumer has read the stage
+            if (tc == 0) {
+                // relaxed: the credits only release the stage's shared memory, whose reads are complete (their
+                // values are already summed and stored); a release arrive would also wait for the global stores
+                // just issued (~4 us under load) and stall the consumers on every unit
+                for (uint32_t j = 1; j < (uint32_t)N; ++j) mbar_arrive_remote_relaxed(credit(s), (c.rank + j) % N);
+                mbar_arrive_relaxed(done(s));
+                if (st != nullptr && sub + 1 == S) st[1] = globaltimer();
             }
         }
     }
-    if (kGlobalAG && threadIdx.x == 0 && units > 0) {
-        // the credits of the last unit: every remote arrive aimed at this CTA has been performed (and my
-        // last pushes were consumed) before the cluster's final barrier, so nothing is in flight at exit
-        c.unit = (uint32_t)units;
-        c.deadline = globaltimer() + c.wait_limit;
-        credit_wait();
-    }
-    if (threadIdx.x == 0) bulk_wait_all0();
     finish(c);   // no CTA leaves while a peer may still push into it
 }
 

@@ -183,6 +183,16 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t bar, uint32_t rank) 
     const uint32_t remote = mapa(bar, rank);
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
 }
+// Arrives without release semantics (PTX .relaxed): they order nothing before them, so they do not wait for
+// this thread's outstanding global stores. For a consumer that only signals "my reads of this buffer are done":
+// those reads have returned their values before the arrive issues.
+__device__ __forceinline__ void mbar_arrive_relaxed(uint32_t bar) {
+    asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t bar, uint32_t rank) {
+    const uint32_t remote = mapa(bar, rank);
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
 // One probe of the phase with parity `parity`; true once it has completed. Acquire at cluster
 // scope, so plain remote stores released by a peer's arrive are visible after success.
 __device__ __forceinline__ bool mbar_try_wait_parity(uint32_t bar, uint32_t parity) {

@@ -130,6 +130,11 @@ struct State {
     unsigned long long wait_limit_ns = 1000000000ull;
     bool pipelined = true;        // batches use a pipelined driver where one exists
     uint64_t unit_bytes = 16384;  // pipelined drivers: largest sub-vector per CTA
+    // Streamed drivers (measured on B200 at 64 KiB per CTA, 2 GiB batches): 16 KiB units, one unit of
+    // reduce-scatter in flight, 3 stages (2 at cluster size 16, where the smaller window fits more clusters).
+    uint64_t stream_unit_bytes = 16384;  // largest sub-vector per CTA
+    int stream_depth = 0;                // stages of the ring; 0: by cluster size as above
+    int stream_lag = 1;                  // units of reduce-scatter in flight
 };
 
 State& st() {
@@ -314,10 +319,10 @@ cudaError_t ensure_attrs(DeviceState& d, const void* fn, int n, uint64_t smem) {
 }
 
 void fill_cfg(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, int n, long long clusters, uint64_t smem,
-              cudaStream_t stream) {
+              cudaStream_t stream, int threads = kThreads) {
     cfg = cudaLaunchConfig_t{};
     cfg.gridDim = dim3((unsigned)(clusters * n), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3((unsigned)threads, 1, 1);
     cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = stream;
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -328,7 +333,7 @@ void fill_cfg(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, int n, long lo
     cfg.numAttrs = 1;
 }
 
-cudaError_t occupancy(DeviceState& d, const void* fn, int n_cta, uint64_t smem, int* out) {
+cudaError_t occupancy(DeviceState& d, const void* fn, int n_cta, uint64_t smem, int* out, int threads = kThreads) {
     auto key = std::make_pair(fn, smem);
     auto it = d.occupancy.find(key);
     if (it != d.occupancy.end()) {
@@ -337,7 +342,7 @@ cudaError_t occupancy(DeviceState& d, const void* fn, int n_cta, uint64_t smem, 
     }
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[1];
-    fill_cfg(cfg, attr, n_cta, 1, smem, nullptr);
+    fill_cfg(cfg, attr, n_cta, 1, smem, nullptr, threads);
     int n = 0;
     cudaError_t r = cudaOccupancyMaxActiveClusters(&n, fn, &cfg);
     if (r != cudaSuccess) return r;
@@ -361,7 +366,7 @@ cudaError_t error_word(DeviceState& d, unsigned** out) {
 // unit_bytes per CTA (default 16 KiB: three unit buffers in 48 KiB, four CTAs per SM); 0 if none.
 // Caller holds st().mu.
 uint32_t pipeline_units(const KernelEntry* e, uint32_t m) {
-    const uint64_t unit = st().unit_bytes;
+    const uint64_t unit = e->stage_pipe != nullptr ? st().stream_unit_bytes : st().unit_bytes;
     const uint64_t bytes = (uint64_t)m * e->elem_bytes;
     const uint32_t s0 = (uint32_t)std::max<uint64_t>(1, (bytes + unit - 1) / unit);
     for (uint32_t s = s0; s <= m && s < s0 + 4096; ++s)
@@ -451,6 +456,7 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
     if (cudaGetDevice(&dev) != cudaSuccess) return DSMEM_ERR_CUDA;
     dsb::BatchArgs a{};
     int resident = 0;
+    int threads = kThreads;
     const void* fn = e->fn;
     {
         State& g = st();
@@ -462,16 +468,25 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
         a.sub = 1;
         if (g.pipelined && (num_clusters > 1 || pipe_only) && e->fn_pipe != nullptr) {
             const uint32_t sub = pipeline_units(e, m);
-            const uint64_t sp = sub ? e->smem_pipe(m / sub) : 0;
+            uint64_t sp = sub ? e->smem_pipe(m / sub) : 0;
             if (sub && sp <= dsb::kSmemLimit && sp <= (uint64_t)d.optin) {
                 fn = e->fn_pipe;
-                smem = sp;
                 a.sub = sub;
+                if (e->stage_pipe != nullptr) {   // streamed: as many stages as asked for and fit (>= 2)
+                    const uint64_t stage = e->stage_pipe(m / sub), lim = std::min<uint64_t>(dsb::kSmemLimit, d.optin);
+                    uint32_t depth = g.stream_depth > 0 ? (uint32_t)g.stream_depth : (e->n >= 16 ? 2u : 3u);
+                    while (depth > 2 && dsb::kD0 + depth * stage > lim) --depth;
+                    sp = dsb::kD0 + depth * stage;
+                    a.depth = depth;
+                    a.lag = (uint32_t)std::max(1, g.stream_lag);
+                    threads = e->threads_pipe;
+                }
+                smem = sp;
             }
         }
         if (fn == e->fn && pipe_only) return DSMEM_ERR_SMEM_LIMIT;
         if (ensure_attrs(d, fn, e->n, smem) != cudaSuccess) return DSMEM_ERR_CUDA;
-        if (occupancy(d, fn, e->n, smem, &resident) != cudaSuccess) return DSMEM_ERR_CUDA;
+        if (occupancy(d, fn, e->n, smem, &resident, threads) != cudaSuccess) return DSMEM_ERR_CUDA;
         if (resident < 1) return DSMEM_ERR_SMEM_LIMIT;   // the cluster cannot be placed (main.cu:221)
         if (error_word(d, &a.err) != cudaSuccess) return DSMEM_ERR_CUDA;
         a.wait_limit_ns = g.wait_limit_ns;
@@ -487,7 +502,7 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
     a.smem_bytes = (uint32_t)smem;
     cudaLaunchConfig_t cfg;
     cudaLaunchAttribute attr[1];
-    fill_cfg(cfg, attr, e->n, clusters, smem, reinterpret_cast<cudaStream_t>(stream));
+    fill_cfg(cfg, attr, e->n, clusters, smem, reinterpret_cast<cudaStream_t>(stream), threads);
     void* args[] = {&a};
     if (cudaLaunchKernelExC(&cfg, fn, args) != cudaSuccess) return DSMEM_ERR_CUDA;
     return DSMEM_OK;
@@ -652,6 +667,17 @@ dsmem_status dsmem_set_pipeline_unit_bytes(size_t bytes) {
     if (bytes < 256 || bytes > 65536 || (bytes & 15u)) return DSMEM_ERR_INVALID_ARGUMENT;
     std::lock_guard<std::mutex> lock(st().mu);
     st().unit_bytes = bytes;
+    return DSMEM_OK;
+}
+
+dsmem_status dsmem_set_stream_pipeline(size_t unit_bytes, int depth, int lag) {
+    if (unit_bytes < 256 || unit_bytes > 65536 || (unit_bytes & 15u) || (depth != 0 && (depth < 2 || depth > 8)) ||
+        lag < 1 || lag >= (depth == 0 ? 2 : depth))
+        return DSMEM_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> lock(st().mu);
+    st().stream_unit_bytes = unit_bytes;
+    st().stream_depth = depth;
+    st().stream_lag = lag;
     return DSMEM_OK;
 }
 

@@ -65,6 +65,29 @@ void add_pipelined(Registry& r, int alg) {
             e.smem_pipe = &smem_fn<PP>;
         }
 }
+template <class A>
+uint64_t stage_fn(uint32_t m) {
+    return A::stage_bytes(m);
+}
+// Attach the streamed batch driver P<N> (rs_global_ag_stream_kernel) to the entry of (alg, N).
+template <template <int, typename, class> class P, int N>
+void add_streamed(Registry& r, int alg) {
+    using PP = P<N, ElemT, Sum>;
+    for (KernelEntry& e : r)
+        if (e.op == 0 && e.alg == alg && e.dtype == DSB_DT && e.n == N) {
+            e.fn_pipe = reinterpret_cast<const void*>(&rs_global_ag_stream_kernel<PP>);
+            e.smem_pipe = &smem_fn<PP>;
+            e.stage_pipe = &stage_fn<PP>;
+            e.threads_pipe = PP::kThreads;
+        }
+}
+template <template <int, typename, class> class P>
+void add_streamed_all_n(Registry& r, int alg) {
+    add_streamed<P, 2>(r, alg);
+    add_streamed<P, 4>(r, alg);
+    add_streamed<P, 8>(r, alg);
+    add_streamed<P, 16>(r, alg);
+}
 template <template <int, typename, class> class P>
 void add_pipelined_all_n(Registry& r, int alg) {
     add_pipelined<P, 2>(r, alg);
@@ -92,7 +115,7 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<AR_TwoShotPush>(r, kTwoShotPush);
     add_pipelined_all_n<AR_TwoShotPipelined>(r, kTwoShotPush);
     add_all_n<AR_RsPushGlobalAg>(r, kRsPushGlobalAg);
-    add_pipelined_all_n<AR_RsPushGlobalAgPipelined>(r, kRsPushGlobalAg);
+    add_streamed_all_n<AR_RsGlobalAgStream>(r, kRsPushGlobalAg);
     add_all_n<AR_ReduceBcastBinomial>(r, kReduceBcastBinomial);
     add_all_n<AR_AtomicAllPush>(r, kAtomicAllPush);
     add_all_n<AR_Mesh2D>(r, kMesh2D);

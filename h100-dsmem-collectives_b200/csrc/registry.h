@@ -18,6 +18,10 @@ struct KernelEntry {
     // than one problem when its shared memory fits; nullptr if the algorithm has none.
     const void* fn_pipe = nullptr;
     uint64_t (*smem_pipe)(uint32_t m) = nullptr;
+    // Streamed drivers (a ring of stages, warp-specialised): bytes of one stage for a unit of m elements
+    // (nullptr: not streamed; the window is smem_pipe(m)) and the block size of fn_pipe.
+    uint64_t (*stage_pipe)(uint32_t m) = nullptr;
+    int threads_pipe = 256;
 };
 
 using Registry = std::vector<KernelEntry>;

@@ -185,6 +185,7 @@ def lib():
         "dsmem_selftest_timeout": (c_int, [c_ull, c_vp]),
         "dsmem_set_pipelined": (c_int, [c_int]),
         "dsmem_set_pipeline_unit_bytes": (c_int, [c_size]),
+        "dsmem_set_stream_pipeline": (c_int, [c_size, c_int, c_int]),
         "dsmem_allreduce_two_shot_noalloc": (c_int, [c_int, c_int, c_size, c_vp, c_vp, c_int,
                                                      ctypes.POINTER(ctypes.c_uint), c_vp]),
         "dsmem_rmsnorm_launch": (c_int, [c_int, c_vp, c_vp, ctypes.c_float, c_ll, c_int, c_int, c_vp, c_vp]),
@@ -342,6 +343,12 @@ def set_pipelined(enable):
 def set_pipeline_unit_bytes(nbytes):
     """Largest sub-vector per CTA of the pipelined drivers (default 16 KiB)."""
     _ok(lib().dsmem_set_pipeline_unit_bytes(int(nbytes)), "dsmem_set_pipeline_unit_bytes")
+
+
+def set_stream_pipeline(unit_bytes=16384, depth=0, lag=1):
+    """Sub-vector size, ring depth (0: by cluster size) and reduce-scatter units in flight of the streamed
+    rs_push_global_ag driver; the defaults are the measured best."""
+    _ok(lib().dsmem_set_stream_pipeline(int(unit_bytes), int(depth), int(lag)), "dsmem_set_stream_pipeline")
 
 
 def autotune_load(path):

@@ -10,8 +10,9 @@ For every op x algorithm x cluster size N in {2, 4, 8, 16} x bytes per CTA P in 
            `--reps` launches; algbw = P / span, busbw = algbw * the op's bus factor (perf_report.py:99-100:
            AllReduce 2(N-1)/N, the others (N-1)/N);
   batch    a grid-filled batch of independent problems (enough for four full waves of resident clusters and
-           at least 64 MiB of input), CUDA events over `--batch-reps` launches; algbw = problems * N * P /
-           time (the whole batch's per-CTA payloads, as bench.py's value).
+           at least `--batch-mib` MiB of input, default 256: pipelined drivers need many problems per resident
+           cluster to reach their steady state), CUDA events over `--batch-reps` launches; algbw = problems * N *
+           P / time (the whole batch's per-CTA payloads, as bench.py's value).
 The AUTO table (one line per (op, N, P, dtype, regime) with the fastest algorithm) is the input of
 dsmem_autotune_table_load; regime `single` picks by span, `batch` by batch throughput.
 """
@@ -36,7 +37,7 @@ ALG_NAMES = {a: (a.name.lower() if a != Alg.MESH_2D else "2d_mesh") for a in Alg
 PIPELINED = (Alg.TWO_SHOT_PUSH, Alg.RS_PUSH_GLOBAL_AG)
 
 
-def measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps):
+def measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps, batch_bytes=256 << 20):
     m = msg_elems(op, n, p, dt)
     per_in = n * in_elems_per_rank(op, n, m)
     per_out = n * out_elems_per_rank(op, n, m)
@@ -52,12 +53,12 @@ def measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps)
     s = st.view(reps, n, STAMPS_PER_RANK).cpu()
     spans = (s[:, :, 1].max(dim=1).values - s[:, :, 0].min(dim=1).values).tolist()
     span_ns = statistics.median(spans[min(5, reps // 4):])
-    # batch: four waves of resident clusters, at least 64 MiB of input, within the buffers
+    # batch: four waves of resident clusters, at least batch_bytes of input, within the buffers
     try:
         res = max_active_clusters(op, alg, dt, n, p)
     except DsmemError:   # a payload only the pipelined driver runs: size the batch by bytes alone
         res = 1
-    problems = max(4 * res, (64 << 20) // (per_in * esz))
+    problems = max(4 * res, batch_bytes // (per_in * esz))
     problems = min(problems, buf_in.numel() // (per_in * esz), buf_out.numel() // (per_out * esz))
     inp = buf_in[: problems * per_in * esz].view(tdt)
     out = buf_out[: problems * per_out * esz].view(tdt)
@@ -77,7 +78,8 @@ def measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps)
             "batch_ms": round(ms, 4), "batch_algbw_GBps": round(problems * n * p / (ms * 1e-3) / 1e9, 1)}
 
 
-def run(dtypes=(Dtype.F32,), reps=60, batch_reps=5, sizes=CLUSTER_SIZES, payloads=PAYLOADS, ops=tuple(Op)):
+def run(dtypes=(Dtype.F32,), reps=60, batch_reps=5, sizes=CLUSTER_SIZES, payloads=PAYLOADS, ops=tuple(Op),
+        batch_bytes=256 << 20):
     import torch
 
     torch.cuda.set_device(0)
@@ -95,7 +97,7 @@ def run(dtypes=(Dtype.F32,), reps=60, batch_reps=5, sizes=CLUSTER_SIZES, payload
                     if qs != Status.OK and not (qs == Status.SMEM_LIMIT and alg in PIPELINED):
                         continue
                     try:
-                        r = measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps)
+                        r = measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps, batch_bytes)
                     except DsmemError as e:
                         r = {"error": str(e)}
                     r.update({"op": OP_NAMES[op], "alg": ALG_NAMES[alg], "n": n, "bytes": p, "dtype": DT_NAMES[dt]})
@@ -139,12 +141,13 @@ def main(argv=None):
     ap.add_argument("--reps", type=int, default=60)
     ap.add_argument("--ops", default="all", help="comma list of allreduce,allgather,reducescatter,alltoall")
     ap.add_argument("--merge", default=None, help="existing table: keep its lines for the (op, dtype) not swept")
+    ap.add_argument("--batch-mib", type=int, default=256, help="input MiB of each batch-regime launch (at least)")
     args = ap.parse_args(argv)
     dts = {"f32": (Dtype.F32,), "bf16": (Dtype.BF16,), "i32": (Dtype.I32,),
            "all": (Dtype.F32, Dtype.BF16, Dtype.I32)}[args.dtype]
     by_name = {v: k for k, v in OP_NAMES.items()}
     ops = tuple(Op) if args.ops == "all" else tuple(by_name[o] for o in args.ops.split(","))
-    res = run(dts, reps=args.reps, ops=ops)
+    res = run(dts, reps=args.reps, ops=ops, batch_bytes=args.batch_mib << 20)
     with open(args.out_json, "w") as f:
         json.dump(res, f)
     text = table(res)

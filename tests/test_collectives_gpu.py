@@ -288,3 +288,66 @@ def test_payload_grid(cuda, orc, op, alg, n):
     if ran == 0:
         pytest.skip("no legal configuration (reference static_assert)")
     assert not failures, "\n".join(failures)
+
+
+STREAM_SETTINGS = ((16384, 0, 1), (4096, 5, 3), (2048, 2, 1), (65536, 3, 2), (1024, 8, 1))
+
+
+@pytest.mark.parametrize("n", D.CLUSTER_SIZES)
+def test_streamed_rs_global_ag_matches_plain(cuda, orc, n):
+    """The streamed batch driver of rs_push_global_ag (warp-specialised ring, reduce-scatter over DSMEM, sums
+    stored straight into every output row) at several (unit, depth, lag) settings -- units per problem from 1 to
+    many, fewer units than stages, several problems per resident cluster -- is bit-equal to the plain driver,
+    which sums the N partials in the same rank order; the plain result is checked against the oracle."""
+    torch = cuda
+    failures = []
+    try:
+        for dt in D.Dtype:
+            for p in (256 * n // 8 if n >= 8 else 256, 4096, 65536, 196608):
+                if D.query(D.Op.ALLREDUCE, D.Alg.RS_PUSH_GLOBAL_AG, dt, n, p)[0] not in (D.Status.OK,
+                                                                                      D.Status.SMEM_LIMIT):
+                    continue
+                m = D.msg_elems(D.Op.ALLREDUCE, n, p, dt)
+                for clusters in (2, 301, 1200):
+                    if p * n * clusters > (256 << 20):
+                        continue
+                    host = make_input(orc, dt, clusters * n * m, "R", clusters + p)
+                    tin = _np_to_torch(torch, host, dt).cuda()
+                    plain = torch.empty_like(tin)
+                    if D.query(D.Op.ALLREDUCE, D.Alg.RS_PUSH_GLOBAL_AG, dt, n, p)[0] == D.Status.OK:
+                        D.set_pipelined(False)
+                        D.collective(D.Op.ALLREDUCE, D.Alg.RS_PUSH_GLOBAL_AG, tin, plain, n, p)
+                        D.check()
+                        D.set_pipelined(True)
+                        ref = orc.reference(0, ORC_DT[dt], n, m, clusters, host)
+                        exact = dt == D.Dtype.I32
+                        tol = 0 if exact else RTOL[dt] * math.ceil(math.log2(n))
+                        bad, _, mr = orc.check(ORC_DT[dt], _torch_to_np(plain, dt), ref, 0 if exact else 1, tol)
+                        if bad:
+                            failures.append(f"plain {dt.name} P={p} clusters={clusters}: {bad} off the oracle")
+                    else:
+                        plain = None   # above the one-piece limit: only the streamed driver runs it
+                    outs = []
+                    for unit, depth, lag in STREAM_SETTINGS:
+                        D.set_stream_pipeline(unit, depth, lag)
+                        out = torch.full_like(tin, float("nan")) if dt != D.Dtype.I32 else torch.full_like(tin, -1)
+                        D.collective(D.Op.ALLREDUCE, D.Alg.RS_PUSH_GLOBAL_AG, tin, out, n, p)
+                        D.check()
+                        outs.append(out)
+                    if plain is None:
+                        plain = outs[0]
+                        ref = orc.reference(0, ORC_DT[dt], n, m, clusters, host)
+                        exact = dt == D.Dtype.I32
+                        tol = 0 if exact else RTOL[dt] * math.ceil(math.log2(n))
+                        bad, _, _ = orc.check(ORC_DT[dt], _torch_to_np(plain, dt), ref, 0 if exact else 1, tol)
+                        if bad:
+                            failures.append(f"streamed {dt.name} P={p} clusters={clusters}: {bad} off the oracle")
+                    for (unit, depth, lag), out in zip(STREAM_SETTINGS, outs):
+                        if not torch.equal(out.view(torch.int16 if dt == D.Dtype.BF16 else torch.int32),
+                                           plain.view(torch.int16 if dt == D.Dtype.BF16 else torch.int32)):
+                            failures.append(f"{dt.name} P={p} clusters={clusters} unit={unit} depth={depth} "
+                                            f"lag={lag}: differs from the plain driver")
+    finally:
+        D.set_pipelined(True)
+        D.set_stream_pipeline()
+    assert not failures, "\n".join(failures[:20])

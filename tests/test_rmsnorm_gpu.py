@@ -108,3 +108,38 @@ def test_rmsnorm_launch_order_of_shapes(cuda, orc):
     kernel's dynamic shared-memory opt-in only grows, so the third launch still fits."""
     for hidden in (4096, 3072, 4096):
         run(cuda, orc, D.Dtype.BF16, 40, hidden, 8, seed=hidden)
+
+
+@pytest.mark.parametrize("n", (2, 8))
+@pytest.mark.parametrize("dt", (D.Dtype.BF16, D.Dtype.F32))
+def test_rmsnorm_reference_golden(cuda, orc, dt, n):
+    """The kernel on the pinned fixture's inputs (64 x 8192, exact in fp16 and bf16) against the reference's own
+    outputs: its wrapper's fp32 expression, and (when recorded) its RMSNormKernel's fp16 output on a B200."""
+    import importlib.util
+    import pathlib
+
+    torch = cuda
+    golden = pathlib.Path(__file__).resolve().parent / "golden"
+    spec = importlib.util.spec_from_file_location("make_rmsnorm_golden", golden / "make_rmsnorm_golden.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    d = dict(np.load(golden / "rmsnorm_golden.npz"))
+    x, w = mod.inputs()
+    if dt == D.Dtype.BF16:
+        tx, tw = torch.from_numpy(x).to(torch.bfloat16).cuda(), torch.from_numpy(w).to(torch.bfloat16).cuda()
+    else:
+        tx, tw = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
+    ty = torch.full_like(tx, float("nan"))
+    D.rmsnorm(tx, tw, float(d["eps"]), cluster_size=n, out=ty)
+    torch.cuda.synchronize()
+    D.rmsnorm_check()
+    got = ty.float().cpu().numpy()[d["kept_rows"]].astype(np.float64)
+    refs = {"reference fp32 expression": d["y_expr"].astype(np.float64)}
+    if "y_kernel_fp16" in d:
+        refs["reference RMSNormKernel (fp16)"] = d["y_kernel_fp16"].view(np.float16).astype(np.float64)
+    for name, ref in refs.items():
+        err = (np.abs(got - ref) / (1.0 + np.abs(ref))).max()
+        # bf16 output rounding (2^-9 relative) for bf16; fp32 rounding, plus the fp16 reference's own
+        # rounding (2^-11) when comparing with the kernel
+        tol = RTOL[dt] if dt == D.Dtype.BF16 else (1e-5 if "expression" in name else 2e-3)
+        assert err <= tol, f"{name}: max rel {err:.3e} > {tol}"
