@@ -10,8 +10,15 @@ the whole batch (inputs 2 GiB per GPU, far larger than the 126 MB L2, so no flus
     e2e          the same metric through the public API on host buffers (dsmem_collective_host): every step
                  copies its input from pinned host memory and its output back, in chunks whose copies in and
                  out overlap; the copies are inside the timed region
-    roofline     HBM: algorithmic bytes per launch = problems x N x 2P (read in, write out)
-    cpu_baseline the CPU oracle (C restatement of the reference's reference()) on a bounded sample
+    roofline     HBM: algorithmic bytes per launch = problems x N x 2P (read in, write out); `dsmem`: the
+                 algorithm's SM-to-SM bytes against the live-measured push ceiling
+    cpu_baseline the reference's own reference() (collectives/harness/main.cu, compiled from the reference
+                 sources into oracle/_ref/) on all host cores for ~10 s (the C oracle port, 1 thread, if that
+                 binary is absent)
+    check        a strided sample of the timed batch's own output against the CPU oracle
+Extras (rank 0): configs[0]'s single-cluster latencies, configs[2]'s RMSNorm, configs[3]'s decoder layer,
+ceilings, and at N = 1 the row-wise and top-k consumers, each with a CPU baseline and its core count; at N > 1
+every rank also runs configs[4]'s tensor-parallel AllReduce + RMSNorm across the N GPUs.
 --impl reference runs the reference's own CPU path (collectives/harness/main.cu reference(), compiled
 from the reference sources into oracle/_ref/) on all host cores, same metric and config.
 Multi-GPU: one process per GPU (torchrun), each GPU its own batch (weak scaling, no inter-GPU traffic).
@@ -171,6 +178,18 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def reference_rate(payload, seconds, threads):
+    """GB/s of per-CTA payload of the reference's own reference() (oracle/_ref binary) on `threads` host
+    threads for ~`seconds`; None if the binary was not built."""
+    exe = ROOT / "oracle" / "_ref" / f"ref_op0_N{CLUSTER_N}_M{payload // 4}_float"
+    if not exe.exists():
+        return None
+    out = subprocess.run([str(exe), "bench", str(seconds), str(threads)], check=True, capture_output=True,
+                         text=True).stdout
+    d = json.loads(out)
+    return d["problems"] * CLUSTER_N * payload / d["seconds"] / 1e9
+
+
 def oracle_rate(payload, seconds):
     """CPU oracle (C, single thread) on a bounded sample: GB/s of per-CTA payload."""
     from oracle import oracle as orc
@@ -193,8 +212,14 @@ def single_cluster_latency(torch, D, reps=200):
     m = p // 4
     res = {}
     ref_h100 = {"ring": 9024, "recursive_doubling": 4864, "two_shot_push": 1440}
-    for name, alg in (("ring", D.Alg.RING), ("recursive_doubling", D.Alg.RECURSIVE_DOUBLING),
-                      ("two_shot_push", D.Alg.TWO_SHOT_PUSH), ("one_shot_pull", D.Alg.ONE_SHOT_PULL)):
+    auto = D.autotune_pick(D.Op.ALLREDUCE, D.Dtype.F32, n, p, 1)
+    algs = [("ring", D.Alg.RING), ("recursive_doubling", D.Alg.RECURSIVE_DOUBLING),
+            ("two_shot_push", D.Alg.TWO_SHOT_PUSH), ("one_shot_pull", D.Alg.ONE_SHOT_PULL),
+            ("ring_credit", D.Alg.RING_CREDIT), ("recursive_doubling_credit", D.Alg.RECURSIVE_DOUBLING_CREDIT),
+            ("rs_push_global_ag", D.Alg.RS_PUSH_GLOBAL_AG)]
+    if all(a != auto for _, a in algs):
+        algs.append((auto.name.lower(), auto))
+    for name, alg in algs:
         tin = torch.rand(n * m, device="cuda") * 2 - 1
         tout = torch.empty_like(tin)
         stamps = torch.zeros(n * 32, dtype=torch.int64, device="cuda")
@@ -209,6 +234,8 @@ def single_cluster_latency(torch, D, reps=200):
         res[name] = {"latency_ns_median": med, "algbw_GBps": round(p / med, 3),
                      "busbw_GBps": round(p / med * 2 * (n - 1) / n, 3),
                      "h100_reference_ns": ref_h100.get(name)}
+    res["auto_pick"] = auto.name.lower()
+    res["timing"] = f"in-kernel span (max exit - min entry stamp), median of {reps} single-cluster launches"
     return res
 
 
@@ -306,6 +333,151 @@ def topk_extras(torch):
         r = TB.measure(torch, s, n)
         out[s] = {k: r[k] for k in ("m", "n", "k", "cluster_size", "us", "h100_us", "vs_h100")}
     return out
+
+
+# SM-to-SM shots per problem: the two-shot pushes 2 (N-1)/N * P per CTA, the reduce-scatter with the all-gather
+# through the outputs (N-1)/N * P
+DSMEM_SHOTS = {"TWO_SHOT_PUSH": 2, "RS_PUSH_GLOBAL_AG": 1}
+
+
+def check_sample(torch, tin, tout, n, m, problems, samples=16):
+    """A strided sample of the timed batch's problems against the CPU oracle (the restatement of the reference's
+    reference() and check(), main.cu:129-173): |got - ref| <= 1e-5 (1 + |ref|) ceil(log2 N)."""
+    from oracle import oracle as orc
+
+    picks = sorted(set(int(i * (problems - 1) / max(1, samples - 1)) for i in range(samples)))
+    bad, worst = 0, 0.0
+    for q in picks:
+        a, b = q * n * m, (q + 1) * n * m
+        host = tin[a:b].cpu().numpy()
+        ref = orc.reference(orc.ALLREDUCE, orc.F32, n, m, 1, host)
+        nb, _, mr = orc.check(orc.F32, tout[a:b].cpu().numpy(), ref, 1, 1e-5 * math.ceil(math.log2(n)))
+        bad += nb
+        worst = max(worst, mr)
+    return {"problems_checked": len(picks), "of": problems, "bad_elements": bad, "max_rel_err": worst,
+            "tolerance": f"1e-5*(1+|ref|)*ceil(log2 N) (main.cu:165)", "ok": bad == 0}
+
+
+def headline_cpu_baseline(p):
+    """The reference's own reference() on all host threads for ~10 s (the reference arm's measurement, on the
+    same box in the same run); the C oracle port on one thread if the reference binary was not built."""
+    threads = os.cpu_count() or 1
+    v = reference_rate(p, 10.0, threads)
+    if v is not None:
+        return {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                "sample": f"reference() of collectives/harness/main.cu (oracle/_ref build), one cluster problem of "
+                          f"the same shape per thread, {threads} threads, ~10 s"}
+    v = oracle_rate(p, seconds=10.0)
+    return {"value": round(v, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": "oracle reference() restatement (C), 1 thread, 16 cluster problems of the same shape, 10 s"}
+
+
+def _timed(fn, seconds):
+    """(calls, elapsed s) of fn() repeated for at least `seconds`."""
+    done, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            return done, el
+
+
+def cpu_extras(extras, p):
+    """CPU baselines beside the extras (rank 0, N = 1): the reference's own reference() where it exists, else the
+    oracle's restatement, single-threaded, on a bounded sample of each workload, scaled to its unit."""
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    if "single_cluster" in extras:
+        exe = ROOT / "oracle" / "_ref" / f"ref_op0_N{CLUSTER_N}_M4096_float"
+        if exe.exists():
+            d = json.loads(subprocess.run([str(exe), "bench", "2.0", "1"], check=True, capture_output=True,
+                                          text=True).stdout)
+            extras["single_cluster"]["cpu_baseline"] = {
+                "value": round(d["seconds"] / d["problems"] * 1e9, 1), "unit": "ns per problem", "cores": 1,
+                "kind": "reference", "sample": "reference() of main.cu, N = 8, 16 KiB per CTA, 1 thread, ~2 s"}
+    if "rmsnorm" in extras:
+        x = orc.normal(1, 512 * 4096, 0, 0.0, 1.0).reshape(512, 4096)
+        w = orc.normal(1, 4096, 1, 1.0, 0.02)
+        calls, el = _timed(lambda: orc.rmsnorm(1, x, w, 1e-6), 2.0)
+        extras["rmsnorm"]["cpu_baseline"] = {
+            "value": round(calls * 512 / el, 1), "unit": "rows/s", "cores": 1, "kind": "port",
+            "sample": "oracle RMSNorm (clusterfusion_rmsnorm.py:65 in double), 512 of the 4096 bf16 rows, ~2 s"}
+    if "decoder" in extras:
+        from dsmem_b200 import decoder_bench as DB
+
+        h, f, S = DB.HID, DB.FFN, DB.S
+        block = orc.f32_to_bf16(np.random.default_rng(0).standard_normal(1 << 20).astype(np.float32) * 0.02)
+        fill = lambda *shape: np.resize(block, int(np.prod(shape))).reshape(shape)   # noqa: E731
+        inv = 10000.0 ** (-np.arange(0, 128, 2) / 128)
+        cs = np.concatenate([np.cos(S * inv)] * 2).astype(np.float32)
+        sn = np.concatenate([np.sin(S * inv)] * 2).astype(np.float32)
+        args = (fill(1, h), fill(1, h), fill(h), fill(3 * h, h), fill(h, h), fill(h), fill(2 * f, h), fill(h, f),
+                fill(1, S + 1, DB.HEADS, 128), fill(1, S + 1, DB.HEADS, 128), cs, sn, S, 1e-5, DB.HEADS)
+        calls, el = _timed(lambda: orc.decoder_layer(*args), 1.0)
+        extras["decoder"]["cpu_baseline"] = {
+            "value": round(calls / el, 2), "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": "oracle decoder layer (reference_fp32 of clusterfusion_llama2_7b_decoder.py:160-180 with the "
+                      "FFN tail, in double), batch 1, full Llama-2-7B shape, S = 4096"}
+    rng = np.random.default_rng(0)
+    for w_, r in extras.get("rowwise", {}).items():
+        rows, cols, k = r["rows"], r["cols"], 16
+        a = lambda: rng.standard_normal((k, cols)).astype(np.float32)   # noqa: E731
+        fn = {"rowwise_quant": (lambda x=a(): orc.rowwise_quant(x)),
+              "lars_momentum": (lambda w=a(), g=a(), m_=a(): orc.lars_momentum(w, g, m_, **orc.LARS_DEFAULTS)),
+              "layernorm_backward": (lambda x=a(), dy=a(): orc.layernorm_backward(x, dy, np.ones(cols, np.float32),
+                                                                                  orc.LN_BWD_EPS)),
+              "pearson_backward": (lambda x=a(), y=a(): orc.pearson_backward(x, y, np.ones(k, np.float32),
+                                                                           orc.PEARSON_EPS)),
+              "softmax_logits_backward": (lambda z=a(), dy=a(): orc.softmax_logits_backward(z, dy)),
+              "weighted_var_backward": (lambda x=a(), wt=np.abs(a()), dy=a(): orc.weighted_var_backward(
+                  x, wt, dy, orc.WVAR_EPS))}[w_]
+        calls, el = _timed(fn, 0.5)
+        r["cpu_baseline"] = {"value": round(el / calls * rows / k * 1e6, 1), "unit": "us", "cores": 1,
+                             "kind": "port", "sample": f"oracle restatement, {k} of the {rows} rows, scaled"}
+    for s_, r in extras.get("topk", {}).items():
+        k = min(2, r["m"])
+        x = rng.standard_normal((k, r["n"])).astype(np.float32)
+        calls, el = _timed(lambda: orc.topk_values(x, r["k"]), 0.5)
+        r["cpu_baseline"] = {"value": round(el / calls * r["m"] / k * 1e6, 1), "unit": "us", "cores": 1,
+                             "kind": "port", "sample": f"oracle top-k values, {k} of the {r['m']} rows, scaled"}
+
+
+def decoder_extras(torch, hbm_peak):
+    """the Llama-2-7B decoder layer, one decode step, batch 1 / 4 / 16 (cluster-8 projections; the
+    attention's cluster size follows the (sequence, head) count), CUDA-graph-timed; tokens/s and HBM fraction."""
+    from dsmem_b200 import decoder_bench as DB
+
+    r = DB.run(batches=(1, 4, 16), clusters=(8,), with_torch=False)
+    out = {"config": r["config"], "timing": "CUDA graph of 10 steps, median of 5 replays"}
+    for b, row in r["batch"].items():
+        out[f"batch{b}"] = {**row["cluster8"], "bytes_per_step": row["bytes_per_step"]}
+    torch.cuda.empty_cache()
+    return out
+
+
+def tp_extras(torch, rank, world):
+    """tensor-parallel AllReduce + RMSNorm over the N GPUs (bf16, hidden 8192, tokens 1 / 64 / 1024 /
+    8192): the fused peer-memory kernel, from its own buffers and from ordinary tensors, and the NCCL composition;
+    max over ranks, CUDA-graph-timed, with the NVLink fraction; a CPU baseline on rank 0."""
+    from dsmem_b200 import tp_bench as TB
+
+    r = TB.run(reps=10, rounds=3, warmup=3)
+    torch.cuda.empty_cache()
+    if rank == 0:
+        import numpy as np
+
+        from oracle import oracle as orc
+
+        xs = [orc.normal(1, 64 * 8192, 7 + k, 0.0, 1.0).reshape(64, 8192) for k in range(world)]
+        w = orc.normal(1, 8192, 1, 1.0, 0.02)
+        calls, el = _timed(lambda: orc.tp_rmsnorm(1, xs, w, 1e-6), 1.0)
+        r["cpu_baseline"] = {"value": round(calls * 64 / el, 1), "unit": "tokens/s", "cores": 1, "kind": "port",
+                             "sample": f"oracle sum of {world} ranks + RMSNorm (double), 64 tokens x 8192, ~1 s"}
+        del np
+    return r
 
 
 def run_ours(args, rank, world, local):
@@ -420,32 +592,38 @@ def run_ours(args, rank, world, local):
            "h2d_bytes_per_step": tin.numel() * 4, "d2h_bytes_per_step": tout.numel() * 4,
            "ms_per_step": round(e2e_ms, 3), "mode": e2e_mode}
 
-    # shared::cluster roofline: bytes each CTA sends per problem (two-shot: 2(N-1)/N * P) against the
-    # measured all-peers push ceiling at this cluster size
+    # shared::cluster roofline: bytes each CTA sends per problem (two-shot: 2(N-1)/N * P; the reduce-scatter
+    # with the all-gather through the outputs: (N-1)/N * P) against the measured push ceiling at this size
     ceil = dsmem_ceiling(D, n)
-    dsmem_bytes = problems * n * 2 * (n - 1) / n * p
+    dsmem_bytes = problems * n * DSMEM_SHOTS.get(resolved.name, 2) * (n - 1) / n * p
     dsmem_achieved = dsmem_bytes / (ms * 1e-3) / 1e9
     roofline["dsmem"] = {"achieved": round(dsmem_achieved, 1), "peak": ceil["peak_GBps"], "unit": "GB/s",
                          "frac": round(dsmem_achieved / ceil["peak_GBps"], 4),
                          "bytes_per_launch": int(dsmem_bytes), "ceilings": ceil,
                          "peak_source": "measured live (dsmem_ceiling_dsmem_bw, best push shape, 1/slope)"}
 
+    # the timed batch's own output, sampled, against the CPU oracle (every rank; outside the timed region)
+    check = check_sample(torch, tin, tout, n, m, problems)
+
     extras = {}
+    if world > 1 and not args.no_extras:
+        # tensor-parallel AllReduce + RMSNorm across the N GPUs (every rank takes part)
+        extras["tp_allreduce_rmsnorm"] = tp_extras(torch, rank, world)
     if rank == 0 and not args.no_extras:
         extras["single_cluster"] = single_cluster_latency(torch, D)
         extras["rmsnorm"] = rmsnorm_config3(torch, D, hbm_peak)
         # ceilings beyond DSMEM and HBM (tcgen05 MMA, L2, shared memory), 1 / slope over two work amounts
         extras["ceilings_sm100"] = D.sm100_ceilings(reps=3)
-        if world == 1:   # informative only: kept out of multi-GPU runs, where the other GPUs wait meanwhile
+        if world == 1:   # kept out of multi-GPU runs, where the other GPUs wait meanwhile
+            extras["decoder"] = decoder_extras(torch, hbm_peak)
             extras["rowwise"] = rowwise_extras(torch, hbm_peak)
             extras["topk"] = topk_extras(torch)
 
     cpu = None
     if rank == 0 and world == 1:
-        v = oracle_rate(p, seconds=10.0)
-        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": 1, "kind": "port",
-               "sample": f"oracle reference() restatement (C), 1 thread, 16 cluster problems of the same "
-                         f"shape repeated for 10 s"}
+        cpu = headline_cpu_baseline(p)
+        if not args.no_extras:
+            cpu_extras(extras, p)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -459,9 +637,11 @@ def run_ours(args, rank, world, local):
                        "problems_per_gpu": problems, "input_bytes_per_gpu": problems * n * p,
                        "l2": "inputs 2 GiB per GPU > 126 MB L2 (no flush)", "parallelism": f"shard{world}"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
-            "clocks": clocks.summary()}
+            "clocks": clocks.summary(), "check": check}
     line.update(extras)
     print(json.dumps(line), flush=True)
+    if not check["ok"]:
+        raise SystemExit(f"result check failed: {check}")
 
 
 def main():

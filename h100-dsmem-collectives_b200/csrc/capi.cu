@@ -278,8 +278,7 @@ int resolve_auto(int op, int dtype, int n, size_t bytes, int regime = 0) {
             if (jt != it->second.begin()) {
                 --jt;
                 const KernelEntry* e = find(op, jt->second, dtype, n);
-                if (e != nullptr && (regime == 1 ? launchable(e, m) : classify(e, m, nullptr) == DSMEM_OK))
-                    return jt->second;
+                if (e != nullptr && launchable(e, m)) return jt->second;
             }
         }
     }
@@ -363,14 +362,15 @@ cudaError_t error_word(DeviceState& d, unsigned** out) {
 }
 
 // Units per problem for a pipelined driver: the smallest split into legal sub-vectors of at most
-// unit_bytes per CTA (default 16 KiB: three unit buffers in 48 KiB, four CTAs per SM); 0 if none.
+// unit_bytes per CTA (default 16 KiB: three unit buffers in 48 KiB, four CTAs per SM) whose smallest window
+// fits the shared-memory limit; 0 if none.
 // Caller holds st().mu.
 uint32_t pipeline_units(const KernelEntry* e, uint32_t m) {
     const uint64_t unit = e->stage_pipe != nullptr ? st().stream_unit_bytes : st().unit_bytes;
     const uint64_t bytes = (uint64_t)m * e->elem_bytes;
     const uint32_t s0 = (uint32_t)std::max<uint64_t>(1, (bytes + unit - 1) / unit);
     for (uint32_t s = s0; s <= m && s < s0 + 4096; ++s)
-        if (m % s == 0 && e->legal(m / s)) return s;
+        if (m % s == 0 && e->legal(m / s) && e->smem_pipe(m / s) <= dsb::kSmemLimit) return s;
     return 0;
 }
 

@@ -203,8 +203,8 @@ def test_shipped_autotune_table_parses(dsmem, tmp_path):
         for op, n, p, dt, alg, regime in lines:
             a = by_name[alg]
             st = dsmem.query(ops[op], a, dts[dt], int(n), int(p))[0]
-            # payloads above the one-piece limit run on the pipelined driver (batches)
-            assert st == dsmem.Status.OK or (st == dsmem.Status.SMEM_LIMIT and a in pipelined and regime == "batch")
+            # payloads above the one-piece limit run on the pipelined / streamed driver (one problem or many)
+            assert st == dsmem.Status.OK or (st == dsmem.Status.SMEM_LIMIT and a in pipelined)
             got = dsmem.autotune_pick(ops[op], dts[dt], int(n), int(p), num_clusters=64 if regime == "batch" else 1)
             assert got == a
     finally:
