@@ -322,7 +322,7 @@ std::mutex g_tp_mu;
 dsmem_status tp_launch(const void* const* xs, void* const* ys, unsigned* const* sigs, unsigned* err, int tp,
                        int rank, int emulate, dsmem_dtype dtype, const void* residual,
                        const void* w, float eps, long long rows, int hidden, int cluster_size,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, unsigned long long wait_limit_ns = 2000000000ull) {
     if (dtype != DSMEM_BF16) return DSMEM_ERR_ILLEGAL_CONFIG;
     if (!(tp == 1 || tp == 2 || tp == 4 || tp == 8) || rank < 0 || rank >= tp) return DSMEM_ERR_INVALID_ARGUMENT;
     const int n = cluster_size;
@@ -384,7 +384,7 @@ dsmem_status tp_launch(const void* const* xs, void* const* ys, unsigned* const* 
     a.res = static_cast<const uint4*>(residual);
     a.w = static_cast<const uint4*>(w);
     a.err = err;
-    a.wait_limit_ns = 2000000000ull;
+    a.wait_limit_ns = wait_limit_ns;
     a.rows = rows;
     a.hidden = hidden;
     a.eps = eps;
@@ -406,6 +406,7 @@ struct dsmem_tp_ctx {
     size_t capacity = 0;             // bytes of each of the x and y regions
     unsigned char* base = nullptr;   // this rank's buffer: [signals 4 KiB][x][y]
     unsigned char* peer[kMaxTp] = {};
+    unsigned long long wait_limit_ns = 2000000000ull;   // each cross-GPU flag wait of a call
 };
 
 extern "C" {
@@ -485,7 +486,7 @@ dsmem_status dsmem_tp_allreduce_rmsnorm(dsmem_tp_t c, dsmem_dtype dtype, const v
         sigs[p] = reinterpret_cast<unsigned*>(c->peer[p]);
     }
     const dsmem_status st = tp_launch(xs, ys, sigs, reinterpret_cast<unsigned*>(c->base) + kSigErr, c->tp, c->rank,
-                                      0, dtype, residual, w, eps, rows, hidden, cluster_size, s);
+                                      0, dtype, residual, w, eps, rows, hidden, cluster_size, s, c->wait_limit_ns);
     if (st != DSMEM_OK) return st;
     if (y != nullptr && y != yb && bytes && cudaMemcpyAsync(y, yb, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
         return DSMEM_ERR_CUDA;
@@ -520,6 +521,12 @@ dsmem_status dsmem_tp_check(dsmem_tp_t c, unsigned* error_bits, unsigned* detail
     if (error_bits) *error_bits = v[0];
     if (detail) *detail = v[1];
     return (v[0] & DSMEM_ERRBIT_TIMEOUT) ? DSMEM_ERR_TIMEOUT : (v[0] & DSMEM_ERRBIT_BOUNDS) ? DSMEM_ERR_BOUNDS : DSMEM_OK;
+}
+
+dsmem_status dsmem_tp_set_wait_limit_ns(dsmem_tp_t c, unsigned long long ns) {
+    if (c == nullptr || ns == 0 || ns > 60000000000ull) return DSMEM_ERR_INVALID_ARGUMENT;
+    c->wait_limit_ns = ns;
+    return DSMEM_OK;
 }
 
 dsmem_status dsmem_tp_close(dsmem_tp_t c) {

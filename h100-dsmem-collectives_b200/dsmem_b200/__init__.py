@@ -223,6 +223,7 @@ def lib():
                                                c_vp, c_vp]),
         "dsmem_tp_check": (c_int, [c_vp, ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_uint)]),
         "dsmem_tp_close": (c_int, [c_vp]),
+        "dsmem_tp_set_wait_limit_ns": (c_int, [c_vp, c_ull]),
         "dsmem_tp_emulate": (c_int, [c_int, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), c_int, c_vp, c_vp,
                                      ctypes.c_float, c_ll, c_int, c_int, c_vp]),
         "dsmem_decoder_workspace_bytes": (c_size, [c_int, c_int, c_int]),

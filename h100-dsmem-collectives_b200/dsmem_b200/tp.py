@@ -106,6 +106,16 @@ class TPContext:
             f"dsmem_tp_allreduce_rmsnorm({tokens}x{hidden}, tp={self.world}, cluster {cluster_size})")
         return out if out is not None else self.buffers(tokens, hidden)[1]
 
+    def set_wait_limit_ns(self, ns):
+        """Limit of each cross-GPU flag wait of this context's calls (dsmem_tp_set_wait_limit_ns; default 2 s)."""
+        _ok(lib().dsmem_tp_set_wait_limit_ns(self._ctx, int(ns)), "dsmem_tp_set_wait_limit_ns")
+
+    def status(self):
+        """(status, error bits, detail) of the device error words, read and cleared (dsmem_tp_check); no raise."""
+        bits, detail = ctypes.c_uint(0), ctypes.c_uint(0)
+        st = lib().dsmem_tp_check(self._ctx, ctypes.byref(bits), ctypes.byref(detail))
+        return Status(st), bits.value, detail.value
+
     def check(self):
         """Raise DsmemError(TIMEOUT/BOUNDS) if a device-side wait or check fired since the last call."""
         bits, detail = ctypes.c_uint(0), ctypes.c_uint(0)

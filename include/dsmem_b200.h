@@ -386,6 +386,11 @@ dsmem_status dsmem_tp_allreduce_rmsnorm(dsmem_tp_t ctx, dsmem_dtype dtype, const
 /* Read and clear the context's device error words (synchronous): TIMEOUT / BOUNDS / OK; detail as in
  * dsmem_last_error_detail (barrier 0x70 + r: entry wait for rank r; 0x78 + r: exit wait). */
 dsmem_status dsmem_tp_check(dsmem_tp_t ctx, unsigned* error_bits, unsigned* detail);
+/* Limit of each cross-GPU flag wait of this context's calls (default 2 s; 1 ns .. 60 s). A call whose peer
+ * never joins gives up after it (at entry, and again at exit), finishes without blocking, and dsmem_tp_check
+ * reports DSMEM_ERR_TIMEOUT. After a timeout the ranks' call epochs disagree: close and reopen the context.
+ * Replaces the reference's host watchdog (collectives/harness/main.cu:277-320) for the cross-GPU path. */
+dsmem_status dsmem_tp_set_wait_limit_ns(dsmem_tp_t ctx, unsigned long long ns);
 dsmem_status dsmem_tp_close(dsmem_tp_t ctx);
 /* The same kernel for `tp` ranks emulated in one launch on one GPU (xs, ys: tp local buffers each; every
  * row computed once and written to all tp y buffers; no flags). For single-GPU parity tests. */

@@ -136,3 +136,75 @@ def test_tp_multi_gpu(cuda, orc, tmp_path, world):
     for r in range(world):
         bad, _, mr = orc.check(1, np.load(tmp_path / f"nccl{r}.npy").reshape(-1), ref.reshape(-1), 1, RTOL)
         assert bad == 0, f"nccl composition rank {r}: {bad} beyond tol (max rel {mr})"
+
+
+# ----------------------------------------------------------------------------- failure detection
+def _absent_rank_main(rank, world, port, absent, out_dir):
+    """Every rank maps the TP buffers; rank `absent` never enters the fused call (it leaves the test between
+    steps, with nothing in flight) and waits on the host until the others have read their status."""
+    import datetime
+    import json
+    import time
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"   # no NVLink multicast object is bound in this test
+    import torch
+    import torch.distributed as dist
+
+    from dsmem_b200 import tp as T
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        rows, hidden = 64, 8192
+        ctx = T.TPContext(T.tp_bytes(rows, hidden))
+        ctx.set_wait_limit_ns(200_000_000)   # 0.2 s per cross-GPU flag wait
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(rank)
+        x = torch.randn(rows, hidden, device="cuda", generator=gen).to(torch.bfloat16)
+        w = torch.ones(hidden, device="cuda", dtype=torch.bfloat16)
+        y = torch.empty_like(x)
+        if rank != absent:
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            ctx.allreduce_rmsnorm(x, w, 1e-6, out=y, cluster_size=8)
+            torch.cuda.synchronize()   # returns: the bounded waits gave up, the kernel finished
+            elapsed = time.perf_counter() - t0
+            st, bits, detail = ctx.status()
+            z = torch.zeros(16, device="cuda")
+            z += 1                     # the context is still usable after the timeout
+            torch.cuda.synchronize()
+            with open(os.path.join(out_dir, f"status{rank}.json"), "w") as f:
+                json.dump({"status": int(st), "bits": bits, "detail": detail, "elapsed_s": elapsed,
+                           "usable": float(z.sum().item())}, f)
+        dist.barrier()   # the absent rank keeps its buffer mapped until every caller's kernel has finished
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", (2, 4))
+def test_tp_absent_rank_times_out(cuda, tmp_path, world):
+    """One rank of `world` never joins the fused AllReduce + RMSNorm call. Every other rank's kernel gives up its
+    cross-GPU flag waits after the context's limit (0.2 s), finishes, and dsmem_tp_check reports TIMEOUT with the
+    detail of the entry wait for the absent rank (barrier 0x70 + rank); the GPU stays usable. No GPU fault, trap or
+    endless wait: the failure is a process that does not call, and the waits are bounded."""
+    import json
+
+    torch = cuda
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    absent = world - 1
+    mp.start_processes(_absent_rank_main, args=(world, _free_port(), absent, str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    for r in range(world):
+        if r == absent:
+            continue
+        s = json.loads((tmp_path / f"status{r}.json").read_text())
+        assert s["status"] == int(D.Status.TIMEOUT), s
+        assert s["bits"] & 1, s
+        assert s["detail"] & 0x80000000 and (s["detail"] >> 24) & 0x7F == 0x70 + absent, hex(s["detail"])
+        assert s["elapsed_s"] < 10.0, s   # entry and exit waits, 0.2 s each, plus the lingering end
+        assert s["usable"] == 16.0
