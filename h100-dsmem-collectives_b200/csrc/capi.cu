@@ -351,10 +351,10 @@ cudaError_t occupancy(DeviceState& d, const void* fn, int n_cta, uint64_t smem, 
 }
 
 cudaError_t error_word(DeviceState& d, unsigned** out) {
-    if (d.err == nullptr) {   // [error bits, first timeout detail, its cluster id, spare]
-        cudaError_t r = cudaMalloc(reinterpret_cast<void**>(&d.err), kErrWords * sizeof(unsigned));
+    if (d.err == nullptr) {   // [error bits, first timeout detail, its cluster id, spare] + a snapshot of them
+        cudaError_t r = cudaMalloc(reinterpret_cast<void**>(&d.err), 2 * kErrWords * sizeof(unsigned));
         if (r != cudaSuccess) return r;
-        r = cudaMemset(d.err, 0, kErrWords * sizeof(unsigned));
+        r = cudaMemset(d.err, 0, 2 * kErrWords * sizeof(unsigned));
         if (r != cudaSuccess) return r;
     }
     *out = d.err;
@@ -419,6 +419,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64) selftest_timeout
     if (threadIdx.x == 0) dsmem::mbar_arrive_expect_tx(c.sa, 16);
     dsb::wait(c, 0);
     dsmem::cluster_sync();
+}
+
+// Read and clear the error words in one atomic step each: a bit a kernel sets while the check runs is either in
+// this snapshot or stays in the word for the next check, never lost between a read and a clear.
+__global__ void take_error_words(unsigned* err) {
+    if (threadIdx.x < kErrWords) err[kErrWords + threadIdx.x] = atomicExch(err + threadIdx.x, 0u);
 }
 
 }  // namespace
@@ -582,9 +588,12 @@ dsmem_status dsmem_last_error_detail(int device, unsigned* error_bits, unsigned*
     unsigned v[kErrWords] = {};
     if (w != nullptr) {
         if (device != prev && cudaSetDevice(device) != cudaSuccess) return DSMEM_ERR_CUDA;
-        cudaError_t r = cudaMemcpy(v, w, sizeof v, cudaMemcpyDeviceToHost);
-        if (r == cudaSuccess) r = cudaMemset(w, 0, sizeof v);
-        if (r == cudaSuccess) r = cudaDeviceSynchronize();
+        cudaError_t r = cudaDeviceSynchronize();
+        if (r == cudaSuccess) {
+            take_error_words<<<1, 32>>>(w);
+            r = cudaGetLastError();
+        }
+        if (r == cudaSuccess) r = cudaMemcpy(v, w + kErrWords, sizeof v, cudaMemcpyDeviceToHost);
         if (device != prev) cudaSetDevice(prev);
         if (r != cudaSuccess) return DSMEM_ERR_CUDA;
     }

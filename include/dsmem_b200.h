@@ -168,14 +168,18 @@ dsmem_alg dsmem_autotune_pick(dsmem_op op, dsmem_dtype dtype, int cluster_size, 
 dsmem_alg dsmem_autotune_pick_ex(dsmem_op op, dsmem_dtype dtype, int cluster_size, size_t bytes_per_cta,
                                  long long num_clusters);
 
-/* Read and clear the device error word of `device` (synchronises that device). */
+/* Read and clear the device error word of `device` (synchronises that device). The word is shared by every
+ * catalogue launch on the device, from any stream or host thread: a read reports the errors of all launches
+ * since the previous read. Each word is read and cleared in one atomic exchange, so a bit set while the read
+ * runs is either returned or kept for the next read, never lost. */
 dsmem_status dsmem_last_error(int device, unsigned* error_bits);
 /* As dsmem_last_error, plus where the first timed-out wait since the last read gave up:
  * detail = 0x80000000 | barrier << 24 | cluster rank << 16 | problem-or-unit counter (low 16 bits),
  * 0 if no wait timed out; cluster = its %clusterid.x. Any pointer may be NULL. No reference
  * counterpart (the reference's hangs end in its host watchdog, collectives/harness/main.cu:277-320). */
 dsmem_status dsmem_last_error_detail(int device, unsigned* error_bits, unsigned* detail, unsigned* cluster);
-/* Synchronise `stream`, then map the device error word to TIMEOUT / BOUNDS (and clear it). */
+/* Synchronise `stream`, then map the device error word to TIMEOUT / BOUNDS (and clear it); as above, the word
+ * also carries errors of launches on other streams since the last read. */
 dsmem_status dsmem_check(dsmem_stream_t stream);
 
 /* Names: "<op>", "<alg>" and the reference file stem "<op>__<alg>__<src>". */
