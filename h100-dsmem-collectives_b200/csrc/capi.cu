@@ -110,6 +110,7 @@ struct DeviceState {
     std::map<const void*, int> smem_attr;          // largest MaxDynamicSharedMemorySize set per kernel
     std::map<std::pair<const void*, uint64_t>, int> occupancy;
     int optin = 0;
+    int sms = 0;
 };
 
 // AUTO table key. regime 0 = one cluster per launch (picked by latency), 1 = batches (by throughput).
@@ -135,6 +136,7 @@ struct State {
     uint64_t stream_unit_bytes = 16384;  // largest sub-vector per CTA
     int stream_depth = 0;                // stages of the ring; 0: by cluster size as above
     int stream_lag = 1;                  // units of reduce-scatter in flight
+    bool stream_set = false;             // dsmem_set_stream_pipeline was called: no launch-size defaults
 };
 
 State& st() {
@@ -251,7 +253,7 @@ void load_default_table() {
     });
 }
 
-uint32_t pipeline_units(const KernelEntry* e, uint32_t m);
+uint32_t pipeline_units(const KernelEntry* e, uint32_t m, uint64_t unit_bytes = 0);
 
 // classify() OK, or a payload above the one-piece limit that the pipelined driver runs in fitting units.
 // Caller holds st().mu.
@@ -295,6 +297,7 @@ DeviceState& device_state(int dev) {
     // caller holds st().mu
     DeviceState& d = st().dev[dev];
     if (d.optin == 0) cudaDeviceGetAttribute(&d.optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (d.sms == 0) cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     return d;
 }
 
@@ -365,8 +368,8 @@ cudaError_t error_word(DeviceState& d, unsigned** out) {
 // unit_bytes per CTA (default 16 KiB: three unit buffers in 48 KiB, four CTAs per SM) whose smallest window
 // fits the shared-memory limit; 0 if none.
 // Caller holds st().mu.
-uint32_t pipeline_units(const KernelEntry* e, uint32_t m) {
-    const uint64_t unit = e->stage_pipe != nullptr ? st().stream_unit_bytes : st().unit_bytes;
+uint32_t pipeline_units(const KernelEntry* e, uint32_t m, uint64_t unit_bytes) {
+    const uint64_t unit = unit_bytes != 0 ? unit_bytes : e->stage_pipe != nullptr ? st().stream_unit_bytes : st().unit_bytes;
     const uint64_t bytes = (uint64_t)m * e->elem_bytes;
     const uint32_t s0 = (uint32_t)std::max<uint64_t>(1, (bytes + unit - 1) / unit);
     for (uint32_t s = s0; s <= m && s < s0 + 4096; ++s)
@@ -472,19 +475,23 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
         // batches use the pipelined driver when the algorithm has one and its shared memory fits (and so
         // does any payload too large for the one-piece kernel)
         a.sub = 1;
+        // Streamed driver, launches of at most one wave (one CTA per SM covers them): 32 KiB units and two units
+        // of reduce-scatter in flight (one at cluster size 16) halve a lone problem's time against the batch
+        // defaults (measured at 128 and 192 KiB per CTA); the window then fits three stages.
+        const bool small = e->stage_pipe != nullptr && !g.stream_set && num_clusters * e->n <= d.sms;
         if (g.pipelined && (num_clusters > 1 || pipe_only) && e->fn_pipe != nullptr) {
-            const uint32_t sub = pipeline_units(e, m);
+            const uint32_t sub = pipeline_units(e, m, small ? 32768 : 0);
             uint64_t sp = sub ? e->smem_pipe(m / sub) : 0;
             if (sub && sp <= dsb::kSmemLimit && sp <= (uint64_t)d.optin) {
                 fn = e->fn_pipe;
                 a.sub = sub;
                 if (e->stage_pipe != nullptr) {   // streamed: as many stages as asked for and fit (>= 2)
                     const uint64_t stage = e->stage_pipe(m / sub), lim = std::min<uint64_t>(dsb::kSmemLimit, d.optin);
-                    uint32_t depth = g.stream_depth > 0 ? (uint32_t)g.stream_depth : (e->n >= 16 ? 2u : 3u);
+                    uint32_t depth = g.stream_depth > 0 ? (uint32_t)g.stream_depth : (e->n >= 16 && !small ? 2u : 3u);
                     while (depth > 2 && dsb::kD0 + depth * stage > lim) --depth;
                     sp = dsb::kD0 + depth * stage;
                     a.depth = depth;
-                    a.lag = (uint32_t)std::max(1, g.stream_lag);
+                    a.lag = small ? (e->n >= 16 ? 1u : 2u) : (uint32_t)std::max(1, g.stream_lag);
                     threads = e->threads_pipe;
                 }
                 smem = sp;
@@ -680,6 +687,14 @@ dsmem_status dsmem_set_pipeline_unit_bytes(size_t bytes) {
 }
 
 dsmem_status dsmem_set_stream_pipeline(size_t unit_bytes, int depth, int lag) {
+    if (unit_bytes == 0 && depth == 0 && lag == 0) {   // back to the measured defaults
+        std::lock_guard<std::mutex> lock(st().mu);
+        st().stream_unit_bytes = 16384;
+        st().stream_depth = 0;
+        st().stream_lag = 1;
+        st().stream_set = false;
+        return DSMEM_OK;
+    }
     if (unit_bytes < 256 || unit_bytes > 65536 || (unit_bytes & 15u) || (depth != 0 && (depth < 2 || depth > 8)) ||
         lag < 1 || lag >= (depth == 0 ? 2 : depth))
         return DSMEM_ERR_INVALID_ARGUMENT;
@@ -687,6 +702,7 @@ dsmem_status dsmem_set_stream_pipeline(size_t unit_bytes, int depth, int lag) {
     st().stream_unit_bytes = unit_bytes;
     st().stream_depth = depth;
     st().stream_lag = lag;
+    st().stream_set = true;
     return DSMEM_OK;
 }
 

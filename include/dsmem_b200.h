@@ -203,10 +203,11 @@ dsmem_status dsmem_set_pipelined(int enable);
  * default 16 KiB). Larger problems are split into equal legal sub-vectors no larger than this. */
 dsmem_status dsmem_set_pipeline_unit_bytes(size_t bytes);
 /* The streamed batch driver of rs_push_global_ag (reduce-scatter over DSMEM, all-gather through the
- * outputs; warp-specialised ring of stages): largest sub-vector per CTA (256 B .. 64 KiB, multiple of 16;
- * default 16 KiB), stages of the ring (2..8, fewer where the window does not fit; 0, the default: 3, or 2 at
- * cluster size 16) and units of reduce-scatter in flight (1 .. depth-1, default 1). Results do not depend on
- * these. */
+ * outputs; warp-specialised ring of stages): largest sub-vector per CTA (256 B .. 64 KiB, multiple of 16),
+ * stages of the ring (2..8, fewer where the window does not fit; 0: by cluster size) and units of
+ * reduce-scatter in flight (1 .. depth-1). Results do not depend on these. Defaults (also restored by
+ * (0, 0, 0)), measured on B200: 16 KiB units, 3 stages (2 at cluster size 16), 1 unit in flight; launches of
+ * at most one wave (clusters x N <= SM count) take 32 KiB units, 3 stages and 2 units in flight (1 at 16). */
 dsmem_status dsmem_set_stream_pipeline(size_t unit_bytes, int depth, int lag);
 
 /* Failure-detection self-test: launches one 2-CTA cluster whose mbarrier is armed for 16 bytes that

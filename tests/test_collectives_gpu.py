@@ -290,7 +290,9 @@ def test_payload_grid(cuda, orc, op, alg, n):
     assert not failures, "\n".join(failures)
 
 
-STREAM_SETTINGS = ((16384, 0, 1), (4096, 5, 3), (2048, 2, 1), (65536, 3, 2), (1024, 8, 1))
+# (0, 0, 0): the measured defaults, which take 32 KiB units for launches of at most one wave (the 2-problem
+# batches below) and 16 KiB units otherwise
+STREAM_SETTINGS = ((0, 0, 0), (16384, 0, 1), (4096, 5, 3), (2048, 2, 1), (65536, 3, 2), (1024, 8, 1))
 
 
 @pytest.mark.parametrize("n", D.CLUSTER_SIZES)
