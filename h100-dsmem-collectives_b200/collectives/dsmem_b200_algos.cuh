@@ -2136,36 +2136,42 @@ __global__ void __launch_bounds__(256) two_shot_pipelined_kernel(const BatchArgs
 // Streamed batch driver of AR_RsPushGlobalAg (alg rs_push_global_ag; a B200 extension): the reduce-scatter
 // shot of the two-shot AllReduce (allreduce__two_shot_push__trtllm.cu:31-45) over the SM-to-SM network, and
 // the all-gather through the outputs, so (N-1)/N * P bytes per CTA cross the SM-to-SM network instead of the
-// two-shot's 2(N-1)/N * P. Warp-specialised and deeply pipelined:
-//   * warp 0, one thread (producer): streams the CTA's units (sub-vectors of U elements of its input rows)
-//     into a ring of D stages by one-CTA bulk copies global -> shared, D - L units ahead, and once a unit
-//     has landed pushes chunk j of it into stage slot (b - j - 1) mod N of CTA j (N - 1 bulk copies
-//     completing on CTA j's reduce-scatter barrier of the stage);
-//   * warps 1..W (consumers): for each unit, wait until their own input and the N - 1 partials of their
-//     chunk b have landed, sum the N partials in rank order 0..N-1 (the plain driver's order, so the result
-//     is the same bit for bit), and store the sum from registers straight into position b of all N output
-//     rows of the problem (16-byte streaming stores, no shared-memory round trip); then one consumer thread
-//     arrives on the stage's credit barrier of every peer and on the local `done` barrier.
-//   * A stage is reused for unit k + D only after the local consumers are done with unit k and all N - 1
-//     peers' credits for unit k have arrived: the peers have consumed the chunks this CTA pushed (so its
-//     bulk copies have finished reading the stage) and freed the slots it pushes into next. L units of
-//     reduce-scatter are in flight while D - L loads stream in; there is no cluster barrier per unit.
-//   * Before leaving, the producer drains the credits of the last D units, so no remote arrive or copy aimed
-//     at this CTA is in flight at exit.
-// Layout: mbarriers in a static array (4 per stage); dynamic window: stage s at kD0 + s * stage_bytes(U),
-// the unit's input (U elements) followed by N - 1 received partials of chunk b (U / N elements each).
+// two-shot's 2(N-1)/N * P. Warp-specialised, with two rings:
+//   * an input ring of DX stages (one unit of U elements of this CTA's input row each) and a slot ring of DR
+//     stages (the N - 1 partials of chunk b that the peers push, U / N elements each). A unit in the
+//     reduce-scatter holds one of each; a unit being loaded holds only an input stage, so DX - DR loads stream
+//     in while DR units are in the reduce-scatter, and no slot buffer sits idle under a load;
+//   * warp 0, one thread (producer): for unit k, waits until its input has landed, waits for the release of
+//     unit k - DR (local consumers done with it, and the credits of all N - 1 peers: they consumed the chunks
+//     this CTA pushed for k - DR, so those bulk copies finished reading their input stage, and freed the slot
+//     stage unit k is pushed into), arms its slot barrier, pushes chunk j of unit k into slot (b - j - 1) mod N
+//     of CTA j (N - 1 bulk copies completing on CTA j's slot barrier), then loads unit k + DX - DR into the input
+//     stage unit k - DR released;
+//   * warps 1..W (consumers): for each unit, wait for their own input and the N - 1 partials of chunk b, sum
+//     the N partials in rank order 0..N-1 (the plain driver's order, so the result is the same bit for bit),
+//     store the sum from registers into position b of all N output rows (16-byte streaming stores); after a
+//     named barrier one consumer thread arrives (relaxed) on the unit's credit barrier of every peer and on the
+//     local `done` barrier of its input stage;
+//   * barrier phases follow from the unit index (stage use (k / stages) & 1), so the producer may wait the same
+//     release twice; no cluster barrier per unit. Before leaving, the producer drains the credits of the last
+//     DR units, so no remote arrive or copy aimed at this CTA is in flight at exit.
+// Layout: mbarriers in a static array; dynamic window: input stages at kD0 + x * U * B, then slot stages of
+// (N - 1) * (U / N) elements each.
 template <int N_, typename T_, class Op_>
 struct AR_RsGlobalAgStream {
     DSB_TRAITS(AllReduce, 0)
-    static constexpr int kMaxDepth = 8;
+    static constexpr int kMaxStages = 8;   // per ring
     static constexpr int kConsumerWarps = 4;
     static constexpr int kThreads = 32 * (1 + kConsumerWarps);
     __host__ __device__ static constexpr bool legal(uint32_t U) { return AR_TwoShotPush<N_, T_, Op_>::legal(U); }
-    __host__ __device__ static constexpr uint64_t stage_bytes(uint32_t U) {
-        return (uint64_t)U * B + (uint64_t)(N_ - 1) * (U / N_) * B;
+    __host__ __device__ static constexpr uint64_t in_stage_bytes(uint32_t U) { return (uint64_t)U * B; }
+    __host__ __device__ static constexpr uint64_t slot_stage_bytes(uint32_t U) { return (uint64_t)(N_ - 1) * (U / N_) * B; }
+    // one input stage and one slot stage (the host sizes the rings from these)
+    __host__ __device__ static constexpr uint64_t stage_bytes(uint32_t U) { return in_stage_bytes(U) + slot_stage_bytes(U); }
+    // smallest launchable window: two input stages, one slot stage
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t U) {
+        return kD0 + 2ull * in_stage_bytes(U) + slot_stage_bytes(U);
     }
-    // smallest launchable window (depth 2); the launcher grows the depth to what it asks for
-    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t U) { return kD0 + 2ull * stage_bytes(U); }
 };
 
 template <class A>
@@ -2174,46 +2180,50 @@ __global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const 
     using Op = typename A::Op;
     constexpr int N = A::kN;
     constexpr uint32_t kNC = 32u * A::kConsumerWarps;   // consumer threads
-    __shared__ __align__(8) unsigned long long bars[4 * A::kMaxDepth];
+    constexpr uint32_t kMax = A::kMaxStages;
+    // full[x], done[x] per input stage; rs[r], credit[r] per slot stage
+    __shared__ __align__(8) unsigned long long bars[4 * kMax];
     Ctx c;
     ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
     flag_init(c);
     const uint32_t S = a.sub, U = a.M / S, UB = U * A::B, CB = UB / N, C = U / N, nl = CB >> 4;
-    const uint32_t stage = (uint32_t)A::stage_bytes(U);
-    const uint32_t D = min(min(a.depth, (a.smem_bytes - kD0) / stage), (uint32_t)A::kMaxDepth);
-    const uint32_t L = min(max(a.lag, 1u), D - 1u);   // units of reduce-scatter in flight
-    auto full = [&](uint32_t s) { return smem_u32(&bars[4 * s + 0]); };
-    auto rs = [&](uint32_t s) { return smem_u32(&bars[4 * s + 1]); };
-    auto credit = [&](uint32_t s) { return smem_u32(&bars[4 * s + 2]); };
-    auto done = [&](uint32_t s) { return smem_u32(&bars[4 * s + 3]); };
+    const uint32_t DX = min(max(a.depth, 2u), kMax), DR = min(max(a.lag, 1u), min(DX - 1u, kMax));
+    const uint32_t slot_base = kD0 + DX * UB, slot_stage = (N - 1) * CB;
+    auto full = [&](uint32_t x) { return smem_u32(&bars[x]); };
+    auto done = [&](uint32_t x) { return smem_u32(&bars[kMax + x]); };
+    auto rs = [&](uint32_t r) { return smem_u32(&bars[2 * kMax + r]); };
+    auto credit = [&](uint32_t r) { return smem_u32(&bars[3 * kMax + r]); };
+    auto X = [&](long long k) { return kD0 + (uint32_t)(k % DX) * UB; };
+    auto R = [&](long long k) { return slot_base + (uint32_t)(k % DR) * slot_stage; };   // slot i at R + i * CB
     if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < D; ++s) {
-            mbar_init(full(s), 1);
-            mbar_init(rs(s), 1);
-            mbar_init(credit(s), N - 1);
-            mbar_init(done(s), 1);
+        for (uint32_t x = 0; x < DX; ++x) {
+            mbar_init(full(x), 1);
+            mbar_init(done(x), 1);
+        }
+        for (uint32_t r = 0; r < DR; ++r) {
+            mbar_init(rs(r), 1);
+            mbar_init(credit(r), N - 1);
         }
         fence_mbar_init();
     }
     cluster_sync();   // every barrier of the cluster initialised before any remote push or arrive
     const uint64_t total = (uint64_t)a.num_problems * N * a.M;   // elements of `in` and of `out`
+    const bool window_ok = slot_base + DR * slot_stage <= a.smem_bytes;
     const T* in = static_cast<const T*>(a.in);
     T* out = static_cast<T*>(a.out);
     const long long step = (long long)num_clusters();
     const long long first = (long long)cluster_id();
     const long long mine = first < a.num_problems ? (a.num_problems - 1 - first) / step + 1 : 0;
-    const long long units = mine * S;
+    const long long units = window_ok ? mine * S : 0;
+    if (!window_ok && threadIdx.x == 0) report(c, DSMEM_ERR_BIT_BOUNDS);
     auto problem_of = [&](long long k) { return first + (k / S) * step; };
     // element offset of row r, sub-vector k % S, of unit k's problem
     auto row_off = [&](long long k, uint32_t r) {
         return ((uint64_t)problem_of(k) * N + r) * a.M + (uint64_t)(k % S) * U;
     };
-    auto X = [&](uint32_t s) { return kD0 + s * stage; };
-    auto R = [&](uint32_t s) { return kD0 + s * stage + UB; };   // slot i at R + i * CB
-    // bounded wait on a static barrier; `ph` holds this thread's parity bit per stage
-    auto await = [&](uint32_t bar, uint32_t& ph, uint32_t s, int id) {
-        const uint32_t par = (ph >> s) & 1u;
-        ph ^= 1u << s;
+    // bounded wait for the phase of stage use `use` (parity use & 1) of barrier `bar`
+    auto await = [&](uint32_t bar, long long use, int id) {
+        const uint32_t par = (uint32_t)(use & 1);
         if (c.dead || mbar_try_wait_parity(bar, par)) return;
         if (!mbar_wait_parity_until(bar, par, c.deadline)) {
             c.dead = true;
@@ -2222,62 +2232,61 @@ __global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const 
     };
     if (threadIdx.x == 0 && units > 0) {
         // ---------------------------------------------------------------- producer
-        uint32_t ph_full = 0, ph_credit = 0, ph_done = 0;
-        auto release = [&](long long j) {   // stage of unit j free: local consumers and every peer done
-            const uint32_t s = (uint32_t)(j % D);
-            await(done(s), ph_done, s, 3);
-            await(credit(s), ph_credit, s, 2);
-        };
+        const long long ahead = (long long)(DX - DR);   // loads streaming in while DR units reduce-scatter
         auto issue_load = [&](long long k) {
-            const uint32_t s = (uint32_t)(k % D);
-            if (k >= (long long)D) release(k - D);
             c.unit = (uint32_t)k;
             const uint64_t off = row_off(k, c.rank);
             if (off + U > total) {
                 report(c, DSMEM_ERR_BIT_BOUNDS);
                 return;
             }
-            mbar_arrive_expect_tx(rs(s), (N - 1) * CB);   // the peers' partials of chunk b for unit k
-            mbar_arrive_expect_tx(full(s), UB);
-            bulk_load_g2s(c.sa + X(s), in + off, UB, full(s));
+            const uint32_t x = (uint32_t)(k % DX);
+            mbar_arrive_expect_tx(full(x), UB);
+            bulk_load_g2s(c.sa + X(k), in + off, UB, full(x));
         };
-        const long long ahead = (long long)(D - L);
+        auto release = [&](long long j) {   // unit j consumed here and at every peer
+            await(done((uint32_t)(j % DX)), j / DX, 3);
+            await(credit((uint32_t)(j % DR)), j / DR, 2);
+        };
         for (long long k = 0; k < units && k < ahead; ++k) issue_load(k);
         for (long long k = 0; k < units; ++k) {
-            const uint32_t s = (uint32_t)(k % D);
             c.deadline = globaltimer() + c.wait_limit;
             if (k % S == 0 && a.smid != nullptr) a.smid[(uint64_t)problem_of(k) * N + c.rank] = smid();
-            await(full(s), ph_full, s, 0);
+            await(full((uint32_t)(k % DX)), k / DX, 0);
+            if (k >= (long long)DR) release(k - DR);
+            const uint32_t r = (uint32_t)(k % DR);
+            mbar_arrive_expect_tx(rs(r), (N - 1) * CB);   // the peers' partials of chunk b for unit k
             for (uint32_t j = 1; j < (uint32_t)N; ++j) {
                 const uint32_t dst = (c.rank + j) % N, slot = (c.rank + N - dst - 1) % N;
-                const uint32_t to = R(s) + slot * CB, from = X(s) + dst * CB;
+                const uint32_t to = R(k) + slot * CB, from = X(k) + dst * CB;
                 if (((to | from | CB) & 15u) != 0u || CB == 0u || to + CB > c.smem_bytes || from + CB > c.smem_bytes) {
                     report(c, DSMEM_ERR_BIT_BOUNDS);
                     continue;
                 }
-                bulk_push(dst, c.sa + to, c.sa + from, CB, rs(s));
+                bulk_push(dst, c.sa + to, c.sa + from, CB, rs(r));
             }
+            // the input stage of unit k + DX - DR is unit k - DR's, released above
             if (k + ahead < units) issue_load(k + ahead);
         }
         c.deadline = globaltimer() + c.wait_limit;
-        for (long long j = units > (long long)D ? units - D : 0; j < units; ++j) release(j);
+        for (long long j = units > (long long)DR ? units - DR : 0; j < units; ++j)
+            await(credit((uint32_t)(j % DR)), j / DR, 2);
     } else if (threadIdx.x >= 32) {
         // ---------------------------------------------------------------- consumers
         const uint32_t tc = threadIdx.x - 32;
-        uint32_t ph_full = 0, ph_rs = 0;
         for (long long k = 0; k < units; ++k) {
-            const uint32_t s = (uint32_t)(k % D), sub = (uint32_t)(k % S);
+            const uint32_t sub = (uint32_t)(k % S);
             c.unit = (uint32_t)k;
             c.deadline = globaltimer() + c.wait_limit;
             unsigned long long* st = a.stamps != nullptr && tc == 0
                                          ? a.stamps + ((uint64_t)problem_of(k) * N + c.rank) * kStamps
                                          : nullptr;
-            await(full(s), ph_full, s, 0);
+            await(full((uint32_t)(k % DX)), k / DX, 0);
             if (st != nullptr && sub == 0) st[0] = globaltimer();
-            await(rs(s), ph_rs, s, 1);
+            await(rs((uint32_t)(k % DR)), k / DR, 1);
             if (st != nullptr && sub + 1 == S) st[2] = globaltimer();
-            const uint4* own = c.ptr<const uint4>(X(s) + c.rank * CB);
-            const uint4* slots = c.ptr<const uint4>(R(s));
+            const uint4* own = c.ptr<const uint4>(X(k) + c.rank * CB);
+            const uint4* slots = c.ptr<const uint4>(R(k));
             uint4* rows[N];
             bool ok = true;
 #pragma unroll
@@ -2302,13 +2311,14 @@ __global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const 
                     for (int r = 0; r < N; ++r) __stcs(rows[r] + u, res);
                 }
             }
-            asm volatile("bar.sync 1, %0;" ::"r"(kNC) : "memory");   // every consumer has read the stage
+            asm volatile("bar.sync 1, %0;" ::"r"(kNC) : "memory");   // every consumer has read the stages
             if (tc == 0) {
-                // relaxed: the credits only release the stage's shared memory, whose reads are complete (their
+                // relaxed: the credits only release the stages' shared memory, whose reads are complete (their
                 // values are already summed and stored); a release arrive would also wait for the global stores
                 // just issued (~4 us under load) and stall the consumers on every unit
-                for (uint32_t j = 1; j < (uint32_t)N; ++j) mbar_arrive_remote_relaxed(credit(s), (c.rank + j) % N);
-                mbar_arrive_relaxed(done(s));
+                for (uint32_t j = 1; j < (uint32_t)N; ++j)
+                    mbar_arrive_remote_relaxed(credit((uint32_t)(k % DR)), (c.rank + j) % N);
+                mbar_arrive_relaxed(done((uint32_t)(k % DX)));
                 if (st != nullptr && sub + 1 == S) st[1] = globaltimer();
             }
         }

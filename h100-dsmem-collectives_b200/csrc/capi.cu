@@ -131,11 +131,11 @@ struct State {
     unsigned long long wait_limit_ns = 1000000000ull;
     bool pipelined = true;        // batches use a pipelined driver where one exists
     uint64_t unit_bytes = 16384;  // pipelined drivers: largest sub-vector per CTA
-    // Streamed drivers (measured on B200 at 64 KiB per CTA, 2 GiB batches): 16 KiB units, one unit of
-    // reduce-scatter in flight, 3 stages (2 at cluster size 16, where the smaller window fits more clusters).
+    // Streamed drivers (measured on B200 at 64 KiB per CTA, 2 GiB batches): 16 KiB units, one slot stage (one
+    // unit of reduce-scatter in flight), input stages by cluster size (kStreamDepth).
     uint64_t stream_unit_bytes = 16384;  // largest sub-vector per CTA
-    int stream_depth = 0;                // stages of the ring; 0: by cluster size as above
-    int stream_lag = 1;                  // units of reduce-scatter in flight
+    int stream_depth = 0;                // input stages; 0: kStreamDepth
+    int stream_lag = 1;                  // slot stages: units of reduce-scatter in flight
     bool stream_set = false;             // dsmem_set_stream_pipeline was called: no launch-size defaults
 };
 
@@ -364,6 +364,11 @@ cudaError_t error_word(DeviceState& d, unsigned** out) {
     return cudaSuccess;
 }
 
+// Input stages of the streamed AllReduce's ring by cluster size (batch launches with one slot stage), measured
+// on B200 at 64 KiB per CTA, 2 GiB batches: 3 at N = 8 (f32 0.733 ms against 0.758 with 2), else 2 (N = 16:
+// 0.970 ms against 1.088 with 3; the smaller window fits more clusters).
+uint32_t kStreamDepth(int n) { return n == 8 ? 3u : 2u; }
+
 // Units per problem for a pipelined driver: the smallest split into legal sub-vectors of at most
 // unit_bytes per CTA (default 16 KiB: three unit buffers in 48 KiB, four CTAs per SM) whose smallest window
 // fits the shared-memory limit; 0 if none.
@@ -475,9 +480,9 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
         // batches use the pipelined driver when the algorithm has one and its shared memory fits (and so
         // does any payload too large for the one-piece kernel)
         a.sub = 1;
-        // Streamed driver, launches of at most one wave (one CTA per SM covers them): 32 KiB units and two units
-        // of reduce-scatter in flight (one at cluster size 16) halve a lone problem's time against the batch
-        // defaults (measured at 128 and 192 KiB per CTA); the window then fits three stages.
+        // Streamed driver, launches of at most one wave (one CTA per SM covers them): 32 KiB units, four input
+        // stages and three units of reduce-scatter in flight about halve a lone problem's time against the batch
+        // defaults (measured at 128 and 192 KiB per CTA, N = 8 and 16).
         const bool small = e->stage_pipe != nullptr && !g.stream_set && num_clusters * e->n <= d.sms;
         if (g.pipelined && (num_clusters > 1 || pipe_only) && e->fn_pipe != nullptr) {
             const uint32_t sub = pipeline_units(e, m, small ? 32768 : 0);
@@ -485,13 +490,21 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
             if (sub && sp <= dsb::kSmemLimit && sp <= (uint64_t)d.optin) {
                 fn = e->fn_pipe;
                 a.sub = sub;
-                if (e->stage_pipe != nullptr) {   // streamed: as many stages as asked for and fit (>= 2)
-                    const uint64_t stage = e->stage_pipe(m / sub), lim = std::min<uint64_t>(dsb::kSmemLimit, d.optin);
-                    uint32_t depth = g.stream_depth > 0 ? (uint32_t)g.stream_depth : (e->n >= 16 && !small ? 2u : 3u);
-                    while (depth > 2 && dsb::kD0 + depth * stage > lim) --depth;
-                    sp = dsb::kD0 + depth * stage;
-                    a.depth = depth;
-                    a.lag = small ? (e->n >= 16 ? 1u : 2u) : (uint32_t)std::max(1, g.stream_lag);
+                if (e->stage_pipe != nullptr) {
+                    // streamed: an input ring of `depth` stages and a slot ring of `lag` stages (units in the
+                    // reduce-scatter), as many as asked for and fit; depth > lag >= 1
+                    const uint32_t u = m / sub;
+                    const uint64_t in = (uint64_t)u * e->elem_bytes, slot = e->stage_pipe(u) - in;
+                    const uint64_t lim = std::min<uint64_t>(dsb::kSmemLimit, d.optin);
+                    uint32_t dr = small ? 3u : (uint32_t)std::max(1, g.stream_lag);
+                    uint32_t dx = g.stream_depth > 0 ? (uint32_t)g.stream_depth : (small ? 4u : kStreamDepth(e->n));
+                    dx = std::max(dx, dr + 1);
+                    auto window = [&] { return dsb::kD0 + dx * in + dr * slot; };
+                    while (window() > lim && dx > dr + 1) --dx;
+                    while (window() > lim && dr > 1) dx = std::max(--dr + 1, dx - 1);
+                    sp = window();
+                    a.depth = dx;
+                    a.lag = dr;
                     threads = e->threads_pipe;
                 }
                 smem = sp;

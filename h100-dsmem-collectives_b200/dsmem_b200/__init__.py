@@ -347,8 +347,8 @@ def set_pipeline_unit_bytes(nbytes):
 
 
 def set_stream_pipeline(unit_bytes=0, depth=0, lag=0):
-    """Sub-vector size, ring depth (0: by cluster size) and reduce-scatter units in flight of the streamed
-    rs_push_global_ag driver; no arguments restore the measured defaults (which also adapt to one-wave launches)."""
+    """Sub-vector size, input stages (0: by cluster size) and slot stages (units of reduce-scatter in flight) of the
+    streamed rs_push_global_ag driver; no arguments restore the measured defaults (which adapt to one-wave launches)."""
     _ok(lib().dsmem_set_stream_pipeline(int(unit_bytes), int(depth), int(lag)), "dsmem_set_stream_pipeline")
 
 

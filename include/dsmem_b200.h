@@ -203,11 +203,12 @@ dsmem_status dsmem_set_pipelined(int enable);
  * default 16 KiB). Larger problems are split into equal legal sub-vectors no larger than this. */
 dsmem_status dsmem_set_pipeline_unit_bytes(size_t bytes);
 /* The streamed batch driver of rs_push_global_ag (reduce-scatter over DSMEM, all-gather through the
- * outputs; warp-specialised ring of stages): largest sub-vector per CTA (256 B .. 64 KiB, multiple of 16),
- * stages of the ring (2..8, fewer where the window does not fit; 0: by cluster size) and units of
- * reduce-scatter in flight (1 .. depth-1). Results do not depend on these. Defaults (also restored by
- * (0, 0, 0)), measured on B200: 16 KiB units, 3 stages (2 at cluster size 16), 1 unit in flight; launches of
- * at most one wave (clusters x N <= SM count) take 32 KiB units, 3 stages and 2 units in flight (1 at 16). */
+ * outputs; warp-specialised, an input ring and a slot ring): largest sub-vector per CTA (256 B .. 64 KiB,
+ * multiple of 16), input stages `depth` (2..8; 0: by cluster size) and slot stages `lag` = units of
+ * reduce-scatter in flight (1 .. depth-1); depth - lag loads stream in meanwhile; fewer stages where the window
+ * does not fit. Results do not depend on these. Defaults (also restored by (0, 0, 0)), measured on B200: 16 KiB
+ * units, 3 input stages at cluster size 8 and 2 otherwise, 1 slot stage; launches of at most one wave
+ * (clusters x N <= SM count) take 32 KiB units, 4 input stages and 3 slot stages. */
 dsmem_status dsmem_set_stream_pipeline(size_t unit_bytes, int depth, int lag);
 
 /* Failure-detection self-test: launches one 2-CTA cluster whose mbarrier is armed for 16 bytes that
