@@ -4,7 +4,8 @@ Single GPU: the kernel for TP ranks emulated in one launch (dsmem_tp_emulate: al
 local, every row computed once and stored into every rank's y). Two or more GPUs: the real path, one
 process per GPU with CUDA-IPC-mapped buffers (skipped when the box has one GPU).
 Oracle: oracle.tp_rmsnorm (h = sum over ranks (+ residual) in double, then clusterfusion_rmsnorm.py:65).
-Tolerance |got - ref| <= 1e-2 * (1 + |ref|) (bf16 output); every rank's y must be bit-identical.
+Tolerance |got - ref| <= 1e-2 * (1 + |ref|) (bf16 output); every rank's y must be bit-identical. The NCCL
+baseline composition accumulates in bf16 over its ring hops: 1e-2 * (TP - 1) * (1 + |ref|).
 """
 import os
 import socket
@@ -133,9 +134,13 @@ def test_tp_multi_gpu(cuda, orc, tmp_path, world):
         assert np.array_equal(ys[r], ys[0]), f"rank {r}'s y differs from rank 0's"
     bad, _, mr = orc.check(1, ys[0].reshape(-1), ref.reshape(-1), 1, RTOL)
     assert bad == 0, f"fused: {bad} beyond tol (max rel {mr})"
+    # the NCCL composition (the baseline) reduces bf16 in bf16, rounding at each of its TP - 1 ring hops, where the
+    # fused kernel sums in fp32 and rounds once: its bound scales with the hops (at TP = 4, 3 of 524,288 elements
+    # came in at 1.047e-2 * (1 + |ref|))
     for r in range(world):
-        bad, _, mr = orc.check(1, np.load(tmp_path / f"nccl{r}.npy").reshape(-1), ref.reshape(-1), 1, RTOL)
-        assert bad == 0, f"nccl composition rank {r}: {bad} beyond tol (max rel {mr})"
+        tol = RTOL * max(1, world - 1)
+        bad, _, mr = orc.check(1, np.load(tmp_path / f"nccl{r}.npy").reshape(-1), ref.reshape(-1), 1, tol)
+        assert bad == 0, f"nccl composition rank {r}: {bad} beyond {tol} (max rel {mr})"
 
 
 # ----------------------------------------------------------------------------- failure detection
