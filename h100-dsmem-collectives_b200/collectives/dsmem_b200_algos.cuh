@@ -2133,52 +2133,82 @@ __global__ void __launch_bounds__(256) two_shot_pipelined_kernel(const BatchArgs
 }
 
 // -----------------------------------------------------------------------------------------------------
-// Streamed batch driver of AR_RsPushGlobalAg (alg rs_push_global_ag; a B200 extension): the reduce-scatter
-// shot of the two-shot AllReduce (allreduce__two_shot_push__trtllm.cu:31-45) over the SM-to-SM network, and
-// the all-gather through the outputs, so (N-1)/N * P bytes per CTA cross the SM-to-SM network instead of the
-// two-shot's 2(N-1)/N * P. Warp-specialised, with two rings:
-//   * an input ring of DX stages (one unit of U elements of this CTA's input row each) and a slot ring of DR
-//     stages (the N - 1 partials of chunk b that the peers push, U / N elements each). A unit in the
-//     reduce-scatter holds one of each; a unit being loaded holds only an input stage, so DX - DR loads stream
-//     in while DR units are in the reduce-scatter, and no slot buffer sits idle under a load;
-//   * warp 0, one thread (producer): for unit k, waits until its input has landed, waits for the release of
-//     unit k - DR (local consumers done with it, and the credits of all N - 1 peers: they consumed the chunks
-//     this CTA pushed for k - DR, so those bulk copies finished reading their input stage, and freed the slot
-//     stage unit k is pushed into), arms its slot barrier, pushes chunk j of unit k into slot (b - j - 1) mod N
-//     of CTA j (N - 1 bulk copies completing on CTA j's slot barrier), then loads unit k + DX - DR into the input
-//     stage unit k - DR released;
-//   * warps 1..W (consumers): for each unit, wait for their own input and the N - 1 partials of chunk b, sum
-//     the N partials in rank order 0..N-1 (the plain driver's order, so the result is the same bit for bit),
-//     store the sum from registers into position b of all N output rows (16-byte streaming stores); after a
-//     named barrier one consumer thread arrives (relaxed) on the unit's credit barrier of every peer and on the
-//     local `done` barrier of its input stage;
-//   * barrier phases follow from the unit index (stage use (k / stages) & 1), so the producer may wait the same
-//     release twice; no cluster barrier per unit. Before leaving, the producer drains the credits of the last
-//     DR units, so no remote arrive or copy aimed at this CTA is in flight at exit.
-// Layout: mbarriers in a static array; dynamic window: input stages at kD0 + x * U * B, then slot stages of
-// (N - 1) * (U / N) elements each.
+// Streamed batch drivers (B200 extensions of the batch regime): warp-specialised, two rings, no cluster barrier
+// per unit. A problem's per-rank data is cut into units (sub-ranges of U elements of every rank block) that flow
+// through:
+//   * an input ring of DX stages (the unit's input: one piece for AllReduce / AllGather, the N pieces for
+//     ReduceScatter / AlltoAll) and a slot ring of DR stages (what the N - 1 peers push for the unit). A unit in
+//     the exchange holds one of each; a unit being loaded holds only an input stage, so DX - DR loads stream in
+//     while DR units are exchanged, and no slot buffer sits idle under a load;
+//   * warp 0, one thread (producer): for unit k, waits until its input has landed, waits for the release of unit
+//     k - DR (local consumers done with it, and the credits of all N - 1 peers: they consumed what this CTA
+//     pushed for k - DR, so those bulk copies finished reading their input stage, and freed the slot stage unit k
+//     is pushed into), arms its slot barrier, pushes to every peer j (slot (b - j - 1) mod N of CTA j, completing
+//     on CTA j's slot barrier), then loads unit k + DX - DR into the input stage unit k - DR released;
+//   * warps 1..W (consumers): wait for the unit's input and slots, combine, store from registers with 16-byte
+//     streaming stores; after a named barrier one consumer thread arrives (relaxed) on the unit's credit barrier
+//     of every peer and on the local `done` barrier of its input stage;
+//   * barrier phases follow from the unit index (stage use (k / stages) & 1); before leaving, the producer drains
+//     the credits of the last DR units, so no remote arrive or copy aimed at this CTA is in flight at exit.
+// Per op (b = this rank, U elements per piece):
+//   AllReduce (alg rs_push_global_ag): the reduce-scatter shot of the two-shot AllReduce
+//     (allreduce__two_shot_push__trtllm.cu:31-45): chunk j (U / N elements) of the unit to CTA j; the consumers
+//     sum the N partials of chunk b in rank order and store the sum into position b of all N output rows (the
+//     all-gather through the outputs): (N-1)/N * P per CTA over DSMEM, half the two-shot's;
+//   ReduceScatter (alg direct_push, reducescatter__direct_push__generic.cu:19-40): piece j to CTA j; the
+//     consumers sum the N pieces for b in rank order (the plain driver's order) into this rank's output row;
+//   AlltoAll (alg direct_push, alltoall__direct_push__generic.cu:17-33): piece j to CTA j; the consumers store
+//     piece r (from rank r) into position r of this rank's output row;
+//   AllGather (alg direct_replicated_push, allgather__direct_replicated_push__credit.cu:20-29): the whole unit to
+//     every peer; the consumers store block r into position r of this rank's output row.
+// Layout: mbarriers in a static array; dynamic window: input stages at kD0 + x * in_stage_bytes(U), then slot
+// stages of slot_stage_bytes(U).
+#define DSB_STREAM_TRAITS(OPKIND, PIECES, PUSH_ELEMS)                                                         \
+    DSB_TRAITS(OPKIND, 0)                                                                                     \
+    static constexpr int kMaxStages = 8;   /* per ring */                                                    \
+    static constexpr int kConsumerWarps = 4;                                                                  \
+    static constexpr int kThreads = 32 * (1 + kConsumerWarps);                                               \
+    static constexpr uint32_t kPieces = PIECES; /* input pieces per unit */                                 \
+    __host__ __device__ static constexpr uint32_t push_elems(uint32_t U) { return PUSH_ELEMS; }              \
+    __host__ __device__ static constexpr uint64_t in_stage_bytes(uint32_t U) { return (uint64_t)kPieces * U * B; } \
+    __host__ __device__ static constexpr uint64_t slot_stage_bytes(uint32_t U) {                             \
+        return (uint64_t)(N_ - 1) * push_elems(U) * B;                                                        \
+    }                                                                                                         \
+    __host__ __device__ static constexpr uint64_t stage_bytes(uint32_t U) {                                  \
+        return in_stage_bytes(U) + slot_stage_bytes(U);                                                       \
+    }                                                                                                         \
+    /* smallest launchable window: two input stages, one slot stage */                                       \
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t U) {                                   \
+        return kD0 + 2ull * in_stage_bytes(U) + slot_stage_bytes(U);                                          \
+    }
+
 template <int N_, typename T_, class Op_>
 struct AR_RsGlobalAgStream {
-    DSB_TRAITS(AllReduce, 0)
-    static constexpr int kMaxStages = 8;   // per ring
-    static constexpr int kConsumerWarps = 4;
-    static constexpr int kThreads = 32 * (1 + kConsumerWarps);
+    DSB_STREAM_TRAITS(AllReduce, 1u, U / N_)
     __host__ __device__ static constexpr bool legal(uint32_t U) { return AR_TwoShotPush<N_, T_, Op_>::legal(U); }
-    __host__ __device__ static constexpr uint64_t in_stage_bytes(uint32_t U) { return (uint64_t)U * B; }
-    __host__ __device__ static constexpr uint64_t slot_stage_bytes(uint32_t U) { return (uint64_t)(N_ - 1) * (U / N_) * B; }
-    // one input stage and one slot stage (the host sizes the rings from these)
-    __host__ __device__ static constexpr uint64_t stage_bytes(uint32_t U) { return in_stage_bytes(U) + slot_stage_bytes(U); }
-    // smallest launchable window: two input stages, one slot stage
-    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t U) {
-        return kD0 + 2ull * in_stage_bytes(U) + slot_stage_bytes(U);
-    }
+};
+template <int N_, typename T_, class Op_>
+struct RS_DirectPushStream {
+    DSB_STREAM_TRAITS(ReduceScatter, (uint32_t)N_, U)
+    __host__ __device__ static constexpr bool legal(uint32_t U) { return mult16(U * B); }
+};
+template <int N_, typename T_, class Op_>
+struct A2A_DirectPushStream {
+    DSB_STREAM_TRAITS(AllToAll, (uint32_t)N_, U)
+    __host__ __device__ static constexpr bool legal(uint32_t U) { return mult16(U * B); }
+};
+template <int N_, typename T_, class Op_>
+struct AG_ReplicatedPushStream {
+    DSB_STREAM_TRAITS(AllGather, 1u, U)
+    __host__ __device__ static constexpr bool legal(uint32_t U) { return mult16(U * B); }
 };
 
 template <class A>
-__global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const BatchArgs a) {
+__device__ __forceinline__ void stream_body(const BatchArgs& a) {
     using T = typename A::T;
     using Op = typename A::Op;
     constexpr int N = A::kN;
+    constexpr OpKind kOp = A::kOp;
     constexpr uint32_t kNC = 32u * A::kConsumerWarps;   // consumer threads
     constexpr uint32_t kMax = A::kMaxStages;
     // full[x], done[x] per input stage; rs[r], credit[r] per slot stage
@@ -2186,15 +2216,17 @@ __global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const 
     Ctx c;
     ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
     flag_init(c);
-    const uint32_t S = a.sub, U = a.M / S, UB = U * A::B, CB = UB / N, C = U / N, nl = CB >> 4;
+    const uint32_t S = a.sub, U = a.M / S, UB = U * A::B;
+    const uint32_t PB = A::push_elems(U) * A::B;                 // bytes pushed to each peer per unit
+    const uint32_t XB = (uint32_t)A::in_stage_bytes(U), RB = (uint32_t)A::slot_stage_bytes(U);
     const uint32_t DX = min(max(a.depth, 2u), kMax), DR = min(max(a.lag, 1u), min(DX - 1u, kMax));
-    const uint32_t slot_base = kD0 + DX * UB, slot_stage = (N - 1) * CB;
+    const uint32_t slot_base = kD0 + DX * XB;
     auto full = [&](uint32_t x) { return smem_u32(&bars[x]); };
     auto done = [&](uint32_t x) { return smem_u32(&bars[kMax + x]); };
     auto rs = [&](uint32_t r) { return smem_u32(&bars[2 * kMax + r]); };
     auto credit = [&](uint32_t r) { return smem_u32(&bars[3 * kMax + r]); };
-    auto X = [&](long long k) { return kD0 + (uint32_t)(k % DX) * UB; };
-    auto R = [&](long long k) { return slot_base + (uint32_t)(k % DR) * slot_stage; };   // slot i at R + i * CB
+    auto X = [&](long long k) { return kD0 + (uint32_t)(k % DX) * XB; };
+    auto R = [&](long long k) { return slot_base + (uint32_t)(k % DR) * RB; };   // slot i at R + i * PB
     if (threadIdx.x == 0) {
         for (uint32_t x = 0; x < DX; ++x) {
             mbar_init(full(x), 1);
@@ -2207,8 +2239,9 @@ __global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const 
         fence_mbar_init();
     }
     cluster_sync();   // every barrier of the cluster initialised before any remote push or arrive
-    const uint64_t total = (uint64_t)a.num_problems * N * a.M;   // elements of `in` and of `out`
-    const bool window_ok = slot_base + DR * slot_stage <= a.smem_bytes;
+    const uint64_t in_r = in_elems_per_rank<A>(a.M), out_r = out_elems_per_rank<A>(a.M);
+    const uint64_t total_in = (uint64_t)a.num_problems * N * in_r, total_out = (uint64_t)a.num_problems * N * out_r;
+    const bool window_ok = slot_base + DR * RB <= a.smem_bytes;
     const T* in = static_cast<const T*>(a.in);
     T* out = static_cast<T*>(a.out);
     const long long step = (long long)num_clusters();
@@ -2217,9 +2250,12 @@ __global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const 
     const long long units = window_ok ? mine * S : 0;
     if (!window_ok && threadIdx.x == 0) report(c, DSMEM_ERR_BIT_BOUNDS);
     auto problem_of = [&](long long k) { return first + (k / S) * step; };
-    // element offset of row r, sub-vector k % S, of unit k's problem
-    auto row_off = [&](long long k, uint32_t r) {
-        return ((uint64_t)problem_of(k) * N + r) * a.M + (uint64_t)(k % S) * U;
+    // rank r's row of unit k's problem, piece j (of M elements), sub-range k % S: element offsets
+    auto in_off = [&](long long k, uint32_t r, uint32_t j) {
+        return ((uint64_t)problem_of(k) * N + r) * in_r + (uint64_t)j * a.M + (uint64_t)(k % S) * U;
+    };
+    auto out_off = [&](long long k, uint32_t r, uint32_t j) {
+        return ((uint64_t)problem_of(k) * N + r) * out_r + (uint64_t)j * a.M + (uint64_t)(k % S) * U;
     };
     // bounded wait for the phase of stage use `use` (parity use & 1) of barrier `bar`
     auto await = [&](uint32_t bar, long long use, int id) {
@@ -2232,17 +2268,17 @@ __global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const 
     };
     if (threadIdx.x == 0 && units > 0) {
         // ---------------------------------------------------------------- producer
-        const long long ahead = (long long)(DX - DR);   // loads streaming in while DR units reduce-scatter
+        const long long ahead = (long long)(DX - DR);   // loads streaming in while DR units are exchanged
         auto issue_load = [&](long long k) {
             c.unit = (uint32_t)k;
-            const uint64_t off = row_off(k, c.rank);
-            if (off + U > total) {
+            const uint32_t x = (uint32_t)(k % DX);
+            if (in_off(k, c.rank, A::kPieces - 1) + U > total_in) {
                 report(c, DSMEM_ERR_BIT_BOUNDS);
                 return;
             }
-            const uint32_t x = (uint32_t)(k % DX);
-            mbar_arrive_expect_tx(full(x), UB);
-            bulk_load_g2s(c.sa + X(k), in + off, UB, full(x));
+            mbar_arrive_expect_tx(full(x), XB);
+            for (uint32_t j = 0; j < A::kPieces; ++j)
+                bulk_load_g2s(c.sa + X(k) + j * UB, in + in_off(k, c.rank, j), UB, full(x));
         };
         auto release = [&](long long j) {   // unit j consumed here and at every peer
             await(done((uint32_t)(j % DX)), j / DX, 3);
@@ -2255,15 +2291,16 @@ __global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const 
             await(full((uint32_t)(k % DX)), k / DX, 0);
             if (k >= (long long)DR) release(k - DR);
             const uint32_t r = (uint32_t)(k % DR);
-            mbar_arrive_expect_tx(rs(r), (N - 1) * CB);   // the peers' partials of chunk b for unit k
+            mbar_arrive_expect_tx(rs(r), (N - 1) * PB);   // what the peers push for unit k
             for (uint32_t j = 1; j < (uint32_t)N; ++j) {
                 const uint32_t dst = (c.rank + j) % N, slot = (c.rank + N - dst - 1) % N;
-                const uint32_t to = R(k) + slot * CB, from = X(k) + dst * CB;
-                if (((to | from | CB) & 15u) != 0u || CB == 0u || to + CB > c.smem_bytes || from + CB > c.smem_bytes) {
+                // AllGather pushes the whole unit; the others the part owned by dst
+                const uint32_t to = R(k) + slot * PB, from = X(k) + (kOp == OpKind::AllGather ? 0u : dst * PB);
+                if (((to | from | PB) & 15u) != 0u || PB == 0u || to + PB > c.smem_bytes || from + PB > c.smem_bytes) {
                     report(c, DSMEM_ERR_BIT_BOUNDS);
                     continue;
                 }
-                bulk_push(dst, c.sa + to, c.sa + from, CB, rs(r));
+                bulk_push(dst, c.sa + to, c.sa + from, PB, rs(r));
             }
             // the input stage of unit k + DX - DR is unit k - DR's, released above
             if (k + ahead < units) issue_load(k + ahead);
@@ -2273,7 +2310,7 @@ __global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const 
             await(credit((uint32_t)(j % DR)), j / DR, 2);
     } else if (threadIdx.x >= 32) {
         // ---------------------------------------------------------------- consumers
-        const uint32_t tc = threadIdx.x - 32;
+        const uint32_t tc = threadIdx.x - 32, nl = PB >> 4;   // 16-byte lanes of one pushed part
         for (long long k = 0; k < units; ++k) {
             const uint32_t sub = (uint32_t)(k % S);
             c.unit = (uint32_t)k;
@@ -2285,37 +2322,57 @@ __global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const 
             if (st != nullptr && sub == 0) st[0] = globaltimer();
             await(rs((uint32_t)(k % DR)), k / DR, 1);
             if (st != nullptr && sub + 1 == S) st[2] = globaltimer();
-            const uint4* own = c.ptr<const uint4>(X(k) + c.rank * CB);
+            // the part from rank r: this rank's own part from the input stage, the others from their slots
+            const uint4* own = c.ptr<const uint4>(X(k) + (kOp == OpKind::AllGather ? 0u : c.rank * PB));
             const uint4* slots = c.ptr<const uint4>(R(k));
-            uint4* rows[N];
-            bool ok = true;
+            auto part = [&](int r) { return r == (int)c.rank ? own : slots + ((r + N - (int)c.rank - 1) % N) * nl; };
+            if constexpr (kOp == OpKind::AllReduce || kOp == OpKind::ReduceScatter) {
+                // AllReduce: the sum of chunk b into position b of all N output rows; ReduceScatter: into this
+                // rank's output row
+                constexpr int kRows = kOp == OpKind::AllReduce ? N : 1;
+                uint4* rows[kRows];
+                bool ok = true;
 #pragma unroll
-            for (int r = 0; r < N; ++r) {
-                const uint64_t o = row_off(k, (uint32_t)r) + (uint64_t)c.rank * C;
-                ok = ok && o + C <= total;
-                rows[r] = reinterpret_cast<uint4*>(out + o);
-            }
-            if (!ok) {
-                if (tc == 0) report(c, DSMEM_ERR_BIT_BOUNDS);
+                for (int r = 0; r < kRows; ++r) {
+                    const uint64_t o = kOp == OpKind::AllReduce
+                                           ? out_off(k, (uint32_t)r, 0) + (uint64_t)c.rank * A::push_elems(U)
+                                           : out_off(k, c.rank, 0);
+                    ok = ok && o + A::push_elems(U) <= total_out;
+                    rows[r] = reinterpret_cast<uint4*>(out + o);
+                }
+                if (!ok) {
+                    if (tc == 0) report(c, DSMEM_ERR_BIT_BOUNDS);
+                } else {
+                    for (uint32_t u = tc; u < nl; u += kNC) {
+                        uint4 v[N];
+#pragma unroll
+                        for (int r = 0; r < N; ++r) v[r] = part(r)[u];
+                        auto acc = Pk<T, Op>::open(v[0]);
+#pragma unroll
+                        for (int r = 1; r < N; ++r) Pk<T, Op>::add(acc, v[r]);
+                        const uint4 res = Pk<T, Op>::close(acc);
+#pragma unroll
+                        for (int r = 0; r < kRows; ++r) __stcs(rows[r] + u, res);
+                    }
+                }
             } else {
-                for (uint32_t u = tc; u < nl; u += kNC) {
-                    uint4 v[N];
-#pragma unroll
-                    for (int r = 0; r < N; ++r)
-                        v[r] = r == (int)c.rank ? own[u] : slots[((r + N - (int)c.rank - 1) % N) * nl + u];
-                    auto acc = Pk<T, Op>::open(v[0]);
-#pragma unroll
-                    for (int r = 1; r < N; ++r) Pk<T, Op>::add(acc, v[r]);
-                    const uint4 res = Pk<T, Op>::close(acc);
-#pragma unroll
-                    for (int r = 0; r < N; ++r) __stcs(rows[r] + u, res);
+                // AlltoAll / AllGather: the part from rank r into position r of this rank's output row
+                if (out_off(k, c.rank, N - 1) + U > total_out) {
+                    if (tc == 0) report(c, DSMEM_ERR_BIT_BOUNDS);
+                } else {
+                    uint4* row = reinterpret_cast<uint4*>(out + out_off(k, c.rank, 0));
+                    const uint32_t stride = a.M * A::B >> 4;   // 16-byte units between the row's positions
+                    for (uint32_t idx = tc; idx < (uint32_t)N * nl; idx += kNC) {
+                        const uint32_t r = idx / nl, u = idx - r * nl;
+                        __stcs(row + (uint64_t)r * stride + u, part((int)r)[u]);
+                    }
                 }
             }
             asm volatile("bar.sync 1, %0;" ::"r"(kNC) : "memory");   // every consumer has read the stages
             if (tc == 0) {
                 // relaxed: the credits only release the stages' shared memory, whose reads are complete (their
-                // values are already summed and stored); a release arrive would also wait for the global stores
-                // just issued (~4 us under load) and stall the consumers on every unit
+                // values are already stored); a release arrive would also wait for the global stores just
+                // issued (~4 us under load) and stall the consumers on every unit
                 for (uint32_t j = 1; j < (uint32_t)N; ++j)
                     mbar_arrive_remote_relaxed(credit((uint32_t)(k % DR)), (c.rank + j) % N);
                 mbar_arrive_relaxed(done((uint32_t)(k % DX)));
@@ -2324,6 +2381,17 @@ __global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const 
         }
     }
     finish(c);   // no CTA leaves while a peer may still push into it
+}
+
+// The AllReduce's streamed driver (the name the profiles and the bench name).
+template <class A>
+__global__ void __launch_bounds__(A::kThreads) rs_global_ag_stream_kernel(const BatchArgs a) {
+    stream_body<A>(a);
+}
+// The streamed drivers of ReduceScatter, AlltoAll and AllGather.
+template <class A>
+__global__ void __launch_bounds__(A::kThreads) collective_stream_kernel(const BatchArgs a) {
+    stream_body<A>(a);
 }
 
 // Reference harness contract (collectives/harness/main.cu): one cluster, compile-time M.

@@ -364,10 +364,15 @@ cudaError_t error_word(DeviceState& d, unsigned** out) {
     return cudaSuccess;
 }
 
-// Input stages of the streamed AllReduce's ring by cluster size (batch launches with one slot stage), measured
-// on B200 at 64 KiB per CTA, 2 GiB batches: 3 at N = 8 (f32 0.733 ms against 0.758 with 2), else 2 (N = 16:
-// 0.970 ms against 1.088 with 3; the smaller window fits more clusters).
-uint32_t kStreamDepth(int n) { return n == 8 ? 3u : 2u; }
+// Input stages of the streamed drivers' ring by op and cluster size (batch launches with one slot stage),
+// measured on B200 at 16-192 KiB per CTA, 1-2 GiB batches. AllReduce: 3 at N = 8 (f32 0.733 ms against 0.758
+// with 2), else 2 (N = 16: 0.970 ms against 1.088 with 3; the smaller window fits more clusters). The other
+// ops (their slot stages are N - 1 whole pieces): 3 at N = 4, and for AlltoAll at N = 8 too; else 2.
+uint32_t kStreamDepth(int op, int n) {
+    if (op == DSMEM_OP_ALLREDUCE) return n == 8 ? 3u : 2u;
+    if (n <= 4 || (op == DSMEM_OP_ALLTOALL && n == 8)) return 3u;
+    return 2u;
+}
 
 // Units per problem for a pipelined driver: the smallest split into legal sub-vectors of at most
 // unit_bytes per CTA (default 16 KiB: three unit buffers in 48 KiB, four CTAs per SM) whose smallest window
@@ -375,7 +380,9 @@ uint32_t kStreamDepth(int n) { return n == 8 ? 3u : 2u; }
 // Caller holds st().mu.
 uint32_t pipeline_units(const KernelEntry* e, uint32_t m, uint64_t unit_bytes) {
     const uint64_t unit = unit_bytes != 0 ? unit_bytes : e->stage_pipe != nullptr ? st().stream_unit_bytes : st().unit_bytes;
-    const uint64_t bytes = (uint64_t)m * e->elem_bytes;
+    // the input of one unit: m elements of the rank block (N pieces of them for the streamed ReduceScatter and
+    // AlltoAll)
+    const uint64_t bytes = e->in_stage_pipe != nullptr ? e->in_stage_pipe(m) : (uint64_t)m * e->elem_bytes;
     const uint32_t s0 = (uint32_t)std::max<uint64_t>(1, (bytes + unit - 1) / unit);
     for (uint32_t s = s0; s <= m && s < s0 + 4096; ++s)
         if (m % s == 0 && e->legal(m / s) && e->smem_pipe(m / s) <= dsb::kSmemLimit) return s;
@@ -494,10 +501,10 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
                     // streamed: an input ring of `depth` stages and a slot ring of `lag` stages (units in the
                     // reduce-scatter), as many as asked for and fit; depth > lag >= 1
                     const uint32_t u = m / sub;
-                    const uint64_t in = (uint64_t)u * e->elem_bytes, slot = e->stage_pipe(u) - in;
+                    const uint64_t in = e->in_stage_pipe(u), slot = e->stage_pipe(u) - in;
                     const uint64_t lim = std::min<uint64_t>(dsb::kSmemLimit, d.optin);
                     uint32_t dr = small ? 3u : (uint32_t)std::max(1, g.stream_lag);
-                    uint32_t dx = g.stream_depth > 0 ? (uint32_t)g.stream_depth : (small ? 4u : kStreamDepth(e->n));
+                    uint32_t dx = g.stream_depth > 0 ? (uint32_t)g.stream_depth : (small ? 4u : kStreamDepth(e->op, e->n));
                     dx = std::max(dx, dr + 1);
                     auto window = [&] { return dsb::kD0 + dx * in + dr * slot; };
                     while (window() > lim && dx > dr + 1) --dx;

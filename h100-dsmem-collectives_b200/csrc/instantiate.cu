@@ -69,15 +69,23 @@ template <class A>
 uint64_t stage_fn(uint32_t m) {
     return A::stage_bytes(m);
 }
-// Attach the streamed batch driver P<N> (rs_global_ag_stream_kernel) to the entry of (alg, N).
+template <class A>
+uint64_t in_stage_fn(uint32_t m) {
+    return A::in_stage_bytes(m);
+}
+// Attach the streamed batch driver P<N> to the entry of (this op, alg, N): the AllReduce's is
+// rs_global_ag_stream_kernel, the other ops' collective_stream_kernel (the same body).
 template <template <int, typename, class> class P, int N>
 void add_streamed(Registry& r, int alg) {
     using PP = P<N, ElemT, Sum>;
+    const void* fn = PP::kOp == OpKind::AllReduce ? reinterpret_cast<const void*>(&rs_global_ag_stream_kernel<PP>)
+                                                   : reinterpret_cast<const void*>(&collective_stream_kernel<PP>);
     for (KernelEntry& e : r)
-        if (e.op == 0 && e.alg == alg && e.dtype == DSB_DT && e.n == N) {
-            e.fn_pipe = reinterpret_cast<const void*>(&rs_global_ag_stream_kernel<PP>);
+        if (e.op == DSB_OP && e.alg == alg && e.dtype == DSB_DT && e.n == N) {
+            e.fn_pipe = fn;
             e.smem_pipe = &smem_fn<PP>;
             e.stage_pipe = &stage_fn<PP>;
+            e.in_stage_pipe = &in_stage_fn<PP>;
             e.threads_pipe = PP::kThreads;
         }
 }
@@ -134,6 +142,7 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<AG_RingCredit>(r, kRingCredit);
     add_all_n<AG_RecursiveDoublingCredit>(r, kRecursiveDoublingCredit);
     add_all_n<AG_BruckCredit>(r, kBruckCredit);
+    add_streamed_all_n<AG_ReplicatedPushStream>(r, kDirectReplicatedPush);
 #elif DSB_OP == 2
     add_all_n<RS_Ring>(r, kRing);
     add_all_n<RS_RecursiveHalving>(r, kRecursiveHalving);
@@ -141,6 +150,7 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<RS_DirectPull>(r, kDirectPull);
     add_all_n<RS_RingCredit>(r, kRingCredit);
     add_all_n<RS_RecursiveHalvingCredit>(r, kRecursiveHalvingCredit);
+    add_streamed_all_n<RS_DirectPushStream>(r, kDirectPush);
 #elif DSB_OP == 4
     add_all_n<BC_DirectPush>(r, kDirectPush);
     add_all_n<BC_DirectPull>(r, kDirectPull);
@@ -152,6 +162,7 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<A2A_Shift>(r, kShift);
     add_all_n<A2A_Bruck>(r, kBruck);
     add_all_n<A2A_DirectPull>(r, kDirectPull);
+    add_streamed_all_n<A2A_DirectPushStream>(r, kDirectPush);
 #endif
 }
 

@@ -21,6 +21,7 @@ struct KernelEntry {
     // Streamed drivers (a ring of stages, warp-specialised): bytes of one stage for a unit of m elements
     // (nullptr: not streamed; the window is smem_pipe(m)) and the block size of fn_pipe.
     uint64_t (*stage_pipe)(uint32_t m) = nullptr;
+    uint64_t (*in_stage_pipe)(uint32_t m) = nullptr;   // the input part of a stage (the slot part is the rest)
     int threads_pipe = 256;
 };
 

@@ -33,8 +33,10 @@ OP_NAMES = {Op.ALLREDUCE: "allreduce", Op.ALLGATHER: "allgather", Op.REDUCESCATT
             Op.ALLTOALL: "alltoall", Op.BROADCAST: "broadcast"}
 DT_NAMES = {Dtype.F32: "f32", Dtype.BF16: "bf16", Dtype.I32: "i32"}
 ALG_NAMES = {a: (a.name.lower() if a != Alg.MESH_2D else "2d_mesh") for a in Alg}   # dsmem_alg_name()
-# algorithms with a pipelined driver: they also run payloads whose one-piece buffers exceed shared memory
-PIPELINED = (Alg.TWO_SHOT_PUSH, Alg.RS_PUSH_GLOBAL_AG)
+# (op, alg) with a pipelined or streamed driver: they also run payloads whose one-piece buffers exceed shared memory
+PIPELINED = {(Op.ALLREDUCE, Alg.TWO_SHOT_PUSH), (Op.ALLREDUCE, Alg.RS_PUSH_GLOBAL_AG),
+             (Op.REDUCESCATTER, Alg.DIRECT_PUSH), (Op.ALLTOALL, Alg.DIRECT_PUSH),
+             (Op.ALLGATHER, Alg.DIRECT_REPLICATED_PUSH)}
 
 
 def measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps, batch_bytes=256 << 20):
@@ -94,7 +96,7 @@ def run(dtypes=(Dtype.F32,), reps=60, batch_reps=5, sizes=CLUSTER_SIZES, payload
             for n in sizes:
                 for p in payloads:
                     qs = query(op, alg, dt, n, p)[0]
-                    if qs != Status.OK and not (qs == Status.SMEM_LIMIT and alg in PIPELINED):
+                    if qs != Status.OK and not (qs == Status.SMEM_LIMIT and (op, alg) in PIPELINED):
                         continue
                     try:
                         r = measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps, batch_bytes)

@@ -198,13 +198,15 @@ def test_shipped_autotune_table_parses(dsmem, tmp_path):
                "reducescatter": dsmem.Op.REDUCESCATTER, "alltoall": dsmem.Op.ALLTOALL,
                "broadcast": dsmem.Op.BROADCAST}
         dts = {"f32": dsmem.Dtype.F32, "bf16": dsmem.Dtype.BF16, "i32": dsmem.Dtype.I32}
-        pipelined = (dsmem.Alg.TWO_SHOT_PUSH, dsmem.Alg.RS_PUSH_GLOBAL_AG)
+        pipelined = {(dsmem.Op.ALLREDUCE, dsmem.Alg.TWO_SHOT_PUSH), (dsmem.Op.ALLREDUCE, dsmem.Alg.RS_PUSH_GLOBAL_AG),
+                     (dsmem.Op.REDUCESCATTER, dsmem.Alg.DIRECT_PUSH), (dsmem.Op.ALLTOALL, dsmem.Alg.DIRECT_PUSH),
+                     (dsmem.Op.ALLGATHER, dsmem.Alg.DIRECT_REPLICATED_PUSH)}
         by_name = {dsmem.lib().dsmem_alg_name(int(x)).decode(): x for x in dsmem.Alg}
         for op, n, p, dt, alg, regime in lines:
             a = by_name[alg]
             st = dsmem.query(ops[op], a, dts[dt], int(n), int(p))[0]
             # payloads above the one-piece limit run on the pipelined / streamed driver (one problem or many)
-            assert st == dsmem.Status.OK or (st == dsmem.Status.SMEM_LIMIT and a in pipelined)
+            assert st == dsmem.Status.OK or (st == dsmem.Status.SMEM_LIMIT and (ops[op], a) in pipelined)
             got = dsmem.autotune_pick(ops[op], dts[dt], int(n), int(p), num_clusters=64 if regime == "batch" else 1)
             assert got == a
     finally:

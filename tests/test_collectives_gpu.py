@@ -257,7 +257,9 @@ def test_config0_exact_inputs(cuda, orc, alg, clusters):
 # two (test_parity already runs 64 and 192 KiB at 1 and 3 clusters). Payloads above the one-piece
 # shared-memory limit run where a pipelined driver takes them (batch regime).
 GRID = [16 * 2 ** k for k in range(0, 14)] + [196608]   # 16 B ... 128 KiB, 192 KiB
-PIPELINED_ALGS = {(D.Op.ALLREDUCE, D.Alg.TWO_SHOT_PUSH), (D.Op.ALLREDUCE, D.Alg.RS_PUSH_GLOBAL_AG)}
+PIPELINED_ALGS = {(D.Op.ALLREDUCE, D.Alg.TWO_SHOT_PUSH), (D.Op.ALLREDUCE, D.Alg.RS_PUSH_GLOBAL_AG),
+                  (D.Op.REDUCESCATTER, D.Alg.DIRECT_PUSH), (D.Op.ALLTOALL, D.Alg.DIRECT_PUSH),
+                  (D.Op.ALLGATHER, D.Alg.DIRECT_REPLICATED_PUSH)}
 
 
 def grid_points(op, alg, n, dt):
@@ -293,62 +295,66 @@ def test_payload_grid(cuda, orc, op, alg, n):
 # (0, 0, 0): the measured defaults, which take 32 KiB units for launches of at most one wave (the 2-problem
 # batches below) and 16 KiB units otherwise
 STREAM_SETTINGS = ((0, 0, 0), (16384, 0, 1), (4096, 5, 3), (2048, 2, 1), (65536, 3, 2), (1024, 8, 1))
+STREAMED = ((D.Op.ALLREDUCE, D.Alg.RS_PUSH_GLOBAL_AG), (D.Op.REDUCESCATTER, D.Alg.DIRECT_PUSH),
+            (D.Op.ALLTOALL, D.Alg.DIRECT_PUSH), (D.Op.ALLGATHER, D.Alg.DIRECT_REPLICATED_PUSH))
 
 
+@pytest.mark.parametrize("op,alg", STREAMED, ids=[f"{o.name.lower()}-{a.name.lower()}" for o, a in STREAMED])
 @pytest.mark.parametrize("n", D.CLUSTER_SIZES)
-def test_streamed_rs_global_ag_matches_plain(cuda, orc, n):
-    """The streamed batch driver of rs_push_global_ag (warp-specialised ring, reduce-scatter over DSMEM, sums
-    stored straight into every output row) at several (unit, depth, lag) settings -- units per problem from 1 to
-    many, fewer units than stages, several problems per resident cluster -- is bit-equal to the plain driver,
-    which sums the N partials in the same rank order; the plain result is checked against the oracle."""
+def test_streamed_matches_plain(cuda, orc, op, alg, n):
+    """The streamed batch drivers (warp-specialised, an input ring and a slot ring, no cluster barrier per unit)
+    at several (unit, input stages, slot stages) settings -- units per problem from 1 to many, fewer units than
+    stages, several problems per resident cluster -- are bit-equal to the plain driver of the same algorithm
+    (AllReduce and ReduceScatter sum the N parts in the same rank order; AlltoAll and AllGather move bytes), and the
+    plain result (or, above the one-piece shared-memory limit, the streamed one) is checked against the oracle."""
     torch = cuda
     failures = []
     try:
         for dt in D.Dtype:
             for p in (256 * n // 8 if n >= 8 else 256, 4096, 65536, 196608):
-                if D.query(D.Op.ALLREDUCE, D.Alg.RS_PUSH_GLOBAL_AG, dt, n, p)[0] not in (D.Status.OK,
-                                                                                      D.Status.SMEM_LIMIT):
+                if op != D.Op.ALLREDUCE and p < 16 * n:
                     continue
-                m = D.msg_elems(D.Op.ALLREDUCE, n, p, dt)
+                if D.query(op, alg, dt, n, p)[0] not in (D.Status.OK, D.Status.SMEM_LIMIT):
+                    continue
+                m = D.msg_elems(op, n, p, dt)
+                nin, nout = n * D.in_elems_per_rank(op, n, m), n * D.out_elems_per_rank(op, n, m)
                 for clusters in (2, 301, 1200):
-                    if p * n * clusters > (256 << 20):
+                    if max(nin, nout) * clusters * D.ELEM_BYTES[dt] > (256 << 20):
                         continue
-                    host = make_input(orc, dt, clusters * n * m, "R", clusters + p)
+                    host = make_input(orc, dt, clusters * nin, "R", clusters + p)
                     tin = _np_to_torch(torch, host, dt).cuda()
-                    plain = torch.empty_like(tin)
-                    if D.query(D.Op.ALLREDUCE, D.Alg.RS_PUSH_GLOBAL_AG, dt, n, p)[0] == D.Status.OK:
+                    ref = orc.reference(int(op), ORC_DT[dt], n, m, clusters, host)
+                    exact = dt == D.Dtype.I32 or op in (D.Op.ALLGATHER, D.Op.ALLTOALL)
+                    tol = 0 if exact else RTOL[dt] * math.ceil(math.log2(n))
+
+                    def empty():
+                        z = torch.full((clusters * nout,), -1, dtype=torch.int32 if dt != D.Dtype.BF16 else torch.int16,
+                                       device="cuda")
+                        return z.view(tin.dtype)
+
+                    plain = None
+                    if D.query(op, alg, dt, n, p)[0] == D.Status.OK:
+                        plain = empty()
                         D.set_pipelined(False)
-                        D.collective(D.Op.ALLREDUCE, D.Alg.RS_PUSH_GLOBAL_AG, tin, plain, n, p)
+                        D.collective(op, alg, tin, plain, n, p)
                         D.check()
                         D.set_pipelined(True)
-                        ref = orc.reference(0, ORC_DT[dt], n, m, clusters, host)
-                        exact = dt == D.Dtype.I32
-                        tol = 0 if exact else RTOL[dt] * math.ceil(math.log2(n))
-                        bad, _, mr = orc.check(ORC_DT[dt], _torch_to_np(plain, dt), ref, 0 if exact else 1, tol)
-                        if bad:
-                            failures.append(f"plain {dt.name} P={p} clusters={clusters}: {bad} off the oracle")
-                    else:
-                        plain = None   # above the one-piece limit: only the streamed driver runs it
                     outs = []
                     for unit, depth, lag in STREAM_SETTINGS:
                         D.set_stream_pipeline(unit, depth, lag)
-                        out = torch.full_like(tin, float("nan")) if dt != D.Dtype.I32 else torch.full_like(tin, -1)
-                        D.collective(D.Op.ALLREDUCE, D.Alg.RS_PUSH_GLOBAL_AG, tin, out, n, p)
+                        out = empty()
+                        D.collective(op, alg, tin, out, n, p)
                         D.check()
                         outs.append(out)
-                    if plain is None:
-                        plain = outs[0]
-                        ref = orc.reference(0, ORC_DT[dt], n, m, clusters, host)
-                        exact = dt == D.Dtype.I32
-                        tol = 0 if exact else RTOL[dt] * math.ceil(math.log2(n))
-                        bad, _, _ = orc.check(ORC_DT[dt], _torch_to_np(plain, dt), ref, 0 if exact else 1, tol)
-                        if bad:
-                            failures.append(f"streamed {dt.name} P={p} clusters={clusters}: {bad} off the oracle")
+                    first = plain if plain is not None else outs[0]
+                    bad, _, mr = orc.check(ORC_DT[dt], _torch_to_np(first, dt), ref, 0 if exact else 1, tol)
+                    if bad:
+                        failures.append(f"{dt.name} P={p} clusters={clusters}: {bad} off the oracle (max rel {mr})")
+                    iv = torch.int16 if dt == D.Dtype.BF16 else torch.int32
                     for (unit, depth, lag), out in zip(STREAM_SETTINGS, outs):
-                        if not torch.equal(out.view(torch.int16 if dt == D.Dtype.BF16 else torch.int32),
-                                           plain.view(torch.int16 if dt == D.Dtype.BF16 else torch.int32)):
+                        if not torch.equal(out.view(iv), first.view(iv)):
                             failures.append(f"{dt.name} P={p} clusters={clusters} unit={unit} depth={depth} "
-                                            f"lag={lag}: differs from the plain driver")
+                                            f"lag={lag}: differs from the {'plain driver' if plain is not None else 'defaults'}")
     finally:
         D.set_pipelined(True)
         D.set_stream_pipeline()
