@@ -226,6 +226,10 @@ def lib():
         "dsmem_tp_set_wait_limit_ns": (c_int, [c_vp, c_ull]),
         "dsmem_tp_emulate": (c_int, [c_int, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), c_int, c_vp, c_vp,
                                      ctypes.c_float, c_ll, c_int, c_int, c_vp]),
+        "dsmem_tp_emulate_oneshot": (c_int, [c_int, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp), c_int, c_vp, c_vp,
+                                             ctypes.c_float, c_ll, c_int, c_int, c_vp]),
+        "dsmem_tp_emulate_check": (c_int, [ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_uint)]),
+        "dsmem_tp_set_oneshot_limit": (c_int, [c_vp, c_size]),
         "dsmem_decoder_workspace_bytes": (c_size, [c_int, c_int, c_int]),
         "dsmem_decoder_layer_launch": (c_int, [ctypes.POINTER(DecoderParams), c_vp]),
         "dsmem_decoder_check": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint)]),
@@ -621,9 +625,10 @@ def decoder_check(device=0):
         raise DsmemError(Status.BOUNDS, "decoder")
 
 
-def tp_emulate(xs, ys, w, eps=1e-6, cluster_size=8, residual=None, stream=None):
-    """The tensor-parallel AllReduce+RMSNorm kernel for len(xs) ranks emulated in one launch on one GPU:
-    every ys[k] = RMSNorm(sum(xs) (+ residual)) * w. bf16 CUDA tensors [rows, hidden]."""
+def tp_emulate(xs, ys, w, eps=1e-6, cluster_size=8, residual=None, stream=None, oneshot=False):
+    """The tensor-parallel AllReduce+RMSNorm kernel for len(xs) ranks emulated on one GPU: every
+    ys[k] = RMSNorm(sum(xs) (+ residual)) * w. bf16 CUDA tensors [rows, hidden]. oneshot=False: the two-shot
+    kernel in one launch; True: the one-shot kernel, every rank's push launched before every rank's reduction."""
     import torch
 
     tp = len(xs)
@@ -636,9 +641,17 @@ def tp_emulate(xs, ys, w, eps=1e-6, cluster_size=8, residual=None, stream=None):
     xa = (ctypes.c_void_p * tp)(*[x.data_ptr() for x in xs])
     ya = (ctypes.c_void_p * tp)(*[y.data_ptr() for y in ys])
     s = stream if stream is not None else torch.cuda.current_stream(xs[0].device).cuda_stream
-    _ok(lib().dsmem_tp_emulate(tp, xa, ya, int(Dtype.BF16), residual.data_ptr() if residual is not None else None,
-                               w.data_ptr(), float(eps), rows, hidden, int(cluster_size), ctypes.c_void_p(s or None)),
-        f"dsmem_tp_emulate(tp={tp}, {rows}x{hidden}, cluster {cluster_size})")
+    fn = lib().dsmem_tp_emulate_oneshot if oneshot else lib().dsmem_tp_emulate
+    _ok(fn(tp, xa, ya, int(Dtype.BF16), residual.data_ptr() if residual is not None else None,
+           w.data_ptr(), float(eps), rows, hidden, int(cluster_size), ctypes.c_void_p(s or None)),
+        f"{fn.__name__}(tp={tp}, {rows}x{hidden}, cluster {cluster_size})")
+
+
+def tp_emulate_check():
+    """Raise DsmemError(TIMEOUT/BOUNDS) if a device-side wait or check of tp_emulate fired (synchronous)."""
+    bits, detail = ctypes.c_uint(0), ctypes.c_uint(0)
+    st = lib().dsmem_tp_emulate_check(ctypes.byref(bits), ctypes.byref(detail))
+    _ok(st, f"dsmem_tp_emulate_check (detail {detail.value:#x})")
 
 
 def dsmem_bandwidth_point(mode, cluster_size, passes, reps=5, ctas_per_sm=1):

@@ -17,6 +17,8 @@ from . import DsmemError, Dtype, Status, _ok, lib
 
 HANDLE_BYTES = 64     # DSMEM_TP_HANDLE_BYTES
 NCCL_UID_BYTES = 128
+LL_SLOT_MAX = 4 << 20          # bytes of one LL sender slot at most (min(2 * capacity, 4 MiB))
+ONESHOT_DEFAULT = 4 << 20      # the context's default one-shot limit
 
 
 def exchange_bytes(local: bytes, group=None) -> list:
@@ -68,6 +70,7 @@ class TPContext:
         x, y, cap = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_size_t()
         _ok(lib().dsmem_tp_buffers(self._ctx, ctypes.byref(x), ctypes.byref(y), ctypes.byref(cap)), "dsmem_tp_buffers")
         self._x, self._y, self.capacity = x.value, y.value, cap.value
+        self._limit = ONESHOT_DEFAULT
 
     def buffers(self, tokens: int, hidden: int):
         """bf16 CUDA tensors [tokens, hidden] viewing the x and y regions (zero-copy input / output)."""
@@ -109,6 +112,21 @@ class TPContext:
     def set_wait_limit_ns(self, ns):
         """Limit of each cross-GPU flag wait of this context's calls (dsmem_tp_set_wait_limit_ns; default 2 s)."""
         _ok(lib().dsmem_tp_set_wait_limit_ns(self._ctx, int(ns)), "dsmem_tp_set_wait_limit_ns")
+
+    def set_oneshot_limit(self, nbytes):
+        """Use the one-shot form while the LL bytes this rank sends, (tp - 1) * rows * hidden * 4, stay within
+        `nbytes` (dsmem_tp_set_oneshot_limit; 0: always the two-shot; default 4 MiB)."""
+        _ok(lib().dsmem_tp_set_oneshot_limit(self._ctx, int(nbytes)), "dsmem_tp_set_oneshot_limit")
+        self._limit = int(nbytes)
+
+    def oneshot_fits(self, tokens, hidden):
+        """Whether a [tokens, hidden] tensor fits one LL slot of this context (the one-shot form's room)."""
+        return int(tokens) * int(hidden) * 4 <= min(2 * self.capacity, LL_SLOT_MAX)
+
+    def oneshot_picked(self, tokens, hidden):
+        """Whether a call of this shape runs the one-shot form under the current limit (the C ABI's rule)."""
+        ll = int(tokens) * int(hidden) * 4
+        return self.world > 1 and self.oneshot_fits(tokens, hidden) and (self.world - 1) * ll <= self._limit
 
     def status(self):
         """(status, error bits, detail) of the device error words, read and cleared (dsmem_tp_check); no raise."""

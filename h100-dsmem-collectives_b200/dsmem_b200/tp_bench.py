@@ -4,14 +4,21 @@
 
 (run from the package directory, or with it on PYTHONPATH). Per rank: bf16 x [T x 8192] ~ N(0,1) with
 seed + rank, residual and w ~ N(1, 0.02), eps 1e-6, cluster 8, T in {1, 64, 1024, 8192}. For each T:
-  fused      dsmem_tp_allreduce_rmsnorm with x already in the context's x region and y left in its y
-             region (the zero-copy use: a producer writes x there, a consumer reads y there);
-  fused_api  the same call from ordinary tensors (copies x in and y out on the stream);
-  nccl       the composition: ncclAllReduce (bf16 sum) then the cluster RMSNorm (dsmem_tp_allreduce_rmsnorm_nccl).
+  fused          dsmem_tp_allreduce_rmsnorm with x already in the context's x region and y left in its y
+                 region (the zero-copy use: a producer writes x there, a consumer reads y there), the form the
+                 context's default one-shot limit picks;
+  fused_api      the same call from ordinary tensors (the two-shot copies x in and y out on the stream; the
+                 one-shot reads and writes them in place);
+  fused_twoshot  `fused` with the two-shot form forced (limit 0);
+  fused_oneshot  `fused` with the one-shot form forced (where the tensor fits one LL slot);
+  nccl           the composition: ncclAllReduce (bf16 sum) then the cluster RMSNorm
+                 (dsmem_tp_allreduce_rmsnorm_nccl).
 Each figure is the median over rounds of the mean over `reps` calls captured in one CUDA graph (so the
-host's launch overhead is not timed), CUDA events on the replay stream, max over ranks. NVLink roofline: each rank must receive (TP-1)/TP of the tensor and send
-(TP-1)/TP of it, so the bound is (TP-1)/TP * T*H*2 bytes / 770 GB/s (measured peer-copy bandwidth per
-direction on this pool); frac = that time / measured time.
+host's launch overhead is not timed), CUDA events on the replay stream, max over ranks. NVLink roofline of a
+bandwidth-optimal AllReduce without in-switch reduction: each direction of a rank's links carries 2 (TP-1)/TP
+of the tensor (the (TP-1)/TP its peers read or receive in the reduce-scatter, and the (TP-1)/TP it sends in the
+all-gather), so the bound is 2 (TP-1)/TP * T*H*2 bytes / 770 GB/s (measured peer-copy bandwidth per direction on
+this pool); frac = that time / measured time (= busbw / 770).
 """
 from __future__ import annotations
 
@@ -47,13 +54,20 @@ def run(tokens=TOKENS, hidden=HIDDEN, cluster=8, reps=20, rounds=5, warmup=5):
             xb, yb = ctx.buffers(t, hidden)
             xb.copy_(x)
             sum_buf = torch.empty_like(x)
-            cases = {
-                "fused": lambda: _zero_copy(ctx, w, res, t, hidden, cluster),
-                "fused_api": lambda: ctx.allreduce_rmsnorm(x, w, 1e-6, residual=res, out=y, cluster_size=cluster),
-                "nccl": lambda: comm.allreduce_rmsnorm(x, w, sum_buf, y, 1e-6, residual=res, cluster_size=cluster),
+            zero_copy = lambda: _zero_copy(ctx, w, res, t, hidden, cluster)   # noqa: E731
+            cases = {   # name: (one-shot limit, call)
+                "fused": (T.ONESHOT_DEFAULT, zero_copy),
+                "fused_api": (T.ONESHOT_DEFAULT,
+                              lambda: ctx.allreduce_rmsnorm(x, w, 1e-6, residual=res, out=y, cluster_size=cluster)),
+                "fused_twoshot": (0, zero_copy),
+                "nccl": (T.ONESHOT_DEFAULT,
+                         lambda: comm.allreduce_rmsnorm(x, w, sum_buf, y, 1e-6, residual=res, cluster_size=cluster)),
             }
+            if world > 1 and ctx.oneshot_fits(t, hidden):
+                cases["fused_oneshot"] = (2 ** 62, zero_copy)
             row = {}
-            for name, fn in cases.items():
+            for name, (limit, fn) in cases.items():
+                ctx.set_oneshot_limit(limit)
                 stream = torch.cuda.Stream()
                 with torch.cuda.stream(stream):
                     for _ in range(warmup):
@@ -81,10 +95,13 @@ def run(tokens=TOKENS, hidden=HIDDEN, cluster=8, reps=20, rounds=5, warmup=5):
                 dist.all_reduce(us, op=dist.ReduceOp.MAX)
                 us = us.item()
                 size = t * hidden * 2
-                bound_us = (world - 1) / world * size / (NVLINK_GBS * 1e9) * 1e6
+                bound_us = 2 * (world - 1) / world * size / (NVLINK_GBS * 1e9) * 1e6
                 row[name] = {"us": round(us, 2), "algbw_GBps": round(size / (us * 1e-6) / 1e9, 1),
                              "busbw_GBps": round(size / (us * 1e-6) / 1e9 * 2 * (world - 1) / world, 1),
                              "nvlink_frac": round(bound_us / us, 4) if world > 1 else None}
+                if name == "fused":
+                    row[name]["form"] = "one-shot" if world > 1 and ctx.oneshot_picked(t, hidden) else "two-shot"
+            ctx.set_oneshot_limit(T.ONESHOT_DEFAULT)
             ctx.check()
             rmsnorm_check()
             out[str(t)] = row

@@ -368,16 +368,26 @@ dsmem_status dsmem_allreduce_two_shot_noalloc(dsmem_dtype dtype, int cluster_siz
  * statistics. Replaces the AllReduce + RMSNorm pipeline of
  * kernels/rmsnorm_lamport__fused_allreduce_rmsnorm__hpcops.cu:37-197 (which the reference declares but
  * never ran, roofline/.../hpcops_rmsnorm_lamport.yaml:35-50) with one fused kernel per rank over NVLink
- * peer memory: reduce-scatter by rows with peer loads, the cluster RMSNorm of the owned rows (DSMEM
- * partial-sum push), all-gather by peer stores. Set-up, per rank:
- *   dsmem_tp_alloc   allocate this rank's buffer (signals + x region + y region, capacity bytes each) and
- *                    return its CUDA IPC handle (DSMEM_TP_HANDLE_BYTES) to share with the other ranks;
+ * peer memory, in one of two forms:
+ *   two-shot  reduce-scatter by rows with peer loads, the cluster RMSNorm of the owned rows (DSMEM
+ *             partial-sum push), all-gather by peer stores; 2 (tp-1)/tp of the tensor crosses NVLink each way;
+ *   one-shot  (small tensors) every rank pushes its x into every peer's LL region (8-byte words of 4 data
+ *             bytes and the call's epoch, polled by the receiver: no flags, no round trip) and reduces and
+ *             normalises every row itself; (tp-1) * rows * hidden * 4 bytes leave each rank.
+ * Both sum the ranks in rank order in fp32 and give the same bits when the residual is the same tensor on
+ * every rank (a replicated residual stream, as in a TP decoder; the two-shot adds the residual of the row's
+ * owning rank, the one-shot each rank's own). Set-up, per rank:
+ *   dsmem_tp_alloc   allocate this rank's buffer (signals + x region + y region, capacity bytes each, and
+ *                    an LL region of 2 x 8 slots of min(2 capacity, 4 MiB)) and return its CUDA IPC handle
+ *                    (DSMEM_TP_HANDLE_BYTES) to share with the other ranks;
  *   dsmem_tp_open    map every rank's buffer (handles: tp handles in rank order);
  *   dsmem_tp_buffers the x and y regions: a producer may write x there and a consumer read y there, which
  *                    saves the copies that dsmem_tp_allreduce_rmsnorm makes for other pointers.
  * dsmem_tp_allreduce_rmsnorm: x (NULL: already in the x region) [rows x hidden]; residual (nullable) and
  * w local; y (NULL: leave in the y region). Every rank calls it with the same shape, in the same order;
- * cross-GPU waits are bounded (2 s) and report DSMEM_ERR_TIMEOUT through dsmem_tp_check.
+ * cross-GPU waits are bounded (2 s) and report DSMEM_ERR_TIMEOUT through dsmem_tp_check. The one-shot form
+ * runs when tp > 1, rows * hidden * 4 fits one LL slot and (tp - 1) * rows * hidden * 4 <= the context's
+ * one-shot limit (dsmem_tp_set_oneshot_limit); it reads x and writes y in place (no copies).
  * Shapes: hidden a multiple of 8 * cluster_size, at most 2 KiB of a row per CTA; rows*hidden*2 <= capacity
  * (else DSMEM_ERR_SCRATCH_LIMIT). tp in {1, 2, 4, 8}.
  */
@@ -390,19 +400,30 @@ dsmem_status dsmem_tp_allreduce_rmsnorm(dsmem_tp_t ctx, dsmem_dtype dtype, const
                                         const void* w, float eps, long long rows, int hidden, int cluster_size,
                                         void* y, dsmem_stream_t stream);
 /* Read and clear the context's device error words (synchronous): TIMEOUT / BOUNDS / OK; detail as in
- * dsmem_last_error_detail (barrier 0x70 + r: entry wait for rank r; 0x78 + r: exit wait). */
+ * dsmem_last_error_detail (barrier 0x70 + r: entry wait for rank r, or the one-shot's wait for rank r's
+ * data; 0x78 + r: exit wait). */
 dsmem_status dsmem_tp_check(dsmem_tp_t ctx, unsigned* error_bits, unsigned* detail);
 /* Limit of each cross-GPU flag wait of this context's calls (default 2 s; 1 ns .. 60 s). A call whose peer
  * never joins gives up after it (at entry, and again at exit), finishes without blocking, and dsmem_tp_check
  * reports DSMEM_ERR_TIMEOUT. After a timeout the ranks' call epochs disagree: close and reopen the context.
  * Replaces the reference's host watchdog (collectives/harness/main.cu:277-320) for the cross-GPU path. */
 dsmem_status dsmem_tp_set_wait_limit_ns(dsmem_tp_t ctx, unsigned long long ns);
+/* The one-shot form's limit on the LL bytes a rank sends per call, (tp - 1) * rows * hidden * 4 (default
+ * 4 MiB; 0: always the two-shot; SIZE_MAX: the one-shot whenever the tensor fits an LL slot). */
+dsmem_status dsmem_tp_set_oneshot_limit(dsmem_tp_t ctx, size_t bytes);
 dsmem_status dsmem_tp_close(dsmem_tp_t ctx);
 /* The same kernel for `tp` ranks emulated in one launch on one GPU (xs, ys: tp local buffers each; every
  * row computed once and written to all tp y buffers; no flags). For single-GPU parity tests. */
 dsmem_status dsmem_tp_emulate(int tp, const void* const* xs, void* const* ys, dsmem_dtype dtype, const void* residual,
                               const void* w, float eps, long long rows, int hidden, int cluster_size,
                               dsmem_stream_t stream);
+/* The one-shot kernel for `tp` ranks on one GPU: every rank's push launched first (into LL regions on this
+ * GPU), then every rank's reduction into its own ys[r]; no launch waits for another. */
+dsmem_status dsmem_tp_emulate_oneshot(int tp, const void* const* xs, void* const* ys, dsmem_dtype dtype,
+                                      const void* residual, const void* w, float eps, long long rows, int hidden,
+                                      int cluster_size, dsmem_stream_t stream);
+/* Read and clear the emulation entry points' device error words (synchronous), as dsmem_tp_check. */
+dsmem_status dsmem_tp_emulate_check(unsigned* error_bits, unsigned* detail);
 
 /*
  * The NCCL composition (the baseline of the fused kernel, and the configs[4] pipeline as the reference

@@ -60,6 +60,37 @@ def test_tp_emulated_matches_oracle(cuda, orc, tp):
     assert not failures, "\n".join(failures)
 
 
+@pytest.mark.parametrize("tp", (2, 4, 8))
+def test_tp_oneshot_emulated_matches_twoshot(cuda, orc, tp):
+    """The one-shot kernel (LL-word push, every rank reduces every row), emulated on one GPU with every rank's
+    push launched before every rank's reduction: each rank's y is the two-shot kernel's, bit for bit (same
+    rank-order fp32 sum, same residual), and within the oracle's tolerance; no device wait gave up."""
+    torch = cuda
+    failures = []
+    for n, rows, hidden, residual in ((8, 64, 8192, True), (8, 17, 8192, False), (16, 33, 8192, True),
+                                      (4, 5, 4096, True), (8, 1, 8192, False), (2, 40, 1024, False)):
+        xs, w, res = _inputs(orc, tp, rows, hidden, seed=3 * rows + tp, residual=residual)
+        txs = [_bf16(torch, x) for x in xs]
+        tw, tres = _bf16(torch, w), (_bf16(torch, res) if residual else None)
+        two = [torch.full((rows, hidden), float("nan"), dtype=torch.bfloat16, device="cuda") for _ in range(tp)]
+        one = [torch.full((rows, hidden), float("nan"), dtype=torch.bfloat16, device="cuda") for _ in range(tp)]
+        D.tp_emulate(txs, two, tw, 1e-6, cluster_size=n, residual=tres)
+        for _ in range(2):   # twice: the second call starts from the first call's LL words (zeroed per call)
+            D.tp_emulate(txs, one, tw, 1e-6, cluster_size=n, residual=tres, oneshot=True)
+        D.tp_emulate_check()
+        ref = orc.tp_rmsnorm(1, xs, w, 1e-6, res)
+        want = _np(two[0])
+        for k in range(tp):
+            got = _np(one[k])
+            if not np.array_equal(got, want):
+                failures.append(f"n={n} rows={rows}: rank {k}: {int((got != want).sum())} elements differ from the "
+                                "two-shot kernel")
+        bad, _, mr = orc.check(1, _np(one[0]).reshape(-1), ref.reshape(-1), 1, RTOL)
+        if bad:
+            failures.append(f"n={n} rows={rows} hidden={hidden} res={residual}: {bad} beyond tol (max rel {mr})")
+    assert not failures, "\n".join(failures)
+
+
 def test_tp_rejects_bad_shapes(cuda):
     torch = cuda
     x = torch.zeros(4, 1000, dtype=torch.bfloat16, device="cuda")
@@ -99,10 +130,28 @@ def _rank_main(rank, world, port, rows, hidden, n, out_dir):
         x = _bf16(torch, xs[rank])
         tw, tr = _bf16(torch, w), _bf16(torch, res)
         y = torch.empty_like(x)
-        for _ in range(3):   # repeated calls exercise the epoch flags and buffer reuse
+        # the two forms interleaved (limit 0: two-shot; 2**62: one-shot), so each call's epoch follows calls of
+        # both kinds and the one-shot's two LL buffers are reused across two-shot calls; every result kept
+        outs = []
+        for path in ("two", "one", "one", "two", "two", "one", "one", "one", "two"):
+            ctx.set_oneshot_limit(0 if path == "two" else 2 ** 62)
+            y.fill_(float("nan"))
             ctx.allreduce_rmsnorm(x, tw, 1e-6, residual=tr, out=y, cluster_size=n)
+            outs.append(_np(y))
+        for r_ in (1, 17):   # ragged row counts through both forms
+            for path in ("one", "two"):
+                ctx.set_oneshot_limit(0 if path == "two" else 2 ** 62)
+                yr = torch.full((r_, hidden), float("nan"), dtype=torch.bfloat16, device="cuda")
+                ctx.allreduce_rmsnorm(x[:r_].contiguous(), tw, 1e-6, residual=tr[:r_].contiguous(), out=yr,
+                                      cluster_size=n)
+                np.save(os.path.join(out_dir, f"y{rank}_r{r_}_{path}.npy"), _np(yr))
+        ctx.set_oneshot_limit(4 << 20)
+        y.fill_(float("nan"))
+        ctx.allreduce_rmsnorm(x, tw, 1e-6, residual=tr, out=y, cluster_size=n)   # the default choice
         torch.cuda.synchronize()
         ctx.check()
+        for k, o in enumerate(outs):
+            np.save(os.path.join(out_dir, f"y{rank}_call{k}.npy"), o)
         comm = T.NcclComm()
         ysum, y2 = torch.empty_like(x), torch.empty_like(x)
         comm.allreduce_rmsnorm(x, tw, ysum, y2, 1e-6, residual=tr, cluster_size=n)
@@ -134,6 +183,20 @@ def test_tp_multi_gpu(cuda, orc, tmp_path, world):
         assert np.array_equal(ys[r], ys[0]), f"rank {r}'s y differs from rank 0's"
     bad, _, mr = orc.check(1, ys[0].reshape(-1), ref.reshape(-1), 1, RTOL)
     assert bad == 0, f"fused: {bad} beyond tol (max rel {mr})"
+    # every call of both forms, on every rank: the same bits
+    for r in range(world):
+        for k in range(9):
+            got = np.load(tmp_path / f"y{r}_call{k}.npy")
+            assert np.array_equal(got, ys[0]), f"rank {r} call {k}: differs from the default call's y"
+    for r_ in (1, 17):
+        ref_r = orc.tp_rmsnorm(1, [x[:r_] for x in xs], w, 1e-6, res[:r_])
+        want = np.load(tmp_path / f"y0_r{r_}_two.npy")
+        bad, _, mr = orc.check(1, want.reshape(-1), ref_r.reshape(-1), 1, RTOL)
+        assert bad == 0, f"{r_} rows: {bad} beyond tol (max rel {mr})"
+        for r in range(world):
+            for path in ("one", "two"):
+                got = np.load(tmp_path / f"y{r}_r{r_}_{path}.npy")
+                assert np.array_equal(got, want), f"{r_} rows, rank {r}, {path}-shot: differs from rank 0's two-shot"
     # the NCCL composition (the baseline) reduces bf16 in bf16, rounding at each of its TP - 1 ring hops, where the
     # fused kernel sums in fp32 and rounds once: its bound scales with the hops (at TP = 4, 3 of 524,288 elements
     # came in at 1.047e-2 * (1 + |ref|))
@@ -144,7 +207,7 @@ def test_tp_multi_gpu(cuda, orc, tmp_path, world):
 
 
 # ----------------------------------------------------------------------------- failure detection
-def _absent_rank_main(rank, world, port, absent, out_dir):
+def _absent_rank_main(rank, world, port, absent, out_dir, path="two"):
     """Every rank maps the TP buffers; rank `absent` never enters the fused call (it leaves the test between
     steps, with nothing in flight) and waits on the host until the others have read their status."""
     import datetime
@@ -164,6 +227,7 @@ def _absent_rank_main(rank, world, port, absent, out_dir):
         rows, hidden = 64, 8192
         ctx = T.TPContext(T.tp_bytes(rows, hidden))
         ctx.set_wait_limit_ns(200_000_000)   # 0.2 s per cross-GPU flag wait
+        ctx.set_oneshot_limit(0 if path == "two" else 2 ** 62)
         gen = torch.Generator(device="cuda")
         gen.manual_seed(rank)
         x = torch.randn(rows, hidden, device="cuda", generator=gen).to(torch.bfloat16)
@@ -188,12 +252,14 @@ def _absent_rank_main(rank, world, port, absent, out_dir):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("path", ("two", "one"))
 @pytest.mark.parametrize("world", (2, 4))
-def test_tp_absent_rank_times_out(cuda, tmp_path, world):
+def test_tp_absent_rank_times_out(cuda, tmp_path, world, path):
     """One rank of `world` never joins the fused AllReduce + RMSNorm call. Every other rank's kernel gives up its
-    cross-GPU flag waits after the context's limit (0.2 s), finishes, and dsmem_tp_check reports TIMEOUT with the
-    detail of the entry wait for the absent rank (barrier 0x70 + rank); the GPU stays usable. No GPU fault, trap or
-    endless wait: the failure is a process that does not call, and the waits are bounded."""
+    cross-GPU waits after the context's limit (0.2 s), finishes, and dsmem_tp_check reports TIMEOUT with the
+    detail of the wait for the absent rank (barrier 0x70 + rank: the two-shot's entry flag, or the one-shot's
+    poll for that rank's LL words); the GPU stays usable. No GPU fault, trap or endless wait: the failure is a
+    process that does not call, and the waits are bounded."""
     import json
 
     torch = cuda
@@ -202,7 +268,7 @@ def test_tp_absent_rank_times_out(cuda, tmp_path, world):
     import torch.multiprocessing as mp
 
     absent = world - 1
-    mp.start_processes(_absent_rank_main, args=(world, _free_port(), absent, str(tmp_path)), nprocs=world,
+    mp.start_processes(_absent_rank_main, args=(world, _free_port(), absent, str(tmp_path), path), nprocs=world,
                        start_method="spawn", join=True)
     for r in range(world):
         if r == absent:
