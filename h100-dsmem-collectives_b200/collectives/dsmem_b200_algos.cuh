@@ -771,6 +771,63 @@ struct AR_Rabenseifner {
     }
 };
 
+// Rabenseifner (allreduce__rabenseifner__mpich.cu:25-67 schedule) with a buffer and an mbarrier per round: the
+// reduce-scatter half sent in round k lands in the partner's scratch range k (M/2, M/4, .. elements) on barrier
+// k; all-gather round k pushes the live range straight into the partner's vector on barrier log2 N + k. That
+// range is exactly what the partner sent this CTA in the reduce-scatter round of the same distance, which this
+// CTA had received (and waited for) before: no copy still reads it. Same halves and operand order as the
+// original.
+template <int N_, typename T_, class Op_>
+struct AR_RabenseifnerCredit {
+    DSB_TRAITS(AllReduce, 2 * ilog2(N_))
+    __host__ __device__ static constexpr bool legal(uint32_t M) {
+        return is_pow2(N_) && N_ >= 2 && M % N_ == 0 && mult16((M / N_) * B);
+    }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) {
+        return kD0 + 1ull * M * B + (1ull * M - M / N_) * B;
+    }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        constexpr int L = ilog2(N_);
+        if (threadIdx.x == 0)
+            for (int k = 0; k < L; ++k) {
+                arm(c, k, (M >> (k + 1)) * B);
+                arm(c, L + k, ((M / N_) << k) * B);
+            }
+        uint32_t lo = 0, hi = M, scr = kD0 + M * B;
+        int k = 0;
+        for (int d = N_ / 2; d >= 1; d >>= 1, ++k) {
+            const uint32_t partner = c.rank ^ (uint32_t)d, mid = (lo + hi) / 2, len = hi - mid;
+            const bool upper = (c.rank & (uint32_t)d) != 0u;
+            const uint32_t send_lo = upper ? lo : mid, keep_lo = upper ? mid : lo;
+            if (threadIdx.x == 0) push<N_>(c, partner, scr, kD0 + send_lo * B, len * B, k);
+            wait(c, k);
+            reduce2<T, Op>(c, kD0 + keep_lo * B, kD0 + keep_lo * B, scr, len * B);
+            fence_proxy_async_smem();
+            __syncthreads();   // the kept half is reduced before thread 0 sends part of it on
+            lo = keep_lo;
+            hi = keep_lo + len;
+            scr += len * B;
+            c.st.round(k);
+        }
+        for (int d = 1, j = 0; d < N_; d <<= 1, ++j) {
+            const uint32_t partner = c.rank ^ (uint32_t)d, len = hi - lo;
+            if (threadIdx.x == 0) push<N_>(c, partner, kD0 + lo * B, kD0 + lo * B, len * B, L + j);
+            wait(c, L + j);
+            if (c.rank & (uint32_t)d) lo -= len;
+            else hi += len;
+            c.st.round(L + j);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
 // allreduce__one_shot_pull__trtllm.cu:22-44. Every CTA loads all N vectors (16-B ld.shared::cluster,
 // all N loads of a packet in flight together) and reduces in rank order, so every CTA ends with the
 // same bits.
@@ -940,6 +997,61 @@ struct AR_ReduceBcastBinomial {
             }
             cluster_sync();
             c.st.round(round);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// Binomial reduce + broadcast (allreduce__reduce_bcast_binomial__mpich.cu:23-61 schedule) with a buffer and an
+// mbarrier per round: in reduce round k (d = 2^k) a rank with b mod 2d == d pushes its partial into scratch k of
+// b - d (barrier k), which adds it; broadcast round d (d = N/2 .. 1) pushes the result from b (b mod 2d == 0)
+// into b + d's vector (barrier log2 N + log2 d). A rank waits only for the copies it receives. The broadcast
+// overwrites a vector that its owner pushed during the reduction only after the root has received everything,
+// so that push had completed. Same pairs and operand order as the original.
+template <int N_, typename T_, class Op_>
+struct AR_ReduceBcastBinomialCredit {
+    DSB_TRAITS(AllReduce, 2 * ilog2(N_))
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && N_ >= 2 && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) {
+        return kD0 + (1ull + ilog2(N_)) * M * B;
+    }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        constexpr int L = ilog2(N_);
+        const uint32_t MB = M * B;
+        if (threadIdx.x == 0)
+            for (int k = 0; k < L; ++k) {
+                const uint32_t d = 1u << k;
+                if (c.rank % (2u * d) == 0u) arm(c, k, MB);       // receives a partial in reduce round k
+                if (c.rank % (2u * d) == d) arm(c, L + k, MB);    // receives the result at broadcast distance d
+            }
+        for (int k = 0; k < L; ++k) {
+            const uint32_t d = 1u << k, m = c.rank % (2u * d), scr = kD0 + (uint32_t)(k + 1) * MB;
+            if (m == d) {
+                if (threadIdx.x == 0) push<N_>(c, c.rank - d, scr, kD0, MB, k);
+                c.st.round(k);
+                break;   // this rank's partial is handed on: it drops out of the reduction
+            }
+            wait(c, k);
+            reduce2<T, Op>(c, kD0, kD0, scr, MB);
+            fence_proxy_async_smem();
+            __syncthreads();   // the partial is whole before thread 0 pushes it on
+            c.st.round(k);
+        }
+        for (int k = L - 1; k >= 0; --k) {
+            const uint32_t d = 1u << k, m = c.rank % (2u * d);
+            if (m == 0u) {
+                if (threadIdx.x == 0) push<N_>(c, c.rank + d, kD0, kD0, MB, L + k);
+            } else if (m == d) {
+                wait(c, L + k);
+            }
+            c.st.round(2 * L - 1 - k);
         }
     }
     static __device__ void store(Ctx& c, T* g, uint32_t M) {
@@ -1407,6 +1519,56 @@ struct AG_GatherBcastBinomial {
     }
 };
 
+// Binomial gather + broadcast (allgather__gather_bcast_binomial__mpich.cu:24-57 schedule) with an mbarrier per
+// round: in gather round k (d = 2^k) a rank with b mod 2d == d pushes its d accumulated slots into slots
+// [d, 2d) of b - d (barrier k); broadcast round d pushes all N slots from b (b mod 2d == 0) to b + d (barrier
+// log2 N + log2 d). Each slot range is written once per problem before the broadcast, and the broadcast
+// overwrites a rank's slots only after the root has gathered everything (so that rank's gather push had
+// completed).
+template <int N_, typename T_, class Op_>
+struct AG_GatherBcastBinomialCredit {
+    DSB_TRAITS(AllGather, 2 * ilog2(N_))
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && N_ >= 2 && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        constexpr int L = ilog2(N_);
+        const uint32_t MB = M * B;
+        if (threadIdx.x == 0)
+            for (int k = 0; k < L; ++k) {
+                const uint32_t d = 1u << k;
+                if (c.rank % (2u * d) == 0u) arm(c, k, d * MB);
+                if (c.rank % (2u * d) == d) arm(c, L + k, N_ * MB);
+            }
+        for (int k = 0; k < L; ++k) {
+            const uint32_t d = 1u << k, m = c.rank % (2u * d);
+            if (m == d) {
+                if (threadIdx.x == 0) push<N_>(c, c.rank - d, kD0 + d * MB, kD0, d * MB, k);
+                c.st.round(k);
+                break;
+            }
+            wait(c, k);
+            c.st.round(k);
+        }
+        for (int k = L - 1; k >= 0; --k) {
+            const uint32_t d = 1u << k, m = c.rank % (2u * d);
+            if (m == 0u) {
+                if (threadIdx.x == 0) push<N_>(c, c.rank + d, kD0, kD0, N_ * MB, L + k);
+            } else if (m == d) {
+                wait(c, L + k);
+            }
+            c.st.round(2 * L - 1 - k);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, N_ * M * B);
+    }
+};
+
 // =====================================================================================================
 //                                            REDUCESCATTER
 // Per rank: in[N*M] (chunk j for rank j) -> out[M] = op over ranks of chunk b.
@@ -1722,6 +1884,37 @@ struct A2A_PairwiseXor {
     }
 };
 
+// Pairwise XOR (alltoall__pairwise_xor__mpich.cu:19-38 schedule) with an mbarrier per round: round i pushes the
+// chunk for partner b ^ i into its receive slot [b] on barrier i - 1 and waits for the partner's chunk on its
+// own barrier i - 1. Every receive slot is written once per problem, so no cluster barrier is needed between
+// rounds (N - 1 barriers: N <= 16).
+template <int N_, typename T_, class Op_>
+struct A2A_PairwiseXorCredit {
+    DSB_TRAITS(AllToAll, N_ - 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && N_ >= 2 && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 2ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, N_ * M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, recv = kD0 + N_ * MB;
+        if (threadIdx.x == 0)
+            for (int i = 1; i < N_; ++i) arm(c, i - 1, MB);
+        s2s(c, recv + c.rank * MB, kD0 + c.rank * MB, MB);
+        for (int i = 1; i < N_; ++i) {
+            const uint32_t p = c.rank ^ (uint32_t)i;
+            if (threadIdx.x == 0) push<N_>(c, p, recv + c.rank * MB, kD0 + p * MB, MB, i - 1);
+            wait(c, i - 1);
+            c.st.round(i - 1);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + N_ * M * B, N_ * M * B);
+    }
+};
+
 // alltoall__shift__generic.cu:19-37. Round i: push chunk (b+i) to CTA b+i, receive from b-i.
 template <int N_, typename T_, class Op_>
 struct A2A_Shift {
@@ -1808,6 +2001,69 @@ struct A2A_Bruck {
         for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
             const uint32_t pos = i / nb, e = i - pos * nb;
             __stcs(o + ((c.rank + N_ - pos) % N_) * nb + e, D[i]);
+        }
+    }
+};
+
+// Bruck AlltoAll (alltoall__bruck__mpich.cu:24-56 schedule, rotations :75-94) with a staging range and an
+// mbarrier per round: round k (d = 2^k) sends the N/2 blocks whose position has bit k set to (b + d) mod N's
+// staging range k (barrier k). Instead of copying staging back, a block's current place is tracked: after
+// round k a position with bit k set lives in staging range k (at its index among those positions), otherwise
+// where it was; so every range is written once per problem and no cluster barrier is needed. Stored with the
+// inverse rotation from each position's final place.
+template <int N_, typename T_, class Op_>
+struct A2A_BruckCredit {
+    DSB_TRAITS(AllToAll, ilog2(N_))
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && N_ >= 2 && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) {
+        return kD0 + 1ull * N_ * M * B + ilog2(N_) * (N_ / 2ull) * M * B;
+    }
+    // Window offset of the block at position `pos` once rounds 0..k-1 are done: staging range j of the highest
+    // round j < k whose bit is set in pos (at pos's index among the positions with bit j set), else D[pos].
+    static __device__ __forceinline__ uint32_t place(uint32_t pos, int k, uint32_t MB) {
+        const uint32_t low = pos & ((1u << k) - 1u);
+        if (low == 0u) return kD0 + pos * MB;
+        const uint32_t j = 31u - __clz(low), d = 1u << j;
+        const uint32_t idx = (pos / (2u * d)) * d + (pos % d);
+        return kD0 + N_ * MB + (j * (N_ / 2u) + idx) * MB;
+    }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        const uint32_t nb = (M * B) >> 4, n = N_ * nb;
+        const uint4* src = reinterpret_cast<const uint4*>(g);
+        uint4* D = c.ptr<uint4>(kD0);
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint32_t j = i / nb, e = i - j * nb;
+            D[((j + N_ - c.rank) % N_) * nb + e] = __ldcs(src + i);
+        }
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        constexpr int L = ilog2(N_);
+        const uint32_t MB = M * B;
+        if (threadIdx.x == 0)
+            for (int k = 0; k < L; ++k) arm(c, k, (N_ / 2) * MB);
+        for (int k = 0; k < L; ++k) {
+            const uint32_t d = 1u << k, to = (c.rank + d) % N_, stage = kD0 + N_ * MB + (uint32_t)k * (N_ / 2) * MB;
+            if (threadIdx.x == 0) {
+                uint32_t s = 0;
+                for (uint32_t pos = 0; pos < (uint32_t)N_; ++pos)
+                    if (pos & d) {
+                        push<N_>(c, to, stage + s * MB, place(pos, k, MB), MB, k);
+                        ++s;
+                    }
+            }
+            wait(c, k);
+            c.st.round(k);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        const uint32_t MB = M * B, nb = MB >> 4, n = N_ * nb;
+        uint4* o = reinterpret_cast<uint4*>(g);
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint32_t pos = i / nb, e = i - pos * nb;
+            const uint4* src = c.ptr<const uint4>(place(pos, ilog2(N_), MB));
+            __stcs(o + ((c.rank + N_ - pos) % N_) * nb + e, src[e]);
         }
     }
 };

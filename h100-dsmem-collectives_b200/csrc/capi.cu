@@ -53,7 +53,10 @@ const char* const kAlgNames[DSMEM_ALG_COUNT] = {"auto",
                                                 "recursive_doubling_credit",
                                                 "binomial",
                                                 "bruck_credit",
-                                                "recursive_halving_credit"};
+                                                "recursive_halving_credit",
+                                                "rabenseifner_credit",
+                                                "pairwise_xor_credit",
+                                                "binomial_credit"};
 const char* const kDtypeNames[] = {"f32", "bf16", "i32"};
 
 // (op, alg) -> reference file stem collectives/<op>__<alg>__<src>.cu

@@ -82,9 +82,12 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 // The epoch of a call: one past the last completed call's, never 0, so that no signal or LL word still at
-// its initial zero matches a call (after 2^32 - 1 calls the epochs repeat).
+// its initial zero matches a call (after 2^32 - 1 calls the epochs repeat). The word was stored by an
+// earlier kernel of this rank's stream, so a relaxed load at GPU scope sees it.
 __device__ __forceinline__ unsigned next_epoch(const unsigned* last) {
-    const unsigned e = ld_acquire_sys(last) + 1u;
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(last) : "memory");
+    const unsigned e = v + 1u;
     return e != 0u ? e : 1u;
 }
 
@@ -375,70 +378,62 @@ __device__ __forceinline__ bool ll_ready(unsigned long long w0, unsigned long lo
     return (unsigned)(w0 >> 32) == epoch && (unsigned)(w1 >> 32) == epoch && (unsigned)(w2 >> 32) == epoch &&
            (unsigned)(w3 >> 32) == epoch;
 }
-// Reads the 16-byte unit at `src` (4 LL words) until every word carries `epoch`, or until the group's deadline
-// (then records rank `p`'s data as the wait that gave up; after that no wait blocks).
-__device__ __forceinline__ uint4 ll_poll(dsb::Ctx& c, const unsigned char* src, unsigned epoch, int p) {
-    unsigned long long w0 = 0, w1 = 0, w2 = 0, w3 = 0;
-    while (!c.dead) {
-        ld_ll(src, w0, w1);
-        ld_ll(src + 16, w2, w3);
-        if (ll_ready(w0, w1, w2, w3, epoch)) break;
-        if (globaltimer() > c.deadline) {
-            c.dead = true;
-            dsb::report_timeout(c, 0x70 + p);   // rank p's data did not arrive
-            break;
-        }
-    }
-    return make_uint4((unsigned)w0, (unsigned)w1, (unsigned)w2, (unsigned)w3);
-}
-
+// One CTA per SM at every width (the one-shot serves small tensors; the registers go to the unit batch).
 template <int N, int TP, int UPL>
-__global__ void __launch_bounds__(kThreadsTp, (UPL >= 4 ? 1 : 2)) tp_oneshot_kernel(const OsArgs a) {
+__global__ void __launch_bounds__(kThreadsTp, 1) tp_oneshot_kernel(const OsArgs a) {
     dsb::Ctx c;
     dsb::ctx_init(c, a.smem_bytes, a.err, a.wait_limit_ns);
-    dsb::flag_init(c);
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t units = a.slice_bytes >> 4;
     const long long row_u4 = a.hidden / 8;
     const long long col_u4 = (long long)c.rank * units;
-    __shared__ unsigned s_epoch;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSets; ++s) mbar_init(c.bar(s), 1);
         fence_mbar_init();
-        // one past the last completed call's epoch (the last CTA of each call stores it), as in the two-shot
-        s_epoch = a.sig != nullptr ? next_epoch(a.sig + kSigEpoch) : a.epoch;
     }
-    __syncthreads();
-    const unsigned epoch = s_epoch;
-    const size_t buf = epoch & 1u;
+    // the cluster barrier that orders the slot barriers' initialisation before any remote st.async: arrived
+    // here, waited for just before this CTA's first push of partials (it overlaps the push and the poll)
+    if (a.phases & 2) cluster_arrive_relaxed();
 
-    // ---- push: this rank's x into slot [rank] of buffer `buf` of every peer, flat over the whole grid
+    // ---- push: this rank's x into slot [rank] of buffer `buf` of every peer, flat over the whole grid, 8 bytes
+    // of x (two LL words, one 16-byte store) per thread and step, so that a warp's store instruction covers 512
+    // contiguous bytes of the peer's slot (LL bytes [16 h, 16 h + 16) carry x bytes [8 h, 8 h + 8)). The first x
+    // load is issued before the epoch load, so the two latencies overlap; every thread reads the epoch itself
+    // (one past the last completed call's: the last CTA of each call stores it; stream-ordered).
+    const long long total = a.rows * row_u4 * 2;   // 8-byte halves of 16-byte units
+    const long long stride = (long long)gridDim.x * kThreadsTp;
+    const long long g0 = (long long)blockIdx.x * kThreadsTp + threadIdx.x;
+    const uint2* xh = reinterpret_cast<const uint2*>(a.x);
+    uint2 v0 = make_uint2(0u, 0u);   // the thread's first half (the grid gives most threads at most a few)
+    if ((a.phases & 1) && g0 < total) v0 = __ldg(xh + g0);
+    const unsigned epoch = a.sig != nullptr ? next_epoch(a.sig + kSigEpoch) : a.epoch;
+    const size_t buf = epoch & 1u;
     if (a.phases & 1) {
-        const long long total = a.rows * row_u4;
-        const long long stride = (long long)gridDim.x * kThreadsTp;
         const unsigned long long f = (unsigned long long)epoch << 32;
         const size_t soff = (buf * kMaxTp + (size_t)a.rank) * a.ll_slot;
-        for (long long g0 = (long long)blockIdx.x * kThreadsTp + threadIdx.x; g0 < total; g0 += kPushUnroll * stride) {
-            uint4 v[kPushUnroll];
-#pragma unroll
-            for (int j = 0; j < kPushUnroll; ++j)
-                if (g0 + j * stride < total) v[j] = __ldg(a.x + g0 + j * stride);
+        for (long long gb = g0; gb < total; gb += kPushUnroll * stride) {
+            uint2 v[kPushUnroll];
 #pragma unroll
             for (int j = 0; j < kPushUnroll; ++j) {
-                const long long gi = g0 + j * stride;
+                if (gb == g0 && j == 0) {
+                    v[j] = v0;
+                } else if (gb + j * stride < total) {
+                    v[j] = __ldg(xh + gb + j * stride);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kPushUnroll; ++j) {
+                const long long gi = gb + j * stride;
                 if (gi >= total) break;
 #pragma unroll
                 for (int p = 0; p < TP; ++p) {
                     if (p == a.rank) continue;
-                    unsigned char* d = a.ll[p] + soff + (size_t)gi * 32u;
-                    st_ll(d, f | v[j].x, f | v[j].y);
-                    st_ll(d + 16, f | v[j].z, f | v[j].w);
+                    st_ll(a.ll[p] + soff + (size_t)gi * 16u, f | v[j].x, f | v[j].y);
                 }
             }
         }
     }
-    if (!(a.phases & 2)) return;   // emulation's push launch: no cluster barrier was passed
-    cluster_sync();   // every CTA's slot barriers initialised before any remote store completes on them
+    if (!(a.phases & 2)) return;   // emulation's push launch: no cluster barrier, no exchange
 
     // ---- every row, split evenly over the clusters
     const long long nclu = (long long)num_clusters(), cq = (long long)cluster_id();
@@ -454,63 +449,93 @@ __global__ void __launch_bounds__(kThreadsTp, (UPL >= 4 ? 1 : 2)) tp_oneshot_ker
         c.deadline = globaltimer() + c.wait_limit;
         const long long row0 = lo + i * kR + (long long)warp * kRowsPerWarp;
         const GroupIdx<UPL> g(row0, hi, row_u4, col_u4, units, lane);
-        constexpr int PB = 1;   // one rank's units at a time: the polled words are this GPU's memory
         f2x acc[kRowsPerWarp][UPL][4];
+        // one rank's units at a time (the polled words are this GPU's memory): every load is issued before
+        // any is checked, and a unit whose words are not yet all this call's is read again until they are, or
+        // until the group's deadline
 #pragma unroll
-        for (int p0 = 0; p0 < TP; p0 += PB) {
-            // every load of the batch is issued before any is checked; a unit whose words are not yet all this
-            // call's is read again until they are, or until the group's deadline
-            uint4 v[PB][kRowsPerWarp][UPL];
-            bool ready[PB][kRowsPerWarp][UPL];
+        for (int p = 0; p < TP; ++p) {
+            uint4 v[kRowsPerWarp][UPL];
+            bool ready[kRowsPerWarp][UPL];
 #pragma unroll
-            for (int pp = 0; pp < PB; ++pp)
+            for (int k = 0; k < kRowsPerWarp; ++k)
+#pragma unroll
+                for (int q = 0; q < UPL; ++q) {
+                    ready[k][q] = true;
+                    if (!g.ok[k][q]) {
+                        v[k][q] = make_uint4(0u, 0u, 0u, 0u);
+                    } else if (p == a.rank) {
+                        v[k][q] = __ldg(a.x + g.idx[k][q]);
+                    } else {
+                        const unsigned char* src = mine + (size_t)p * a.ll_slot + (size_t)g.idx[k][q] * 32u;
+                        unsigned long long w0, w1, w2, w3;
+                        ld_ll(src, w0, w1);
+                        ld_ll(src + 16, w2, w3);
+                        v[k][q] = make_uint4((unsigned)w0, (unsigned)w1, (unsigned)w2, (unsigned)w3);
+                        ready[k][q] = ll_ready(w0, w1, w2, w3, epoch);
+                    }
+                }
+            // the units not yet ready are read again together, one round trip per pass for all of them
+            bool all = true;
+#pragma unroll
+            for (int k = 0; k < kRowsPerWarp; ++k)
+#pragma unroll
+                for (int q = 0; q < UPL; ++q) all = all && ready[k][q];
+            while (!all && !c.dead) {
+                if (globaltimer() > c.deadline) {
+                    c.dead = true;
+                    dsb::report_timeout(c, 0x70 + p);   // rank p's data did not arrive
+                    break;
+                }
+                all = true;
 #pragma unroll
                 for (int k = 0; k < kRowsPerWarp; ++k)
 #pragma unroll
-                    for (int q = 0; q < UPL; ++q) {
-                        const int p = p0 + pp;
-                        ready[pp][k][q] = true;
-                        if (!g.ok[k][q]) {
-                            v[pp][k][q] = make_uint4(0u, 0u, 0u, 0u);
-                        } else if (p == a.rank) {
-                            v[pp][k][q] = __ldg(a.x + g.idx[k][q]);
-                        } else {
+                    for (int q = 0; q < UPL; ++q)
+                        if (!ready[k][q]) {
                             const unsigned char* src = mine + (size_t)p * a.ll_slot + (size_t)g.idx[k][q] * 32u;
                             unsigned long long w0, w1, w2, w3;
                             ld_ll(src, w0, w1);
                             ld_ll(src + 16, w2, w3);
-                            v[pp][k][q] = make_uint4((unsigned)w0, (unsigned)w1, (unsigned)w2, (unsigned)w3);
-                            ready[pp][k][q] = ll_ready(w0, w1, w2, w3, epoch);
+                            v[k][q] = make_uint4((unsigned)w0, (unsigned)w1, (unsigned)w2, (unsigned)w3);
+                            ready[k][q] = ll_ready(w0, w1, w2, w3, epoch);
+                            all = all && ready[k][q];
                         }
-                    }
+            }
 #pragma unroll
-            for (int pp = 0; pp < PB; ++pp)
+            for (int k = 0; k < kRowsPerWarp; ++k)
 #pragma unroll
-                for (int k = 0; k < kRowsPerWarp; ++k)
-#pragma unroll
-                    for (int q = 0; q < UPL; ++q) {
-                        const int p = p0 + pp;
-                        if (!ready[pp][k][q])
-                            v[pp][k][q] = ll_poll(c, mine + (size_t)p * a.ll_slot + (size_t)g.idx[k][q] * 32u, epoch, p);
-                        accumulate(acc[k][q], v[pp][k][q], p);
-                    }
+                for (int q = 0; q < UPL; ++q) accumulate(acc[k][q], v[k][q], p);
         }
+        if (i == 0) cluster_wait();
+        // The exchange may wait one more limit: a warp with no units in this group passes the poll at once and
+        // waits here for partials that warps still polling send only after their poll ends (data, or its
+        // deadline), so only a missing rank's poll reports the timeout.
+        c.deadline += c.wait_limit;
         normalise_group<N, UPL, kWReg>(c, acc, g, row0, hi, (int)(i & (kSets - 1)), a.res, a.w, wr, col_u4, units,
                                        a.eps, inv_hidden, [&](long long u, uint4 yv) { a.y[u] = yv; });
     }
+    if (iters == 0) cluster_wait();   // every arrive is matched (the same iters on every CTA of a cluster)
     // ---- exit: the last CTA stores the call's epoch for the next call (stream-ordered after this kernel)
     if (a.sig != nullptr) {
         __syncthreads();
         if (threadIdx.x == 0) {
-            __threadfence();
-            const unsigned prev = atomicAdd(a.sig + kSigCounter, 1u);
+            unsigned prev;
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(a.sig + kSigCounter) : "memory");
             if (prev == gridDim.x - 1) {
                 a.sig[kSigCounter] = 0u;
                 a.sig[kSigEpoch] = epoch;
             }
         }
     }
-    dsb::finish(c);
+    // No cluster barrier at the end: every remote write to this CTA (the partials of each group) completed on
+    // a slot barrier this CTA waited for. A CTA whose wait gave up lingers instead, so partials still in flight
+    // to it land before it exits.
+    if (__syncthreads_or(c.dead ? 1 : 0)) {
+        const unsigned long long until = globaltimer() + dsb::kSettleNs;
+        while (globaltimer() < until) {
+        }
+    }
 }
 
 template <int N, int TP>
@@ -670,10 +695,11 @@ dsmem_status oneshot_launch(const void* x, void* y, unsigned char* const* lls, s
     cudaLaunchAttribute attr[1];
     int resident = 0;
     if (dsmem_status st = tp_config(fn, n, stream, cfg, attr, &resident); st != DSMEM_OK) return st;
-    // clusters for the row groups, or enough CTAs that each thread pushes at most kPushUnroll units;
-    // every CTA resident (the exit counter is passed by all of them)
-    const long long total = rows * (long long)(hidden / 8);
-    const long long push_ctas = (total + (long long)kThreadsTp * kPushUnroll - 1) / ((long long)kThreadsTp * kPushUnroll);
+    // clusters for the row groups, or enough CTAs that each thread pushes one half unit (up to every resident
+    // cluster: the push's remote stores go out at a limited rate per SM); every CTA resident (the exit
+    // counter is passed by all of them)
+    const long long total = rows * (long long)(hidden / 4);   // 8-byte halves pushed, one per thread
+    const long long push_ctas = (total + kThreadsTp - 1) / kThreadsTp;
     const long long want = std::max<long long>((rows + kR - 1) / kR, (push_ctas + n - 1) / n);
     const long long clusters = std::max<long long>(1, std::min<long long>(want, resident));
     cfg.gridDim = dim3((unsigned)(clusters * n), 1, 1);
@@ -703,8 +729,9 @@ dsmem_status oneshot_launch(const void* x, void* y, unsigned char* const* lls, s
 
 // ------------------------------------------------------------------------------------------ TP context
 namespace {
-// Default one-shot limit: the LL bytes a rank sends, (tp - 1) * rows * hidden * 4.
-constexpr size_t kOneShotDefault = size_t(4) << 20;
+// Default one-shot limit on the LL bytes a rank sends, (tp - 1) * rows * hidden * 4: measured at hidden 8192,
+// the one-shot is the faster form at 1 and 64 tokens on TP 2 (6 MiB at TP 4, where it still wins).
+constexpr size_t kOneShotDefault = size_t(16) << 20;
 size_t ll_offset(size_t capacity) { return kSignalBytes + 2 * capacity; }
 
 // Error words of the one-GPU emulation entry points, one set per device (read by dsmem_tp_emulate_check).

@@ -38,7 +38,8 @@ enum : int {
     kAtomicAllPush = 11, kMesh2D = 12, kDirectShift = 13, kBruck = 14, kDirectPull = 15,
     kGatherBcastBinomial = 16, kRecursiveHalving = 17, kDirectPush = 18, kPairwiseExchange = 19,
     kPairwiseXor = 20, kShift = 21, kRsPushGlobalAg = 22, kRingCredit = 23, kRecursiveDoublingCredit = 24,
-    kBinomial = 25, kBruckCredit = 26, kRecursiveHalvingCredit = 27
+    kBinomial = 25, kBruckCredit = 26, kRecursiveHalvingCredit = 27, kRabenseifnerCredit = 28,
+    kPairwiseXorCredit = 29, kBinomialCredit = 30
 };
 
 template <template <int, typename, class> class A, int N>
@@ -131,6 +132,8 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add<AR_RingCredit, 4>(r, kRingCredit);
     add<AR_RingCredit, 8>(r, kRingCredit);
     add_all_n<AR_RecursiveDoublingCredit>(r, kRecursiveDoublingCredit);
+    add_all_n<AR_RabenseifnerCredit>(r, kRabenseifnerCredit);
+    add_all_n<AR_ReduceBcastBinomialCredit>(r, kBinomialCredit);
 #elif DSB_OP == 1
     add_all_n<AG_RecursiveDoubling>(r, kRecursiveDoubling);
     add_all_n<AG_DirectShift>(r, kDirectShift);
@@ -142,6 +145,7 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<AG_RingCredit>(r, kRingCredit);
     add_all_n<AG_RecursiveDoublingCredit>(r, kRecursiveDoublingCredit);
     add_all_n<AG_BruckCredit>(r, kBruckCredit);
+    add_all_n<AG_GatherBcastBinomialCredit>(r, kBinomialCredit);
     add_streamed_all_n<AG_ReplicatedPushStream>(r, kDirectReplicatedPush);
 #elif DSB_OP == 2
     add_all_n<RS_Ring>(r, kRing);
@@ -161,6 +165,8 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<A2A_PairwiseXor>(r, kPairwiseXor);
     add_all_n<A2A_Shift>(r, kShift);
     add_all_n<A2A_Bruck>(r, kBruck);
+    add_all_n<A2A_PairwiseXorCredit>(r, kPairwiseXorCredit);
+    add_all_n<A2A_BruckCredit>(r, kBruckCredit);
     add_all_n<A2A_DirectPull>(r, kDirectPull);
     add_streamed_all_n<A2A_DirectPushStream>(r, kDirectPush);
 #endif

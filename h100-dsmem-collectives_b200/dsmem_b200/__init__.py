@@ -59,6 +59,9 @@ class Alg(enum.IntEnum):
     BINOMIAL = 25            # broadcast (B200 extension)
     BRUCK_CREDIT = 26        # B200 extension: allgather Bruck, a buffer range + mbarrier per round
     RECURSIVE_HALVING_CREDIT = 27   # B200 extension: reducescatter halving, a buffer + mbarrier per round
+    RABENSEIFNER_CREDIT = 28  # B200 extension: Rabenseifner AllReduce, a buffer + mbarrier per round
+    PAIRWISE_XOR_CREDIT = 29  # B200 extension: pairwise XOR AlltoAll, an mbarrier per round
+    BINOMIAL_CREDIT = 30      # B200 extension: binomial reduce/gather + broadcast, a buffer + mbarrier per round
 
 
 class Dtype(enum.IntEnum):
@@ -127,6 +130,11 @@ EXTENSIONS = {
     (Op.ALLGATHER, Alg.BRUCK_CREDIT): "allgather__bruck_credit (B200 extension)",
     (Op.REDUCESCATTER, Alg.RING_CREDIT): "reducescatter__ring_credit (B200 extension)",
     (Op.REDUCESCATTER, Alg.RECURSIVE_HALVING_CREDIT): "reducescatter__recursive_halving_credit (B200 extension)",
+    (Op.ALLREDUCE, Alg.RABENSEIFNER_CREDIT): "allreduce__rabenseifner_credit (B200 extension)",
+    (Op.ALLREDUCE, Alg.BINOMIAL_CREDIT): "allreduce__reduce_bcast_binomial_credit (B200 extension)",
+    (Op.ALLGATHER, Alg.BINOMIAL_CREDIT): "allgather__gather_bcast_binomial_credit (B200 extension)",
+    (Op.ALLTOALL, Alg.PAIRWISE_XOR_CREDIT): "alltoall__pairwise_xor_credit (B200 extension)",
+    (Op.ALLTOALL, Alg.BRUCK_CREDIT): "alltoall__bruck_credit (B200 extension)",
     (Op.BROADCAST, Alg.DIRECT_PUSH): "broadcast__direct_push (B200 extension)",
     (Op.BROADCAST, Alg.DIRECT_PULL): "broadcast__direct_pull (B200 extension)",
     (Op.BROADCAST, Alg.BINOMIAL): "broadcast__binomial (B200 extension)",

@@ -18,7 +18,7 @@ from . import DsmemError, Dtype, Status, _ok, lib
 HANDLE_BYTES = 64     # DSMEM_TP_HANDLE_BYTES
 NCCL_UID_BYTES = 128
 LL_SLOT_MAX = 4 << 20          # bytes of one LL sender slot at most (min(2 * capacity, 4 MiB))
-ONESHOT_DEFAULT = 4 << 20      # the context's default one-shot limit
+ONESHOT_DEFAULT = 16 << 20     # the context's default one-shot limit
 
 
 def exchange_bytes(local: bytes, group=None) -> list:
@@ -115,7 +115,7 @@ class TPContext:
 
     def set_oneshot_limit(self, nbytes):
         """Use the one-shot form while the LL bytes this rank sends, (tp - 1) * rows * hidden * 4, stay within
-        `nbytes` (dsmem_tp_set_oneshot_limit; 0: always the two-shot; default 4 MiB)."""
+        `nbytes` (dsmem_tp_set_oneshot_limit; 0: always the two-shot; default 16 MiB)."""
         _ok(lib().dsmem_tp_set_oneshot_limit(self._ctx, int(nbytes)), "dsmem_tp_set_oneshot_limit")
         self._limit = int(nbytes)
 

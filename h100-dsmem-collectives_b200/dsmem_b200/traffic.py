@@ -47,11 +47,12 @@ def dsmem_bytes(op, alg, n, p, dtype):
                 Alg.DIRECT_REPLICATED_PUSH: everyone, Alg.ONE_SHOT_PULL: everyone,
                 Alg.ATOMIC_ALL_PUSH: n * (n - 1) * acc,
                 Alg.PULL_REDUCE_SCATTER_PUSH_ALLGATHER: 2 * (n - 1) * blk,
-                Alg.RABENSEIFNER: 2 * (n - 1) * blk, Alg.TWO_SHOT_PUSH: 2 * (n - 1) * blk,
-                Alg.REDUCE_BCAST_BINOMIAL: 2 * (n - 1) * blk, Alg.RS_PUSH_GLOBAL_AG: (n - 1) * blk,
+                Alg.RABENSEIFNER: 2 * (n - 1) * blk, Alg.RABENSEIFNER_CREDIT: 2 * (n - 1) * blk,
+                Alg.TWO_SHOT_PUSH: 2 * (n - 1) * blk,
+                Alg.REDUCE_BCAST_BINOMIAL: 2 * (n - 1) * blk, Alg.BINOMIAL_CREDIT: 2 * (n - 1) * blk, Alg.RS_PUSH_GLOBAL_AG: (n - 1) * blk,
                 Alg.MESH_2D: _mesh2d(n, blk)}.get(alg)
     if op == Op.ALLGATHER:
-        if alg == Alg.GATHER_BCAST_BINOMIAL:
+        if alg in (Alg.GATHER_BCAST_BINOMIAL, Alg.BINOMIAL_CREDIT):
             return (n // 2) * lg * blk + (n - 1) * n * blk
         return everyone if alg in (Alg.RECURSIVE_DOUBLING, Alg.RECURSIVE_DOUBLING_CREDIT, Alg.DIRECT_SHIFT,
                                    Alg.DIRECT_REPLICATED_PUSH, Alg.RING, Alg.RING_CREDIT, Alg.BRUCK,
@@ -60,10 +61,10 @@ def dsmem_bytes(op, alg, n, p, dtype):
         return everyone if alg in (Alg.RING, Alg.RING_CREDIT, Alg.RECURSIVE_HALVING, Alg.RECURSIVE_HALVING_CREDIT,
                                    Alg.DIRECT_PUSH, Alg.DIRECT_PULL) else None
     if op == Op.ALLTOALL:
-        if alg == Alg.BRUCK:
+        if alg in (Alg.BRUCK, Alg.BRUCK_CREDIT):
             return n * (n // 2) * lg * blk
-        return everyone if alg in (Alg.PAIRWISE_EXCHANGE, Alg.DIRECT_PUSH, Alg.PAIRWISE_XOR, Alg.SHIFT,
-                                   Alg.DIRECT_PULL) else None
+        return everyone if alg in (Alg.PAIRWISE_EXCHANGE, Alg.DIRECT_PUSH, Alg.PAIRWISE_XOR, Alg.PAIRWISE_XOR_CREDIT,
+                                   Alg.SHIFT, Alg.DIRECT_PULL) else None
     if op == Op.BROADCAST:
         return (n - 1) * blk if alg in (Alg.DIRECT_PUSH, Alg.DIRECT_PULL, Alg.BINOMIAL) else None
     return None

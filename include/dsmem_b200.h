@@ -93,9 +93,14 @@ typedef enum {
     DSMEM_ALG_RING_CREDIT = 23,                       /* allreduce (N <= 8), allgather, reducescatter */
     DSMEM_ALG_RECURSIVE_DOUBLING_CREDIT = 24,         /* allreduce, allgather                    */
     DSMEM_ALG_BINOMIAL = 25,                          /* broadcast                               */
-    DSMEM_ALG_BRUCK_CREDIT = 26,                      /* allgather (Bruck, a barrier per round)  */
+    DSMEM_ALG_BRUCK_CREDIT = 26,                      /* allgather, alltoall                     */
     DSMEM_ALG_RECURSIVE_HALVING_CREDIT = 27,          /* reducescatter                           */
-    DSMEM_ALG_COUNT = 28
+    /* B200 extensions, no reference file: more of the deferred mbarrier-credit forms (same rounds, partners
+     * and arithmetic as the originals, no barrier.cluster between rounds). */
+    DSMEM_ALG_RABENSEIFNER_CREDIT = 28,               /* allreduce                               */
+    DSMEM_ALG_PAIRWISE_XOR_CREDIT = 29,               /* alltoall                                */
+    DSMEM_ALG_BINOMIAL_CREDIT = 30,                   /* allreduce (reduce + broadcast), allgather (gather + broadcast) */
+    DSMEM_ALG_COUNT = 31
 } dsmem_alg;
 
 /* ELEM_T of the reference (float | int, main.cu:99) plus bf16. */
@@ -409,7 +414,7 @@ dsmem_status dsmem_tp_check(dsmem_tp_t ctx, unsigned* error_bits, unsigned* deta
  * Replaces the reference's host watchdog (collectives/harness/main.cu:277-320) for the cross-GPU path. */
 dsmem_status dsmem_tp_set_wait_limit_ns(dsmem_tp_t ctx, unsigned long long ns);
 /* The one-shot form's limit on the LL bytes a rank sends per call, (tp - 1) * rows * hidden * 4 (default
- * 4 MiB; 0: always the two-shot; SIZE_MAX: the one-shot whenever the tensor fits an LL slot). */
+ * 16 MiB; 0: always the two-shot; SIZE_MAX: the one-shot whenever the tensor fits an LL slot). */
 dsmem_status dsmem_tp_set_oneshot_limit(dsmem_tp_t ctx, size_t bytes);
 dsmem_status dsmem_tp_close(dsmem_tp_t ctx);
 /* The same kernel for `tp` ranks emulated in one launch on one GPU (xs, ys: tp local buffers each; every

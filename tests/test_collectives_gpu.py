@@ -359,3 +359,51 @@ def test_streamed_matches_plain(cuda, orc, op, alg, n):
         D.set_pipelined(True)
         D.set_stream_pipeline()
     assert not failures, "\n".join(failures[:20])
+
+
+# mbarrier-credit forms against their barrier-per-round originals: same rounds, partners and operand order, so
+# the same bits for every dtype (random inputs, one and 37 clusters)
+CREDIT_PAIRS = (
+    (D.Op.ALLREDUCE, D.Alg.RING_CREDIT, D.Alg.RING),
+    (D.Op.ALLREDUCE, D.Alg.RECURSIVE_DOUBLING_CREDIT, D.Alg.RECURSIVE_DOUBLING),
+    (D.Op.ALLREDUCE, D.Alg.RABENSEIFNER_CREDIT, D.Alg.RABENSEIFNER),
+    (D.Op.ALLREDUCE, D.Alg.BINOMIAL_CREDIT, D.Alg.REDUCE_BCAST_BINOMIAL),
+    (D.Op.ALLGATHER, D.Alg.RING_CREDIT, D.Alg.RING),
+    (D.Op.ALLGATHER, D.Alg.RECURSIVE_DOUBLING_CREDIT, D.Alg.RECURSIVE_DOUBLING),
+    (D.Op.ALLGATHER, D.Alg.BRUCK_CREDIT, D.Alg.BRUCK),
+    (D.Op.ALLGATHER, D.Alg.BINOMIAL_CREDIT, D.Alg.GATHER_BCAST_BINOMIAL),
+    (D.Op.REDUCESCATTER, D.Alg.RING_CREDIT, D.Alg.RING),
+    (D.Op.REDUCESCATTER, D.Alg.RECURSIVE_HALVING_CREDIT, D.Alg.RECURSIVE_HALVING),
+    (D.Op.ALLTOALL, D.Alg.PAIRWISE_XOR_CREDIT, D.Alg.PAIRWISE_XOR),
+    (D.Op.ALLTOALL, D.Alg.BRUCK_CREDIT, D.Alg.BRUCK),
+)
+
+
+@pytest.mark.parametrize("op,credit,orig", CREDIT_PAIRS, ids=[f"{NAMES[(o, c)]}" for (o, c, _) in CREDIT_PAIRS])
+def test_credit_matches_original(cuda, orc, op, credit, orig):
+    torch = cuda
+    ran, failures = 0, []
+    for n in D.CLUSTER_SIZES:
+        for dt in D.Dtype:
+            for p in (256, 4096, 16384):
+                if any(D.query(op, a, dt, n, p)[0] != D.Status.OK for a in (credit, orig)):
+                    continue
+                m = D.msg_elems(op, n, p, dt)
+                for clusters in (1, 37):
+                    nin = clusters * n * D.in_elems_per_rank(op, n, m)
+                    nout = clusters * n * D.out_elems_per_rank(op, n, m)
+                    host = make_input(orc, dt, nin, "R", seed=11 * p + n + clusters)
+                    tin = _np_to_torch(torch, host, dt).cuda()
+                    outs = []
+                    for a in (credit, orig):
+                        t = torch.full((nout,), -1, dtype=torch.int16 if dt == D.Dtype.BF16 else torch.int32,
+                                       device="cuda").view(tin.dtype)
+                        D.collective(op, a, tin, t, n, p)
+                        D.check()
+                        outs.append(_torch_to_np(t, dt).view(np.uint8))
+                    if not np.array_equal(outs[0], outs[1]):
+                        failures.append(f"N={n} {dt.name} P={p} clusters={clusters}: differs from {orig.name}")
+                    ran += 1
+    if ran == 0:
+        pytest.skip("no configuration legal for both forms")
+    assert not failures, "\n".join(failures)

@@ -145,7 +145,7 @@ def _rank_main(rank, world, port, rows, hidden, n, out_dir):
                 ctx.allreduce_rmsnorm(x[:r_].contiguous(), tw, 1e-6, residual=tr[:r_].contiguous(), out=yr,
                                       cluster_size=n)
                 np.save(os.path.join(out_dir, f"y{rank}_r{r_}_{path}.npy"), _np(yr))
-        ctx.set_oneshot_limit(4 << 20)
+        ctx.set_oneshot_limit(16 << 20)
         y.fill_(float("nan"))
         ctx.allreduce_rmsnorm(x, tw, 1e-6, residual=tr, out=y, cluster_size=n)   # the default choice
         torch.cuda.synchronize()
