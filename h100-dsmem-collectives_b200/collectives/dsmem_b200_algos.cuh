@@ -461,6 +461,40 @@ struct AR_ShiftAccumulateBulk {
     }
 };
 
+// Shift-accumulate bulk (allreduce__shift_accumulate_bulk__clusterfusion.cu:29-51 schedule, N == 4) with a buffer
+// and an mbarrier per round: round i pushes the running vector into buffer i of CTA b + i (barrier i - 1), which
+// then holds running vector + received and becomes the running vector; the original's operand order.
+template <int N_, typename T_, class Op_>
+struct AR_ShiftAccumulateBulkCredit {
+    DSB_TRAITS(AllReduce, N_ - 2)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return N_ == 4 && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + (N_ - 1ull) * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B;
+        if (threadIdx.x == 0)
+            for (int i = 1; i < N_ - 1; ++i) arm(c, i - 1, MB);
+        uint32_t cur = kD0;
+        for (int i = 1; i < N_ - 1; ++i) {
+            const uint32_t buf = kD0 + (uint32_t)i * MB;
+            if (threadIdx.x == 0) push<N_>(c, (c.rank + i) % N_, buf, cur, MB, i - 1);
+            wait(c, i - 1);
+            reduce2<T, Op>(c, buf, cur, buf, MB);
+            fence_proxy_async_smem();
+            __syncthreads();   // the new running vector is whole before thread 0 pushes it
+            cur = buf;
+            c.st.round(i - 1);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0 + (N_ - 2u) * M * B, M * B);
+    }
+};
+
 // Accumulator element of the remote-atomic algorithms: bf16 sums accumulate in fp32 (a chain of N-1
 // remote adds rounded to bf16 after each add drifted beyond the bf16 tolerance at N = 16); f32 and int32
 // accumulate in their own type. Values are widened on load and narrowed on store.

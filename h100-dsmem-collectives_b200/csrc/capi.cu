@@ -56,7 +56,8 @@ const char* const kAlgNames[DSMEM_ALG_COUNT] = {"auto",
                                                 "recursive_halving_credit",
                                                 "rabenseifner_credit",
                                                 "pairwise_xor_credit",
-                                                "binomial_credit"};
+                                                "binomial_credit",
+                                                "shift_accumulate_bulk_credit"};
 const char* const kDtypeNames[] = {"f32", "bf16", "i32"};
 
 // (op, alg) -> reference file stem collectives/<op>__<alg>__<src>.cu

@@ -39,7 +39,7 @@ enum : int {
     kGatherBcastBinomial = 16, kRecursiveHalving = 17, kDirectPush = 18, kPairwiseExchange = 19,
     kPairwiseXor = 20, kShift = 21, kRsPushGlobalAg = 22, kRingCredit = 23, kRecursiveDoublingCredit = 24,
     kBinomial = 25, kBruckCredit = 26, kRecursiveHalvingCredit = 27, kRabenseifnerCredit = 28,
-    kPairwiseXorCredit = 29, kBinomialCredit = 30
+    kPairwiseXorCredit = 29, kBinomialCredit = 30, kShiftAccBulkCredit = 31
 };
 
 template <template <int, typename, class> class A, int N>
@@ -114,6 +114,7 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
 #if DSB_OP == 0
     add_all_n<AR_RecursiveDoubling>(r, kRecursiveDoubling);
     add<AR_ShiftAccumulateBulk, 4>(r, kShiftAccBulk);
+    add<AR_ShiftAccumulateBulkCredit, 4>(r, kShiftAccBulkCredit);
     add<AR_ShiftAccumulateAtomic, 2>(r, kShiftAccAtomic);
     add<AR_ShiftAccumulateAtomic, 4>(r, kShiftAccAtomic);
     add_all_n<AR_DirectReplicatedPush>(r, kDirectReplicatedPush);

@@ -62,6 +62,7 @@ class Alg(enum.IntEnum):
     RABENSEIFNER_CREDIT = 28  # B200 extension: Rabenseifner AllReduce, a buffer + mbarrier per round
     PAIRWISE_XOR_CREDIT = 29  # B200 extension: pairwise XOR AlltoAll, an mbarrier per round
     BINOMIAL_CREDIT = 30      # B200 extension: binomial reduce/gather + broadcast, a buffer + mbarrier per round
+    SHIFT_ACCUMULATE_BULK_CREDIT = 31   # B200 extension: shift-accumulate bulk AllReduce (N = 4), per-round buffers
 
 
 class Dtype(enum.IntEnum):
@@ -132,6 +133,7 @@ EXTENSIONS = {
     (Op.REDUCESCATTER, Alg.RECURSIVE_HALVING_CREDIT): "reducescatter__recursive_halving_credit (B200 extension)",
     (Op.ALLREDUCE, Alg.RABENSEIFNER_CREDIT): "allreduce__rabenseifner_credit (B200 extension)",
     (Op.ALLREDUCE, Alg.BINOMIAL_CREDIT): "allreduce__reduce_bcast_binomial_credit (B200 extension)",
+    (Op.ALLREDUCE, Alg.SHIFT_ACCUMULATE_BULK_CREDIT): "allreduce__shift_accumulate_bulk_credit (B200 extension)",
     (Op.ALLGATHER, Alg.BINOMIAL_CREDIT): "allgather__gather_bcast_binomial_credit (B200 extension)",
     (Op.ALLTOALL, Alg.PAIRWISE_XOR_CREDIT): "alltoall__pairwise_xor_credit (B200 extension)",
     (Op.ALLTOALL, Alg.BRUCK_CREDIT): "alltoall__bruck_credit (B200 extension)",

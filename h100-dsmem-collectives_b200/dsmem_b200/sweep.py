@@ -1,7 +1,7 @@
 """Catalogue sweep on one B200 and the measured AUTO table.
 
     python -m dsmem_b200.sweep [--out-table autotune_b200.tsv] [--out-json sweep.json] [--dtype f32]
-                               [--ops allreduce,...] [--merge old_table.tsv]
+                               [--ops allreduce,...] [--regime both|single] [--merge old_table.tsv]
 
 For every op x algorithm x cluster size N in {2, 4, 8, 16} x bytes per CTA P in {256 B .. 128 KiB, 192 KiB}
 (the reference sweep's grid, driver.py:156-163) that is legal, two figures:
@@ -14,7 +14,9 @@ For every op x algorithm x cluster size N in {2, 4, 8, 16} x bytes per CTA P in 
            cluster to reach their steady state), CUDA events over `--batch-reps` launches; algbw = problems * N *
            P / time (the whole batch's per-CTA payloads, as bench.py's value).
 The AUTO table (one line per (op, N, P, dtype, regime) with the fastest algorithm) is the input of
-dsmem_autotune_table_load; regime `single` picks by span, `batch` by batch throughput.
+dsmem_autotune_table_load; regime `single` picks by span, `batch` by batch throughput. `--regime single` measures
+the single figure only (every algorithm, a few seconds per op), and `--merge` then replaces only the table's
+single lines of the swept (op, dtype): the way to enter latency variants without re-running the batch regime.
 """
 from __future__ import annotations
 
@@ -39,7 +41,8 @@ PIPELINED = {(Op.ALLREDUCE, Alg.TWO_SHOT_PUSH), (Op.ALLREDUCE, Alg.RS_PUSH_GLOBA
              (Op.ALLGATHER, Alg.DIRECT_REPLICATED_PUSH)}
 
 
-def measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps, batch_bytes=256 << 20):
+def measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps, batch_bytes=256 << 20,
+            batch=True):
     m = msg_elems(op, n, p, dt)
     per_in = n * in_elems_per_rank(op, n, m)
     per_out = n * out_elems_per_rank(op, n, m)
@@ -55,6 +58,11 @@ def measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps,
     s = st.view(reps, n, STAMPS_PER_RANK).cpu()
     spans = (s[:, :, 1].max(dim=1).values - s[:, :, 0].min(dim=1).values).tolist()
     span_ns = statistics.median(spans[min(5, reps // 4):])
+    algbw_single = p / span_ns
+    single = {"span_ns": round(span_ns, 1), "algbw_GBps": round(algbw_single, 3),
+              "busbw_GBps": round(algbw_single * BUS[op](n), 3)}
+    if not batch:
+        return single
     # batch: four waves of resident clusters, at least batch_bytes of input, within the buffers
     try:
         res = max_active_clusters(op, alg, dt, n, p)
@@ -74,14 +82,12 @@ def measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps,
     torch.cuda.synchronize()
     check()
     ms = e0.elapsed_time(e1) / batch_reps
-    algbw_single = p / span_ns
-    return {"span_ns": round(span_ns, 1), "algbw_GBps": round(algbw_single, 3),
-            "busbw_GBps": round(algbw_single * BUS[op](n), 3), "batch_problems": problems,
-            "batch_ms": round(ms, 4), "batch_algbw_GBps": round(problems * n * p / (ms * 1e-3) / 1e9, 1)}
+    return {**single, "batch_problems": problems, "batch_ms": round(ms, 4),
+            "batch_algbw_GBps": round(problems * n * p / (ms * 1e-3) / 1e9, 1)}
 
 
 def run(dtypes=(Dtype.F32,), reps=60, batch_reps=5, sizes=CLUSTER_SIZES, payloads=PAYLOADS, ops=tuple(Op),
-        batch_bytes=256 << 20):
+        batch_bytes=256 << 20, batch=True):
     import torch
 
     torch.cuda.set_device(0)
@@ -99,7 +105,8 @@ def run(dtypes=(Dtype.F32,), reps=60, batch_reps=5, sizes=CLUSTER_SIZES, payload
                     if qs != Status.OK and not (qs == Status.SMEM_LIMIT and (op, alg) in PIPELINED):
                         continue
                     try:
-                        r = measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps, batch_bytes)
+                        r = measure(torch, op, alg, n, p, dt, reps, batch_reps, buf_in, buf_out, stamps, batch_bytes,
+                                    batch=batch)
                     except DsmemError as e:
                         r = {"error": str(e)}
                     r.update({"op": OP_NAMES[op], "alg": ALG_NAMES[alg], "n": n, "bytes": p, "dtype": DT_NAMES[dt]})
@@ -107,11 +114,12 @@ def run(dtypes=(Dtype.F32,), reps=60, batch_reps=5, sizes=CLUSTER_SIZES, payload
     return results
 
 
-def merge(old_text, new_text, results):
-    """The lines of `old_text` whose (op, dtype) the sweep `results` did not cover, then `new_text`'s."""
+def merge(old_text, new_text, results, regimes=("single", "batch")):
+    """The lines of `old_text` whose (op, dtype, regime) the sweep `results` did not cover, then `new_text`'s."""
     covered = {(r["op"], r["dtype"]) for r in results}
     keep = [ln for ln in old_text.splitlines()
-            if ln.strip() and not ln.startswith("#") and (ln.split()[0], ln.split()[3]) not in covered]
+            if ln.strip() and not ln.startswith("#")
+            and ((ln.split()[0], ln.split()[3]) not in covered or ln.split()[5] not in regimes)]
     new = [ln for ln in new_text.splitlines() if ln.strip() and not ln.startswith("#")]
     head = "# op cluster_size bytes_per_cta dtype alg regime  (measured on B200 by dsmem_b200.sweep)"
     key = lambda ln: (ln.split()[0], int(ln.split()[1]), int(ln.split()[2]), ln.split()[3], ln.split()[5])
@@ -126,6 +134,8 @@ def table(results):
             continue
         for regime, key, better in (("single", "span_ns", lambda a, b: a < b),
                                     ("batch", "batch_algbw_GBps", lambda a, b: a > b)):
+            if key not in r:
+                continue
             k = (r["op"], r["n"], r["bytes"], r["dtype"], regime)
             if k not in best or better(r[key], best[k][key]):
                 best[k] = r
@@ -144,18 +154,21 @@ def main(argv=None):
     ap.add_argument("--ops", default="all", help="comma list of allreduce,allgather,reducescatter,alltoall")
     ap.add_argument("--merge", default=None, help="existing table: keep its lines for the (op, dtype) not swept")
     ap.add_argument("--batch-mib", type=int, default=256, help="input MiB of each batch-regime launch (at least)")
+    ap.add_argument("--regime", default="both", choices=["both", "single"],
+                    help="single: one cluster per launch only (no batch launches; --merge keeps the batch lines)")
     args = ap.parse_args(argv)
     dts = {"f32": (Dtype.F32,), "bf16": (Dtype.BF16,), "i32": (Dtype.I32,),
            "all": (Dtype.F32, Dtype.BF16, Dtype.I32)}[args.dtype]
     by_name = {v: k for k, v in OP_NAMES.items()}
     ops = tuple(Op) if args.ops == "all" else tuple(by_name[o] for o in args.ops.split(","))
-    res = run(dts, reps=args.reps, ops=ops, batch_bytes=args.batch_mib << 20)
+    batch = args.regime == "both"
+    res = run(dts, reps=args.reps, ops=ops, batch_bytes=args.batch_mib << 20, batch=batch)
     with open(args.out_json, "w") as f:
         json.dump(res, f)
     text = table(res)
     if args.merge:
         with open(args.merge) as f:
-            text = merge(f.read(), text, res)
+            text = merge(f.read(), text, res, ("single", "batch") if batch else ("single",))
     with open(args.out_table, "w") as f:
         f.write(text)
     print(f"{len(res)} configurations; table -> {args.out_table}; results -> {args.out_json}", flush=True)

@@ -42,7 +42,7 @@ def dsmem_bytes(op, alg, n, p, dtype):
         acc = 4 * m if dtype == Dtype.BF16 else blk   # remote atomics accumulate bf16 in fp32
         return {Alg.RING: 2 * (n - 1) * blk, Alg.RING_CREDIT: 2 * (n - 1) * blk,
                 Alg.RECURSIVE_DOUBLING: n * lg * blk, Alg.RECURSIVE_DOUBLING_CREDIT: n * lg * blk,
-                Alg.SHIFT_ACCUMULATE_BULK: n * (n - 2) * blk,
+                Alg.SHIFT_ACCUMULATE_BULK: n * (n - 2) * blk, Alg.SHIFT_ACCUMULATE_BULK_CREDIT: n * (n - 2) * blk,
                 Alg.SHIFT_ACCUMULATE_ATOMIC: n * max(1, n - 2) * acc,
                 Alg.DIRECT_REPLICATED_PUSH: everyone, Alg.ONE_SHOT_PULL: everyone,
                 Alg.ATOMIC_ALL_PUSH: n * (n - 1) * acc,

@@ -100,7 +100,8 @@ typedef enum {
     DSMEM_ALG_RABENSEIFNER_CREDIT = 28,               /* allreduce                               */
     DSMEM_ALG_PAIRWISE_XOR_CREDIT = 29,               /* alltoall                                */
     DSMEM_ALG_BINOMIAL_CREDIT = 30,                   /* allreduce (reduce + broadcast), allgather (gather + broadcast) */
-    DSMEM_ALG_COUNT = 31
+    DSMEM_ALG_SHIFT_ACCUMULATE_BULK_CREDIT = 31,      /* allreduce (N = 4)                       */
+    DSMEM_ALG_COUNT = 32
 } dsmem_alg;
 
 /* ELEM_T of the reference (float | int, main.cu:99) plus bf16. */

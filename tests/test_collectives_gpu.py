@@ -48,7 +48,8 @@ def bf16_chain(op, alg, n):
     (ceil(log2 N)); one-round algorithms accumulate in fp32 and round once. The bf16 bound is
     1e-2 * (1 + |ref|) per rounding of that chain, never below the reference's ceil(log2 N) factor (main.cu:165)."""
     chained = {(D.Op.ALLREDUCE, D.Alg.RING), (D.Op.ALLREDUCE, D.Alg.RING_CREDIT), (D.Op.REDUCESCATTER, D.Alg.RING),
-               (D.Op.REDUCESCATTER, D.Alg.RING_CREDIT), (D.Op.ALLREDUCE, D.Alg.SHIFT_ACCUMULATE_BULK)}
+               (D.Op.REDUCESCATTER, D.Alg.RING_CREDIT), (D.Op.ALLREDUCE, D.Alg.SHIFT_ACCUMULATE_BULK),
+               (D.Op.ALLREDUCE, D.Alg.SHIFT_ACCUMULATE_BULK_CREDIT)}
     return max(n - 1 if (op, alg) in chained else 1, math.ceil(math.log2(n)))
 
 
@@ -368,6 +369,7 @@ CREDIT_PAIRS = (
     (D.Op.ALLREDUCE, D.Alg.RECURSIVE_DOUBLING_CREDIT, D.Alg.RECURSIVE_DOUBLING),
     (D.Op.ALLREDUCE, D.Alg.RABENSEIFNER_CREDIT, D.Alg.RABENSEIFNER),
     (D.Op.ALLREDUCE, D.Alg.BINOMIAL_CREDIT, D.Alg.REDUCE_BCAST_BINOMIAL),
+    (D.Op.ALLREDUCE, D.Alg.SHIFT_ACCUMULATE_BULK_CREDIT, D.Alg.SHIFT_ACCUMULATE_BULK),
     (D.Op.ALLGATHER, D.Alg.RING_CREDIT, D.Alg.RING),
     (D.Op.ALLGATHER, D.Alg.RECURSIVE_DOUBLING_CREDIT, D.Alg.RECURSIVE_DOUBLING),
     (D.Op.ALLGATHER, D.Alg.BRUCK_CREDIT, D.Alg.BRUCK),
