@@ -52,14 +52,37 @@ def measure(torch, name, n_cta, k=2048, reps=50, trials=5):
             "h100_us": H100_US[name], "vs_h100": round(H100_US[name] / us, 3)}
 
 
+def profile_launches(torch, plan=(("m16_n64k", 4), ("m8_n240k", 8)), warm=3):
+    """The launch sequence an ncu capture selects from: `warm` launches of each (shape, cluster) of `plan` in turn,
+    then one more of each (so `-s warm*len(plan) -c len(plan)` captures one warm launch per shape)."""
+    data = {}
+    for name, c in plan:
+        m, n = SHAPES[name]
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(m * n)
+        data[name] = (torch.randn(m, n, device="cuda", generator=gen),
+                      torch.empty(m, 2048, dtype=torch.int32, device="cuda"), c)
+    for name in [nm for nm, _ in plan for _ in range(warm)] + [nm for nm, _ in plan]:
+        x, out, c = data[name]
+        D.topk(x, k=2048, cluster_size=c, out=out)
+    torch.cuda.synchronize()
+    D.topk_check()
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--shapes", default=",".join(SHAPES))
     ap.add_argument("--clusters", default="4,8,16")
+    ap.add_argument("--profile-launches", action="store_true",
+                    help="no timing: 3 launches each of m16_n64k (cluster 4) and m8_n240k (cluster 8), then one more of "
+                         "each, for an ncu capture with -s 6 -c 2")
     args = ap.parse_args(argv)
     import torch
 
     torch.cuda.set_device(0)
+    if args.profile_launches:
+        profile_launches(torch)
+        return
     for s in args.shapes.split(","):
         for c in map(int, args.clusters.split(",")):
             try:
