@@ -906,17 +906,24 @@ struct AR_TwoShotPush {
         g2s(c, kD0, g, M * B);
         fence_proxy_async_smem();
     }
+    // Shot 1: thread 0 pushes chunk j into slot [b] of CTA j (bulk copies). Shot 2 is fused with the reduction:
+    // each thread stores the 16-byte units it reduced straight into every peer's copy of chunk b (st.async on
+    // the peer's barrier 1), with no block barrier or bulk copy between the two shots. Both barriers are armed
+    // before this CTA's first push, so no peer's second shot can reach barrier 1 before its arm. A peer's
+    // region for chunk b is free once my barrier 0 completed: its shot-1 copy out of it had landed here.
     static __device__ void exec(Ctx& c, uint32_t M) {
         const uint32_t CB = (M / N_) * B, slots = kD0 + M * B, n = CB >> 4;
         if (threadIdx.x == 0) {
             arm(c, 0, (N_ - 1) * CB);
+            arm(c, 1, (N_ - 1) * CB);
             for (uint32_t j = 1; j < (uint32_t)N_; ++j) {
                 const uint32_t dst = (c.rank + j) % N_;
                 push<N_>(c, dst, slots + c.rank * CB, kD0 + dst * CB, CB, 0);
             }
         }
         wait(c, 0);   // every peer's partial of my chunk has landed (so their reads of it are done)
-        uint4* mine = c.ptr<uint4>(kD0 + c.rank * CB);
+        const uint32_t own = kD0 + c.rank * CB;
+        uint4* mine = c.ptr<uint4>(own);
         const uint4* ps = c.ptr<const uint4>(slots);
         for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) {
             uint4 v[N_];
@@ -925,18 +932,13 @@ struct AR_TwoShotPush {
             auto a = Pk<T, Op>::open(v[0]);
 #pragma unroll
             for (int r = 1; r < N_; ++r) Pk<T, Op>::add(a, v[r]);
-            mine[u] = Pk<T, Op>::close(a);
+            const uint4 red = Pk<T, Op>::close(a);
+            mine[u] = red;
+#pragma unroll
+            for (uint32_t j = 1; j < (uint32_t)N_; ++j)
+                st_async_v4((c.rank + j) % N_, c.sa + own + u * 16u, red, c.bar(1));   // shared::cta addresses
         }
-        fence_proxy_async_smem();
-        __syncthreads();
         c.st.round(0);
-        if (threadIdx.x == 0) {
-            arm(c, 1, (N_ - 1) * CB);
-            for (uint32_t j = 1; j < (uint32_t)N_; ++j) {
-                const uint32_t dst = (c.rank + j) % N_;
-                push<N_>(c, dst, kD0 + c.rank * CB, kD0 + c.rank * CB, CB, 1);
-            }
-        }
         wait(c, 1);
         c.st.round(1);
     }
