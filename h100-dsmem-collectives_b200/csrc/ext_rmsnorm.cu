@@ -327,7 +327,14 @@ __global__ void __launch_bounds__(kThreadsRms, kCtasPerSm) rmsnorm_cluster_kerne
             }
         }
     }
-    dsb::finish(c);   // no CTA leaves while a peer may still store into its slots
+    // No cluster barrier at the end: every remote store into this CTA (the partial sums of each group) completed
+    // on a sum barrier its normalising warps waited for. A CTA whose wait gave up lingers instead, so partials
+    // still in flight to it land before it exits.
+    if (__syncthreads_or(c.dead ? 1 : 0)) {
+        const unsigned long long until = globaltimer() + dsb::kSettleNs;
+        while (globaltimer() < until) {
+        }
+    }
 }
 
 struct RmsKey {

@@ -454,7 +454,14 @@ __global__ void __launch_bounds__(kThreadsTk, 1) topk_cluster_kernel(const __gri
         }
         __syncthreads();   // the segment, the scratch and the count slots are free for the next row
     }
-    dsb::finish(c);
+    // No cluster barrier at the end: every remote write into this CTA (histogram shots, counts) completed on a
+    // barrier it waited for, and its own last bulk copies (the all-gather shot) had landed before any peer sent
+    // the counts this CTA waited for. A CTA whose wait gave up lingers instead.
+    if (__syncthreads_or(c.dead ? 1 : 0)) {
+        const unsigned long long until = globaltimer() + dsb::kSettleNs;
+        while (globaltimer() < until) {
+        }
+    }
 }
 
 std::mutex g_mu;
