@@ -450,62 +450,84 @@ __global__ void __launch_bounds__(kThreadsTp, 1) tp_oneshot_kernel(const OsArgs 
         const long long row0 = lo + i * kR + (long long)warp * kRowsPerWarp;
         const GroupIdx<UPL> g(row0, hi, row_u4, col_u4, units, lane);
         f2x acc[kRowsPerWarp][UPL][4];
-        // one rank's units at a time (the polled words are this GPU's memory): every load is issued before
-        // any is checked, and a unit whose words are not yet all this call's is read again until they are, or
-        // until the group's deadline
+        // PB ranks' units at a time (at most 64 registers of units per lane, and fewer ranks than TP: a batch of
+        // every rank let the compiler index the batch by this rank at run time, through local memory): every load
+        // of the batch is issued before any is checked; the units not yet ready are read again together, one
+        // round trip per pass for all of them, until they are or until the group's deadline; then they join the
+        // sum in rank order
+        constexpr int PB0 = UPL >= 4 ? 2 : (UPL == 2 ? 4 : 8);
+        constexpr int PB = TP / 2 < 1 ? 1 : (TP / 2 < PB0 ? TP / 2 : PB0);   // a divisor of TP
+        static_assert(TP % PB == 0, "rank batches must tile the TP ranks");
 #pragma unroll
-        for (int p = 0; p < TP; ++p) {
-            uint4 v[kRowsPerWarp][UPL];
-            bool ready[kRowsPerWarp][UPL];
+        for (int p0 = 0; p0 < TP; p0 += PB) {
+            uint4 v[PB][kRowsPerWarp][UPL];
+            bool ready[PB][kRowsPerWarp][UPL];
 #pragma unroll
-            for (int k = 0; k < kRowsPerWarp; ++k)
-#pragma unroll
-                for (int q = 0; q < UPL; ++q) {
-                    ready[k][q] = true;
-                    if (!g.ok[k][q]) {
-                        v[k][q] = make_uint4(0u, 0u, 0u, 0u);
-                    } else if (p == a.rank) {
-                        v[k][q] = __ldg(a.x + g.idx[k][q]);
-                    } else {
-                        const unsigned char* src = mine + (size_t)p * a.ll_slot + (size_t)g.idx[k][q] * 32u;
-                        unsigned long long w0, w1, w2, w3;
-                        ld_ll(src, w0, w1);
-                        ld_ll(src + 16, w2, w3);
-                        v[k][q] = make_uint4((unsigned)w0, (unsigned)w1, (unsigned)w2, (unsigned)w3);
-                        ready[k][q] = ll_ready(w0, w1, w2, w3, epoch);
-                    }
-                }
-            // the units not yet ready are read again together, one round trip per pass for all of them
-            bool all = true;
-#pragma unroll
-            for (int k = 0; k < kRowsPerWarp; ++k)
-#pragma unroll
-                for (int q = 0; q < UPL; ++q) all = all && ready[k][q];
-            while (!all && !c.dead) {
-                if (globaltimer() > c.deadline) {
-                    c.dead = true;
-                    dsb::report_timeout(c, 0x70 + p);   // rank p's data did not arrive
-                    break;
-                }
-                all = true;
+            for (int pp = 0; pp < PB; ++pp)
 #pragma unroll
                 for (int k = 0; k < kRowsPerWarp; ++k)
 #pragma unroll
-                    for (int q = 0; q < UPL; ++q)
-                        if (!ready[k][q]) {
+                    for (int q = 0; q < UPL; ++q) {
+                        const int p = p0 + pp;
+                        ready[pp][k][q] = true;
+                        if (!g.ok[k][q]) {
+                            v[pp][k][q] = make_uint4(0u, 0u, 0u, 0u);
+                        } else if (p == a.rank) {
+                            v[pp][k][q] = __ldg(a.x + g.idx[k][q]);
+                        } else {
                             const unsigned char* src = mine + (size_t)p * a.ll_slot + (size_t)g.idx[k][q] * 32u;
                             unsigned long long w0, w1, w2, w3;
                             ld_ll(src, w0, w1);
                             ld_ll(src + 16, w2, w3);
-                            v[k][q] = make_uint4((unsigned)w0, (unsigned)w1, (unsigned)w2, (unsigned)w3);
-                            ready[k][q] = ll_ready(w0, w1, w2, w3, epoch);
-                            all = all && ready[k][q];
+                            v[pp][k][q] = make_uint4((unsigned)w0, (unsigned)w1, (unsigned)w2, (unsigned)w3);
+                            ready[pp][k][q] = ll_ready(w0, w1, w2, w3, epoch);
                         }
+                    }
+            bool all = true;
+#pragma unroll
+            for (int pp = 0; pp < PB; ++pp)
+#pragma unroll
+                for (int k = 0; k < kRowsPerWarp; ++k)
+#pragma unroll
+                    for (int q = 0; q < UPL; ++q) all = all && ready[pp][k][q];
+            while (!all && !c.dead) {
+                if (globaltimer() > c.deadline) {
+                    c.dead = true;
+                    int first = p0;   // the lowest rank of the batch whose data did not arrive
+#pragma unroll
+                    for (int pp = PB - 1; pp >= 0; --pp)
+#pragma unroll
+                        for (int k = 0; k < kRowsPerWarp; ++k)
+#pragma unroll
+                            for (int q = 0; q < UPL; ++q)
+                                if (!ready[pp][k][q]) first = p0 + pp;
+                    dsb::report_timeout(c, 0x70 + first);   // that rank's data did not arrive
+                    break;
+                }
+                all = true;
+#pragma unroll
+                for (int pp = 0; pp < PB; ++pp)
+#pragma unroll
+                    for (int k = 0; k < kRowsPerWarp; ++k)
+#pragma unroll
+                        for (int q = 0; q < UPL; ++q)
+                            if (!ready[pp][k][q]) {
+                                const unsigned char* src =
+                                    mine + (size_t)(p0 + pp) * a.ll_slot + (size_t)g.idx[k][q] * 32u;
+                                unsigned long long w0, w1, w2, w3;
+                                ld_ll(src, w0, w1);
+                                ld_ll(src + 16, w2, w3);
+                                v[pp][k][q] = make_uint4((unsigned)w0, (unsigned)w1, (unsigned)w2, (unsigned)w3);
+                                ready[pp][k][q] = ll_ready(w0, w1, w2, w3, epoch);
+                                all = all && ready[pp][k][q];
+                            }
             }
 #pragma unroll
-            for (int k = 0; k < kRowsPerWarp; ++k)
+            for (int pp = 0; pp < PB; ++pp)
 #pragma unroll
-                for (int q = 0; q < UPL; ++q) accumulate(acc[k][q], v[k][q], p);
+                for (int k = 0; k < kRowsPerWarp; ++k)
+#pragma unroll
+                    for (int q = 0; q < UPL; ++q) accumulate(acc[k][q], v[pp][k][q], p0 + pp);
         }
         if (i == 0) cluster_wait();
         // The exchange may wait one more limit: a warp with no units in this group passes the poll at once and
