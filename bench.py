@@ -460,8 +460,8 @@ def decoder_extras(torch, hbm_peak):
 
 def tp_extras(torch, rank, world):
     """tensor-parallel AllReduce + RMSNorm over the N GPUs (bf16, hidden 8192, tokens 1 / 64 / 1024 /
-    8192): the fused peer-memory kernel, from its own buffers and from ordinary tensors, and the NCCL composition;
-    max over ranks, CUDA-graph-timed, with the NVLink fraction; a CPU baseline on rank 0."""
+    8192): the fused peer-memory call (its default form, each form forced, and from ordinary tensors) and the NCCL
+    composition; max over ranks, CUDA-graph-timed, with the NVLink fraction; a CPU baseline on rank 0."""
     from dsmem_b200 import tp_bench as TB
 
     r = TB.run(reps=10, rounds=3, warmup=3)
