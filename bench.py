@@ -18,7 +18,8 @@ the whole batch (inputs 2 GiB per GPU, far larger than the 126 MB L2, so no flus
     check        a strided sample of the timed batch's own output against the CPU oracle
 Extras (rank 0): configs[0]'s single-cluster latencies, configs[2]'s RMSNorm, configs[3]'s decoder layer,
 ceilings, and at N = 1 the row-wise and top-k consumers, each with a CPU baseline and its core count; at N > 1
-every rank also runs configs[4]'s tensor-parallel AllReduce + RMSNorm across the N GPUs.
+every rank also runs configs[4]'s tensor-parallel AllReduce + RMSNorm across the N GPUs, whose result at 64 and
+1,024 tokens (one-shot and two-shot forms) is checked against the CPU oracle (tokens.<T>.check).
 --impl reference runs the reference's own CPU path (collectives/harness/main.cu reference(), compiled
 from the reference sources into oracle/_ref/) on all host cores, same metric and config.
 Multi-GPU: one process per GPU (torchrun), each GPU its own batch (weak scaling, no inter-GPU traffic).
@@ -458,13 +459,53 @@ def decoder_extras(torch, hbm_peak):
     return out
 
 
+def tp_check(torch, rank, world, ctx, tokens, hidden, cluster, x, w):
+    """The fused call's result at 64 tokens (the one-shot form) and 1,024 (the two-shot) against the CPU oracle:
+    y = RMSNorm(sum of every rank's x) * w without a residual, from a NaN-filled output; every rank's y gathered
+    to rank 0, which checks them bit-identical and within 1e-2 * (1 + |ref|) (bf16 output). Every rank takes the
+    same steps; None at other token counts and on ranks other than 0."""
+    if tokens not in (64, 1024):
+        return None
+    import numpy as np
+    import torch.distributed as dist
+
+    y = torch.full_like(x, float("nan"))
+    ctx.allreduce_rmsnorm(x, w, 1e-6, residual=None, out=y, cluster_size=cluster)
+    torch.cuda.synchronize()
+    xs = [torch.empty_like(x) for _ in range(world)]
+    ys = [torch.empty_like(y) for _ in range(world)]
+    dist.all_gather(xs, x)
+    dist.all_gather(ys, y)
+    if rank != 0:
+        return None
+    form = "one-shot" if ctx.oneshot_picked(tokens, hidden) else "two-shot"
+    try:   # rank 0 alone from here: nothing may raise past this point, or the ranks' steps would part
+        from oracle import oracle as orc
+
+        def bits(t):
+            return t.cpu().view(torch.int16).numpy().view(np.uint16)
+
+        ref = orc.tp_rmsnorm(1, [bits(a) for a in xs], bits(w), 1e-6)
+        got = [bits(a) for a in ys]
+        same = all(np.array_equal(g, got[0]) for g in got[1:])
+        bad, _, mr = orc.check(1, got[0].reshape(-1), ref.reshape(-1), 1, 1e-2)
+    except Exception as err:  # noqa: BLE001 -- reported in the line
+        return {"ok": False, "form": form, "error": f"{type(err).__name__}: {err}"}
+    return {"ok": bool(bad == 0 and same), "form": form, "bad_elements": int(bad), "max_rel": float(mr),
+            "ranks_bit_identical": bool(same),
+            "oracle": "oracle.tp_rmsnorm (sum of the ranks' x in double, RMSNorm, x w), tol 1e-2 (1 + |ref|)"}
+
+
 def tp_extras(torch, rank, world):
     """tensor-parallel AllReduce + RMSNorm over the N GPUs (bf16, hidden 8192, tokens 1 / 64 / 1024 /
     8192): the fused peer-memory call (its default form, each form forced, and from ordinary tensors) and the NCCL
     composition; max over ranks, CUDA-graph-timed, with the NVLink fraction; a CPU baseline on rank 0."""
     from dsmem_b200 import tp_bench as TB
 
-    r = TB.run(reps=10, rounds=3, warmup=3)
+    try:
+        r = TB.run(reps=10, rounds=3, warmup=3, on_tokens=lambda *a: tp_check(torch, rank, world, *a))
+    except Exception as err:  # noqa: BLE001 -- raised alike on every rank (argument or launch errors); the
+        r = {"error": f"{type(err).__name__}: {err}"}   # headline line is still printed
     torch.cuda.empty_cache()
     if rank == 0:
         import numpy as np

@@ -30,11 +30,28 @@ HIDDEN = 8192
 TOKENS = (1, 64, 1024, 8192)
 
 
-def run(tokens=TOKENS, hidden=HIDDEN, cluster=8, reps=20, rounds=5, warmup=5):
+def _device_errors(ctx, dev_index):
+    """(any error, text) of this rank's TP error words and RMSNorm error bits, read and cleared; no raise."""
+    import ctypes
+
+    from . import Status, lib
+
+    st, bits, detail = ctx.status()
+    rbits = ctypes.c_uint(0)
+    rst = lib().dsmem_rmsnorm_check(int(dev_index), ctypes.byref(rbits))
+    bad = st != Status.OK or rst != 0 or bool(rbits.value & 1)
+    return bad, f"tp {st.name} (bits {bits:#x}, detail {detail:#x}), rmsnorm bits {rbits.value:#x}"
+
+
+def run(tokens=TOKENS, hidden=HIDDEN, cluster=8, reps=20, rounds=5, warmup=5, on_tokens=None):
+    """Times every case of every token count; returns the table. Every rank takes the same collective steps:
+    device errors (a cross-GPU wait that gave up) are agreed on by an all-reduce after each token count, and
+    all ranks stop together, with the table's row saying so, instead of one rank raising alone.
+    on_tokens(ctx, tokens, hidden, cluster, x, w): called on every rank after each token count's timing (a
+    result check, for instance); its return value goes into the row as "check"."""
     import torch
     import torch.distributed as dist
 
-    from . import rmsnorm_check
     from . import tp as T
 
     rank, world = dist.get_rank(), dist.get_world_size()
@@ -102,9 +119,15 @@ def run(tokens=TOKENS, hidden=HIDDEN, cluster=8, reps=20, rounds=5, warmup=5):
                 if name == "fused":
                     row[name]["form"] = "one-shot" if world > 1 and ctx.oneshot_picked(t, hidden) else "two-shot"
             ctx.set_oneshot_limit(T.ONESHOT_DEFAULT)
-            ctx.check()
-            rmsnorm_check()
+            if on_tokens is not None:
+                row["check"] = on_tokens(ctx, t, hidden, cluster, x, w)
+            bad, text = _device_errors(ctx, dev.index)
+            flag = torch.tensor([1 if bad else 0], device=dev)
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX)
             out[str(t)] = row
+            if flag.item():
+                row["error"] = f"device error words set on a rank (this rank: {text}); later token counts not run"
+                break
             dist.barrier()
     finally:
         torch.cuda.synchronize()
