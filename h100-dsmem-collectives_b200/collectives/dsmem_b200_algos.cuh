@@ -34,7 +34,9 @@
 namespace dsb {
 using namespace dsmem;
 
-enum class OpKind : int { AllReduce = 0, AllGather = 1, ReduceScatter = 2, AllToAll = 3, Broadcast = 4 };
+enum class OpKind : int {
+    AllReduce = 0, AllGather = 1, ReduceScatter = 2, AllToAll = 3, Broadcast = 4, Reduce = 5, Gather = 6, Scatter = 7
+};
 
 constexpr uint32_t kBarArea = 128;
 constexpr uint32_t kD0 = kBarArea;
@@ -2129,17 +2131,24 @@ struct A2A_DirectPull {
 };
 
 // --------------------------------------------------------------------------- element counts per rank
+// One rank block of M elements in: AllReduce, AllGather, Broadcast, Reduce, Gather; N blocks (one per peer):
+// ReduceScatter, AlltoAll, Scatter. Out: one block for AllReduce, ReduceScatter, Broadcast, Reduce, Scatter;
+// N blocks for AllGather, AlltoAll, Gather.
+__host__ __device__ constexpr bool one_block_in(OpKind k) {
+    return k == OpKind::AllReduce || k == OpKind::AllGather || k == OpKind::Broadcast || k == OpKind::Reduce ||
+           k == OpKind::Gather;
+}
+__host__ __device__ constexpr bool one_block_out(OpKind k) {
+    return k == OpKind::AllReduce || k == OpKind::ReduceScatter || k == OpKind::Broadcast || k == OpKind::Reduce ||
+           k == OpKind::Scatter;
+}
 template <class A>
 __host__ __device__ constexpr uint64_t in_elems_per_rank(uint32_t M) {
-    return (A::kOp == OpKind::AllReduce || A::kOp == OpKind::AllGather || A::kOp == OpKind::Broadcast)
-               ? (uint64_t)M
-               : (uint64_t)A::kN * M;
+    return one_block_in(A::kOp) ? (uint64_t)M : (uint64_t)A::kN * M;
 }
 template <class A>
 __host__ __device__ constexpr uint64_t out_elems_per_rank(uint32_t M) {
-    return (A::kOp == OpKind::AllReduce || A::kOp == OpKind::ReduceScatter || A::kOp == OpKind::Broadcast)
-               ? (uint64_t)M
-               : (uint64_t)A::kN * M;
+    return one_block_out(A::kOp) ? (uint64_t)M : (uint64_t)A::kN * M;
 }
 
 // --------------------------------------------------------------------------- drivers
@@ -2292,6 +2301,305 @@ struct BC_Binomial {
                 const uint32_t dst = c.rank + (1u << k);
                 if (dst < (uint32_t)N_) push<N_>(c, dst, kD0, kD0, MB, 0);
             }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// ---- Reduce, Gather and Scatter rooted at rank 0 (B200 extensions, no reference file: the other rooted
+// collectives beside the Broadcast; direct push, direct pull and binomial, no TMA multicast). Per rank:
+//   Reduce   in[M] -> out[M] of rank 0 = op over the ranks' vectors; the other ranks' out blocks are not written;
+//   Gather   in[M] -> out[N*M] of rank 0 = the ranks' vectors in rank order; the other ranks' out blocks are not
+//            written;
+//   Scatter  in[N*M] of rank 0 (the other ranks' in blocks are not read) -> out[M] of rank r = block r of it.
+// Payload convention: P = M * sizeof(T) for the Reduce (as the AllReduce), P = N * M * sizeof(T) for the Gather
+// and the Scatter (as the AllGather and the ReduceScatter). Every CTA of a launch has the same window, sized for
+// the root's buffers.
+
+// Every rank but 0 pushes its vector into slot b of rank 0 (one bulk copy, one aggregate barrier); rank 0 sums
+// the N slots in rank order, accumulating in fp32 for bf16 (one rounding).
+template <int N_, typename T_, class Op_>
+struct RD_DirectPush {
+    DSB_TRAITS(Reduce, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();   // the bulk push reads it through the async proxy
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B, n = MB >> 4;
+        if (c.rank == 0) {
+            if (threadIdx.x == 0) arm(c, 0, (N_ - 1) * MB);
+            wait(c, 0);
+            uint4* p = c.ptr<uint4>(kD0);
+            for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) {
+                uint4 v[N_];
+#pragma unroll
+                for (int r = 0; r < N_; ++r) v[r] = p[r * n + u];
+                auto a = Pk<T, Op>::open(v[0]);
+#pragma unroll
+                for (int r = 1; r < N_; ++r) Pk<T, Op>::add(a, v[r]);
+                p[u] = Pk<T, Op>::close(a);
+            }
+        } else if (threadIdx.x == 0) {
+            push<N_>(c, 0, kD0 + c.rank * MB, kD0, MB, 0);
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        if (c.rank != 0) return;
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// Rank 0 reads every peer's vector with 16-byte remote loads and sums them in rank order into its own buffer
+// (fp32 accumulation for bf16); the driver's exit cluster barrier keeps the peers' buffers until it is done.
+template <int N_, typename T_, class Op_>
+struct RD_DirectPull {
+    DSB_TRAITS(Reduce, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) { g2s(c, kD0, g, M * B); }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        if (c.rank == 0) {
+            const uint32_t n = (M * B) >> 4;
+            uint4* p = c.ptr<uint4>(kD0);
+            uint32_t base[N_];
+#pragma unroll
+            for (int r = 1; r < N_; ++r) base[r] = mapa(c.sa + kD0, r);
+            for (uint32_t u = threadIdx.x; u < n; u += blockDim.x) {
+                uint4 v[N_];
+                v[0] = p[u];
+#pragma unroll
+                for (int r = 1; r < N_; ++r) v[r] = ld_cluster_v4(base[r] + 16u * u);
+                auto a = Pk<T, Op>::open(v[0]);
+#pragma unroll
+                for (int r = 1; r < N_; ++r) Pk<T, Op>::add(a, v[r]);
+                p[u] = Pk<T, Op>::close(a);
+            }
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        if (c.rank != 0) return;
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// Binomial tree to rank 0, the reduce half of the binomial AllReduce with a buffer and an mbarrier per round:
+// in round k (d = 2^k) a rank with b mod 2d == d pushes its partial into scratch k of b - d and drops out; b - d
+// adds it into its own partial. A rank waits only for the copies it receives; no cluster barrier between
+// rounds. The element type rounds once per round (as the AllReduce's binomial).
+template <int N_, typename T_, class Op_>
+struct RD_Binomial {
+    DSB_TRAITS(Reduce, ilog2(N_))
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && N_ >= 2 && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) {
+        return kD0 + (1ull + ilog2(N_)) * M * B;
+    }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        constexpr int L = ilog2(N_);
+        const uint32_t MB = M * B;
+        if (threadIdx.x == 0)
+            for (int k = 0; k < L; ++k)
+                if (c.rank % (2u << k) == 0u) arm(c, k, MB);   // receives a partial in round k
+        for (int k = 0; k < L; ++k) {
+            const uint32_t d = 1u << k, m = c.rank % (2u * d), scr = kD0 + (uint32_t)(k + 1) * MB;
+            if (m == d) {
+                if (threadIdx.x == 0) push<N_>(c, c.rank - d, scr, kD0, MB, k);
+                c.st.round(k);
+                break;
+            }
+            wait(c, k);
+            reduce2<T, Op>(c, kD0, kD0, scr, MB);
+            fence_proxy_async_smem();
+            __syncthreads();   // the partial is whole before thread 0 pushes it on
+            c.st.round(k);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        if (c.rank != 0) return;
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// Every rank but 0 pushes its vector into slot b of rank 0 (one bulk copy, one aggregate barrier).
+template <int N_, typename T_, class Op_>
+struct GA_DirectPush {
+    DSB_TRAITS(Gather, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B;
+        if (c.rank == 0) {
+            if (threadIdx.x == 0) arm(c, 0, (N_ - 1) * MB);
+            wait(c, 0);
+        } else if (threadIdx.x == 0) {
+            push<N_>(c, 0, kD0 + c.rank * MB, kD0, MB, 0);
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        if (c.rank != 0) return;
+        __syncthreads();
+        s2g(c, g, kD0, N_ * M * B);
+    }
+};
+
+// Rank 0 reads every peer's vector into slot b with 16-byte remote loads.
+template <int N_, typename T_, class Op_>
+struct GA_DirectPull {
+    DSB_TRAITS(Gather, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) { g2s(c, kD0, g, M * B); }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        if (c.rank == 0) {
+            const uint32_t n = (M * B) >> 4;
+            uint4* D = c.ptr<uint4>(kD0);
+            for (uint32_t idx = n + threadIdx.x; idx < N_ * n; idx += blockDim.x) {
+                const uint32_t r = idx / n, u = idx - r * n;
+                D[idx] = ld_cluster_v4(mapa(c.sa + kD0 + 16u * u, r));
+            }
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        if (c.rank != 0) return;
+        __syncthreads();
+        s2g(c, g, kD0, N_ * M * B);
+    }
+};
+
+// Binomial tree to rank 0, the gather half of the binomial AllGather with an mbarrier per round: in round k
+// (d = 2^k) a rank with b mod 2d == d sends the d blocks it holds (its own and those gathered so far, ranks
+// b .. b + d - 1) into blocks [d, 2d) of b - d, and drops out. No cluster barrier between rounds.
+template <int N_, typename T_, class Op_>
+struct GA_Binomial {
+    DSB_TRAITS(Gather, ilog2(N_))
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && N_ >= 2 && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        g2s(c, kD0, g, M * B);
+        fence_proxy_async_smem();
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        constexpr int L = ilog2(N_);
+        const uint32_t MB = M * B;
+        if (threadIdx.x == 0)
+            for (int k = 0; k < L; ++k)
+                if (c.rank % (2u << k) == 0u) arm(c, k, (1u << k) * MB);
+        for (int k = 0; k < L; ++k) {
+            const uint32_t d = 1u << k, m = c.rank % (2u * d);
+            if (m == d) {
+                if (threadIdx.x == 0) push<N_>(c, c.rank - d, kD0 + d * MB, kD0, d * MB, k);
+                c.st.round(k);
+                break;
+            }
+            wait(c, k);
+            c.st.round(k);
+        }
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        if (c.rank != 0) return;
+        __syncthreads();
+        s2g(c, g, kD0, N_ * M * B);
+    }
+};
+
+// Rank 0 pushes block r of its input into rank r (N - 1 bulk copies, one round).
+template <int N_, typename T_, class Op_>
+struct SC_DirectPush {
+    DSB_TRAITS(Scatter, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        if (c.rank == 0) {
+            g2s(c, kD0, g, N_ * M * B);
+            fence_proxy_async_smem();
+        }
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B;
+        if (c.rank == 0) {
+            if (threadIdx.x == 0)
+                for (uint32_t r = 1; r < (uint32_t)N_; ++r) push<N_>(c, r, kD0, kD0 + r * MB, MB, 0);
+        } else {
+            if (threadIdx.x == 0) arm(c, 0, MB);
+            wait(c, 0);
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// Every rank but 0 reads block b of rank 0's input with 16-byte remote loads.
+template <int N_, typename T_, class Op_>
+struct SC_DirectPull {
+    DSB_TRAITS(Scatter, 0)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        if (c.rank == 0) g2s(c, kD0, g, N_ * M * B);
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        if (c.rank != 0) {
+            const uint32_t n = (M * B) >> 4, src = mapa(c.sa + kD0 + c.rank * M * B, 0u);
+            uint4* dst = c.ptr<uint4>(kD0);
+#pragma unroll 4
+            for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = ld_cluster_v4(src + 16u * i);
+        }
+        c.st.round(0);
+    }
+    static __device__ void store(Ctx& c, T* g, uint32_t M) {
+        __syncthreads();
+        s2g(c, g, kD0, M * B);
+    }
+};
+
+// Binomial tree from rank 0: rounds d = N/2 .. 1; a rank holding blocks of ranks b .. b + 2d - 1 (blocks
+// [0, 2d) of its buffer) sends the upper half, blocks [d, 2d), into blocks [0, d) of b + d. Rank r > 0 receives
+// once, from r - lowbit(r), on its one barrier, and forwards in the later (smaller) rounds; no cluster barrier
+// between rounds.
+template <int N_, typename T_, class Op_>
+struct SC_Binomial {
+    DSB_TRAITS(Scatter, 1)
+    __host__ __device__ static constexpr bool legal(uint32_t M) { return is_pow2(N_) && N_ >= 2 && mult16(M * B); }
+    __host__ __device__ static constexpr uint64_t smem_bytes(uint32_t M) { return kD0 + 1ull * N_ * M * B; }
+    static __device__ void load(Ctx& c, const T* g, uint32_t M) {
+        if (c.rank == 0) {
+            g2s(c, kD0, g, N_ * M * B);
+            fence_proxy_async_smem();
+        }
+    }
+    static __device__ void exec(Ctx& c, uint32_t M) {
+        const uint32_t MB = M * B;
+        uint32_t span = (uint32_t)N_;   // blocks this rank holds once its copy has landed
+        if (c.rank != 0) {
+            span = c.rank & (0u - c.rank);   // lowest set bit: blocks of ranks rank .. rank + span - 1
+            if (threadIdx.x == 0) arm(c, 0, span * MB);
+            wait(c, 0);
+        }
+        if (threadIdx.x == 0)
+            for (uint32_t d = span / 2u; d >= 1u; d /= 2u) push<N_>(c, c.rank + d, kD0, kD0 + d * MB, d * MB, 0);
         c.st.round(0);
     }
     static __device__ void store(Ctx& c, T* g, uint32_t M) {

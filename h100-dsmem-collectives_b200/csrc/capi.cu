@@ -25,7 +25,9 @@ using dsb::Registry;
 
 constexpr int kThreads = 256;
 
-const char* const kOpNames[] = {"allreduce", "allgather", "reducescatter", "alltoall", "broadcast"};
+const char* const kOpNames[] = {"allreduce", "allgather", "reducescatter", "alltoall", "broadcast",
+                                "reduce",    "gather",    "scatter"};
+constexpr int kNumOps = 8;
 const char* const kAlgNames[DSMEM_ALG_COUNT] = {"auto",
                                                 "ring",
                                                 "recursive_doubling",
@@ -98,12 +100,15 @@ const Stem kStems[] = {
 };
 
 // Built-in AUTO order per op when no measured table entry applies: first legal candidate wins.
-const std::vector<int> kDefaultOrder[5] = {
+const std::vector<int> kDefaultOrder[kNumOps] = {
     {DSMEM_ALG_TWO_SHOT_PUSH, DSMEM_ALG_ONE_SHOT_PULL, DSMEM_ALG_RABENSEIFNER, DSMEM_ALG_RING,
      DSMEM_ALG_RECURSIVE_DOUBLING, DSMEM_ALG_PULL_REDUCE_SCATTER_PUSH_ALLGATHER},
     {DSMEM_ALG_DIRECT_PULL, DSMEM_ALG_DIRECT_REPLICATED_PUSH, DSMEM_ALG_BRUCK, DSMEM_ALG_RING},
     {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_DIRECT_PULL, DSMEM_ALG_RECURSIVE_HALVING, DSMEM_ALG_RING},
     {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_DIRECT_PULL, DSMEM_ALG_SHIFT, DSMEM_ALG_PAIRWISE_XOR},
+    {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_BINOMIAL, DSMEM_ALG_DIRECT_PULL},
+    {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_BINOMIAL, DSMEM_ALG_DIRECT_PULL},
+    {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_BINOMIAL, DSMEM_ALG_DIRECT_PULL},
     {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_BINOMIAL, DSMEM_ALG_DIRECT_PULL},
 };
 
@@ -166,6 +171,15 @@ const Registry& registry() {
         dsb::register_op4_dt0(s.reg);
         dsb::register_op4_dt1(s.reg);
         dsb::register_op4_dt2(s.reg);
+        dsb::register_op5_dt0(s.reg);
+        dsb::register_op5_dt1(s.reg);
+        dsb::register_op5_dt2(s.reg);
+        dsb::register_op6_dt0(s.reg);
+        dsb::register_op6_dt1(s.reg);
+        dsb::register_op6_dt2(s.reg);
+        dsb::register_op7_dt0(s.reg);
+        dsb::register_op7_dt1(s.reg);
+        dsb::register_op7_dt2(s.reg);
     });
     return s.reg;
 }
@@ -180,14 +194,15 @@ int elem_bytes(int dtype) { return dtype == DSMEM_BF16 ? 2 : 4; }
 
 // Elements per rank block from the payload convention; 0 if P does not divide.
 uint32_t msg_elems(int op, int dtype, int n, size_t bytes) {
-    const size_t unit = (size_t)elem_bytes(dtype) * (op == DSMEM_OP_ALLREDUCE || op == DSMEM_OP_BROADCAST ? 1 : (size_t)n);
+    const size_t unit = (size_t)elem_bytes(dtype) *
+                        (op == DSMEM_OP_ALLREDUCE || op == DSMEM_OP_BROADCAST || op == DSMEM_OP_REDUCE ? 1 : (size_t)n);
     if (bytes == 0 || bytes % unit != 0) return 0;
     const size_t m = bytes / unit;
     return m > 0xffffffffull ? 0u : (uint32_t)m;
 }
 
 bool valid_enums(int op, int alg, int dtype, int n) {
-    return op >= 0 && op <= 4 && alg >= 0 && alg < DSMEM_ALG_COUNT && dtype >= 0 && dtype <= 2 &&
+    return op >= 0 && op < kNumOps && alg >= 0 && alg < DSMEM_ALG_COUNT && dtype >= 0 && dtype <= 2 &&
            (n == 2 || n == 4 || n == 8 || n == 16);
 }
 
@@ -218,7 +233,7 @@ dsmem_status parse_table(const char* path, std::map<TuneKey, std::map<uint64_t, 
             else if (regs != "single") return DSMEM_ERR_INVALID_ARGUMENT;
         }
         int op = -1, dt = -1, alg = -1;
-        for (int i = 0; i < 5; ++i)
+        for (int i = 0; i < kNumOps; ++i)
             if (ops == kOpNames[i]) op = i;
         for (int i = 0; i < 3; ++i)
             if (dts == kDtypeNames[i]) dt = i;
@@ -650,7 +665,7 @@ dsmem_status dsmem_check(dsmem_stream_t stream) {
     return DSMEM_OK;
 }
 
-const char* dsmem_op_name(dsmem_op op) { return (op >= 0 && op <= 4) ? kOpNames[op] : "?"; }
+const char* dsmem_op_name(dsmem_op op) { return (op >= 0 && op < kNumOps) ? kOpNames[op] : "?"; }
 const char* dsmem_alg_name(dsmem_alg alg) { return (alg >= 0 && alg < DSMEM_ALG_COUNT) ? kAlgNames[alg] : "?"; }
 const char* dsmem_dtype_name(dsmem_dtype dt) { return (dt >= 0 && dt <= 2) ? kDtypeNames[dt] : "?"; }
 

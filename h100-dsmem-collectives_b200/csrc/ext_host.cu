@@ -66,18 +66,22 @@ extern "C" dsmem_status dsmem_collective_host(dsmem_op op, dsmem_alg alg, dsmem_
                                               size_t bytes_per_cta, const void* host_in, void* host_out,
                                               long long num_clusters, long long chunk_clusters) {
     if (host_in == nullptr || host_out == nullptr || num_clusters < 0) return DSMEM_ERR_INVALID_ARGUMENT;
-    if ((int)op < 0 || (int)op > 4 || (int)dtype < 0 || (int)dtype > 2) return DSMEM_ERR_INVALID_ARGUMENT;
+    if ((int)op < 0 || (int)op > 7 || (int)dtype < 0 || (int)dtype > 2) return DSMEM_ERR_INVALID_ARGUMENT;
     if (!(cluster_size == 2 || cluster_size == 4 || cluster_size == 8 || cluster_size == 16))
         return DSMEM_ERR_INVALID_ARGUMENT;
     // elements per rank block (the payload convention of dsmem_collective_launch)
     const size_t n = (size_t)cluster_size, eb = dtype == DSMEM_BF16 ? 2 : 4;
-    const bool per_peer_in = op == DSMEM_OP_REDUCESCATTER || op == DSMEM_OP_ALLTOALL;
-    const bool per_peer_out = op == DSMEM_OP_ALLGATHER || op == DSMEM_OP_ALLTOALL;
-    const size_t unit = eb * (op == DSMEM_OP_ALLREDUCE || op == DSMEM_OP_BROADCAST ? 1 : n);
+    const bool per_peer_in = op == DSMEM_OP_REDUCESCATTER || op == DSMEM_OP_ALLTOALL || op == DSMEM_OP_SCATTER;
+    const bool per_peer_out = op == DSMEM_OP_ALLGATHER || op == DSMEM_OP_ALLTOALL || op == DSMEM_OP_GATHER;
+    // the rooted Reduce and Gather write rank 0's out block only: only those blocks are copied back, so the
+    // other ranks' blocks of host_out keep their contents, as on the device
+    const bool root_out_only = op == DSMEM_OP_REDUCE || op == DSMEM_OP_GATHER;
+    const size_t unit = eb * (op == DSMEM_OP_ALLREDUCE || op == DSMEM_OP_BROADCAST || op == DSMEM_OP_REDUCE ? 1 : n);
     if (bytes_per_cta == 0 || bytes_per_cta % unit != 0) return DSMEM_ERR_ILLEGAL_CONFIG;
     const size_t m = bytes_per_cta / unit;
     const size_t in_pp = n * (per_peer_in ? n : 1) * m * eb;     // input bytes per cluster problem
     const size_t out_pp = n * (per_peer_out ? n : 1) * m * eb;   // output bytes per cluster problem
+    const size_t out_root = (per_peer_out ? n : 1) * m * eb;     // bytes of rank 0's out block
     if (num_clusters == 0) return DSMEM_OK;
     long long cc = chunk_clusters > 0 ? chunk_clusters
                                       : std::max<long long>(1, (long long)(kChunkTarget / std::max(in_pp, out_pp)));
@@ -113,7 +117,10 @@ extern "C" dsmem_status dsmem_collective_host(dsmem_op op, dsmem_alg alg, dsmem_
         if (status != DSMEM_OK) break;
         ok = cudaEventRecord(p.k_done[b], p.s[1]) == cudaSuccess &&
              cudaStreamWaitEvent(p.s[2], p.k_done[b], 0) == cudaSuccess &&
-             cudaMemcpyAsync(dst, p.dout[b], (size_t)np * out_pp, cudaMemcpyDeviceToHost, p.s[2]) == cudaSuccess &&
+             (root_out_only ? cudaMemcpy2DAsync(dst, out_pp, p.dout[b], out_pp, out_root, (size_t)np,
+                                                cudaMemcpyDeviceToHost, p.s[2])
+                            : cudaMemcpyAsync(dst, p.dout[b], (size_t)np * out_pp, cudaMemcpyDeviceToHost, p.s[2])) ==
+                 cudaSuccess &&
              cudaEventRecord(p.out_done[b], p.s[2]) == cudaSuccess;
         if (!ok) status = DSMEM_ERR_CUDA;
     }

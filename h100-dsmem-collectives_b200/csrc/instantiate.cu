@@ -1,11 +1,11 @@
-// instantiate.cu -- compiled once per (op, dtype) with -DDSB_OP=<0..3> -DDSB_DT=<0..2>; instantiates
+// instantiate.cu -- compiled once per (op, dtype) with -DDSB_OP=<0..7> -DDSB_DT=<0..2>; instantiates
 // batch_kernel<Alg<N, T, Sum>> for every algorithm of that op and every cluster size the algorithm's
 // static constraints allow, and registers them for the C ABI.
 #include "../collectives/dsmem_b200_algos.cuh"
 #include "registry.h"
 
 #ifndef DSB_OP
-#error "compile with -DDSB_OP=<0 allreduce|1 allgather|2 reducescatter|3 alltoall>"
+#error "compile with -DDSB_OP=<0 allreduce|1 allgather|2 reducescatter|3 alltoall|4 broadcast|5 reduce|6 gather|7 scatter>"
 #endif
 #ifndef DSB_DT
 #error "compile with -DDSB_DT=<0 f32|1 bf16|2 i32>"
@@ -160,7 +160,19 @@ void DSB_REG_NAME(DSB_OP, DSB_DT)(Registry& r) {
     add_all_n<BC_DirectPush>(r, kDirectPush);
     add_all_n<BC_DirectPull>(r, kDirectPull);
     add_all_n<BC_Binomial>(r, kBinomial);
-#else
+#elif DSB_OP == 5
+    add_all_n<RD_DirectPush>(r, kDirectPush);
+    add_all_n<RD_DirectPull>(r, kDirectPull);
+    add_all_n<RD_Binomial>(r, kBinomial);
+#elif DSB_OP == 6
+    add_all_n<GA_DirectPush>(r, kDirectPush);
+    add_all_n<GA_DirectPull>(r, kDirectPull);
+    add_all_n<GA_Binomial>(r, kBinomial);
+#elif DSB_OP == 7
+    add_all_n<SC_DirectPush>(r, kDirectPush);
+    add_all_n<SC_DirectPull>(r, kDirectPull);
+    add_all_n<SC_Binomial>(r, kBinomial);
+#elif DSB_OP == 3
     add<A2A_PairwiseExchange, 2>(r, kPairwiseExchange);
     add_all_n<A2A_DirectPush>(r, kDirectPush);
     add_all_n<A2A_PairwiseXor>(r, kPairwiseXor);

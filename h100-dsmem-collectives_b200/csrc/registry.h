@@ -43,5 +43,14 @@ void register_op3_dt2(Registry&);
 void register_op4_dt0(Registry&);
 void register_op4_dt1(Registry&);
 void register_op4_dt2(Registry&);
+void register_op5_dt0(Registry&);
+void register_op5_dt1(Registry&);
+void register_op5_dt2(Registry&);
+void register_op6_dt0(Registry&);
+void register_op6_dt1(Registry&);
+void register_op6_dt2(Registry&);
+void register_op7_dt0(Registry&);
+void register_op7_dt1(Registry&);
+void register_op7_dt2(Registry&);
 
 }  // namespace dsb

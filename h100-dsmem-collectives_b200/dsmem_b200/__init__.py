@@ -28,6 +28,9 @@ class Op(enum.IntEnum):
     REDUCESCATTER = 2
     ALLTOALL = 3
     BROADCAST = 4   # B200 extension (no reference file): rank 0's vector to every rank
+    REDUCE = 5      # B200 extension: op over the ranks' vectors into rank 0 (other ranks' out not written)
+    GATHER = 6      # B200 extension: the ranks' vectors into rank 0, in rank order (other ranks' out not written)
+    SCATTER = 7     # B200 extension: block r of rank 0's input to rank r
 
 
 class Alg(enum.IntEnum):
@@ -56,7 +59,7 @@ class Alg(enum.IntEnum):
     RS_PUSH_GLOBAL_AG = 22   # B200 extension (no reference file): DSMEM reduce-scatter, all-gather via the outputs
     RING_CREDIT = 23         # B200 extension: ring AllReduce, a buffer + mbarrier per round (N <= 8)
     RECURSIVE_DOUBLING_CREDIT = 24   # B200 extension: recursive doubling, a buffer + mbarrier per round
-    BINOMIAL = 25            # broadcast (B200 extension)
+    BINOMIAL = 25            # broadcast, reduce, gather, scatter (B200 extensions)
     BRUCK_CREDIT = 26        # B200 extension: allgather Bruck, a buffer range + mbarrier per round
     RECURSIVE_HALVING_CREDIT = 27   # B200 extension: reducescatter halving, a buffer + mbarrier per round
     RABENSEIFNER_CREDIT = 28  # B200 extension: Rabenseifner AllReduce, a buffer + mbarrier per round
@@ -140,7 +143,18 @@ EXTENSIONS = {
     (Op.BROADCAST, Alg.DIRECT_PUSH): "broadcast__direct_push (B200 extension)",
     (Op.BROADCAST, Alg.DIRECT_PULL): "broadcast__direct_pull (B200 extension)",
     (Op.BROADCAST, Alg.BINOMIAL): "broadcast__binomial (B200 extension)",
+    (Op.REDUCE, Alg.DIRECT_PUSH): "reduce__direct_push (B200 extension)",
+    (Op.REDUCE, Alg.DIRECT_PULL): "reduce__direct_pull (B200 extension)",
+    (Op.REDUCE, Alg.BINOMIAL): "reduce__binomial (B200 extension)",
+    (Op.GATHER, Alg.DIRECT_PUSH): "gather__direct_push (B200 extension)",
+    (Op.GATHER, Alg.DIRECT_PULL): "gather__direct_pull (B200 extension)",
+    (Op.GATHER, Alg.BINOMIAL): "gather__binomial (B200 extension)",
+    (Op.SCATTER, Alg.DIRECT_PUSH): "scatter__direct_push (B200 extension)",
+    (Op.SCATTER, Alg.DIRECT_PULL): "scatter__direct_pull (B200 extension)",
+    (Op.SCATTER, Alg.BINOMIAL): "scatter__binomial (B200 extension)",
 }
+# Ops whose collective writes rank 0's out block only (the other ranks' out blocks keep their contents).
+ROOT_OUT_ONLY = (Op.REDUCE, Op.GATHER)
 
 
 class DecoderParams(ctypes.Structure):
@@ -270,24 +284,27 @@ def _ok(status, what):
 
 
 # ----------------------------------------------------------------------------------- layouts
+_ONE_BLOCK_PAYLOAD = (Op.ALLREDUCE, Op.BROADCAST, Op.REDUCE)   # P = M * sizeof(T); the other ops P = N * M * sizeof(T)
+
+
 def msg_elems(op, n, bytes_per_cta, dtype):
     """M (elements per rank block) of payload P (nccl-tests convention, main.cu:97)."""
-    unit = ELEM_BYTES[Dtype(dtype)] * (1 if Op(op) in (Op.ALLREDUCE, Op.BROADCAST) else n)
+    unit = ELEM_BYTES[Dtype(dtype)] * (1 if Op(op) in _ONE_BLOCK_PAYLOAD else n)
     if bytes_per_cta % unit:
         raise ValueError(f"payload {bytes_per_cta} B is not a multiple of {unit} B")
     return bytes_per_cta // unit
 
 
 def payload_bytes(op, n, m, dtype):
-    return m * ELEM_BYTES[Dtype(dtype)] * (1 if Op(op) == Op.ALLREDUCE else n)
+    return m * ELEM_BYTES[Dtype(dtype)] * (1 if Op(op) in _ONE_BLOCK_PAYLOAD else n)
 
 
 def in_elems_per_rank(op, n, m):
-    return m if Op(op) in (Op.ALLREDUCE, Op.ALLGATHER, Op.BROADCAST) else n * m
+    return m if Op(op) in (Op.ALLREDUCE, Op.ALLGATHER, Op.BROADCAST, Op.REDUCE, Op.GATHER) else n * m
 
 
 def out_elems_per_rank(op, n, m):
-    return m if Op(op) in (Op.ALLREDUCE, Op.REDUCESCATTER, Op.BROADCAST) else n * m
+    return m if Op(op) in (Op.ALLREDUCE, Op.REDUCESCATTER, Op.BROADCAST, Op.REDUCE, Op.SCATTER) else n * m
 
 
 def algorithms(op):

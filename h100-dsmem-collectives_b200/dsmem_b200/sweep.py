@@ -30,9 +30,11 @@ from . import (CATALOGUE, CLUSTER_SIZES, EXTENSIONS, STAMPS_PER_RANK, Alg, Dtype
 PAYLOADS = [256 << k for k in range(10)] + [196608]
 BUS = {Op.ALLREDUCE: lambda n: 2 * (n - 1) / n, Op.ALLGATHER: lambda n: (n - 1) / n,
        Op.REDUCESCATTER: lambda n: (n - 1) / n, Op.ALLTOALL: lambda n: (n - 1) / n,
-       Op.BROADCAST: lambda n: 1.0}   # nccl-tests: broadcast busbw = algbw
+       Op.BROADCAST: lambda n: 1.0, Op.REDUCE: lambda n: 1.0,   # nccl-tests: broadcast / reduce busbw = algbw
+       Op.GATHER: lambda n: (n - 1) / n, Op.SCATTER: lambda n: (n - 1) / n}
 OP_NAMES = {Op.ALLREDUCE: "allreduce", Op.ALLGATHER: "allgather", Op.REDUCESCATTER: "reducescatter",
-            Op.ALLTOALL: "alltoall", Op.BROADCAST: "broadcast"}
+            Op.ALLTOALL: "alltoall", Op.BROADCAST: "broadcast", Op.REDUCE: "reduce", Op.GATHER: "gather",
+            Op.SCATTER: "scatter"}
 DT_NAMES = {Dtype.F32: "f32", Dtype.BF16: "bf16", Dtype.I32: "i32"}
 ALG_NAMES = {a: (a.name.lower() if a != Alg.MESH_2D else "2d_mesh") for a in Alg}   # dsmem_alg_name()
 # (op, alg) with a pipelined or streamed driver: they also run payloads whose one-piece buffers exceed shared memory
@@ -151,7 +153,7 @@ def main(argv=None):
     ap.add_argument("--out-json", default="sweep_b200.json")
     ap.add_argument("--dtype", default="f32", choices=["f32", "bf16", "i32", "all"])
     ap.add_argument("--reps", type=int, default=60)
-    ap.add_argument("--ops", default="all", help="comma list of allreduce,allgather,reducescatter,alltoall")
+    ap.add_argument("--ops", default="all", help="comma list of allreduce,allgather,reducescatter,alltoall,broadcast,reduce,gather,scatter")
     ap.add_argument("--merge", default=None, help="existing table: keep its lines for the (op, dtype) not swept")
     ap.add_argument("--batch-mib", type=int, default=256, help="input MiB of each batch-regime launch (at least)")
     ap.add_argument("--regime", default="both", choices=["both", "single"],

@@ -67,6 +67,12 @@ def dsmem_bytes(op, alg, n, p, dtype):
                                    Alg.SHIFT, Alg.DIRECT_PULL) else None
     if op == Op.BROADCAST:
         return (n - 1) * blk if alg in (Alg.DIRECT_PUSH, Alg.DIRECT_PULL, Alg.BINOMIAL) else None
+    if op in (Op.REDUCE, Op.GATHER, Op.SCATTER):
+        if alg in (Alg.DIRECT_PUSH, Alg.DIRECT_PULL) or (op == Op.REDUCE and alg == Alg.BINOMIAL):
+            return (n - 1) * blk   # every non-root block crosses once (a reduce tree sends one partial per rank)
+        if alg == Alg.BINOMIAL:
+            return (n // 2) * lg * blk   # each round moves N/2 blocks (gather up, or scatter down, the tree)
+        return None
     return None
 
 

@@ -56,7 +56,18 @@ typedef enum {
     DSMEM_OP_ALLTOALL = 3,
     /* B200 extension, no reference file: broadcast of rank 0's vector (M elements per rank in and out;
      * P = M * sizeof(T) as for allreduce), algorithms DIRECT_PUSH, DIRECT_PULL and BINOMIAL. */
-    DSMEM_OP_BROADCAST = 4
+    DSMEM_OP_BROADCAST = 4,
+    /* B200 extensions, no reference file: the other collectives rooted at rank 0, algorithms DIRECT_PUSH,
+     * DIRECT_PULL and BINOMIAL each.
+     *   REDUCE   in M elements per rank, out M per rank; rank 0's out = op over the ranks' vectors (P = M *
+     *            sizeof(T), as for allreduce). The other ranks' out blocks are not written.
+     *   GATHER   in M per rank, out N * M per rank; rank 0's out = the ranks' vectors in rank order (P = N * M *
+     *            sizeof(T), as for allgather). The other ranks' out blocks are not written.
+     *   SCATTER  in N * M per rank, of which only rank 0's is read; out M per rank: rank r gets block r of rank
+     *            0's input (P = N * M * sizeof(T), as for reducescatter). */
+    DSMEM_OP_REDUCE = 5,
+    DSMEM_OP_GATHER = 6,
+    DSMEM_OP_SCATTER = 7
 } dsmem_op;
 
 /* The <alg> component of the reference file names collectives/<op>__<alg>__<src>.cu
@@ -77,10 +88,10 @@ typedef enum {
     DSMEM_ALG_2D_MESH = 12,                           /* allreduce                               */
     DSMEM_ALG_DIRECT_SHIFT = 13,                      /* allgather                               */
     DSMEM_ALG_BRUCK = 14,                             /* allgather, alltoall                     */
-    DSMEM_ALG_DIRECT_PULL = 15,                       /* allgather, reducescatter, alltoall      */
+    DSMEM_ALG_DIRECT_PULL = 15,                       /* allgather, reducescatter, alltoall, rooted */
     DSMEM_ALG_GATHER_BCAST_BINOMIAL = 16,             /* allgather                               */
     DSMEM_ALG_RECURSIVE_HALVING = 17,                 /* reducescatter                           */
-    DSMEM_ALG_DIRECT_PUSH = 18,                       /* reducescatter, alltoall                 */
+    DSMEM_ALG_DIRECT_PUSH = 18,                       /* reducescatter, alltoall, rooted         */
     DSMEM_ALG_PAIRWISE_EXCHANGE = 19,                 /* alltoall (N = 2)                        */
     DSMEM_ALG_PAIRWISE_XOR = 20,                      /* alltoall                                */
     DSMEM_ALG_SHIFT = 21,                             /* alltoall                                */
@@ -92,7 +103,7 @@ typedef enum {
      * variants the reference defers, collectives/ROADMAP.md:38-45); same arithmetic as the originals. */
     DSMEM_ALG_RING_CREDIT = 23,                       /* allreduce (N <= 8), allgather, reducescatter */
     DSMEM_ALG_RECURSIVE_DOUBLING_CREDIT = 24,         /* allreduce, allgather                    */
-    DSMEM_ALG_BINOMIAL = 25,                          /* broadcast                               */
+    DSMEM_ALG_BINOMIAL = 25,                          /* broadcast, reduce, gather, scatter      */
     DSMEM_ALG_BRUCK_CREDIT = 26,                      /* allgather, alltoall                     */
     DSMEM_ALG_RECURSIVE_HALVING_CREDIT = 27,          /* reducescatter                           */
     /* B200 extensions, no reference file: more of the deferred mbarrier-credit forms (same rounds, partners
@@ -141,8 +152,9 @@ dsmem_status dsmem_collective_launch_ex(dsmem_op op, dsmem_alg alg, dsmem_dtype 
  * works, slower), laid out as for dsmem_collective_launch; on return out holds the results. The batch streams
  * through double-buffered device staging in chunks of chunk_clusters problems (0: about 64 MiB per chunk):
  * the host-to-device copy of chunk i+1, the collective on chunk i and the device-to-host copy of chunk i-1
- * overlap on three streams. AUTO is resolved once for the whole batch. Device errors as dsmem_check. The
- * host-side counterpart of the reference harness's reference() on host arrays (main.cu:129-149). */
+ * overlap on three streams. AUTO is resolved once for the whole batch. Device errors as dsmem_check. For
+ * REDUCE and GATHER only rank 0's out block of each problem is copied back; the other blocks of out keep their
+ * contents. The host-side counterpart of the reference harness's reference() on host arrays (main.cu:129-149). */
 dsmem_status dsmem_collective_host(dsmem_op op, dsmem_alg alg, dsmem_dtype dtype, int cluster_size,
                                    size_t bytes_per_cta, const void* host_in, void* host_out, long long num_clusters,
                                    long long chunk_clusters);

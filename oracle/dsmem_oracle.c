@@ -135,20 +135,44 @@ void orc_fill_normal(int dtype, void* buf, size_t n, uint64_t seed, double mean,
 
 /* ------------------------------------------------------------------ reference */
 size_t orc_in_elems(int op, int n, size_t m) {
-    return (op == ORC_ALLREDUCE || op == ORC_ALLGATHER || op == ORC_BROADCAST) ? m : (size_t)n * m;
+    return (op == ORC_ALLREDUCE || op == ORC_ALLGATHER || op == ORC_BROADCAST || op == ORC_REDUCE || op == ORC_GATHER)
+               ? m
+               : (size_t)n * m;
 }
 size_t orc_out_elems(int op, int n, size_t m) {
-    return (op == ORC_ALLREDUCE || op == ORC_REDUCESCATTER || op == ORC_BROADCAST) ? m : (size_t)n * m;
+    return (op == ORC_ALLREDUCE || op == ORC_REDUCESCATTER || op == ORC_BROADCAST || op == ORC_REDUCE ||
+            op == ORC_SCATTER)
+               ? m
+               : (size_t)n * m;
 }
 
-/* main.cu:129-149, one problem per cluster c (offsets c*N*in_elems / c*N*out_elems). */
+/* main.cu:129-149, one problem per cluster c (offsets c*N*in_elems / c*N*out_elems). The rooted extensions:
+ * REDUCE gives rank 0 the sum of the ranks' vectors, GATHER gives rank 0 the ranks' vectors in rank order, and
+ * the other ranks' out blocks of both are not written by the collective (0 here: a test compares them with the
+ * output's contents before the call); SCATTER gives rank b block b of rank 0's input. */
 void orc_reference(int op, int dtype, int n, size_t m, long long clusters, const void* in, double* ref) {
     const size_t ie = orc_in_elems(op, n, m), oe = orc_out_elems(op, n, m);
     for (long long c = 0; c < clusters; ++c) {
         const size_t ib = (size_t)c * n * ie, ob = (size_t)c * n * oe;
         for (int b = 0; b < n; ++b)
             for (size_t i = 0; i < m; ++i) {
-                if (op == ORC_ALLREDUCE) {
+                if (op == ORC_REDUCE || op == ORC_GATHER) {
+                    if (b != 0) {   /* not written */
+                        for (int r = 0; r < (op == ORC_GATHER ? n : 1); ++r) ref[ob + (size_t)b * oe + (size_t)r * m + i] = 0.0;
+                    } else if (op == ORC_GATHER) {
+                        for (int r = 0; r < n; ++r) ref[ob + (size_t)r * m + i] = load_elem(dtype, in, ib + (size_t)r * m + i);
+                    } else if (dtype == ORC_I32) {
+                        long long s = 0;
+                        for (int r = 0; r < n; ++r) s += ((const int32_t*)in)[ib + (size_t)r * m + i];
+                        ref[ob + i] = (double)s;
+                    } else {
+                        double s = 0;
+                        for (int r = 0; r < n; ++r) s += load_elem(dtype, in, ib + (size_t)r * m + i);
+                        ref[ob + i] = s;
+                    }
+                } else if (op == ORC_SCATTER) {   /* block b of rank 0's input */
+                    ref[ob + (size_t)b * m + i] = load_elem(dtype, in, ib + (size_t)b * m + i);
+                } else if (op == ORC_ALLREDUCE) {
                     if (dtype == ORC_I32) {
                         long long s = 0;
                         for (int r = 0; r < n; ++r) s += ((const int32_t*)in)[ib + (size_t)r * m + i];

@@ -24,7 +24,11 @@ extern "C" {
 #endif
 
 enum { ORC_F32 = 0, ORC_BF16 = 1, ORC_I32 = 2 };
-enum { ORC_ALLREDUCE = 0, ORC_ALLGATHER = 1, ORC_REDUCESCATTER = 2, ORC_ALLTOALL = 3, ORC_BROADCAST = 4 };
+/* 4..7 are B200 extensions with no reference file (rooted at rank 0): broadcast, reduce, gather, scatter. */
+enum {
+    ORC_ALLREDUCE = 0, ORC_ALLGATHER = 1, ORC_REDUCESCATTER = 2, ORC_ALLTOALL = 3, ORC_BROADCAST = 4, ORC_REDUCE = 5,
+    ORC_GATHER = 6, ORC_SCATTER = 7
+};
 
 /* mt19937_64 (Matsumoto & Nishimura 2000), the engine of the reference's pattern B. */
 typedef struct {

@@ -17,6 +17,7 @@ LIB = HERE / "_build" / "liboracle.so"
 F32, BF16, I32 = 0, 1, 2
 ALLREDUCE, ALLGATHER, REDUCESCATTER, ALLTOALL = 0, 1, 2, 3
 BROADCAST = 4   # B200 extension: rank 0's vector to every rank (no reference file)
+REDUCE, GATHER, SCATTER = 5, 6, 7   # B200 extensions rooted at rank 0 (no reference file)
 NP_DTYPE = {F32: np.float32, BF16: np.uint16, I32: np.int32}  # bf16 carried as raw uint16 bits
 
 _lib = None
@@ -77,11 +78,21 @@ def _p(a):
 
 
 def in_elems(op, n, m):
-    return m if op in (ALLREDUCE, ALLGATHER, BROADCAST) else n * m
+    return m if op in (ALLREDUCE, ALLGATHER, BROADCAST, REDUCE, GATHER) else n * m
 
 
 def out_elems(op, n, m):
-    return m if op in (ALLREDUCE, REDUCESCATTER, BROADCAST) else n * m
+    return m if op in (ALLREDUCE, REDUCESCATTER, BROADCAST, REDUCE, SCATTER) else n * m
+
+
+def written(op, n, m, clusters):
+    """Boolean mask over a batch's output: the elements the collective writes. REDUCE and GATHER write rank 0's out
+    block of each problem only (the other blocks keep their contents); every other op writes every element."""
+    oe = out_elems(op, n, m)
+    mask = np.ones(clusters * n * oe, dtype=bool)
+    if op in (REDUCE, GATHER):
+        mask.reshape(clusters, n, oe)[:, 1:, :] = False
+    return mask
 
 
 def pattern_a(dtype, count):

@@ -130,6 +130,36 @@ def test_legality_and_smem_match_reference_matrix(dsmem):
     assert checked > 2000
 
 
+def test_rooted_ops_legality_smem_and_names(dsmem):
+    """The rooted extensions (no reference file): names, payload convention (Reduce P = M B, Gather and Scatter
+    P = N M B), legality (16-byte rank blocks) and the window each algorithm declares, sized for rank 0's
+    buffers; AUTO's built-in order prefers the direct push where it fits."""
+    L, O, A = dsmem.lib(), dsmem.Op, dsmem.Alg
+    assert [L.dsmem_op_name(int(o)) for o in (O.REDUCE, O.GATHER, O.SCATTER)] == [b"reduce", b"gather", b"scatter"]
+    lg = {2: 1, 4: 2, 8: 3, 16: 4}
+    window = {  # elements of the window, from N and M
+        (O.REDUCE, A.DIRECT_PUSH): lambda n, m: n * m, (O.REDUCE, A.DIRECT_PULL): lambda n, m: m,
+        (O.REDUCE, A.BINOMIAL): lambda n, m: (1 + lg[n]) * m,
+        **{(o, a): (lambda n, m: n * m) for o in (O.GATHER, O.SCATTER) for a in (A.DIRECT_PUSH, A.DIRECT_PULL, A.BINOMIAL)},
+    }
+    for (op, alg), win in window.items():
+        assert (op, alg) in dsmem.EXTENSIONS
+        for dt in dsmem.Dtype:
+            b = dsmem.ELEM_BYTES[dt]
+            for n in dsmem.CLUSTER_SIZES:
+                for p in PAYLOADS:
+                    unit = b * (1 if op == O.REDUCE else n)
+                    status, smem, legal = dsmem.query(op, alg, dt, n, p)
+                    m = p // unit
+                    if p % unit or (m * b) % 16:
+                        assert status == dsmem.Status.ILLEGAL_CONFIG and not legal, (op, alg, dt, n, p)
+                        continue
+                    assert smem == 128 + win(n, m) * b, (op.name, alg.name, dt.name, n, p, smem)
+                    assert status == (dsmem.Status.OK if smem <= SMEM_LIMIT else dsmem.Status.SMEM_LIMIT)
+    empty_pick = dsmem.autotune_pick(O.GATHER, dsmem.Dtype.F32, 8, 16384)
+    assert empty_pick in (A.DIRECT_PUSH, A.DIRECT_PULL, A.BINOMIAL)
+
+
 def test_auto_defaults_and_table(dsmem, tmp_path):
     Op, Alg, Dt = dsmem.Op, dsmem.Alg, dsmem.Dtype
     empty = tmp_path / "empty.txt"
@@ -196,7 +226,8 @@ def test_shipped_autotune_table_parses(dsmem, tmp_path):
         assert lines
         ops = {"allreduce": dsmem.Op.ALLREDUCE, "allgather": dsmem.Op.ALLGATHER,
                "reducescatter": dsmem.Op.REDUCESCATTER, "alltoall": dsmem.Op.ALLTOALL,
-               "broadcast": dsmem.Op.BROADCAST}
+               "broadcast": dsmem.Op.BROADCAST, "reduce": dsmem.Op.REDUCE, "gather": dsmem.Op.GATHER,
+               "scatter": dsmem.Op.SCATTER}
         dts = {"f32": dsmem.Dtype.F32, "bf16": dsmem.Dtype.BF16, "i32": dsmem.Dtype.I32}
         pipelined = {(dsmem.Op.ALLREDUCE, dsmem.Alg.TWO_SHOT_PUSH), (dsmem.Op.ALLREDUCE, dsmem.Alg.RS_PUSH_GLOBAL_AG),
                      (dsmem.Op.REDUCESCATTER, dsmem.Alg.DIRECT_PUSH), (dsmem.Op.ALLTOALL, dsmem.Alg.DIRECT_PUSH),

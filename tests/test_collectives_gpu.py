@@ -7,8 +7,9 @@ For each (op, alg, N) of the catalogue and each dtype, payloads P in {smallest l
     rtol 1e-5 (f32) and 1e-2 (bf16); f32 also within the unscaled 1e-5 * (1 + |ref|); for bf16 the factor is
     the algorithm's chain of bf16 roundings where that is longer (rings: N - 1 hops; bf16_chain);
   * seeded U[-2^15, 2^15) int32: exact;
-  * AllGather / AlltoAll: exact for every input.
-Outputs are poisoned (all-ones bits) before each launch, so an element the kernel never wrote fails.
+  * AllGather / AlltoAll (and the rooted Broadcast, Gather and Scatter): exact for every input.
+Outputs are poisoned (all-ones bits) before each launch, so an element the kernel never wrote fails; for the
+rooted Reduce and Gather, which write rank 0's out block only, the other ranks' blocks must still hold the poison.
 """
 import math
 
@@ -39,6 +40,9 @@ def _torch_to_np(t, dt):
 
 
 ORC_DT = {D.Dtype.F32: 0, D.Dtype.BF16: 1, D.Dtype.I32: 2}
+EXACT_OPS = (D.Op.ALLGATHER, D.Op.ALLTOALL, D.Op.BROADCAST, D.Op.GATHER, D.Op.SCATTER)   # pure data movement
+# the poison of run_case's outputs, as the bits _torch_to_np returns them
+POISON = {D.Dtype.BF16: (np.uint16, 0xFFFF), D.Dtype.F32: (np.uint32, 0xFFFFFFFF), D.Dtype.I32: (np.int32, 2 ** 31 - 1)}
 RTOL = {D.Dtype.F32: 1e-5, D.Dtype.BF16: 1e-2}
 
 
@@ -80,7 +84,13 @@ def run_case(torch, orc, op, alg, n, dt, p, clusters, pattern, seed=0):
     D.check()
     got = _torch_to_np(tout, dt)
     ref = orc.reference(int(op), ORC_DT[dt], n, m, clusters, host)
-    exact = pattern == "A" or dt == D.Dtype.I32 or op in (D.Op.ALLGATHER, D.Op.ALLTOALL, D.Op.BROADCAST)
+    if op in D.ROOT_OUT_ONLY:   # only rank 0's out blocks are written: the others keep the poison
+        mask = orc.written(int(op), n, m, clusters)
+        kind, bits = POISON[dt]
+        untouched = got[~mask].view(kind)
+        assert (untouched == bits).all(), f"{int((untouched != bits).sum())} elements of non-root out blocks written"
+        got, ref = got[mask], ref[mask]
+    exact = pattern == "A" or dt == D.Dtype.I32 or op in EXACT_OPS
     if exact:
         bad, ma, mr = orc.check(ORC_DT[dt], got, ref, 0)
         assert bad == 0, f"{bad} inexact elements (max abs {ma})"

@@ -74,3 +74,28 @@ def test_broadcast_reference_is_rank0_vector(orc):
         for b in range(n):
             got = ref[(c * n + b) * m:(c * n + b + 1) * m]
             assert (got == inp[c * n * m:c * n * m + m]).all()
+
+
+def test_rooted_references(orc):
+    """The rooted restatements (B200 extension ops 5-7): REDUCE gives rank 0 the sum of the ranks' vectors,
+    GATHER gives rank 0 the vectors in rank order, and neither writes the other ranks' out blocks (written()
+    marks them); SCATTER gives rank b block b of rank 0's input. Per cluster, int32 exact and f32."""
+    n, m, clusters = 4, 8, 3
+    for dt in (0, 2):
+        for op in (orc.REDUCE, orc.GATHER, orc.SCATTER):
+            ie, oe = orc.in_elems(op, n, m), orc.out_elems(op, n, m)
+            count = clusters * n * ie
+            inp = (orc.uniform_int(count, 5, -1000, 1000) if dt == 2 else orc.uniform_real(0, count, 5, -1.0, 1.0))
+            ref = orc.reference(op, dt, n, m, clusters, inp).reshape(clusters, n, oe)
+            x = inp.astype(np.float64).reshape(clusters, n, ie)
+            mask = orc.written(op, n, m, clusters).reshape(clusters, n, oe)
+            if op == orc.REDUCE:
+                assert np.allclose(ref[:, 0], x.sum(axis=1), rtol=0, atol=1e-12)
+            elif op == orc.GATHER:
+                assert np.array_equal(ref[:, 0], x.reshape(clusters, n * m))
+            else:
+                assert np.array_equal(ref, x[:, 0].reshape(clusters, n, m))
+            if op == orc.SCATTER:
+                assert mask.all()
+            else:
+                assert mask[:, 0].all() and not mask[:, 1:].any()

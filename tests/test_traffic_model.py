@@ -43,11 +43,32 @@ def replay(op, alg, n, blk):
         moves += [n * blk] * (n - 1)   # broadcast of the full buffer
     elif (op, alg) == (D.Op.BROADCAST, D.Alg.BINOMIAL):
         moves += [blk] * (n - 1)
+    elif (op, alg) == (D.Op.REDUCE, D.Alg.BINOMIAL):
+        d = 1
+        while d < n:   # ranks with r mod 2d == d send their one-block partial to r - d
+            moves += [blk for r in range(n) if r % (2 * d) == d]
+            d *= 2
+    elif (op, alg) == (D.Op.GATHER, D.Alg.BINOMIAL):
+        d = 1
+        while d < n:   # ranks with r mod 2d == d send the d blocks they hold to r - d
+            moves += [d * blk for r in range(n) if r % (2 * d) == d]
+            d *= 2
+    elif (op, alg) == (D.Op.SCATTER, D.Alg.BINOMIAL):
+        held = {0: n}   # rank -> blocks it holds (ranks r .. r + held - 1)
+        d = n // 2
+        while d >= 1:   # ranks holding 2d blocks send the upper d to r + d
+            for r in [r for r, h in held.items() if h == 2 * d]:
+                moves.append(d * blk)
+                held[r], held[r + d] = d, d
+            d //= 2
+        assert sorted(held) == list(range(n)) and all(h == 1 for h in held.values())
     return sum(moves)
 
 
 @pytest.mark.parametrize("op,alg", [(D.Op.ALLREDUCE, D.Alg.RABENSEIFNER), (D.Op.ALLTOALL, D.Alg.BRUCK),
-                                    (D.Op.ALLGATHER, D.Alg.GATHER_BCAST_BINOMIAL), (D.Op.BROADCAST, D.Alg.BINOMIAL)])
+                                    (D.Op.ALLGATHER, D.Alg.GATHER_BCAST_BINOMIAL), (D.Op.BROADCAST, D.Alg.BINOMIAL),
+                                    (D.Op.REDUCE, D.Alg.BINOMIAL), (D.Op.GATHER, D.Alg.BINOMIAL),
+                                    (D.Op.SCATTER, D.Alg.BINOMIAL)])
 @pytest.mark.parametrize("n", D.CLUSTER_SIZES)
 def test_model_matches_replayed_schedule(op, alg, n):
     p = 16384
@@ -65,6 +86,9 @@ def test_model_per_cta_figures_at_n8_16k():
     assert per_cta(D.Op.ALLREDUCE, D.Alg.ONE_SHOT_PULL) == (n - 1) * p
     for op in (D.Op.ALLGATHER, D.Op.REDUCESCATTER, D.Op.ALLTOALL):   # P = N M B: (N-1)/N P per CTA
         assert per_cta(op, D.Alg.DIRECT_PULL) == (n - 1) / n * p
+    # rooted: every non-root block crosses once; Reduce P = M B, Gather / Scatter P = N M B
+    assert per_cta(D.Op.REDUCE, D.Alg.DIRECT_PUSH) == (n - 1) / n * p
+    assert per_cta(D.Op.GATHER, D.Alg.DIRECT_PUSH) == per_cta(D.Op.SCATTER, D.Alg.DIRECT_PULL) == (n - 1) / n ** 2 * p
 
 
 def test_model_covers_every_registered_algorithm():
