@@ -461,9 +461,10 @@ def decoder_extras(torch, hbm_peak):
 
 def tp_check(torch, rank, world, ctx, tokens, hidden, cluster, x, w):
     """The fused call's result at 64 tokens (the one-shot form) and 1,024 (the two-shot) against the CPU oracle:
-    y = RMSNorm(sum of every rank's x) * w without a residual, from a NaN-filled output; every rank's y gathered
-    to rank 0, which checks them bit-identical and within 1e-2 * (1 + |ref|) (bf16 output). Every rank takes the
-    same steps; None at other token counts and on ranks other than 0."""
+    y = RMSNorm(sum of every rank's x) * w without a residual, from a NaN-filled output (w is the same on every
+    rank, as in a TP layer); every rank's y gathered to rank 0, which checks them bit-identical and within
+    1e-2 * (1 + |ref|) (bf16 output). Every rank takes the same steps; None at other token counts and on ranks
+    other than 0."""
     if tokens not in (64, 1024):
         return None
     import numpy as np

@@ -3,7 +3,8 @@
     torchrun --nnodes 1 --nproc-per-node 2 --master-addr 127.0.0.1 -m dsmem_b200.tp_bench
 
 (run from the package directory, or with it on PYTHONPATH). Per rank: bf16 x [T x 8192] ~ N(0,1) with
-seed + rank, residual and w ~ N(1, 0.02), eps 1e-6, cluster 8, T in {1, 64, 1024, 8192}. For each T:
+seed + rank; the residual ~ N(0,1) and w ~ N(1, 0.02) from one seed shared by every rank (a TP layer's
+normalisation weight and residual stream are replicated); eps 1e-6, cluster 8, T in {1, 64, 1024, 8192}. For each T:
   fused          dsmem_tp_allreduce_rmsnorm with x already in the context's x region and y left in its y
                  region (the zero-copy use: a producer writes x there, a consumer reads y there), the form the
                  context's default one-shot limit picks;
@@ -57,16 +58,18 @@ def run(tokens=TOKENS, hidden=HIDDEN, cluster=8, reps=20, rounds=5, warmup=5, on
     rank, world = dist.get_rank(), dist.get_world_size()
     dev = torch.device("cuda", torch.cuda.current_device())
     gen = torch.Generator(device=dev)
-    gen.manual_seed(1234 + rank)
+    gen.manual_seed(1234 + rank)      # x: each rank's own
+    shared = torch.Generator(device=dev)
+    shared.manual_seed(4321)          # w and the residual: the same on every rank (drawn in the same order)
     tmax = max(tokens)
     ctx = T.TPContext(T.tp_bytes(tmax, hidden))
     comm = T.NcclComm()
-    w = (1 + 0.02 * torch.randn(hidden, device=dev, generator=gen)).to(torch.bfloat16)
+    w = (1 + 0.02 * torch.randn(hidden, device=dev, generator=shared)).to(torch.bfloat16)
     out = {}
     try:
         for t in tokens:
             x = torch.randn(t, hidden, device=dev, generator=gen).to(torch.bfloat16)
-            res = torch.randn(t, hidden, device=dev, generator=gen).to(torch.bfloat16)
+            res = torch.randn(t, hidden, device=dev, generator=shared).to(torch.bfloat16)
             y = torch.empty_like(x)
             xb, yb = ctx.buffers(t, hidden)
             xb.copy_(x)
