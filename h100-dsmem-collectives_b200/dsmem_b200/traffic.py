@@ -12,6 +12,8 @@ msg_elems), "sent once to every peer" is (N-1) M B per CTA.
         consumer kernels (RMSNorm, top-k, the TP kernel emulated on one GPU); meant to run under
         ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum,
               l1tex__m_l1tex2xbar_write_bytes_mem_dshared.sum,l1tex__m_xbar2l1tex_read_bytes_mem_dshared.sum
+    python -m dsmem_b200.traffic run --ops reduce,gather,scatter --every-alg --out cases.json
+        the same for the named ops only, every legal algorithm (no consumers)
     python -m dsmem_b200.traffic summarize --cases cases.json --ncu launches.csv [--peaks peaks.json]
         pairs the captured launches with the cases (in order) and prints the markdown table of profiles/.
 """
@@ -89,15 +91,27 @@ CAPTURE_SIZES = (2, 4, 8, 16)
 CAPTURE_PAYLOADS = (16384, 65536)
 
 
-def cases():
-    """The captured configurations, in launch order."""
+def cases(ops=None, every_alg=False):
+    """The captured configurations, in launch order: the AUTO batch pick of each (op, N, P) of CAPTURE_OPS, the
+    two-shot beside it, and the consumers; with `ops`, the collectives of those ops only (no consumers), and with
+    `every_alg`, every registered algorithm legal at that (N, P) instead of AUTO's pick."""
+    from . import CATALOGUE, EXTENSIONS, Status, query
+
     out = []
-    for op in CAPTURE_OPS:
+    for op in (ops or CAPTURE_OPS):
         for n in CAPTURE_SIZES:
             for p in CAPTURE_PAYLOADS:
-                alg = autotune_pick(op, Dtype.F32, n, p, num_clusters=64)
-                if alg != Alg.AUTO:
-                    out.append({"kind": "collective", "op": op.name, "alg": alg.name, "n": n, "p": p, "dtype": "F32"})
+                if every_alg:
+                    algs = [a for (o, a) in list(CATALOGUE) + list(EXTENSIONS)
+                            if o == op and query(op, a, Dtype.F32, n, p)[0] == Status.OK]
+                else:
+                    algs = [autotune_pick(op, Dtype.F32, n, p, num_clusters=64)]
+                for alg in algs:
+                    if alg != Alg.AUTO:
+                        out.append({"kind": "collective", "op": op.name, "alg": alg.name, "n": n, "p": p,
+                                    "dtype": "F32"})
+    if ops:
+        return out
     for n in (8, 16):   # the DSMEM-bound two-shot beside the HBM-bound pick, for the SM-to-SM fraction
         c = {"kind": "collective", "op": "ALLREDUCE", "alg": "TWO_SHOT_PUSH", "n": n, "p": 65536, "dtype": "F32"}
         if c not in out:
@@ -108,14 +122,14 @@ def cases():
     return out
 
 
-def run(problems=64, out=None):
+def run(problems=64, out=None, ops=None, every_alg=False):
     """Launch every case once (a synchronisation between cases), recording the list."""
     import torch
 
     from . import collective, in_elems_per_rank, out_elems_per_rank, rmsnorm, tp_emulate, topk
 
     torch.cuda.set_device(0)
-    todo = cases()
+    todo = cases(ops, every_alg)
     for c in todo:
         if c["kind"] == "collective":
             op, alg, n, p = Op[c["op"]], Alg[c["alg"]], c["n"], c["p"]
@@ -164,7 +178,7 @@ def _ncu_rows(path):
     for r in csv.DictReader(lines):
         name = r.get("Kernel Name", "")
         if not (name.startswith("void dsb::") or "dsmem" in name or "rmsnorm" in name or "topk" in name
-                or "tp_allreduce" in name or "rowwise" in name):
+                or "tp_allreduce" in name or "rowwise" in name or "batch_kernel" in name or "_kernel<" in name):
             continue
         key = int(r["ID"])
         v = float(r["Metric Value"].replace(",", ""))
@@ -206,13 +220,16 @@ def main(argv=None):
     r = sub.add_parser("run")
     r.add_argument("--out", default="traffic_cases.json")
     r.add_argument("--problems", type=int, default=64)
+    r.add_argument("--ops", default=None, help="comma list of op names (e.g. reduce,gather,scatter): those ops only")
+    r.add_argument("--every-alg", action="store_true", help="every legal algorithm, not only AUTO's batch pick")
     s = sub.add_parser("summarize")
     s.add_argument("--cases", required=True)
     s.add_argument("--ncu", required=True)
     s.add_argument("--peaks", default=None)
     a = ap.parse_args(argv)
     if a.cmd == "run":
-        todo = run(a.problems, a.out)
+        ops = tuple(Op[o.upper()] for o in a.ops.split(",")) if a.ops else None
+        todo = run(a.problems, a.out, ops, a.every_alg)
         print(f"{len(todo)} cases launched -> {a.out}")
     else:
         peaks = json.load(open(a.peaks)) if a.peaks else None
