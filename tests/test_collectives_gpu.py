@@ -66,7 +66,7 @@ def make_input(orc, dt, count, pattern, seed):
     return orc.uniform_real(odt, count, seed, -1.0, 1.0)
 
 
-def run_case(torch, orc, op, alg, n, dt, p, clusters, pattern, seed=0):
+def run_case(torch, orc, op, alg, n, dt, p, clusters, pattern, seed=0, max_resident_clusters=0):
     m = D.msg_elems(op, n, p, dt)
     nin = clusters * n * D.in_elems_per_rank(op, n, m)
     nout = clusters * n * D.out_elems_per_rank(op, n, m)
@@ -80,7 +80,7 @@ def run_case(torch, orc, op, alg, n, dt, p, clusters, pattern, seed=0):
         tout = torch.full((nout,), -1, dtype=torch.int32, device="cuda").view(tdt)
     else:
         tout = torch.full((nout,), 2 ** 31 - 1, dtype=torch.int32, device="cuda")
-    D.collective(op, alg, tin, tout, n, p)
+    D.collective(op, alg, tin, tout, n, p, max_resident_clusters=max_resident_clusters)
     D.check()
     got = _torch_to_np(tout, dt)
     ref = orc.reference(int(op), ORC_DT[dt], n, m, clusters, host)
@@ -185,6 +185,28 @@ def test_resident_cap_and_repeat(cuda, orc):
             outs.append(tout.cpu().numpy())
     for o in outs[1:]:
         assert np.array_equal(o, outs[0])
+
+
+ROOTED = [(o, a) for (o, a) in D.EXTENSIONS if o in (D.Op.BROADCAST, D.Op.REDUCE, D.Op.GATHER, D.Op.SCATTER)]
+
+
+@pytest.mark.parametrize("op,alg", ROOTED, ids=[NAMES[k] for k in ROOTED])
+def test_rooted_many_problems_per_cluster(cuda, orc, op, alg):
+    """The rooted ops' persistent loop: 23 problems through 1 and 3 resident clusters (each cluster runs several
+    problems in a row, so every mbarrier goes through several phases and every buffer is reused), against the
+    oracle, f32 random and int32 exact, at N = 2, 8 and 16."""
+    failures = []
+    for n in (2, 8, 16):
+        for dt, pattern in ((D.Dtype.F32, "R"), (D.Dtype.I32, "R"), (D.Dtype.BF16, "A")):
+            p = 4096 if D.query(op, alg, dt, n, 4096)[0] == D.Status.OK else 256 * n
+            if D.query(op, alg, dt, n, p)[0] != D.Status.OK:
+                continue
+            for cap in (1, 3):
+                try:
+                    run_case(cuda, orc, op, alg, n, dt, p, 23, pattern, seed=31 * n + cap, max_resident_clusters=cap)
+                except (AssertionError, D.DsmemError) as e:
+                    failures.append(f"N={n} {dt.name} P={p} resident={cap}: {e}")
+    assert not failures, "\n".join(failures)
 
 
 def test_stamps_and_smid(cuda):
