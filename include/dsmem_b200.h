@@ -17,8 +17,11 @@
  *   ALLGATHER      in [c][b][M]            out[c][b][N][M]  (main.cu:137-138)
  *   REDUCESCATTER  in [c][b][N][M]         out[c][b][M]     (main.cu:139-142)
  *   ALLTOALL       in [c][b][N][M]         out[c][b][N][M]  (main.cu:143-145)
+ *   BROADCAST, REDUCE in [c][b][M]         out[c][b][M]     (rooted at rank 0, no reference file)
+ *   GATHER         in [c][b][M]            out[c][b][N][M]  (rooted at rank 0, no reference file)
+ *   SCATTER        in [c][b][N][M]         out[c][b][M]     (rooted at rank 0, no reference file)
  * bytes_per_cta is the nccl-tests payload P of the reference sweep (main.cu:97, driver.py:156-163):
- *   ALLREDUCE P = M * sizeof(T); every other op P = N * M * sizeof(T).
+ *   ALLREDUCE (and BROADCAST, REDUCE) P = M * sizeof(T); every other op P = N * M * sizeof(T).
  */
 #ifndef DSMEM_B200_H
 #define DSMEM_B200_H
