@@ -16,7 +16,8 @@ the whole batch (inputs 2 GiB per GPU, far larger than the 126 MB L2, so no flus
                  sources into oracle/_ref/) on all host cores for ~10 s (the C oracle port, 1 thread, if that
                  binary is absent)
     check        a strided sample of the timed batch's own output against the CPU oracle
-Extras (rank 0): configs[0]'s single-cluster latencies, configs[2]'s RMSNorm, configs[3]'s decoder layer,
+Extras (rank 0): configs[0]'s single-cluster latencies and its algorithms in a grid-filled batch (f32 and int32),
+configs[2]'s RMSNorm, configs[3]'s decoder layer,
 ceilings, and at N = 1 the row-wise and top-k consumers, each with a CPU baseline and its core count; at N > 1
 every rank also runs configs[4]'s tensor-parallel AllReduce + RMSNorm across the N GPUs, whose result at 64 and
 1,024 tokens (one-shot and two-shot forms) is checked against the CPU oracle (tokens.<T>.check).
@@ -240,6 +241,61 @@ def single_cluster_latency(torch, D, reps=200):
     return res
 
 
+def config0_batch(torch, D, hbm_peak, reps=5):
+    """configs[0]'s algorithms in a grid-filled batch: the ring and recursive-doubling AllReduce and their
+    mbarrier-credit forms, N = 8, 4,096 elements (16 KiB) per CTA, f32 U(-1,1) and int32 U[-1000, 1000], 8,192
+    problems (1 GiB of input per launch, larger than the L2). CUDA events over `reps` launches after three
+    warm-ups; a strided sample of each batch's output against the oracle (int32 bit-exact, f32 within
+    1e-5 (1 + |ref|) ceil(log2 N)). Any failure is reported in the entry instead of ending the run."""
+    from oracle import oracle as orc
+
+    n, m = 8, 4096
+    p = m * 4
+    problems = (1 << 30) // (n * p)
+    algs = (("ring", D.Alg.RING), ("recursive_doubling", D.Alg.RECURSIVE_DOUBLING),
+            ("ring_credit", D.Alg.RING_CREDIT), ("recursive_doubling_credit", D.Alg.RECURSIVE_DOUBLING_CREDIT))
+    res = {"problems": problems, "bytes_per_cta": p, "cluster_size": n,
+           "timing": f"CUDA events over {reps} launches of the whole batch, after 3 warm-ups"}
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    for dname, odt in (("f32", orc.F32), ("i32", orc.I32)):
+        try:
+            if odt == orc.F32:
+                tin = torch.rand(problems * n * m, device="cuda", generator=g) * 2 - 1
+            else:
+                tin = torch.randint(-1000, 1001, (problems * n * m,), dtype=torch.int32, device="cuda", generator=g)
+            tout = torch.empty_like(tin)
+            for name, alg in algs:
+                for _ in range(3):
+                    D.collective(D.Op.ALLREDUCE, alg, tin, tout, n, p)
+                D.check()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    D.collective(D.Op.ALLREDUCE, alg, tin, tout, n, p)
+                e1.record()
+                torch.cuda.synchronize()
+                D.check()
+                ms = e0.elapsed_time(e1) / reps
+                bad = 0
+                for q in sorted({int(i * (problems - 1) / 7) for i in range(8)}):
+                    a, b = q * n * m, (q + 1) * n * m
+                    ref = orc.reference(orc.ALLREDUCE, odt, n, m, 1, tin[a:b].cpu().numpy())
+                    got = tout[a:b].cpu().numpy()
+                    bad += (orc.check(odt, got, ref, 0)[0] if odt == orc.I32
+                            else orc.check(odt, got, ref, 1, 1e-5 * math.ceil(math.log2(n)))[0])
+                res[f"{name}_{dname}"] = {
+                    "ms": round(ms, 4), "algbw_GBps": round(problems * n * p / (ms * 1e-3) / 1e9, 1),
+                    "hbm_frac": round(2 * problems * n * p / (ms * 1e-3) / 1e9 / hbm_peak, 4),
+                    "check": {"problems_checked": 8, "bad_elements": int(bad), "ok": bad == 0}}
+            del tin, tout
+        except Exception as err:  # noqa: BLE001 -- reported in the line; the headline stands
+            res[f"error_{dname}"] = f"{type(err).__name__}: {err}"
+    torch.cuda.empty_cache()
+    return res
+
+
 def rmsnorm_config3(torch, D, hbm_peak, reps=50):
     """bf16 [4096 x 4096] ~ N(0,1), w ~ N(1, 0.02), eps 1e-6, cluster 8 per row.
     The 64 MiB of traffic fits the 126 MB L2, so every launch must start from cold rows (the reference's
@@ -399,6 +455,14 @@ def cpu_extras(extras, p):
             extras["single_cluster"]["cpu_baseline"] = {
                 "value": round(d["seconds"] / d["problems"] * 1e9, 1), "unit": "ns per problem", "cores": 1,
                 "kind": "reference", "sample": "reference() of main.cu, N = 8, 16 KiB per CTA, 1 thread, ~2 s"}
+    if "config0_batch" in extras:
+        threads = os.cpu_count() or 1
+        v = reference_rate(16384, 3.0, threads)
+        if v is not None:
+            extras["config0_batch"]["cpu_baseline"] = {
+                "value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                "sample": f"reference() of main.cu (oracle/_ref build), N = 8, 16 KiB per CTA, f32, one problem per "
+                          f"thread, {threads} threads, ~3 s"}
     if "rmsnorm" in extras:
         x = orc.normal(1, 512 * 4096, 0, 0.0, 1.0).reshape(512, 4096)
         w = orc.normal(1, 4096, 1, 1.0, 0.02)
@@ -653,6 +717,7 @@ def run_ours(args, rank, world, local):
         extras["tp_allreduce_rmsnorm"] = tp_extras(torch, rank, world)
     if rank == 0 and not args.no_extras:
         extras["single_cluster"] = single_cluster_latency(torch, D)
+        extras["config0_batch"] = config0_batch(torch, D, hbm_peak)
         extras["rmsnorm"] = rmsnorm_config3(torch, D, hbm_peak)
         # ceilings beyond DSMEM and HBM (tcgen05 MMA, L2, shared memory), 1 / slope over two work amounts
         extras["ceilings_sm100"] = D.sm100_ceilings(reps=3)
