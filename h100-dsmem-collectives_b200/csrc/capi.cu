@@ -107,9 +107,9 @@ const std::vector<int> kDefaultOrder[kNumOps] = {
     {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_DIRECT_PULL, DSMEM_ALG_RECURSIVE_HALVING, DSMEM_ALG_RING},
     {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_DIRECT_PULL, DSMEM_ALG_SHIFT, DSMEM_ALG_PAIRWISE_XOR},
     {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_BINOMIAL, DSMEM_ALG_DIRECT_PULL},
-    {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_BINOMIAL, DSMEM_ALG_DIRECT_PULL},
-    {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_BINOMIAL, DSMEM_ALG_DIRECT_PULL},
-    {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_BINOMIAL, DSMEM_ALG_DIRECT_PULL},
+    {DSMEM_ALG_DIRECT_PULL, DSMEM_ALG_BINOMIAL, DSMEM_ALG_DIRECT_PUSH},   // reduce: the root's loads feed its sum
+    {DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_DIRECT_PULL, DSMEM_ALG_BINOMIAL},   // gather
+    {DSMEM_ALG_DIRECT_PULL, DSMEM_ALG_DIRECT_PUSH, DSMEM_ALG_BINOMIAL},   // scatter
 };
 
 constexpr size_t kErrWords = 4;
