@@ -21,6 +21,34 @@ def declared_functions(path):
     return sorted(set(re.findall(r"\b(dsmem_[a-z0-9_]+)\s*\(", text)))
 
 
+def test_header_compiles_as_c_and_cxx_and_links(dsmem, tmp_path):
+    """A C caller and a C++ caller that take the address of every declared entry point compile against
+    include/dsmem_b200.h (C99 and C++11, warnings as errors), link against lib/libdsmem_b200.so with unmangled
+    names, and load and run (no GPU call is made)."""
+    import os
+    import shutil
+    import subprocess
+
+    names = declared_functions(HEADER)
+    body = ",\n".join(f"        (fn)&{n}" for n in names)
+    src = ('#include "dsmem_b200.h"\n#include <stdio.h>\ntypedef void (*fn)(void);\nint main(void) {\n'
+           f"    fn table[] = {{\n{body}\n    }};\n"
+           '    printf("%d\\n", (int)(sizeof table / sizeof table[0]));\n    return 0;\n}\n')
+    libdir = str(dsmem.LIB_PATH.parent)
+    cuda_lib = "/usr/local/cuda/lib64"
+    for compiler, std, ext in (("gcc", "-std=c99", "c"), ("g++", "-std=c++11", "cpp")):
+        if shutil.which(compiler) is None:
+            pytest.skip(f"{compiler} not found")
+        path = tmp_path / f"abi.{ext}"
+        path.write_text(src)
+        exe = tmp_path / f"abi_{ext}"
+        subprocess.run([compiler, std, "-Wall", "-Wextra", "-Werror", f"-I{HEADER.parent}", str(path), "-o", str(exe),
+                        f"-L{libdir}", "-ldsmem_b200", f"-Wl,-rpath-link,{cuda_lib}"], check=True)
+        env = dict(os.environ, LD_LIBRARY_PATH=":".join([libdir, cuda_lib, os.environ.get("LD_LIBRARY_PATH", "")]))
+        out = subprocess.run([str(exe)], check=True, capture_output=True, text=True, env=env).stdout
+        assert int(out) == len(names)
+
+
 def test_library_exports_every_declared_symbol(dsmem):
     names = declared_functions(HEADER)
     assert len(names) >= 15
