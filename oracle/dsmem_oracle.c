@@ -150,7 +150,8 @@ size_t orc_out_elems(int op, int n, size_t m) {
  * REDUCE gives rank 0 the sum of the ranks' vectors, GATHER gives rank 0 the ranks' vectors in rank order, and
  * the other ranks' out blocks of both are not written by the collective (0 here: a test compares them with the
  * output's contents before the call); SCATTER gives rank b block b of rank 0's input. */
-void orc_reference(int op, int dtype, int n, size_t m, long long clusters, const void* in, double* ref) {
+static inline __attribute__((always_inline)) void reference_impl(int op, int dtype, int n, size_t m,
+                                                                 long long clusters, const void* in, double* ref) {
     const size_t ie = orc_in_elems(op, n, m), oe = orc_out_elems(op, n, m);
     for (long long c = 0; c < clusters; ++c) {
         const size_t ib = (size_t)c * n * ie, ob = (size_t)c * n * oe;
@@ -206,6 +207,38 @@ void orc_reference(int op, int dtype, int n, size_t m, long long clusters, const
             }
     }
 }
+
+/* One call per (op, element type, cluster size) with all three as constants, so the compiler specialises each
+ * loop nest (the per-element type switch and the op branch fold away, the rank loop unrolls); the arithmetic is
+ * the same in every case. */
+#define ORC_REF_N(OP, DT)                                                                            \
+    switch (n) {                                                                                     \
+        case 2: reference_impl(OP, DT, 2, m, clusters, in, ref); return;                             \
+        case 4: reference_impl(OP, DT, 4, m, clusters, in, ref); return;                             \
+        case 8: reference_impl(OP, DT, 8, m, clusters, in, ref); return;                             \
+        case 16: reference_impl(OP, DT, 16, m, clusters, in, ref); return;                           \
+        default: reference_impl(OP, DT, n, m, clusters, in, ref); return;                            \
+    }
+#define ORC_REF_DTYPES(OP)                                                                           \
+    switch (dtype) {                                                                                 \
+        case ORC_F32: ORC_REF_N(OP, ORC_F32)                                                         \
+        case ORC_BF16: ORC_REF_N(OP, ORC_BF16)                                                       \
+        default: ORC_REF_N(OP, ORC_I32)                                                              \
+    }
+void orc_reference(int op, int dtype, int n, size_t m, long long clusters, const void* in, double* ref) {
+    switch (op) {
+        case ORC_ALLREDUCE: ORC_REF_DTYPES(ORC_ALLREDUCE)
+        case ORC_ALLGATHER: ORC_REF_DTYPES(ORC_ALLGATHER)
+        case ORC_REDUCESCATTER: ORC_REF_DTYPES(ORC_REDUCESCATTER)
+        case ORC_BROADCAST: ORC_REF_DTYPES(ORC_BROADCAST)
+        case ORC_REDUCE: ORC_REF_DTYPES(ORC_REDUCE)
+        case ORC_GATHER: ORC_REF_DTYPES(ORC_GATHER)
+        case ORC_SCATTER: ORC_REF_DTYPES(ORC_SCATTER)
+        default: ORC_REF_DTYPES(ORC_ALLTOALL)
+    }
+}
+#undef ORC_REF_DTYPES
+#undef ORC_REF_N
 
 /* main.cu:156-173. */
 long long orc_check(int dtype, size_t n, const void* out, const double* ref, int mode, double tol, double* max_abs,
